@@ -1,0 +1,143 @@
+/*
+ * b4gemv.h -- C ABI of the B200 (sm_100a) fused 4-bit dequantisation GEMV.
+ *
+ * Drop-in for the GEMV path of QuantumDrizzy/int4-gemv.  The reference has no
+ * library: callers include src/kernels.cuh and launch its __global__ functions
+ * with <<<>>> on the legacy default stream (src/int4_gemv.cu:56-68).  Each
+ * entry point below replaces one of those kernels or host functions, named in
+ * its comment, over the SAME buffers: packed codes, fp16 scales / fp32 absmax,
+ * fp16 x and fp32 y have identical layouts, so reference-quantised weights drop
+ * straight in.
+ *
+ * Conventions
+ *   - Every buffer is owned by the caller.  Device pointers for the GEMV,
+ *     dequant and *_device entry points, host pointers for the host quantisers.
+ *   - Return value: a cudaError_t value (0 = cudaSuccess).  Bad shapes, null
+ *     pointers or an unusable config return cudaErrorInvalidValue (1) before
+ *     anything is launched; launch failures return the CUDA error.  Nothing
+ *     exits the process (the reference's CUDA_CHECK does, kernels.cuh:13-21).
+ *   - in_f must be a positive multiple of 128 (INT4) or 64 (NF4); the
+ *     reference silently drops a ragged tail (kernels.cuh:36,101), this ABI
+ *     rejects it.
+ *   - Work is enqueued on `stream` (NULL = legacy default stream) and returns
+ *     without synchronising.  No host-global mutable state: any host thread
+ *     may call on its own stream concurrently.
+ *   - Vector paths need 16-byte (or 8-byte) aligned codes and x; other
+ *     alignments fall back to 4-byte loads, never to the CPU.
+ */
+#ifndef B4GEMV_H
+#define B4GEMV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B4_GROUP 128     /* INT4 columns per fp16 scale   (kernels.cuh:12) */
+#define B4_NF4_BLOCK 64  /* NF4 columns per fp32 absmax   (kernels.cuh:85) */
+
+#define B4_FMT_INT4_G128 0
+#define B4_FMT_NF4_B64 1
+
+#define B4_ABI_VERSION 1
+
+/* Same type as cudaStream_t, spelled without the CUDA headers. */
+typedef struct CUstream_st* b4_stream_t;
+
+/* Launch geometry of the GEMV kernel.  b4_gemv_default_config() fills it with
+ * the dispatch rule's choice; b4_gemv_ex() takes any valid one (the sweeps
+ * that fit the rule use it).  One CTA holds warps_k * row_groups warps; warps
+ * that share a row group split in_f and reduce through shared memory. */
+typedef struct b4_gemv_config {
+    int vec_words;     /* packed words per lane load: 1, 2 or 4                */
+    int rows_per_warp; /* rows a warp accumulates at once: 1, 2, 4 or 8        */
+    int warps_k;       /* warps sharing one row group along in_f: 1..16        */
+    int row_groups;    /* row groups per CTA; warps_k * row_groups <= 16       */
+    int batch_tile;    /* batch rows per pass over the weights: 1, 2 or 4      */
+    int nf4_lut;       /* NF4 code-book lookup: 0 warp shuffle, 1 shared memory */
+    int x_tile;        /* columns of x staged in shared memory per pass, 0 = auto */
+    int flags;         /* B4_FLAG_* */
+} b4_gemv_config;
+
+/* Launch as a programmatic dependent of the previous kernel in the stream:
+ * the weight stream starts before the producer of x has finished. */
+#define B4_FLAG_PDL 1
+
+/* ---- GEMV: y[b][r] = sum_k dequant(W)[r][k] * x[b][k], b < m ----------------
+ * qw     : uint32 [out_f][in_f/8] packed codes
+ * scales : fp16   [out_f][in_f/128]        absmax : fp32 [out_f][in_f/64]
+ * x      : fp16   [m][in_f]                y      : fp32 [m][out_f]
+ * fp32 accumulation; y is within 1e-3 max relative error of a double GEMV
+ * over the dequantised weights (order of summation differs from the
+ * reference's, so y is not bit-identical to it). */
+
+/* Replaces int4_gemv_warp_per_row (kernels.cuh:26-30) and its launch
+ * (int4_gemv.cu:40-41,65-67); m > 1 is new. */
+int b4_gemv_int4_g128(const uint32_t* qw, const void* scales, const void* x, float* y,
+                      int in_f, int out_f, int m, b4_stream_t stream);
+
+/* Replaces nf4_gemv_warp_per_row (kernels.cuh:87-91), nf4_gemv_block_per_row
+ * (kernels.cuh:211-215) and the dispatch rule choosing between them
+ * (int4_gemv.cu:52-63); m > 1 is new. */
+int b4_gemv_nf4_b64(const uint32_t* qw, const float* absmax, const void* x, float* y,
+                    int in_f, int out_f, int m, b4_stream_t stream);
+
+/* The dispatch rule (int4_gemv.cu:52-53, refitted for 148 SMs): the config
+ * b4_gemv_int4_g128 / b4_gemv_nf4_b64 would use for this shape. */
+int b4_gemv_default_config(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg);
+
+/* Any format with an explicit config: the launch the reference's sweeps make
+ * by hand (diag_aspect.cu:54-56,253-256,262-266). */
+int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y,
+               int in_f, int out_f, int m, const b4_gemv_config* cfg, b4_stream_t stream);
+
+/* nf4_gemv_block_per_row (kernels.cuh:211-215) with its launch geometry
+ * <<<out_f, warps_per_block*32>>> (int4_gemv.cu:56-58): one CTA per row,
+ * warps_per_block (1..16) warps split in_f and reduce in shared memory. */
+int b4_gemv_nf4_b64_block_per_row(const uint32_t* qw, const float* absmax, const void* x,
+                                  float* y, int in_f, int out_f, int warps_per_block,
+                                  b4_stream_t stream);
+
+/* ---- Dequantisation: the W_dequant reconstruction, bit-exact --------------
+ * w_out fp32 [out_f][in_f] = (code-8)*float(scale) or NF4[code]*absmax: the
+ * `deq` output of quantise()/quantise_nf4() (kernels.cuh:290,331). */
+int b4_dequant_int4_g128(const uint32_t* qw, const void* scales, float* w_out,
+                         int in_f, int out_f, b4_stream_t stream);
+int b4_dequant_nf4_b64(const uint32_t* qw, const float* absmax, float* w_out,
+                       int in_f, int out_f, b4_stream_t stream);
+
+/* Unpacked codes, one byte per column: codes[r][k] = nibble k%8 of
+ * qw[r][k/8] (the packing of kernels.cuh:289,329).  in_f % 8 == 0. */
+int b4_unpack_codes(const uint32_t* qw, uint8_t* codes, int in_f, int out_f,
+                    b4_stream_t stream);
+
+/* ---- Quantisers -------------------------------------------------------------
+ * Host: quantise() (kernels.cuh:268-297) and quantise_nf4() (kernels.cuh:
+ * 308-339), byte-identical output, spread over `nthreads` host threads
+ * (<= 0: all online cores).  W fp32 [out_f][in_f]; scales fp16 bits; deq may
+ * be NULL. */
+int b4_quantise_int4_g128(const float* W, int out_f, int in_f, uint32_t* packed,
+                          uint16_t* scales, float* deq, int nthreads);
+int b4_quantise_nf4_b64(const float* W, int out_f, int in_f, uint32_t* packed,
+                        float* absmax, float* deq, int nthreads);
+
+/* Device: the same two quantisers on the GPU (IEEE division and rounding,
+ * byte-identical to the host ones).  Device pointers; deq may be NULL. */
+int b4_quantise_int4_g128_device(const float* W, int out_f, int in_f, uint32_t* packed,
+                                 void* scales, float* deq, b4_stream_t stream);
+int b4_quantise_nf4_b64_device(const float* W, int out_f, int in_f, uint32_t* packed,
+                               float* absmax, float* deq, b4_stream_t stream);
+
+/* ---- Misc -------------------------------------------------------------------
+ * One empty kernel launch: the empty-launch floor that bench/baseline.py:71-76
+ * measures (there with a 1x1 fp16 matmul) and that bounds the narrow shapes. */
+int b4_empty_launch(b4_stream_t stream);
+
+const char* b4_status_string(int status);
+int b4_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B4GEMV_H */

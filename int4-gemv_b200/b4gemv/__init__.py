@@ -1,0 +1,196 @@
+"""Python host side of the B200 fused 4-bit dequantisation GEMV.
+
+Thin wrappers over the C ABI (include/b4gemv.h, libb4gemv.so) that take torch
+tensors for device buffers and numpy arrays for host buffers.  Names and
+argument meaning follow the reference's host API (QuantumDrizzy/int4-gemv,
+src/kernels.cuh): ``quantise`` / ``quantise_nf4`` (kernels.cuh:270,308), the
+``GROUP`` / ``NF4_BLOCK`` constants (kernels.cuh:12,85) and one GEMV per
+format (kernels.cuh:26,87).  Every GPU call goes through the CUDA library;
+there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ._lib import (FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, B4Error,
+                   GemvConfig, check, load)
+
+__all__ = [
+    "GROUP", "NF4_BLOCK", "FMT_INT4_G128", "FMT_NF4_B64", "FLAG_PDL", "B4Error",
+    "GemvConfig", "load", "quantise", "quantise_nf4", "gemv_int4", "gemv_nf4", "gemv",
+    "gemv_nf4_block_per_row", "dequant_int4", "dequant_nf4", "unpack_codes",
+    "quantise_device", "quantise_nf4_device", "default_config", "median",
+]
+
+
+def _ptr(a) -> ctypes.c_void_p:
+    if isinstance(a, np.ndarray):
+        return ctypes.c_void_p(a.ctypes.data)
+    return ctypes.c_void_p(a.data_ptr())
+
+
+def _stream(stream=None) -> ctypes.c_void_p:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+# ---- host quantisers (kernels.cuh:268-339) ---------------------------------
+
+def quantise(W: np.ndarray, nthreads: int = 0):
+    """INT4 g128: returns (packed uint32 [out][in/8], scales fp16 [out][in/128],
+    deq fp32 [out][in]) byte-identical to the reference's quantise()."""
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    out_f, in_f = W.shape
+    packed = np.zeros((out_f, in_f // 8), np.uint32)
+    scales = np.zeros((out_f, max(in_f // GROUP, 1)), np.float16)
+    deq = np.zeros((out_f, in_f), np.float32)
+    check("b4_quantise_int4_g128",
+          load().b4_quantise_int4_g128(_ptr(W), out_f, in_f, _ptr(packed), _ptr(scales), _ptr(deq),
+                                       nthreads))
+    return packed, scales, deq
+
+
+def quantise_nf4(W: np.ndarray, nthreads: int = 0):
+    """NF4 b64: returns (packed uint32 [out][in/8], absmax fp32 [out][in/64],
+    deq fp32 [out][in]) byte-identical to the reference's quantise_nf4()."""
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    out_f, in_f = W.shape
+    packed = np.zeros((out_f, in_f // 8), np.uint32)
+    absmax = np.zeros((out_f, max(in_f // NF4_BLOCK, 1)), np.float32)
+    deq = np.zeros((out_f, in_f), np.float32)
+    check("b4_quantise_nf4_b64",
+          load().b4_quantise_nf4_b64(_ptr(W), out_f, in_f, _ptr(packed), _ptr(absmax), _ptr(deq),
+                                     nthreads))
+    return packed, absmax, deq
+
+
+def median(v):
+    """kernels.cuh:341-345: the upper median (element len/2 after sorting)."""
+    s = sorted(v)
+    return s[len(s) // 2]
+
+
+# ---- device quantisers -------------------------------------------------------
+
+def quantise_device(W, with_deq: bool = False, stream=None):
+    """INT4 g128 on the GPU.  W: float32 CUDA tensor [out][in].  Returns
+    (packed int32 [out][in/8], scales fp16 [out][in/128], deq or None)."""
+    import torch
+    assert W.is_cuda and W.dtype == torch.float32 and W.is_contiguous()
+    out_f, in_f = W.shape
+    packed = torch.empty((out_f, in_f // 8), dtype=torch.int32, device=W.device)
+    scales = torch.empty((out_f, max(in_f // GROUP, 1)), dtype=torch.float16, device=W.device)
+    deq = torch.empty_like(W) if with_deq else None
+    check("b4_quantise_int4_g128_device",
+          load().b4_quantise_int4_g128_device(_ptr(W), out_f, in_f, _ptr(packed), _ptr(scales),
+                                              _ptr(deq) if deq is not None else None,
+                                              _stream(stream)))
+    return packed, scales, deq
+
+
+def quantise_nf4_device(W, with_deq: bool = False, stream=None):
+    """NF4 b64 on the GPU.  Returns (packed int32, absmax fp32, deq or None)."""
+    import torch
+    assert W.is_cuda and W.dtype == torch.float32 and W.is_contiguous()
+    out_f, in_f = W.shape
+    packed = torch.empty((out_f, in_f // 8), dtype=torch.int32, device=W.device)
+    absmax = torch.empty((out_f, max(in_f // NF4_BLOCK, 1)), dtype=torch.float32, device=W.device)
+    deq = torch.empty_like(W) if with_deq else None
+    check("b4_quantise_nf4_b64_device",
+          load().b4_quantise_nf4_b64_device(_ptr(W), out_f, in_f, _ptr(packed), _ptr(absmax),
+                                            _ptr(deq) if deq is not None else None,
+                                            _stream(stream)))
+    return packed, absmax, deq
+
+
+# ---- GEMV ----------------------------------------------------------------------
+
+def default_config(fmt: int, in_f: int, out_f: int, m: int = 1) -> dict:
+    c = GemvConfig()
+    check("b4_gemv_default_config", load().b4_gemv_default_config(fmt, in_f, out_f, m, ctypes.byref(c)))
+    return c.as_dict()
+
+
+def _gemv_args(qw, scale, x, y):
+    import torch
+    assert qw.is_cuda and qw.dtype in (torch.int32, torch.uint32) and qw.is_contiguous()
+    out_f, words = qw.shape
+    in_f = words * 8
+    x2 = x.reshape(-1, in_f) if x.dim() != 2 else x
+    assert x2.dtype == torch.float16 and x2.is_contiguous() and x2.shape[1] == in_f
+    m = x2.shape[0]
+    if y is None:
+        y = torch.empty((m, out_f), dtype=torch.float32, device=qw.device)
+    assert y.dtype == torch.float32 and y.is_contiguous() and y.numel() == m * out_f
+    return out_f, in_f, m, x2, y
+
+
+def gemv(fmt: int, qw, scale, x, y=None, config: dict | None = None, stream=None):
+    """y[m][out] = dequant(qw, scale) @ x[m][in]^T through b4_gemv_ex."""
+    out_f, in_f, m, x2, y = _gemv_args(qw, scale, x, y)
+    cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
+    check("b4_gemv_ex", load().b4_gemv_ex(fmt, _ptr(qw), _ptr(scale), _ptr(x2), _ptr(y), in_f, out_f, m,
+                                          cfg, _stream(stream)))
+    return y
+
+
+def gemv_int4(qw, scales, x, y=None, stream=None):
+    """b4_gemv_int4_g128: the INT4 g128 GEMV with the dispatch rule's config."""
+    out_f, in_f, m, x2, y = _gemv_args(qw, scales, x, y)
+    check("b4_gemv_int4_g128", load().b4_gemv_int4_g128(_ptr(qw), _ptr(scales), _ptr(x2), _ptr(y), in_f,
+                                                        out_f, m, _stream(stream)))
+    return y
+
+
+def gemv_nf4(qw, absmax, x, y=None, stream=None):
+    """b4_gemv_nf4_b64: the NF4 b64 GEMV with the dispatch rule's config."""
+    out_f, in_f, m, x2, y = _gemv_args(qw, absmax, x, y)
+    check("b4_gemv_nf4_b64", load().b4_gemv_nf4_b64(_ptr(qw), _ptr(absmax), _ptr(x2), _ptr(y), in_f,
+                                                    out_f, m, _stream(stream)))
+    return y
+
+
+def gemv_nf4_block_per_row(qw, absmax, x, warps_per_block: int, y=None, stream=None):
+    out_f, in_f, m, x2, y = _gemv_args(qw, absmax, x, y)
+    assert m == 1
+    check("b4_gemv_nf4_b64_block_per_row",
+          load().b4_gemv_nf4_b64_block_per_row(_ptr(qw), _ptr(absmax), _ptr(x2), _ptr(y), in_f, out_f,
+                                               warps_per_block, _stream(stream)))
+    return y
+
+
+# ---- bit-exact format helpers -------------------------------------------------
+
+def dequant_int4(qw, scales, out=None, stream=None):
+    import torch
+    out_f, words = qw.shape
+    in_f = words * 8
+    if out is None:
+        out = torch.empty((out_f, in_f), dtype=torch.float32, device=qw.device)
+    check("b4_dequant_int4_g128", load().b4_dequant_int4_g128(_ptr(qw), _ptr(scales), _ptr(out), in_f, out_f,
+                                                              _stream(stream)))
+    return out
+
+
+def dequant_nf4(qw, absmax, out=None, stream=None):
+    import torch
+    out_f, words = qw.shape
+    in_f = words * 8
+    if out is None:
+        out = torch.empty((out_f, in_f), dtype=torch.float32, device=qw.device)
+    check("b4_dequant_nf4_b64", load().b4_dequant_nf4_b64(_ptr(qw), _ptr(absmax), _ptr(out), in_f, out_f,
+                                                          _stream(stream)))
+    return out
+
+
+def unpack_codes(qw, out=None, stream=None):
+    import torch
+    out_f, words = qw.shape
+    in_f = words * 8
+    if out is None:
+        out = torch.empty((out_f, in_f), dtype=torch.uint8, device=qw.device)
+    check("b4_unpack_codes", load().b4_unpack_codes(_ptr(qw), _ptr(out), in_f, out_f, _stream(stream)))
+    return out

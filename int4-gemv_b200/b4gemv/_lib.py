@@ -1,0 +1,101 @@
+"""ctypes binding of libb4gemv.so, the C ABI declared in include/b4gemv.h.
+
+The library is built in-tree (``make -C int4-gemv_b200``) and loaded from
+``int4-gemv_b200/lib/libb4gemv.so``.  There is no fallback: if the library is
+missing, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_ROOT, "lib", "libb4gemv.so")
+
+FMT_INT4_G128 = 0
+FMT_NF4_B64 = 1
+GROUP = 128
+NF4_BLOCK = 64
+FLAG_PDL = 1
+
+
+class GemvConfig(ctypes.Structure):
+    """b4_gemv_config (include/b4gemv.h)."""
+
+    _fields_ = [
+        ("vec_words", ctypes.c_int),
+        ("rows_per_warp", ctypes.c_int),
+        ("warps_k", ctypes.c_int),
+        ("row_groups", ctypes.c_int),
+        ("batch_tile", ctypes.c_int),
+        ("nf4_lut", ctypes.c_int),
+        ("x_tile", ctypes.c_int),
+        ("flags", ctypes.c_int),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "GemvConfig":
+        c = cls()
+        for name, _ in cls._fields_:
+            setattr(c, name, int(d.get(name, 0)))
+        return c
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+
+# name -> (restype, argtypes); every symbol of include/b4gemv.h
+SIGNATURES = {
+    "b4_gemv_int4_g128": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "b4_gemv_nf4_b64": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "b4_gemv_default_config": (_I, [_I, _I, _I, _I, ctypes.POINTER(GemvConfig)]),
+    "b4_gemv_ex": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P]),
+    "b4_gemv_nf4_b64_block_per_row": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "b4_dequant_int4_g128": (_I, [_P, _P, _P, _I, _I, _P]),
+    "b4_dequant_nf4_b64": (_I, [_P, _P, _P, _I, _I, _P]),
+    "b4_unpack_codes": (_I, [_P, _P, _I, _I, _P]),
+    "b4_quantise_int4_g128": (_I, [_P, _I, _I, _P, _P, _P, _I]),
+    "b4_quantise_nf4_b64": (_I, [_P, _I, _I, _P, _P, _P, _I]),
+    "b4_quantise_int4_g128_device": (_I, [_P, _I, _I, _P, _P, _P, _P]),
+    "b4_quantise_nf4_b64_device": (_I, [_P, _I, _I, _P, _P, _P, _P]),
+    "b4_empty_launch": (_I, [_P]),
+    "b4_status_string": (ctypes.c_char_p, [_I]),
+    "b4_abi_version": (_I, []),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads (once) and returns libb4gemv.so with every signature declared."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build the CUDA library first "
+            "(make -C int4-gemv_b200, or __graft_entry__.build())")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class B4Error(RuntimeError):
+    """A non-zero status (a cudaError_t value) from the C ABI."""
+
+    def __init__(self, fn: str, status: int):
+        msg = load().b4_status_string(status)
+        super().__init__(f"{fn} failed: status {status} ({msg.decode() if msg else '?'})")
+        self.status = status
+
+
+def check(fn: str, status: int) -> None:
+    if status != 0:
+        raise B4Error(fn, status)

@@ -1,0 +1,141 @@
+// b4_common.cuh -- formats and device helpers shared by the sm_100a kernels.
+//
+// Weight formats (byte-identical to QuantumDrizzy/int4-gemv, src/kernels.cuh):
+//   packed codes : uint32 [out_f][in_f/8]; column k is nibble k%8 of word k/8,
+//                  low nibble first                          (kernels.cuh:289)
+//   INT4 g128    : fp16 scale [out_f][in_f/128], w = (code-8) * scale
+//                                                     (kernels.cuh:12,50,282)
+//   NF4  b64     : fp32 absmax [out_f][in_f/64],  w = NF4[code] * absmax
+//                                                  (kernels.cuh:78-85,121,322)
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace b4 {
+
+constexpr int kGroup = 128;     // INT4 columns per fp16 scale
+constexpr int kNf4Block = 64;   // NF4 columns per fp32 absmax
+
+enum Format : int { kInt4 = 0, kNf4 = 1 };
+
+// The canonical 16-entry NormalFloat table (the bitsandbytes NF4 code book),
+// the same 16 float literals as kernels.cuh:78-83.
+#define B4_NF4_VALUES                                                          \
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f, \
+        -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f,  \
+        0.0f, 0.07958029955625534f, 0.16093020141124725f,                     \
+        0.24611230194568634f, 0.33791524171829224f, 0.44070982933044434f,     \
+        0.5626170039176941f, 0.7229568362236023f, 1.0f
+
+// One copy per translation unit (no relocatable device code).
+static __constant__ float c_nf4_table[16] = {B4_NF4_VALUES};
+
+// ---- global loads -----------------------------------------------------------
+// Packed codes are read exactly once per GEMV: non-coherent path, no L1
+// allocation, so they do not evict x, scales or the reduction scratch.
+template <int VW>
+struct WordVec;
+template <>
+struct WordVec<1> { uint32_t w[1]; };
+template <>
+struct WordVec<2> { uint32_t w[2]; };
+template <>
+struct WordVec<4> { uint32_t w[4]; };
+
+template <int VW>
+__device__ __forceinline__ WordVec<VW> ld_stream(const uint32_t* p);
+
+template <>
+__device__ __forceinline__ WordVec<1> ld_stream<1>(const uint32_t* p)
+{
+    WordVec<1> v;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v.w[0]) : "l"(p));
+    return v;
+}
+template <>
+__device__ __forceinline__ WordVec<2> ld_stream<2>(const uint32_t* p)
+{
+    WordVec<2> v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+        : "=r"(v.w[0]), "=r"(v.w[1]) : "l"(p));
+    return v;
+}
+template <>
+__device__ __forceinline__ WordVec<4> ld_stream<4>(const uint32_t* p)
+{
+    WordVec<4> v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]) : "l"(p));
+    return v;
+}
+
+// ---- INT4 decode ------------------------------------------------------------
+// One LOP3 turns two nibbles into two exact fp16 integers: OR-ing a nibble into
+// the mantissa of 1024.0 (0x6400) gives 1024+n, into bits 4..7 of the mantissa
+// of 64.0 (0x5400) gives 64+n.  One HSUB2 then yields code-8 exactly (all
+// values are small integers).  For a word w with nibbles n0..n7 this returns
+//   h[0] = (n0-8, n4-8)   h[1] = (n1-8, n5-8)
+//   h[2] = (n2-8, n6-8)   h[3] = (n3-8, n7-8)
+// as half2 (low half first).  x is staged in the matching pair order.
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic)
+{
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(a), "r"(mask), "r"(magic));
+    return r;  // (a & mask) | magic
+}
+
+__device__ __forceinline__ void int4_word_to_half2(uint32_t w, uint32_t h[4])
+{
+    const uint32_t w8 = w >> 8;
+    const uint32_t t0 = lop3_and_or(w, 0x000f000fu, 0x64006400u);
+    const uint32_t t1 = lop3_and_or(w, 0x00f000f0u, 0x54005400u);
+    const uint32_t t2 = lop3_and_or(w8, 0x000f000fu, 0x64006400u);
+    const uint32_t t3 = lop3_and_or(w8, 0x00f000f0u, 0x54005400u);
+    // 1032 = 0x6408, 72 = 0x5480 in fp16
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[0]) : "r"(t0), "r"(0x64086408u));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[1]) : "r"(t1), "r"(0x54805480u));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2]) : "r"(t2), "r"(0x64086408u));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[3]) : "r"(t3), "r"(0x54805480u));
+}
+
+// Two fp32 accumulations from fp16 pairs with one rounding each (sm_100
+// mixed-precision FMA): acc_lo += a.lo*b.lo, acc_hi += a.hi*b.hi.
+__device__ __forceinline__ void fma2_f32_f16(float& acc_lo, float& acc_hi, uint32_t a, uint32_t b)
+{
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %2;\n\t"
+        "mov.b32 {bl, bh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.f16 %1, ah, bh, %1;\n\t}"
+        : "+f"(acc_lo), "+f"(acc_hi)
+        : "r"(a), "r"(b));
+}
+
+// Reorders the 8 fp16 values of one word's columns, x0..x7 held as four
+// half2 (x0,x1)(x2,x3)(x4,x5)(x6,x7), into the decode's pair order
+// (x0,x4)(x1,x5)(x2,x6)(x3,x7).
+__device__ __forceinline__ uint4 int4_pair_order(uint4 v)
+{
+    uint4 r;
+    r.x = __byte_perm(v.x, v.z, 0x5410);  // x0, x4
+    r.y = __byte_perm(v.x, v.z, 0x7632);  // x1, x5
+    r.z = __byte_perm(v.y, v.w, 0x5410);  // x2, x6
+    r.w = __byte_perm(v.y, v.w, 0x7632);  // x3, x7
+    return r;
+}
+
+// ---- NF4 decode ---------------------------------------------------------------
+// Warp-register code book: lane L holds NF4[L & 15]; a shuffle with the packed
+// word shifted right by 4k as the source lane reads NF4[nibble k], since the
+// shuffle uses only the low 5 bits of the lane index and lanes 16..31 mirror
+// lanes 0..15.
+__device__ __forceinline__ float nf4_lane_value(int lane) { return c_nf4_table[lane & 15]; }
+
+__device__ __forceinline__ float nf4_lookup_shfl(float lut, uint32_t idx)
+{
+    return __shfl_sync(0xffffffffu, lut, (int)idx);
+}
+
+}  // namespace b4

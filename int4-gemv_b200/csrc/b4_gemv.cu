@@ -1,0 +1,261 @@
+// b4_gemv.cu -- host side of the GEMV: shape checks, the dispatch rule and the
+// launch of b4_gemv_kernel, behind the extern "C" entry points of b4gemv.h.
+#include <algorithm>
+#include <atomic>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "b4_gemv_kernel.cuh"
+#include "b4_internal.h"
+
+namespace b4 {
+
+namespace {
+
+constexpr int kMaxWarps = 16;
+
+bool aligned(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+void* pick_kernel(int fmt, int vw, int rw, int mb, int lut)
+{
+    if (fmt == kInt4) {
+        if (lut != 0) return nullptr;
+        switch (vw) {
+            case 1: return gemv_kernel_int4_v1(rw, mb, 0);
+            case 2: return gemv_kernel_int4_v2(rw, mb, 0);
+            case 4: return gemv_kernel_int4_v4(rw, mb, 0);
+        }
+    } else {
+        switch (vw) {
+            case 1: return gemv_kernel_nf4_v1(rw, mb, lut);
+            case 2: return gemv_kernel_nf4_v2(rw, mb, lut);
+            case 4: return gemv_kernel_nf4_v4(rw, mb, lut);
+        }
+    }
+    return nullptr;
+}
+
+// Raises a kernel's dynamic shared-memory limit on the current device once
+// per (kernel, device, size).  The cache is the only host-side state of the
+// library; it is guarded by a mutex and changes no result, so concurrent
+// callers stay safe, and a launch inside stream capture makes no attribute
+// call after the first eager launch of the same kernel and size.
+cudaError_t ensure_smem(const void* fn, int dev, size_t smem)
+{
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> done;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& have = done[{fn, dev}];
+    if (have >= smem) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) have = smem;
+    return e;
+}
+
+__global__ void empty_kernel() {}
+
+// Largest shared-memory footprint the dispatch rule aims for, so that two
+// CTAs fit on one SM.
+constexpr int kSmemBudget = 96 * 1024;
+
+}  // namespace
+
+int check_problem(const GemvProblem& p)
+{
+    if (p.fmt != kInt4 && p.fmt != kNf4) return cudaErrorInvalidValue;
+    if (!p.qw || !p.scale || !p.x || !p.y) return cudaErrorInvalidValue;
+    if (p.in_f <= 0 || p.out_f <= 0 || p.m <= 0) return cudaErrorInvalidValue;
+    const int unit = p.fmt == kInt4 ? kGroup : kNf4Block;
+    if (p.in_f % unit) return cudaErrorInvalidValue;
+    if (p.x_ld < p.in_f || p.y_ld < p.out_f) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 4) || !aligned(p.y, 4) || !aligned(p.x, 2)) return cudaErrorInvalidValue;
+    if (!aligned(p.scale, p.fmt == kInt4 ? 2 : 4)) return cudaErrorInvalidValue;
+    return cudaSuccess;
+}
+
+void default_config(const GemvProblem& p, b4_gemv_config* cfg)
+{
+    const int words = p.in_f / 8;
+    int vw = 1;
+    if (aligned(p.qw, 16) && words % 4 == 0) vw = 4;
+    else if (aligned(p.qw, 8) && words % 2 == 0) vw = 2;
+    const int chunks = words / vw;
+
+    int mb = p.m >= 4 ? 4 : (p.m >= 2 ? 2 : 1);
+    if (vw == 1) mb = 1;
+
+    const int sms = 148;  // the rule is fitted to B200; it stays valid elsewhere
+    int rw = 4;
+    if ((p.out_f + rw - 1) / rw < sms * 8) rw = 2;
+    if ((p.out_f + rw - 1) / rw < sms * 8) rw = 1;
+    if (vw == 1) rw = rw >= 4 ? 4 : 1;
+    if (mb == 4 && rw == 8) rw = 4;
+
+    const int groups = (p.out_f + rw - 1) / rw;
+    int kw = 1;
+    while (kw < 8 && (long long)groups * kw < sms * 16LL && chunks >= 32 * kw * 2) kw *= 2;
+    int rg = std::max(1, 8 / kw);
+
+    cfg->vec_words = vw;
+    cfg->rows_per_warp = rw;
+    cfg->warps_k = kw;
+    cfg->row_groups = rg;
+    cfg->batch_tile = mb;
+    cfg->nf4_lut = 0;
+    cfg->x_tile = 0;
+    cfg->flags = 0;
+}
+
+int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    const int vw = c.vec_words, rw = c.rows_per_warp, kw = c.warps_k, rg = c.row_groups;
+    const int mb = c.batch_tile, lut = c.nf4_lut;
+    if (kw < 1 || kw > kMaxWarps || rg < 1 || kw * rg > kMaxWarps) return cudaErrorInvalidValue;
+    // 16-warp CTAs exist only for the single-row, single-batch variants
+    // (MaxThreads in b4_gemv_kernel.cuh).
+    if ((rw > 1 || mb > 1) && kw * rg > 8) return cudaErrorInvalidValue;
+    const int words = p.in_f / 8;
+    if (vw != 1 && vw != 2 && vw != 4) return cudaErrorInvalidValue;
+    if (words % vw) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 4u * vw)) return cudaErrorInvalidValue;
+    void* fn = pick_kernel(p.fmt, vw, rw, mb, lut);
+    if (!fn) return cudaErrorInvalidValue;
+
+    const int chunks = words / vw;
+    const int S = p.fmt == kInt4 ? vw : 2 * vw;
+    const int cols_per_chunk = 8 * vw;
+    int tile_chunks;
+    if (c.x_tile > 0) {
+        if (c.x_tile % cols_per_chunk) return cudaErrorInvalidValue;
+        tile_chunks = std::min(chunks, c.x_tile / cols_per_chunk);
+    } else {
+        const int budget_chunks = kSmemBudget / (mb * S * 16);
+        tile_chunks = std::min(chunks, std::max(32 * kw, budget_chunks / (32 * kw) * (32 * kw)));
+    }
+    if (tile_chunks < 1) return cudaErrorInvalidValue;
+
+    const size_t smem = (size_t)mb * tile_chunks * S * 16 + (size_t)rg * kw * mb * rw * 4 + 64;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int smem_max = 0;
+    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (smem > (size_t)smem_max) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        e = ensure_smem(fn, dev, smem);
+        if (e != cudaSuccess) return e;
+    }
+
+    KParams kp;
+    kp.qw = p.qw;
+    kp.scale = p.scale;
+    kp.x = static_cast<const __half*>(p.x);
+    kp.y = p.y;
+    kp.in_f = p.in_f;
+    kp.out_f = p.out_f;
+    kp.m = p.m;
+    kp.x_ld = p.x_ld;
+    kp.y_ld = p.y_ld;
+    kp.kw = kw;
+    kp.rg = rg;
+    kp.tile_chunks = tile_chunks;
+    const unsigned xa = p.fmt == kInt4 ? 16u : 8u;
+    kp.x_vec = aligned(p.x, xa) && ((p.x_ld * 2) % xa == 0);
+
+    const long long rows_per_cta = (long long)rg * rw;
+    long long grid = (p.out_f + rows_per_cta - 1) / rows_per_cta;
+    if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)grid);
+    lc.blockDim = dim3(32 * kw * rg);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (c.flags & B4_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+    }
+    void* args[] = {&kp};
+    e = cudaLaunchKernelExC(&lc, fn, args);
+    return e;
+}
+
+}  // namespace b4
+
+using namespace b4;
+
+extern "C" {
+
+int b4_gemv_default_config(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg)
+{
+    if (!cfg) return cudaErrorInvalidValue;
+    GemvProblem p{fmt, reinterpret_cast<const uint32_t*>(256), reinterpret_cast<const void*>(256),
+                  reinterpret_cast<const void*>(256), reinterpret_cast<float*>(256),
+                  in_f, out_f, m, in_f, out_f};
+    const int e = check_problem(p);
+    if (e != cudaSuccess) return e;
+    default_config(p, cfg);
+    return cudaSuccess;
+}
+
+int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y,
+               int in_f, int out_f, int m, const b4_gemv_config* cfg, b4_stream_t stream)
+{
+    GemvProblem p{fmt, qw, scale, x, y, in_f, out_f, m, in_f, out_f};
+    int e = check_problem(p);
+    if (e != cudaSuccess) return e;
+    b4_gemv_config c;
+    if (cfg) c = *cfg;
+    else default_config(p, &c);
+    return launch_gemv(p, c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int b4_gemv_int4_g128(const uint32_t* qw, const void* scales, const void* x, float* y,
+                      int in_f, int out_f, int m, b4_stream_t stream)
+{
+    return b4_gemv_ex(kInt4, qw, scales, x, y, in_f, out_f, m, nullptr, stream);
+}
+
+int b4_gemv_nf4_b64(const uint32_t* qw, const float* absmax, const void* x, float* y,
+                    int in_f, int out_f, int m, b4_stream_t stream)
+{
+    return b4_gemv_ex(kNf4, qw, absmax, x, y, in_f, out_f, m, nullptr, stream);
+}
+
+int b4_gemv_nf4_b64_block_per_row(const uint32_t* qw, const float* absmax, const void* x,
+                                  float* y, int in_f, int out_f, int warps_per_block,
+                                  b4_stream_t stream)
+{
+    if (warps_per_block < 1 || warps_per_block > kMaxWarps) return cudaErrorInvalidValue;
+    GemvProblem p{kNf4, qw, absmax, x, y, in_f, out_f, 1, in_f, out_f};
+    int e = check_problem(p);
+    if (e != cudaSuccess) return e;
+    b4_gemv_config c;
+    default_config(p, &c);
+    c.rows_per_warp = 1;
+    c.warps_k = warps_per_block;
+    c.row_groups = 1;
+    c.batch_tile = 1;
+    if (c.vec_words == 1) c.rows_per_warp = 1;
+    return launch_gemv(p, c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int b4_empty_launch(b4_stream_t stream)
+{
+    empty_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>();
+    return cudaGetLastError();
+}
+
+const char* b4_status_string(int status)
+{
+    return cudaGetErrorString(static_cast<cudaError_t>(status));
+}
+
+int b4_abi_version(void) { return B4_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,32 @@
+// b4_internal.h -- host-side interfaces between the C-ABI layer and the kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/b4gemv.h"
+
+namespace b4 {
+
+// Everything one GEMV launch needs.  Pointers are device (or managed) memory.
+struct GemvProblem {
+    int fmt;              // kInt4 / kNf4
+    const uint32_t* qw;   // [out_f][in_f/8]
+    const void* scale;    // INT4: __half [out_f][in_f/128]; NF4: float [out_f][in_f/64]
+    const void* x;        // __half [m][x_ld]
+    float* y;             // float [m][y_ld]
+    int in_f, out_f, m;
+    long long x_ld, y_ld; // leading dimensions (elements) of the batch rows
+};
+
+// Shape checks shared by every entry point: returns cudaSuccess or
+// cudaErrorInvalidValue.
+int check_problem(const GemvProblem& p);
+
+// Fills cfg with the dispatch rule's choice for this problem.
+void default_config(const GemvProblem& p, b4_gemv_config* cfg);
+
+// Validates cfg against p (and the pointer alignment it needs) and launches.
+int launch_gemv(const GemvProblem& p, const b4_gemv_config& cfg, cudaStream_t st);
+
+}  // namespace b4

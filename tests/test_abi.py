@@ -1,0 +1,102 @@
+"""The C ABI library on a machine without a GPU: it loads, exports every
+symbol include/b4gemv.h declares, and its host-only logic (shape checks, the
+dispatch rule, the host quantisers) works."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import b4gemv
+from b4gemv import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+QWEN = [(3584, 3584), (512, 3584), (18944, 3584), (3584, 18944)]
+LLAMA_TP = [(8192, 8192), (1024, 8192), (28672, 8192), (8192, 28672), (1024, 1024), (128, 8192), (8192, 3584),
+            (3584, 8192)]
+
+
+def declared_symbols():
+    text = open(os.path.join(ROOT, "include", "b4gemv.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(b4_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = b4gemv.load()
+    syms = declared_symbols()
+    assert len(syms) >= 14
+    for s in syms:
+        assert hasattr(lib, s), s
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+    assert lib.b4_abi_version() == 1
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("out_f,in_f", QWEN + LLAMA_TP)
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 8, 16])
+def test_default_config_is_valid(fmt, out_f, in_f, m):
+    c = b4gemv.default_config(fmt, in_f, out_f, m)
+    assert c["vec_words"] in (1, 2, 4) and (in_f // 8) % c["vec_words"] == 0
+    assert c["rows_per_warp"] in (1, 2, 4, 8)
+    assert c["batch_tile"] in (1, 2, 4)
+    assert 1 <= c["warps_k"] * c["row_groups"] <= (16 if c["rows_per_warp"] * c["batch_tile"] == 1 else 8)
+
+
+def test_invalid_shapes_are_rejected_before_any_launch():
+    lib = b4gemv.load()
+    bogus = ctypes.c_void_p(4096)
+    inv = 1  # cudaErrorInvalidValue
+    # in_f not a multiple of the group / block
+    assert lib.b4_gemv_int4_g128(bogus, bogus, bogus, bogus, 100, 8, 1, None) == inv
+    assert lib.b4_gemv_int4_g128(bogus, bogus, bogus, bogus, 64, 8, 1, None) == inv
+    assert lib.b4_gemv_nf4_b64(bogus, bogus, bogus, bogus, 96, 8, 1, None) == inv
+    # empty / negative sizes, null pointers
+    assert lib.b4_gemv_nf4_b64(bogus, bogus, bogus, bogus, 64, 0, 1, None) == inv
+    assert lib.b4_gemv_nf4_b64(bogus, bogus, bogus, bogus, 64, 8, 0, None) == inv
+    assert lib.b4_gemv_nf4_b64(None, bogus, bogus, bogus, 64, 8, 1, None) == inv
+    # misaligned packed words (the reference assumes 4-byte alignment)
+    assert lib.b4_gemv_nf4_b64(ctypes.c_void_p(4098), bogus, bogus, bogus, 64, 8, 1, None) == inv
+    # a config the kernel set does not contain
+    cfg = _lib.GemvConfig(vec_words=3, rows_per_warp=1, warps_k=1, row_groups=1, batch_tile=1)
+    assert lib.b4_gemv_ex(1, bogus, bogus, bogus, bogus, 64, 8, 1, ctypes.byref(cfg), None) == inv
+    assert lib.b4_dequant_int4_g128(bogus, bogus, bogus, 96, 8, None) == inv
+    assert lib.b4_unpack_codes(bogus, bogus, 12, 8, None) == inv
+    assert lib.b4_quantise_nf4_b64_device(bogus, 8, 100, bogus, bogus, None, None) == inv
+    assert lib.b4_status_string(1).decode() != ""
+
+
+def test_host_quantisers_match_reference_fixtures(golden):
+    for name, g in golden.items():
+        for nthreads in (1, 3):
+            p, s, d = b4gemv.quantise(g["W"], nthreads=nthreads)
+            assert p.tobytes() == g["int4_packed"].tobytes(), name
+            assert s.view(np.uint16).tobytes() == g["int4_scales"].tobytes(), name
+            assert d.tobytes() == g["int4_deq"].tobytes(), name
+            pn, a, dn = b4gemv.quantise_nf4(g["W"], nthreads=nthreads)
+            assert pn.tobytes() == g["nf4_packed"].tobytes(), name
+            assert a.tobytes() == g["nf4_absmax"].tobytes(), name
+            assert dn.tobytes() == g["nf4_deq"].tobytes(), name
+
+
+def test_host_quantisers_match_oracle_random(oracle):
+    rng = np.random.default_rng(3)
+    for t in range(6):
+        o, n = int(rng.integers(1, 40)), 128 * int(rng.integers(1, 9))
+        W = (rng.standard_normal((o, n)) * 10 ** rng.uniform(-8, 5)).astype(np.float32)
+        W.flat[rng.integers(0, W.size, 3)] = [np.nan, np.inf, 0.0]
+        p, s, d = b4gemv.quantise(W)
+        op, os_, od = oracle.quantise(W)
+        assert p.tobytes() == op.tobytes() and s.view(np.uint16).tobytes() == os_.tobytes()
+        assert d.tobytes() == od.tobytes()
+        pn, a, dn = b4gemv.quantise_nf4(W)
+        opn, oa, odn = oracle.quantise_nf4(W)
+        assert pn.tobytes() == opn.tobytes() and a.tobytes() == oa.tobytes() and dn.tobytes() == odn.tobytes()
+
+
+def test_median_is_the_reference_upper_median():
+    assert b4gemv.median([3.0, 1.0, 2.0, 4.0]) == 3.0
+    assert b4gemv.median([5.0]) == 5.0

@@ -1,0 +1,244 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle, through the C ABI.
+
+Bars: packed codes, dequantised values and the W_dequant reconstruction are
+bit-exact; y is within TOL max relative error (max|y-ref| / max|ref|, the
+metric of int4_gemv.cu:74-81) of a double-precision GEMV over the same
+dequantised weights and fp16 x.
+"""
+from __future__ import annotations
+
+import itertools
+
+import numpy as np
+import pytest
+
+import b4gemv
+from oracle_py import rel_err
+
+TOL = 1e-3
+pytestmark = pytest.mark.gpu
+
+QWEN = {"q_proj": (3584, 3584), "k_proj": (512, 3584), "v_proj": (512, 3584), "o_proj": (3584, 3584),
+        "gate_proj": (18944, 3584), "up_proj": (18944, 3584), "down_proj": (3584, 18944)}
+
+
+def to_dev(a, dev):
+    import torch
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    if a.dtype == np.uint16:
+        a = a.view(np.float16)
+    return torch.from_numpy(a).to(dev)
+
+
+def quantised(fmt, W, dev):
+    """Host-quantised weights on the device: (qw, scale)."""
+    if fmt == 0:
+        p, s, _ = b4gemv.quantise(W)
+        return to_dev(p, dev), to_dev(s, dev)
+    p, a, _ = b4gemv.quantise_nf4(W)
+    return to_dev(p, dev), to_dev(a, dev)
+
+
+def f64_ref(oracle, fmt, qw, scale, X):
+    p = qw.cpu().numpy().view(np.uint32)
+    s = scale.cpu().numpy()
+    return oracle.gemv_f64(fmt == 1, p, s.view(np.uint16) if fmt == 0 else s, X)
+
+
+def rand_problem(rng, out_f, in_f, m=1):
+    W = (rng.standard_normal((out_f, in_f)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((m, in_f)).astype(np.float16)
+    return W, X
+
+
+# ---- bit-exact format kernels ---------------------------------------------------
+
+@pytest.mark.parametrize("case", ["kat_glibc", "gauss_33x384", "gauss_5x640", "edge"])
+def test_device_quantiser_dequant_and_codes_bit_exact(cuda, golden, oracle, case):
+    import torch
+    g = golden[case]
+    W = torch.from_numpy(g["W"]).to(cuda)
+    p, s, d = b4gemv.quantise_device(W, with_deq=True)
+    pn, a, dn = b4gemv.quantise_nf4_device(W, with_deq=True)
+    torch.cuda.synchronize()
+    assert p.cpu().numpy().view(np.uint32).tobytes() == g["int4_packed"].tobytes()
+    assert s.cpu().numpy().view(np.uint16).tobytes() == g["int4_scales"].tobytes()
+    assert d.cpu().numpy().tobytes() == g["int4_deq"].tobytes()
+    assert pn.cpu().numpy().view(np.uint32).tobytes() == g["nf4_packed"].tobytes()
+    assert a.cpu().numpy().tobytes() == g["nf4_absmax"].tobytes()
+    assert dn.cpu().numpy().tobytes() == g["nf4_deq"].tobytes()
+    # W_dequant reconstruction and unpacked codes from the reference's buffers
+    qw = to_dev(g["int4_packed"], cuda)
+    assert b4gemv.dequant_int4(qw, to_dev(g["int4_scales"], cuda)).cpu().numpy().tobytes() == g["int4_deq"].tobytes()
+    qn = to_dev(g["nf4_packed"], cuda)
+    assert b4gemv.dequant_nf4(qn, to_dev(g["nf4_absmax"], cuda)).cpu().numpy().tobytes() == g["nf4_deq"].tobytes()
+    in_f = g["W"].shape[1]
+    assert np.array_equal(b4gemv.unpack_codes(qw).cpu().numpy(), oracle.unpack(g["int4_packed"], in_f))
+
+
+def test_device_quantiser_bit_exact_at_qwen_size(cuda):
+    import torch
+    rng = np.random.default_rng(11)
+    for out_f, in_f in [(512, 3584), (256, 18944)]:
+        W = (rng.standard_normal((out_f, in_f)) * 0.02).astype(np.float32)
+        p, s, d = b4gemv.quantise(W)
+        pn, a, dn = b4gemv.quantise_nf4(W)
+        Wd = torch.from_numpy(W).to(cuda)
+        gp, gs, gd = b4gemv.quantise_device(Wd, with_deq=True)
+        gpn, ga, gdn = b4gemv.quantise_nf4_device(Wd, with_deq=True)
+        assert gp.cpu().numpy().view(np.uint32).tobytes() == p.tobytes()
+        assert gs.cpu().numpy().tobytes() == s.tobytes() and gd.cpu().numpy().tobytes() == d.tobytes()
+        assert gpn.cpu().numpy().view(np.uint32).tobytes() == pn.tobytes()
+        assert ga.cpu().numpy().tobytes() == a.tobytes() and gdn.cpu().numpy().tobytes() == dn.tobytes()
+        assert b4gemv.dequant_nf4(gpn, ga).cpu().numpy().tobytes() == dn.tobytes()
+        assert b4gemv.dequant_int4(gp, gs).cpu().numpy().tobytes() == d.tobytes()
+
+
+# ---- GEMV parity ------------------------------------------------------------------
+
+@pytest.mark.parametrize("case", ["kat_glibc", "gauss_7x128", "gauss_33x384", "gauss_8x1024", "gauss_1x128",
+                                  "gauss_5x640", "gauss_16x256"])
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_gemv_golden_cases(cuda, golden, oracle, case, fmt):
+    g = golden[case]
+    if fmt == 0:
+        qw, sc = to_dev(g["int4_packed"], cuda), to_dev(g["int4_scales"], cuda)
+        y = b4gemv.gemv_int4(qw, sc, to_dev(g["x"], cuda))
+    else:
+        qw, sc = to_dev(g["nf4_packed"], cuda), to_dev(g["nf4_absmax"], cuda)
+        y = b4gemv.gemv_nf4(qw, sc, to_dev(g["x"], cuda))
+    ref = f64_ref(oracle, fmt, qw, sc, g["x"])
+    assert rel_err(y.cpu().numpy(), ref) < TOL
+
+
+def test_gemv_edge_case_nan_rows(cuda, golden, oracle):
+    """Rows whose dequantised weights hold NaN (fp16 scale overflow) give NaN;
+    the other rows stay within tolerance."""
+    g = golden["edge"]
+    for fmt, p, s in [(0, g["int4_packed"], g["int4_scales"]), (1, g["nf4_packed"], g["nf4_absmax"])]:
+        qw, sc = to_dev(p, cuda), to_dev(s, cuda)
+        y = b4gemv.gemv(fmt, qw, sc, to_dev(g["x"], cuda)).cpu().numpy()[0]
+        ref = f64_ref(oracle, fmt, qw, sc, g["x"])[0]
+        assert np.array_equal(np.isnan(y), np.isnan(ref))
+        ok = ~np.isnan(ref)
+        assert rel_err(y[ok], ref[ok]) < TOL
+
+
+def kernel_configs():
+    """Every instantiated kernel (vec_words, rows_per_warp, batch_tile, nf4_lut)."""
+    out = []
+    for fmt in (0, 1):
+        for lut in ((0,) if fmt == 0 else (0, 1)):
+            for vw, rw in [(1, 1), (1, 4)]:
+                out.append((fmt, vw, rw, 1, lut))
+            for vw in (2, 4):
+                for mb in (1, 2, 4):
+                    for rw in (1, 2, 4, 8):
+                        if not (mb == 4 and rw == 8):
+                            out.append((fmt, vw, rw, mb, lut))
+    return out
+
+
+@pytest.mark.parametrize("fmt,vw,rw,mb,lut", kernel_configs())
+def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut):
+    rng = np.random.default_rng(1000 + fmt * 100 + vw * 10 + rw + mb * 7 + lut)
+    for out_f, in_f, m in [(37, 1152, 1), (9, 512, 3), (70, 3584, 5)]:
+        W, X = rand_problem(rng, out_f, in_f, m)
+        qw, sc = quantised(fmt, W, cuda)
+        ref = f64_ref(oracle, fmt, qw, sc, X)
+        Xd = to_dev(X, cuda)
+        for kw, rg in [(1, 1), (2, 2), (4, 1), (1, 4)]:
+            if (rw > 1 or mb > 1) and kw * rg > 8:
+                continue
+            cfg = dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=mb, nf4_lut=lut)
+            y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+            assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+        # several x tiles in shared memory
+        cfg = dict(vec_words=vw, rows_per_warp=rw, warps_k=2, row_groups=1, batch_tile=mb, nf4_lut=lut,
+                   x_tile=8 * vw * 32)
+        y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+        assert rel_err(y, ref) < TOL, ("x_tile", out_f, in_f, m, cfg)
+
+
+@pytest.mark.parametrize("name", list(QWEN))
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_gemv_qwen_shapes(cuda, oracle, name, fmt):
+    out_f, in_f = QWEN[name]
+    rng = np.random.default_rng(hash(name) % 1000 + fmt)
+    W, X = rand_problem(rng, out_f, in_f)
+    qw, sc = quantised(fmt, W, cuda)
+    y = (b4gemv.gemv_int4 if fmt == 0 else b4gemv.gemv_nf4)(qw, sc, to_dev(X, cuda)).cpu().numpy()
+    ref = f64_ref(oracle, fmt, qw, sc, X)
+    assert rel_err(y, ref) < TOL
+
+
+@pytest.mark.parametrize("m", [2, 3, 4, 8, 16])
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_gemv_small_batch(cuda, oracle, m, fmt):
+    rng = np.random.default_rng(50 + m)
+    W, X = rand_problem(rng, 1000, 2048, m)
+    qw, sc = quantised(fmt, W, cuda)
+    y = b4gemv.gemv(fmt, qw, sc, to_dev(X, cuda)).cpu().numpy()
+    assert rel_err(y, f64_ref(oracle, fmt, qw, sc, X)) < TOL
+
+
+def test_gemv_misaligned_buffers_use_narrow_loads(cuda, oracle):
+    """Codes at a 4-byte (not 16-byte) offset and x at a 2-byte offset: the
+    4-byte load path runs and the result is unchanged."""
+    import torch
+    rng = np.random.default_rng(5)
+    W, X = rand_problem(rng, 64, 1024)
+    for fmt in (0, 1):
+        qw, sc = quantised(fmt, W, cuda)
+        big = torch.zeros(qw.numel() + 1, dtype=torch.int32, device=cuda)
+        big[1:] = qw.reshape(-1)
+        qw_off = big[1:].view(qw.shape)
+        xb = torch.zeros(1024 + 1, dtype=torch.float16, device=cuda)
+        xb[1:] = to_dev(X[0], cuda)
+        x_off = xb[1:]
+        assert qw_off.data_ptr() % 16 == 4 and x_off.data_ptr() % 4 == 2
+        cfg = b4gemv.default_config(fmt, 1024, 64, 1)
+        y = b4gemv.gemv(fmt, qw_off, sc, x_off.view(1, 1024)).cpu().numpy()
+        assert rel_err(y, f64_ref(oracle, fmt, qw, sc, X)) < TOL
+        assert cfg["vec_words"] == 4  # the rule itself prefers 16-byte loads
+
+
+@pytest.mark.parametrize("wpb", [1, 2, 4, 8, 16])
+def test_nf4_block_per_row_entry(cuda, oracle, wpb):
+    rng = np.random.default_rng(wpb)
+    W, X = rand_problem(rng, 96, 18944 // 4)
+    qw, sc = quantised(1, W, cuda)
+    y = b4gemv.gemv_nf4_block_per_row(qw, sc, to_dev(X, cuda), wpb).cpu().numpy()
+    assert rel_err(y, f64_ref(oracle, 1, qw, sc, X)) < TOL
+
+
+def test_pdl_launch_after_producer(cuda, oracle):
+    """With the PDL flag the GEMV starts before the kernel that writes x has
+    finished, and still reads the final x."""
+    import torch
+    rng = np.random.default_rng(9)
+    W, X = rand_problem(rng, 3584, 3584)
+    for fmt in (0, 1):
+        qw, sc = quantised(fmt, W, cuda)
+        cfg = b4gemv.default_config(fmt, 3584, 3584, 1)
+        cfg["flags"] = b4gemv.FLAG_PDL
+        xsrc = to_dev(X, cuda)
+        x = torch.zeros_like(xsrc)
+        for _ in range(3):
+            x.zero_()
+            x.copy_(xsrc)          # the producer kernel
+            y = b4gemv.gemv(fmt, qw, sc, x, config=cfg)
+        assert rel_err(y.cpu().numpy(), f64_ref(oracle, fmt, qw, sc, X)) < TOL
+
+
+def test_results_are_deterministic(cuda):
+    rng = np.random.default_rng(12)
+    W, X = rand_problem(rng, 3584, 18944)
+    for fmt in (0, 1):
+        qw, sc = quantised(fmt, W, cuda)
+        Xd = to_dev(X, cuda)
+        a = b4gemv.gemv(fmt, qw, sc, Xd).cpu().numpy()
+        b = b4gemv.gemv(fmt, qw, sc, Xd).cpu().numpy()
+        assert a.tobytes() == b.tobytes()
