@@ -457,7 +457,7 @@ def run_ours(args, d):
     t_soak = time.time()
     run_steps(max(W, 3), False)
     torch.cuda.synchronize()
-    soak_until = time.time() + 1.0
+    soak_until = time.time() + args.soak_seconds
     while time.time() < soak_until:
         g_main.replay()
         torch.cuda.synchronize()
@@ -634,6 +634,8 @@ def main():
     ap.add_argument("--detail", action="store_true", help="also per-shape chained us for INT4 and NF4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--soak-seconds", type=float, default=1.0,
+                    help="untimed load before the timed region, for the clock samples")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,0 +1,203 @@
+"""Launch-geometry sweeps and profiling drivers (the role of the reference's
+src/diag_aspect.cu on B200): the measurements the dispatch rule is fitted to.
+
+  python -m b4gemv.diag sweep   [--fmt nf4|int4|both] [--shapes q_proj,...] [--json out.json]
+      every kernel configuration in a grid, per shape: us per GEMV over 100
+      graph-chained launches rotating over weight copies larger than L2.
+  python -m b4gemv.diag aspect  [--fmt nf4|int4]
+      the three sweeps of diag_aspect.cu:346-358 (aspect ratio at constant
+      weight count, rows at fixed x, x size at fixed rows) with the dispatch
+      rule's config.
+  python -m b4gemv.diag run     --fmt nf4 --shape gate_proj [--launches 4] [--config k=v,...]
+      a few launches of one GEMV (the command profiled by ncu).
+Run from int4-gemv_b200/ (or with it on sys.path).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import itertools
+import json
+import sys
+
+from . import FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
+
+SHAPES = {"q_proj": (3584, 3584), "k_proj": (512, 3584), "v_proj": (512, 3584), "o_proj": (3584, 3584),
+          "gate_proj": (18944, 3584), "up_proj": (18944, 3584), "down_proj": (3584, 18944),
+          # Llama-3-70B layer and its tensor-parallel shards
+          "l70_qo": (8192, 8192), "l70_kv": (1024, 8192), "l70_gu": (28672, 8192), "l70_down": (8192, 28672)}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def alg_bytes(fmt, out_f, in_f, m=1):
+    scale = out_f * (in_f // 64) * 4 if fmt == FMT_NF4_B64 else out_f * (in_f // 128) * 2
+    return out_f * in_f // 2 + scale + m * in_f * 2
+
+
+class Problem:
+    """Device buffers for one shape: enough weight copies to exceed 4x L2."""
+
+    def __init__(self, torch, fmt, out_f, in_f, m=1, seed=0, copies=None):
+        from . import quantise_device, quantise_nf4_device
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        W = torch.randn((out_f, in_f), generator=g, device=dev) * 0.02
+        qw, sc, _ = (quantise_nf4_device if fmt == FMT_NF4_B64 else quantise_device)(W)
+        del W
+        nb = alg_bytes(fmt, out_f, in_f)
+        n = copies or max(2, min(64, -(-4 * L2_BYTES // nb)))
+        self.copies = [(qw, sc)] + [(qw.clone(), sc.clone()) for _ in range(n - 1)]
+        self.x = torch.randn((m, in_f), generator=g, device=dev).half()
+        self.y = torch.empty((m, out_f), device=dev)
+        self.fmt, self.out_f, self.in_f, self.m = fmt, out_f, in_f, m
+        self.ptrs = [(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(s.data_ptr())) for q, s in self.copies]
+
+    def launch(self, k, cfg, stream):
+        q, s = self.ptrs[k % len(self.ptrs)]
+        return load().b4_gemv_ex(self.fmt, q, s, ctypes.c_void_p(self.x.data_ptr()),
+                                 ctypes.c_void_p(self.y.data_ptr()), self.in_f, self.out_f, self.m,
+                                 ctypes.byref(cfg) if cfg is not None else None, stream)
+
+
+def time_chained(torch, prob, cfg, reps=100):
+    """us per GEMV over `reps` launches captured in one CUDA graph; None if
+    the config is rejected."""
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if prob.launch(0, cfg, stream) != 0:
+        return None
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(g, stream=cs, capture_error_mode="relaxed"):
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for k in range(reps):
+            prob.launch(k, cfg, st)
+    torch.cuda.current_stream().wait_stream(cs)
+    g.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(3):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        best = us if best is None else min(best, us)
+    del g
+    return best
+
+
+def config_grid(fmt, m=1):
+    luts = (0,) if fmt == FMT_INT4_G128 else (0, 1)
+    mbs = (1,) if m == 1 else ((2,) if m == 2 else (4,))
+    for vw, rw, kw, rg, mb, lut in itertools.product((2, 4), (1, 2, 4, 8), (1, 2, 4, 8), (1, 2, 4, 8), mbs, luts):
+        if mb == 4 and rw == 8:
+            continue
+        if kw * rg > 8 or kw * rg < 2:
+            continue
+        yield dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=mb, nf4_lut=lut,
+                   x_tile=0, flags=0)
+
+
+def cmd_sweep(args, torch):
+    fmts = {"nf4": [FMT_NF4_B64], "int4": [FMT_INT4_G128], "both": [FMT_INT4_G128, FMT_NF4_B64]}[args.fmt]
+    names = args.shapes.split(",") if args.shapes else list(SHAPES)[:7]
+    out = []
+    for fmt in fmts:
+        for name in names:
+            out_f, in_f = SHAPES[name]
+            prob = Problem(torch, fmt, out_f, in_f, m=args.m)
+            nb = alg_bytes(fmt, out_f, in_f, args.m)
+            dflt = GemvConfig()
+            check("default_config", load().b4_gemv_default_config(fmt, in_f, out_f, args.m, ctypes.byref(dflt)))
+            rows = []
+            us_d = time_chained(torch, prob, dflt)
+            rows.append(("default", dflt.as_dict(), us_d))
+            for c in config_grid(fmt, args.m):
+                us = time_chained(torch, prob, GemvConfig.from_dict(c))
+                if us is not None:
+                    rows.append(("grid", c, us))
+            rows.sort(key=lambda r: r[2])
+            best = rows[0]
+            print(f"{'nf4' if fmt else 'int4'} {name:10s} {out_f}x{in_f} m={args.m}: default {us_d:.3f} us "
+                  f"({nb / us_d / 1e3:.0f} GB/s)  best {best[2]:.3f} us ({nb / best[2] / 1e3:.0f} GB/s) {best[1]}",
+                  flush=True)
+            out.append({"fmt": "nf4" if fmt else "int4", "shape": name, "out_f": out_f, "in_f": in_f, "m": args.m,
+                        "bytes": nb, "default": {"cfg": dflt.as_dict(), "us": us_d},
+                        "top": [{"cfg": c, "us": us} for _, c, us in rows[:12]],
+                        "all": [[c["vec_words"], c["rows_per_warp"], c["warps_k"], c["row_groups"], c["batch_tile"],
+                                 c["nf4_lut"], round(us, 3)] for _, c, us in rows]})
+            del prob
+            torch.cuda.empty_cache()
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(out, f)
+
+
+def cmd_aspect(args, torch):
+    fmt = FMT_NF4_B64 if args.fmt == "nf4" else FMT_INT4_G128
+    sweeps = {
+        "aspect": [(18944, 3584), (9472, 7168), (4736, 14336), (3584, 18944), (2368, 28672), (1184, 57344)],
+        "rows": [(1184, 3584), (2368, 3584), (4736, 3584), (9472, 3584), (18944, 3584), (37888, 3584)],
+        "x": [(3584, 3584), (3584, 7168), (3584, 14336), (3584, 18944), (3584, 28672), (3584, 57344)],
+    }
+    for title, cases in sweeps.items():
+        print(f"sweep {title}")
+        for out_f, in_f in cases:
+            prob = Problem(torch, fmt, out_f, in_f)
+            us = time_chained(torch, prob, None)
+            nb = alg_bytes(fmt, out_f, in_f)
+            print(f"  {out_f:6d}x{in_f:<6d} {us:8.3f} us {nb / us / 1e3:8.0f} GB/s "
+                  f"{out_f * in_f / us / 1e3:8.0f} MW/ms", flush=True)
+            del prob
+            torch.cuda.empty_cache()
+
+
+def cmd_run(args, torch):
+    fmt = FMT_NF4_B64 if args.fmt == "nf4" else FMT_INT4_G128
+    out_f, in_f = SHAPES[args.shape]
+    prob = Problem(torch, fmt, out_f, in_f, m=args.m, copies=args.copies)
+    cfg = None
+    if args.config:
+        d = GemvConfig()
+        check("default_config", load().b4_gemv_default_config(fmt, in_f, out_f, args.m, ctypes.byref(d)))
+        c = d.as_dict()
+        for kv in args.config.split(","):
+            k, v = kv.split("=")
+            c[k] = int(v)
+        cfg = GemvConfig.from_dict(c)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for k in range(args.launches):
+        check("b4_gemv_ex", prob.launch(k, cfg, stream))
+    torch.cuda.synchronize()
+    print(f"ran {args.launches} launches of {args.fmt} {args.shape} {out_f}x{in_f} m={args.m}")
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="python -m b4gemv.diag")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    s = sub.add_parser("sweep")
+    s.add_argument("--fmt", default="both", choices=["nf4", "int4", "both"])
+    s.add_argument("--shapes", default="")
+    s.add_argument("--m", type=int, default=1)
+    s.add_argument("--json", default="")
+    a = sub.add_parser("aspect")
+    a.add_argument("--fmt", default="nf4", choices=["nf4", "int4"])
+    r = sub.add_parser("run")
+    r.add_argument("--fmt", default="nf4", choices=["nf4", "int4"])
+    r.add_argument("--shape", default="gate_proj", choices=list(SHAPES))
+    r.add_argument("--m", type=int, default=1)
+    r.add_argument("--launches", type=int, default=4)
+    r.add_argument("--copies", type=int, default=4)
+    r.add_argument("--config", default="")
+    args = ap.parse_args(argv)
+    import torch
+    torch.cuda.init()
+    {"sweep": cmd_sweep, "aspect": cmd_aspect, "run": cmd_run}[args.cmd](args, torch)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
