@@ -129,6 +129,46 @@ int b4_quantise_int4_g128_device(const float* W, int out_f, int in_f, uint32_t* 
 int b4_quantise_nf4_b64_device(const float* W, int out_f, int in_f, uint32_t* packed,
                                float* absmax, float* deq, b4_stream_t stream);
 
+/* ---- Tensor-parallel decode layer -------------------------------------------
+ * New (the reference has no multi-GPU code, README.md:175).  Column-parallel
+ * projections (q/k/v/gate/up) need no entry point: a rank's rows are a
+ * contiguous slice of qw/scales, passed to the GEMV as is.  Row-parallel
+ * projections (o/down) hold a column shard (b4_shard_columns) and finish with
+ * an all-reduce of fp32 y (b4_tp_gemv_allreduce).  NCCL is loaded at run time.
+ * Statuses >= B4_STATUS_NCCL_BASE are NCCL results (base + ncclResult_t). */
+#define B4_STATUS_NCCL_BASE 10000
+#define B4_STATUS_NCCL_MISSING 10900 /* no libnccl.so.2 in the process or on the path */
+#define B4_STATUS_TIMEOUT 10901      /* b4_nccl_wait deadline passed; communicator aborted */
+
+typedef struct b4_nccl_id { char internal[128]; } b4_nccl_id; /* = ncclUniqueId */
+
+int b4_nccl_get_unique_id(b4_nccl_id* id);
+/* ncclCommInitRank; *comm receives the ncclComm_t. */
+int b4_nccl_comm_init(void** comm, int nranks, const b4_nccl_id* id, int rank);
+int b4_nccl_comm_destroy(void* comm);
+/* Host-side failure detection: waits for `stream` with a deadline, polling
+ * ncclCommGetAsyncError; on an NCCL error or the deadline it aborts the
+ * communicator (ncclCommAbort) and returns the error / B4_STATUS_TIMEOUT. */
+int b4_nccl_wait(void* comm, b4_stream_t stream, int timeout_ms);
+
+/* Columns [col0, col0+ncols) of every row of a packed weight (and the matching
+ * scales / absmax) into contiguous buffers: qw_out [out_f][ncols/8],
+ * scale_out [out_f][ncols/unit], unit = 128 (INT4) or 64 (NF4); col0 and ncols
+ * multiples of unit.  Device pointers. */
+int b4_shard_columns(int fmt, const uint32_t* qw, const void* scale, int in_f, int out_f, int col0,
+                     int ncols, uint32_t* qw_out, void* scale_out, b4_stream_t stream);
+
+/* Row-parallel GEMV: y = this rank's partial (column shard . x_shard), then
+ * ncclAllReduce(y, y, m*out_f, fp32, sum) on the same stream. */
+int b4_tp_gemv_allreduce(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard,
+                         float* y, int in_shard, int out_f, int m, void* nccl_comm, b4_stream_t stream);
+
+/* Elementwise glue of the decode layer: out = fp16(silu(gate) * up) (the MLP
+ * activation between gate/up and down) and out = fp16(in). */
+int b4_swiglu_f16(const float* gate, const float* up, void* out, long long n, b4_stream_t stream);
+int b4_cast_f16(const float* in, void* out, long long n, b4_stream_t stream);
+const char* b4_nccl_error_string(int status);
+
 /* ---- Misc -------------------------------------------------------------------
  * One empty kernel launch: the empty-launch floor that bench/baseline.py:71-76
  * measures (there with a 1x1 fp16 matmul) and that bounds the narrow shapes. */

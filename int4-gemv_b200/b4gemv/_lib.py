@@ -62,6 +62,15 @@ SIGNATURES = {
     "b4_quantise_int4_g128_device": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "b4_quantise_nf4_b64_device": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "b4_empty_launch": (_I, [_P]),
+    "b4_nccl_get_unique_id": (_I, [_P]),
+    "b4_nccl_comm_init": (_I, [ctypes.POINTER(ctypes.c_void_p), _I, _P, _I]),
+    "b4_nccl_comm_destroy": (_I, [_P]),
+    "b4_nccl_wait": (_I, [_P, _P, _I]),
+    "b4_shard_columns": (_I, [_I, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "b4_tp_gemv_allreduce": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "b4_swiglu_f16": (_I, [_P, _P, _P, ctypes.c_longlong, _P]),
+    "b4_cast_f16": (_I, [_P, _P, ctypes.c_longlong, _P]),
+    "b4_nccl_error_string": (ctypes.c_char_p, [_I]),
     "b4_status_string": (ctypes.c_char_p, [_I]),
     "b4_abi_version": (_I, []),
 }

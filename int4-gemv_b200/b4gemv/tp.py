@@ -1,0 +1,184 @@
+"""Tensor-parallel decode layer over NVLink (one process per GPU).
+
+A Llama-style decoder layer's seven projections at batch 1, sharded over a
+tensor-parallel group of T ranks:
+
+  column-parallel (rows split, no communication):  q, k, v, gate, up
+  row-parallel (in_f split on group boundaries, then an all-reduce of fp32 y):
+                                                     o, down
+
+Data flow of one decode step on each rank (attention itself is out of scope:
+its output shard is an input):
+
+  x (fp16, replicated) -> q, k, v shards
+  attn shard (fp16)    -> o partial -> all-reduce -> h (fp32) -> fp16
+  h                    -> gate, up shards -> silu(gate) * up (fp16) -> down partial
+                       -> all-reduce -> y (fp32, replicated)
+
+The GEMVs, the sharding copies, the activation and the all-reduce are C ABI
+calls (include/b4gemv.h); torch.distributed is only used to hand the NCCL
+unique id from rank 0 to the others.  The reference has no multi-GPU code.
+"""
+from __future__ import annotations
+
+import ctypes
+
+from ._lib import FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, check, load
+
+
+def row_range(n: int, tp: int, rank: int):
+    """Rows [r0, r1) of rank `rank` when n rows are split over tp ranks as
+    evenly as possible (column-parallel projections)."""
+    return n * rank // tp, n * (rank + 1) // tp
+
+
+def col_range(in_f: int, unit: int, tp: int, rank: int):
+    """Columns [c0, c1) of rank `rank` for a row-parallel projection: in_f is
+    split on `unit` boundaries (128 for INT4 groups, 64 for NF4 blocks)."""
+    if in_f % unit:
+        raise ValueError(f"in_f={in_f} is not a multiple of {unit}")
+    units = in_f // unit
+    if units < tp:
+        raise ValueError(f"{units} groups cannot be split over {tp} ranks")
+    u0, u1 = units * rank // tp, units * (rank + 1) // tp
+    return u0 * unit, u1 * unit
+
+
+def fmt_unit(fmt: int) -> int:
+    return GROUP if fmt == FMT_INT4_G128 else NF4_BLOCK
+
+
+class NcclComm:
+    """An NCCL communicator created through the C ABI; the unique id travels
+    from rank 0 over torch.distributed (any backend)."""
+
+    def __init__(self, rank: int, world: int, group=None):
+        import torch.distributed as dist
+        lib = load()
+        uid = ctypes.create_string_buffer(128)
+        if rank == 0:
+            check("b4_nccl_get_unique_id", lib.b4_nccl_get_unique_id(uid))
+        obj = [bytes(uid.raw) if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        uid = ctypes.create_string_buffer(obj[0], 128)
+        self.ptr = ctypes.c_void_p()
+        check("b4_nccl_comm_init", lib.b4_nccl_comm_init(ctypes.byref(self.ptr), world, uid, rank))
+        self.rank, self.world = rank, world
+
+    def wait(self, stream, timeout_ms: int = 10000) -> int:
+        """Host-side wait with a deadline; aborts the communicator on failure
+        and returns the status (0 on success)."""
+        return load().b4_nccl_wait(self.ptr, ctypes.c_void_p(stream.cuda_stream), timeout_ms)
+
+    def destroy(self):
+        if self.ptr:
+            load().b4_nccl_comm_destroy(self.ptr)
+            self.ptr = ctypes.c_void_p()
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def quantise_full(fmt, out_f, in_f, seed, device):
+    """W ~ N(0, 0.02) from a seeded device generator, quantised on the device:
+    the same full matrix on every rank."""
+    import torch
+    from . import quantise_device, quantise_nf4_device
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    W = torch.randn((out_f, in_f), generator=g, device=device) * 0.02
+    qw, sc, _ = (quantise_nf4_device if fmt == FMT_NF4_B64 else quantise_device)(W)
+    del W
+    return qw, sc
+
+
+def shard_columns(fmt, qw, sc, c0, c1, stream=None):
+    """Contiguous copy of columns [c0, c1) of a packed weight and its scales."""
+    import torch
+    out_f, words = qw.shape
+    in_f = words * 8
+    unit = fmt_unit(fmt)
+    q_out = torch.empty((out_f, (c1 - c0) // 8), dtype=qw.dtype, device=qw.device)
+    s_out = torch.empty((out_f, (c1 - c0) // unit), dtype=sc.dtype, device=sc.device)
+    st = stream if stream is not None else torch.cuda.current_stream()
+    check("b4_shard_columns", load().b4_shard_columns(fmt, _p(qw), _p(sc), in_f, out_f, c0, c1 - c0, _p(q_out),
+                                                      _p(s_out), ctypes.c_void_p(st.cuda_stream)))
+    return q_out, s_out
+
+
+class TPDecodeLayer:
+    """One decoder layer's projections sharded over `tp` ranks.
+
+    Shapes (Llama-3-70B defaults): hidden 8192, intermediate 28672, q 8192
+    rows (64 heads x 128), k/v 1024 rows (8 heads x 128)."""
+
+    NAMES = ("q", "k", "v", "o", "gate", "up", "down")
+
+    def __init__(self, fmt, rank, tp, comm, device, hidden=8192, inter=28672, q_out=8192, kv_out=1024, seed=0):
+        import torch
+        self.fmt, self.rank, self.tp, self.comm, self.device = fmt, rank, tp, comm, device
+        self.hidden, self.inter, self.q_out, self.kv_out = hidden, inter, q_out, kv_out
+        unit = fmt_unit(fmt)
+        # (name, out_f, in_f, kind)
+        self.specs = [("q", q_out, hidden, "col"), ("k", kv_out, hidden, "col"), ("v", kv_out, hidden, "col"),
+                      ("o", hidden, q_out, "row"), ("gate", inter, hidden, "col"), ("up", inter, hidden, "col"),
+                      ("down", hidden, inter, "row")]
+        self.w = {}
+        self.ranges = {}
+        for i, (name, out_f, in_f, kind) in enumerate(self.specs):
+            qw, sc = quantise_full(fmt, out_f, in_f, seed * 100 + i, device)
+            if kind == "col":
+                r0, r1 = row_range(out_f, tp, rank)
+                self.w[name] = (qw[r0:r1].contiguous(), sc[r0:r1].contiguous())
+                self.ranges[name] = (r0, r1)
+            else:
+                c0, c1 = col_range(in_f, unit, tp, rank)
+                self.w[name] = shard_columns(fmt, qw, sc, c0, c1)
+                self.ranges[name] = (c0, c1)
+            del qw, sc
+        # the attention output shard feeding o is this rank's q heads
+        assert tp == 1 or self.ranges["o"] == self.ranges["q"], "q rows and o columns must shard alike"
+        f32 = dict(dtype=torch.float32, device=device)
+        f16 = dict(dtype=torch.float16, device=device)
+        rq, rk, rg = (self.ranges[n][1] - self.ranges[n][0] for n in ("q", "k", "gate"))
+        self.buf = {"q": torch.empty((1, rq), **f32), "k": torch.empty((1, rk), **f32),
+                    "v": torch.empty((1, rk), **f32), "h": torch.empty((1, hidden), **f32),
+                    "h16": torch.empty((1, hidden), **f16), "gate": torch.empty((1, rg), **f32),
+                    "up": torch.empty((1, rg), **f32), "act": torch.empty((1, rg), **f16),
+                    "y": torch.empty((1, hidden), **f32)}
+        torch.cuda.synchronize(device)
+
+    def weight_bytes(self) -> int:
+        """Algorithmic bytes this rank streams per step (codes + scales)."""
+        return sum(q.numel() * 4 + s.numel() * s.element_size() for q, s in self.w.values())
+
+    def _gemv(self, name, x, y, stream):
+        qw, sc = self.w[name]
+        check(f"gemv {name}", load().b4_gemv_ex(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
+                                                 qw.shape[0], 1, None, stream))
+
+    def _rowpar(self, name, x, y, stream):
+        qw, sc = self.w[name]
+        if self.tp == 1:
+            return self._gemv(name, x, y, stream)
+        check(f"tp {name}", load().b4_tp_gemv_allreduce(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
+                                                         qw.shape[0], 1, self.comm.ptr, stream))
+
+    def forward(self, x, attn, stream=None):
+        """x: fp16 [1, hidden] (replicated); attn: fp16 [1, q shard] (this
+        rank's heads of the attention output).  Returns y fp32 [1, hidden]."""
+        import torch
+        st = stream if stream is not None else torch.cuda.current_stream()
+        s = ctypes.c_void_p(st.cuda_stream)
+        b, lib = self.buf, load()
+        self._gemv("q", x, b["q"], s)
+        self._gemv("k", x, b["k"], s)
+        self._gemv("v", x, b["v"], s)
+        self._rowpar("o", attn, b["h"], s)
+        check("cast", lib.b4_cast_f16(_p(b["h"]), _p(b["h16"]), b["h"].numel(), s))
+        self._gemv("gate", b["h16"], b["gate"], s)
+        self._gemv("up", b["h16"], b["up"], s)
+        check("swiglu", lib.b4_swiglu_f16(_p(b["gate"]), _p(b["up"]), _p(b["act"]), b["act"].numel(), s))
+        self._rowpar("down", b["act"], b["y"], s)
+        return b["y"]

@@ -253,6 +253,7 @@ int b4_empty_launch(b4_stream_t stream)
 
 const char* b4_status_string(int status)
 {
+    if (status >= B4_STATUS_NCCL_BASE) return b4_nccl_error_string(status);
     return cudaGetErrorString(static_cast<cudaError_t>(status));
 }
 
