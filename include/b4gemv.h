@@ -58,7 +58,15 @@ typedef struct b4_gemv_config {
     int nf4_lut;       /* NF4 code-book lookup: 0 warp shuffle, 1 shared memory */
     int x_tile;        /* columns of x staged in shared memory per pass, 0 = auto */
     int flags;         /* B4_FLAG_* */
+    int engine;        /* B4_ENGINE_*: which pipe does the multiply-accumulates   */
 } b4_gemv_config;
+
+/* CUDA cores: fp32 FMA (INT4 and NF4).  rows_per_warp 1/2/4/8, batch_tile 1/2/4. */
+#define B4_ENGINE_FMA 0
+/* Tensor pipe (INT4 only): register-operand MMA, exact fp16 (code-8) and x,
+ * fp32 accumulate.  rows_per_warp 16 or 32, batch_tile 8 or 16 (the MMA's N:
+ * batch rows ride along for free), vec_words 4, x_tile a multiple of 128. */
+#define B4_ENGINE_MMA 1
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
  * the weight stream starts before the producer of x has finished. */

@@ -17,6 +17,8 @@ FMT_NF4_B64 = 1
 GROUP = 128
 NF4_BLOCK = 64
 FLAG_PDL = 1
+ENGINE_FMA = 0
+ENGINE_MMA = 1
 
 
 class GemvConfig(ctypes.Structure):
@@ -31,6 +33,7 @@ class GemvConfig(ctypes.Structure):
         ("nf4_lut", ctypes.c_int),
         ("x_tile", ctypes.c_int),
         ("flags", ctypes.c_int),
+        ("engine", ctypes.c_int),
     ]
 
     def as_dict(self) -> dict:

@@ -91,6 +91,11 @@ def time_chained(torch, prob, cfg, reps=100):
 
 
 def config_grid(fmt, m=1):
+    if fmt == FMT_INT4_G128:
+        for rw, kw, rg, nt in itertools.product((16, 32), (1, 2, 4, 8), (1, 2, 4, 8), (8, 16)):
+            if kw * rg <= 8 and (nt == 8 or m > 8):
+                yield dict(vec_words=4, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=nt, nf4_lut=0,
+                           x_tile=0, flags=0, engine=1)
     luts = (0,) if fmt == FMT_INT4_G128 else (0, 1)
     mbs = (1,) if m == 1 else ((2,) if m == 2 else (4,))
     for vw, rw, kw, rg, mb, lut in itertools.product((2, 4), (1, 2, 4, 8), (1, 2, 4, 8), (1, 2, 4, 8), mbs, luts):
@@ -99,7 +104,7 @@ def config_grid(fmt, m=1):
         if kw * rg > 8 or kw * rg < 2:
             continue
         yield dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=mb, nf4_lut=lut,
-                   x_tile=0, flags=0)
+                   x_tile=0, flags=0, engine=0)
 
 
 def cmd_sweep(args, torch):
@@ -128,8 +133,8 @@ def cmd_sweep(args, torch):
             out.append({"fmt": "nf4" if fmt else "int4", "shape": name, "out_f": out_f, "in_f": in_f, "m": args.m,
                         "bytes": nb, "default": {"cfg": dflt.as_dict(), "us": us_d},
                         "top": [{"cfg": c, "us": us} for _, c, us in rows[:12]],
-                        "all": [[c["vec_words"], c["rows_per_warp"], c["warps_k"], c["row_groups"], c["batch_tile"],
-                                 c["nf4_lut"], round(us, 3)] for _, c, us in rows]})
+                        "all": [[c.get("engine", 0), c["vec_words"], c["rows_per_warp"], c["warps_k"], c["row_groups"],
+                                 c["batch_tile"], c["nf4_lut"], round(us, 3)] for _, c, us in rows]})
             del prob
             torch.cuda.empty_cache()
     if args.json:

@@ -100,6 +100,29 @@ __device__ __forceinline__ void int4_word_to_half2(uint32_t w, uint32_t h[4])
     asm("sub.f16x2 %0, %1, %2;" : "=r"(h[3]) : "r"(t3), "r"(0x54805480u));
 }
 
+// INT4 decode to fp32 for the CUDA-core kernel: OR-ing nibble j into the
+// mantissa of 2^23 (0x4b000000) gives 2^23 + n_j * 2^p_j exactly, for nibble
+// positions p_j <= 19; nibbles 5..7 are taken from w >> 12 so that
+// p = {0, 4, 8, 12, 16, 8, 12, 16}.  Subtracting 2^23 + 8 * 2^p_j (exact:
+// integers below 2^24) leaves (n_j - 8) * 2^p_j; d[k] holds codes 2k, 2k+1.
+__device__ __forceinline__ void int4_word_to_f32x2(uint32_t w, float2 d[4])
+{
+    const uint32_t hi = w >> 12;
+    const uint32_t m = 0x4b000000u;
+    const float f0 = __uint_as_float(lop3_and_or(w, 0x0000000fu, m));
+    const float f1 = __uint_as_float(lop3_and_or(w, 0x000000f0u, m));
+    const float f2 = __uint_as_float(lop3_and_or(w, 0x00000f00u, m));
+    const float f3 = __uint_as_float(lop3_and_or(w, 0x0000f000u, m));
+    const float f4 = __uint_as_float(lop3_and_or(w, 0x000f0000u, m));
+    const float f5 = __uint_as_float(lop3_and_or(hi, 0x00000f00u, m));
+    const float f6 = __uint_as_float(lop3_and_or(hi, 0x0000f000u, m));
+    const float f7 = __uint_as_float(lop3_and_or(hi, 0x000f0000u, m));
+    d[0] = __fadd2_rn(make_float2(f0, f1), make_float2(-(0x1p23f + 8.0f), -(0x1p23f + 128.0f)));
+    d[1] = __fadd2_rn(make_float2(f2, f3), make_float2(-(0x1p23f + 2048.0f), -(0x1p23f + 32768.0f)));
+    d[2] = __fadd2_rn(make_float2(f4, f5), make_float2(-(0x1p23f + 524288.0f), -(0x1p23f + 2048.0f)));
+    d[3] = __fadd2_rn(make_float2(f6, f7), make_float2(-(0x1p23f + 32768.0f), -(0x1p23f + 524288.0f)));
+}
+
 // Two fp32 accumulations from fp16 pairs with one rounding each (sm_100
 // mixed-precision FMA): acc_lo += a.lo*b.lo, acc_hi += a.hi*b.hi.
 __device__ __forceinline__ void fma2_f32_f16(float& acc_lo, float& acc_hi, uint32_t a, uint32_t b)

@@ -7,6 +7,7 @@
 #include <utility>
 
 #include "b4_gemv_kernel.cuh"
+#include "b4_gemv_mma.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -77,6 +78,27 @@ int check_problem(const GemvProblem& p)
 void default_config(const GemvProblem& p, b4_gemv_config* cfg)
 {
     const int words = p.in_f / 8;
+    const int sms = 148;  // the rule is fitted to B200; it stays valid elsewhere
+    cfg->nf4_lut = 0;
+    cfg->x_tile = 0;
+    cfg->flags = 0;
+
+    // INT4 with 16-byte aligned codes: multiply-accumulates on the tensor pipe.
+    if (p.fmt == kInt4 && aligned(p.qw, 16)) {
+        const int groups = p.in_f / kGroup;
+        const int row_groups = (p.out_f + 15) / 16;
+        int kw = 1;
+        while (kw < 8 && (long long)row_groups * kw < sms * 16LL && groups >= 2 * (2 * kw)) kw *= 2;
+        int rg = std::max(1, std::min(8 / kw, row_groups / (2 * sms)));
+        cfg->engine = B4_ENGINE_MMA;
+        cfg->vec_words = 4;
+        cfg->rows_per_warp = 16;
+        cfg->warps_k = kw;
+        cfg->row_groups = rg;
+        cfg->batch_tile = p.m > 8 ? 16 : 8;
+        return;
+    }
+
     int vw = 1;
     if (aligned(p.qw, 16) && words % 4 == 0) vw = 4;
     else if (aligned(p.qw, 8) && words % 2 == 0) vw = 2;
@@ -85,30 +107,31 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     int mb = p.m >= 4 ? 4 : (p.m >= 2 ? 2 : 1);
     if (vw == 1) mb = 1;
 
-    const int sms = 148;  // the rule is fitted to B200; it stays valid elsewhere
     int rw = 4;
     if ((p.out_f + rw - 1) / rw < sms * 8) rw = 2;
     if ((p.out_f + rw - 1) / rw < sms * 8) rw = 1;
     if (vw == 1) rw = rw >= 4 ? 4 : 1;
     if (mb == 4 && rw == 8) rw = 4;
 
-    const int groups = (p.out_f + rw - 1) / rw;
+    const int grps = (p.out_f + rw - 1) / rw;
     int kw = 1;
-    while (kw < 8 && (long long)groups * kw < sms * 16LL && chunks >= 32 * kw * 2) kw *= 2;
+    while (kw < 8 && (long long)grps * kw < sms * 16LL && chunks >= 32 * kw * 2) kw *= 2;
     int rg = std::max(1, 8 / kw);
 
+    cfg->engine = B4_ENGINE_FMA;
     cfg->vec_words = vw;
     cfg->rows_per_warp = rw;
     cfg->warps_k = kw;
     cfg->row_groups = rg;
     cfg->batch_tile = mb;
-    cfg->nf4_lut = 0;
-    cfg->x_tile = 0;
-    cfg->flags = 0;
 }
+
+int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
+    if (c.engine == B4_ENGINE_MMA) return launch_gemv_mma(p, c, st);
+    if (c.engine != B4_ENGINE_FMA) return cudaErrorInvalidValue;
     const int vw = c.vec_words, rw = c.rows_per_warp, kw = c.warps_k, rg = c.row_groups;
     const int mb = c.batch_tile, lut = c.nf4_lut;
     if (kw < 1 || kw > kMaxWarps || rg < 1 || kw * rg > kMaxWarps) return cudaErrorInvalidValue;
@@ -183,6 +206,82 @@ int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
     void* args[] = {&kp};
     e = cudaLaunchKernelExC(&lc, fn, args);
     return e;
+}
+
+namespace {
+
+cudaError_t launch_common(void* fn, const GemvProblem& p, KParams& kp, long long grid, int threads, size_t smem,
+                          int flags, cudaStream_t st)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int smem_max = 0;
+    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (smem > (size_t)smem_max) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        e = ensure_smem(fn, dev, smem);
+        if (e != cudaSuccess) return e;
+    }
+    if (grid < 1 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)grid);
+    lc.blockDim = dim3(threads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (flags & B4_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+    }
+    void* args[] = {&kp};
+    return cudaLaunchKernelExC(&lc, fn, args);
+}
+
+}  // namespace
+
+int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    if (p.fmt != kInt4) return cudaErrorInvalidValue;
+    if (c.vec_words != 4 || (c.rows_per_warp != 16 && c.rows_per_warp != 32)) return cudaErrorInvalidValue;
+    if (c.batch_tile != 8 && c.batch_tile != 16) return cudaErrorInvalidValue;
+    const int kw = c.warps_k, rg = c.row_groups;
+    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 16)) return cudaErrorInvalidValue;
+    const int rt = c.rows_per_warp / 16, nt = c.batch_tile / 8;
+    void* fn = gemv_kernel_int4_mma(rt, nt);
+    if (!fn) return cudaErrorInvalidValue;
+    const int groups = p.in_f / kGroup;
+    const int nb_max = std::min(p.m, c.batch_tile);
+    int tile_groups;
+    if (c.x_tile > 0) {
+        if (c.x_tile % kGroup) return cudaErrorInvalidValue;
+        tile_groups = std::min(groups, c.x_tile / kGroup);
+    } else {
+        tile_groups = std::min(groups, std::max(kw, kSmemBudget / (nb_max * 256) / kw * kw));
+    }
+    if (tile_groups < 1) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)nb_max * tile_groups * 256 + (kw > 1 ? (size_t)rg * kw * rt * nt * 4 * 32 * 4 : 0);
+    KParams kp;
+    kp.qw = p.qw;
+    kp.scale = p.scale;
+    kp.x = static_cast<const __half*>(p.x);
+    kp.y = p.y;
+    kp.in_f = p.in_f;
+    kp.out_f = p.out_f;
+    kp.m = p.m;
+    kp.x_ld = p.x_ld;
+    kp.y_ld = p.y_ld;
+    kp.kw = kw;
+    kp.rg = rg;
+    kp.tile_chunks = tile_groups;
+    kp.x_vec = aligned(p.x, 16) && ((p.x_ld * 2) % 16 == 0);
+    const long long rows_per_cta = (long long)rg * c.rows_per_warp;
+    const long long grid = (p.out_f + rows_per_cta - 1) / rows_per_cta;
+    return launch_common(fn, p, kp, grid, 32 * kw * rg, smem, c.flags, st);
 }
 
 }  // namespace b4

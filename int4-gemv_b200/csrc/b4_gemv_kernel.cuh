@@ -19,13 +19,17 @@
 //    order; NF4: fp32), swizzled so that the 16-byte reads of 8 consecutive
 //    lanes hit 8 distinct bank groups.  One staged chunk of x serves all RW
 //    rows and all decode work of the chunk is shared by MB batch rows.
-//  * Decode.  INT4: LOP3 + HSUB2 give exact fp16 (code-8) pairs, multiplied
-//    into fp32 by the sm_100 mixed fp16*fp16+fp32 FMA; the group scale is
-//    applied once per chunk (a chunk never crosses a 128-column group).
+//  * Decode.  INT4: one LOP3 per code ORs the nibble into the mantissa of
+//    2^23 and one packed FADD2 per two codes subtracts 2^23 + 8*2^p, leaving
+//    (code-8)*2^p exactly in fp32; x was staged pre-scaled by 2^-p, so the
+//    packed FFMA2 accumulates (code-8)*x with one rounding per product.  The
+//    group scale is applied once per chunk (a chunk never crosses a group).
 //    NF4: the 16-entry code book sits in the warp's registers (lane L holds
 //    NF4[L&15]) and a shuffle does each lookup, as in the reference
 //    (kernels.cuh:64-76); optionally a shared-memory copy does it instead.
-//    fp32 FMA with x; absmax applied once per chunk.
+//    Packed FFMA2 with fp32 x; absmax applied once per chunk.
+//  (The INT4 default is the tensor-pipe kernel of b4_gemv_mma.cuh; this one
+//   serves INT4 codes that are not 16-byte aligned.)
 #pragma once
 
 #include "b4_common.cuh"
@@ -45,10 +49,10 @@ struct KParams {
     int x_vec;        // x rows may be read with 16-byte (INT4) / 8-byte (NF4) loads
 };
 
-// 16-byte shared-memory slots of staged x per chunk.
+// 16-byte shared-memory slots of staged x per chunk: 8 fp32 values per word.
 template <int F, int VW>
 struct XSlots {
-    static constexpr int S = (F == kInt4) ? VW : 2 * VW;
+    static constexpr int S = 2 * VW;
 };
 
 // Physical slot of logical slot s of tile-relative chunk c: XOR-swizzled so
@@ -63,6 +67,11 @@ __device__ __forceinline__ int swz(int c, int s)
         return c * S + (s ^ ((c / (8 / S)) & (S - 1)));
 }
 
+// x staged as fp32, 8 values (two 16-byte slots) per packed word.  NF4: the
+// values in column order.  INT4: column j of the word pre-multiplied by
+// 2^-p_j, p = {0, 4, 8, 12, 16, 8, 12, 16}, the bit position at which the
+// magic-number decode leaves nibble j (int4_word_to_f32x2); the scaling is a
+// power of two, so every product stays exact.
 template <int F, int VW, int MB>
 __device__ __forceinline__ void stage_x(const KParams& p, uint4* xs, int mb0, int t0, int tn)
 {
@@ -77,34 +86,30 @@ __device__ __forceinline__ void stage_x(const KParams& p, uint4* xs, int mb0, in
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (mb0 + b < p.m) {
             const __half* xrow = p.x + (long long)(mb0 + b) * p.x_ld;
-            if constexpr (F == kInt4) {
-                const long long col = ((long long)(t0 + c) * VW + s) * 8;
-                uint4 raw;
-                if (p.x_vec) {
-                    raw = __ldg(reinterpret_cast<const uint4*>(xrow + col));
-                } else {
-                    const unsigned short* h = reinterpret_cast<const unsigned short*>(xrow + col);
-                    raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
-                    raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
-                    raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
-                    raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
-                }
-                v = int4_pair_order(raw);
+            const long long col = ((long long)(t0 + c) * VW + (s >> 1)) * 8 + (s & 1) * 4;
+            __half2 lo, hi;
+            if (p.x_vec) {
+                const uint2 raw = __ldg(reinterpret_cast<const uint2*>(xrow + col));
+                lo = *reinterpret_cast<const __half2*>(&raw.x);
+                hi = *reinterpret_cast<const __half2*>(&raw.y);
             } else {
-                const long long col = ((long long)(t0 + c) * VW + (s >> 1)) * 8 + (s & 1) * 4;
-                __half2 lo, hi;
-                if (p.x_vec) {
-                    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(xrow + col));
-                    lo = *reinterpret_cast<const __half2*>(&raw.x);
-                    hi = *reinterpret_cast<const __half2*>(&raw.y);
-                } else {
-                    lo = __halves2half2(xrow[col + 0], xrow[col + 1]);
-                    hi = __halves2half2(xrow[col + 2], xrow[col + 3]);
-                }
-                const float2 a = __half22float2(lo), d = __half22float2(hi);
-                v = make_uint4(__float_as_uint(a.x), __float_as_uint(a.y),
-                               __float_as_uint(d.x), __float_as_uint(d.y));
+                lo = __halves2half2(xrow[col + 0], xrow[col + 1]);
+                hi = __halves2half2(xrow[col + 2], xrow[col + 3]);
             }
+            float2 a = __half22float2(lo), d = __half22float2(hi);
+            if constexpr (F == kInt4) {
+                if ((s & 1) == 0) {          // columns 0..3: 2^0, 2^-4, 2^-8, 2^-12
+                    a.y *= 0x1p-4f;
+                    d.x *= 0x1p-8f;
+                    d.y *= 0x1p-12f;
+                } else {                     // columns 4..7: 2^-16, 2^-8, 2^-12, 2^-16
+                    a.x *= 0x1p-16f;
+                    a.y *= 0x1p-8f;
+                    d.x *= 0x1p-12f;
+                    d.y *= 0x1p-16f;
+                }
+            }
+            v = make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(d.x), __float_as_uint(d.y));
         }
         xs[b * per_b + swz<S>(c, s)] = v;
     }
@@ -149,58 +154,41 @@ __device__ __forceinline__ void gemv_step(const Frag<VW, RW>& cur, const uint4 (
 {
 #pragma unroll
     for (int i = 0; i < RW; ++i) {
-        if constexpr (F == kInt4) {
-            float plo[MB], phi[MB];
+        float2 pa[MB];
 #pragma unroll
-            for (int b = 0; b < MB; ++b) plo[b] = phi[b] = 0.0f;
+        for (int b = 0; b < MB; ++b) pa[b] = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int v = 0; v < VW; ++v) {
-                uint32_t h[4];
-                int4_word_to_half2(cur.w[i].w[v], h);
+        for (int v = 0; v < VW; ++v) {
+            const uint32_t w = cur.w[i].w[v];
+            float2 d[4];
+            if constexpr (F == kInt4) {
+                int4_word_to_f32x2(w, d);
+            } else {
 #pragma unroll
-                for (int b = 0; b < MB; ++b) {
-                    fma2_f32_f16(plo[b], phi[b], h[0], xv[b][v].x);
-                    fma2_f32_f16(plo[b], phi[b], h[1], xv[b][v].y);
-                    fma2_f32_f16(plo[b], phi[b], h[2], xv[b][v].z);
-                    fma2_f32_f16(plo[b], phi[b], h[3], xv[b][v].w);
-                }
-            }
-#pragma unroll
-            for (int b = 0; b < MB; ++b) acc[b][i] = fmaf(plo[b] + phi[b], cur.s[i], acc[b][i]);
-        } else {
-            float pa[MB], pb[MB];
-#pragma unroll
-            for (int b = 0; b < MB; ++b) pa[b] = pb[b] = 0.0f;
-#pragma unroll
-            for (int v = 0; v < VW; ++v) {
-                const uint32_t w = cur.w[i].w[v];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    float t;
-                    if constexpr (LUT == 0)
-                        t = nf4_lookup_shfl(lut, w >> (4 * k));
-                    else
-                        t = lut_s[(w >> (4 * k)) & 15u];
-#pragma unroll
-                    for (int b = 0; b < MB; ++b) {
-                        const uint4 q = xv[b][2 * v + (k >> 2)];
-                        const uint32_t xb = (k & 3) == 0 ? q.x : (k & 3) == 1 ? q.y : (k & 3) == 2 ? q.z : q.w;
-                        if (k & 1)
-                            pb[b] = fmaf(t, __uint_as_float(xb), pb[b]);
-                        else
-                            pa[b] = fmaf(t, __uint_as_float(xb), pa[b]);
+                for (int k = 0; k < 4; ++k) {
+                    if constexpr (LUT == 0) {
+                        d[k].x = nf4_lookup_shfl(lut, w >> (8 * k));
+                        d[k].y = nf4_lookup_shfl(lut, w >> (8 * k + 4));
+                    } else {
+                        d[k].x = lut_s[(w >> (8 * k)) & 15u];
+                        d[k].y = lut_s[(w >> (8 * k + 4)) & 15u];
                     }
                 }
             }
 #pragma unroll
-            for (int b = 0; b < MB; ++b) acc[b][i] = fmaf(pa[b] + pb[b], cur.s[i], acc[b][i]);
+            for (int b = 0; b < MB; ++b) {
+                const uint4 q0 = xv[b][2 * v], q1 = xv[b][2 * v + 1];
+                pa[b] = __ffma2_rn(d[0], make_float2(__uint_as_float(q0.x), __uint_as_float(q0.y)), pa[b]);
+                pa[b] = __ffma2_rn(d[1], make_float2(__uint_as_float(q0.z), __uint_as_float(q0.w)), pa[b]);
+                pa[b] = __ffma2_rn(d[2], make_float2(__uint_as_float(q1.x), __uint_as_float(q1.y)), pa[b]);
+                pa[b] = __ffma2_rn(d[3], make_float2(__uint_as_float(q1.z), __uint_as_float(q1.w)), pa[b]);
+            }
         }
+#pragma unroll
+        for (int b = 0; b < MB; ++b) acc[b][i] = fmaf(pa[b].x + pa[b].y, cur.s[i], acc[b][i]);
     }
 }
 
-// Grid: any number of CTAs; CTA j handles row tiles j, j + gridDim.x, ...
-// (a row tile is rg row groups of RW rows).  With one x tile and m <= MB the
-// CTA stages x once and keeps it for all its row tiles.
 // Threads per CTA the kernel is compiled for: 16 warps only for the
 // single-row, single-batch variants (the reference's block-per-row shapes);
 // 8 warps otherwise, which leaves up to 255 registers per thread.

@@ -23,6 +23,17 @@ __device__ __forceinline__ int lround_int(float q)
     return (int)(uint32_t)(unsigned long long)l;
 }
 
+// x86 SSE arithmetic turns an invalid operation on non-NaN operands (here
+// only 0 * inf, when a group's fp16 scale overflowed) into the "default NaN"
+// 0xffc00000; the GPU produces 0x7fffffff.  Dequantised values are rewritten to
+// the x86 bits so the device output is byte-identical to the reference's
+// host-computed `deq` (kernels.cuh:290,331).  No operand here is ever NaN:
+// scales and absmax come from a max that skips NaN.
+__device__ __forceinline__ float host_nan(float v)
+{
+    return isnan(v) ? __uint_as_float(0xffc00000u) : v;
+}
+
 // One thread per packed word: 8 dequantised columns.
 template <int F>
 __global__ void dequant_kernel(const uint32_t* __restrict__ qw, const void* __restrict__ scale,
@@ -43,7 +54,7 @@ __global__ void dequant_kernel(const uint32_t* __restrict__ qw, const void* __re
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const int code = (w >> (4 * k)) & 0xf;
-            v[k] = (F == kInt4) ? __fmul_rn((float)(code - 8), s) : __fmul_rn(c_nf4_table[code], s);
+            v[k] = host_nan((F == kInt4) ? __fmul_rn((float)(code - 8), s) : __fmul_rn(c_nf4_table[code], s));
         }
         float* o = out + i * 8;
         if (vec_out) {
@@ -115,7 +126,7 @@ __global__ void quant_int4_kernel(const float* __restrict__ W, int out_f, int in
         int code = lround_int(__fdiv_rn(w[k], s_used)) + 8;
         code = min(15, max(0, code));
         nib |= (uint32_t)code << (4 * k);
-        if (deq) deq[off + k] = __fmul_rn((float)(code - 8), s_used);
+        if (deq) deq[off + k] = host_nan(__fmul_rn((float)(code - 8), s_used));
     }
     const uint32_t other = __shfl_down_sync(0xffffffffu, nib, 1);
     if ((lane & 1) == 0) packed[(off >> 3)] = nib | (other << 16);
@@ -153,7 +164,7 @@ __global__ void quant_nf4_kernel(const float* __restrict__ W, int out_f, int in_
             if (d < bd) { bd = d; best = c; }
         }
         byte |= (uint32_t)best << (4 * k);
-        if (deq) deq[off + k] = __fmul_rn(c_nf4_table[best], amax);
+        if (deq) deq[off + k] = host_nan(__fmul_rn(c_nf4_table[best], amax));
     }
     const uint32_t b1 = __shfl_down_sync(0xffffffffu, byte, 1);
     const uint32_t b2 = __shfl_down_sync(0xffffffffu, byte, 2);

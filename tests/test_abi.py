@@ -41,9 +41,15 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_default_config_is_valid(fmt, out_f, in_f, m):
     c = b4gemv.default_config(fmt, in_f, out_f, m)
     assert c["vec_words"] in (1, 2, 4) and (in_f // 8) % c["vec_words"] == 0
-    assert c["rows_per_warp"] in (1, 2, 4, 8)
-    assert c["batch_tile"] in (1, 2, 4)
-    assert 1 <= c["warps_k"] * c["row_groups"] <= (16 if c["rows_per_warp"] * c["batch_tile"] == 1 else 8)
+    if c["engine"] == 1:
+        assert fmt == 0 and c["vec_words"] == 4
+        assert c["rows_per_warp"] in (16, 32) and c["batch_tile"] in (8, 16)
+        assert 1 <= c["warps_k"] * c["row_groups"] <= 8
+    else:
+        assert c["engine"] == 0
+        assert c["rows_per_warp"] in (1, 2, 4, 8)
+        assert c["batch_tile"] in (1, 2, 4)
+        assert 1 <= c["warps_k"] * c["row_groups"] <= (16 if c["rows_per_warp"] * c["batch_tile"] == 1 else 8)
 
 
 def test_invalid_shapes_are_rejected_before_any_launch():
@@ -63,6 +69,9 @@ def test_invalid_shapes_are_rejected_before_any_launch():
     # a config the kernel set does not contain
     cfg = _lib.GemvConfig(vec_words=3, rows_per_warp=1, warps_k=1, row_groups=1, batch_tile=1)
     assert lib.b4_gemv_ex(1, bogus, bogus, bogus, bogus, 64, 8, 1, ctypes.byref(cfg), None) == inv
+    # the tensor-pipe engine is INT4 only
+    cfg = _lib.GemvConfig(vec_words=4, rows_per_warp=16, warps_k=1, row_groups=1, batch_tile=8, engine=1)
+    assert lib.b4_gemv_ex(1, bogus, bogus, bogus, bogus, 128, 8, 1, ctypes.byref(cfg), None) == inv
     assert lib.b4_dequant_int4_g128(bogus, bogus, bogus, 96, 8, None) == inv
     assert lib.b4_unpack_codes(bogus, bogus, 12, 8, None) == inv
     assert lib.b4_quantise_nf4_b64_device(bogus, 8, 100, bogus, bogus, None, None) == inv

@@ -128,23 +128,26 @@ def test_gemv_edge_case_nan_rows(cuda, golden, oracle):
 
 def kernel_configs():
     """Every instantiated kernel (vec_words, rows_per_warp, batch_tile, nf4_lut)."""
-    out = []
+    out = [(0, 4, rw, mb, 0, 1) for rw in (16, 32) for mb in (8, 16)]  # tensor-pipe INT4
     for fmt in (0, 1):
         for lut in ((0,) if fmt == 0 else (0, 1)):
             for vw, rw in [(1, 1), (1, 4)]:
-                out.append((fmt, vw, rw, 1, lut))
+                out.append((fmt, vw, rw, 1, lut, 0))
             for vw in (2, 4):
                 for mb in (1, 2, 4):
                     for rw in (1, 2, 4, 8):
                         if not (mb == 4 and rw == 8):
-                            out.append((fmt, vw, rw, mb, lut))
+                            out.append((fmt, vw, rw, mb, lut, 0))
     return out
 
 
-@pytest.mark.parametrize("fmt,vw,rw,mb,lut", kernel_configs())
-def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut):
-    rng = np.random.default_rng(1000 + fmt * 100 + vw * 10 + rw + mb * 7 + lut)
-    for out_f, in_f, m in [(37, 1152, 1), (9, 512, 3), (70, 3584, 5)]:
+@pytest.mark.parametrize("fmt,vw,rw,mb,lut,engine", kernel_configs())
+def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
+    rng = np.random.default_rng(1000 + fmt * 100 + vw * 10 + rw + mb * 7 + lut + engine)
+    cases = [(37, 1152, 1), (9, 512, 3), (70, 3584, 5)]
+    if engine == 1:
+        cases += [(100, 1024, 11), (33, 2048, 16), (48, 640, 8), (16, 128, 1)]
+    for out_f, in_f, m in cases:
         W, X = rand_problem(rng, out_f, in_f, m)
         qw, sc = quantised(fmt, W, cuda)
         ref = f64_ref(oracle, fmt, qw, sc, X)
@@ -152,12 +155,13 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut):
         for kw, rg in [(1, 1), (2, 2), (4, 1), (1, 4)]:
             if (rw > 1 or mb > 1) and kw * rg > 8:
                 continue
-            cfg = dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=mb, nf4_lut=lut)
+            cfg = dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=mb, nf4_lut=lut,
+                       engine=engine)
             y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
             assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
         # several x tiles in shared memory
         cfg = dict(vec_words=vw, rows_per_warp=rw, warps_k=2, row_groups=1, batch_tile=mb, nf4_lut=lut,
-                   x_tile=8 * vw * 32)
+                   x_tile=(128 if engine == 1 else 8 * vw * 32), engine=engine)
         y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
         assert rel_err(y, ref) < TOL, ("x_tile", out_f, in_f, m, cfg)
 
