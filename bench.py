@@ -417,6 +417,76 @@ def cpu_fused_baseline(sets, xs, budget_s=10.0):
                       f"{el:.1f} s, {threads} threads on {os.cpu_count()} host cores"}
 
 
+def chain_bench(b4, torch, dev):
+    """28 Qwen2.5-7B layers x 7 INT4 projections in one
+    CUDA graph, one token; us per token with and without programmatic
+    dependent launch."""
+    from b4gemv.chain import DecodeChain
+    ch = DecodeChain(torch, dev, fmt=0, layers=28)
+    peak, _ = measured_peak()
+    out = {"config": "configs[2]: 28 layers x q/k/v/o/gate/up/down INT4 g128, batch 1, one CUDA graph",
+           "bytes_per_token": ch.bytes, "gemvs_per_token": len(ch.calls)}
+    for pdl in (False, True):
+        us = ch.time_token(pdl)
+        out["pdl" if pdl else "plain"] = {"us_per_token": round(us, 2), "gbs": round(ch.bytes / us / 1e3, 1),
+                                          "frac": round(ch.bytes / us / 1e3 / peak, 4)}
+    del ch
+    torch.cuda.empty_cache()
+    return out
+
+
+def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
+    """the Llama-3-70B decode layer's projections sharded
+    over the N ranks of this run (column-parallel q/k/v/gate/up, row-parallel
+    o/down + NCCL all-reduce of fp32 y), replayed from a CUDA graph; us per
+    layer is the max over ranks."""
+    from b4gemv.tp import NcclComm, TPDecodeLayer
+    comm = NcclComm(d.rank, d.world) if d.world > 1 else None
+    layer = TPDecodeLayer(fmt, d.rank, d.world, comm, dev, seed=5)
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    x = torch.randn((1, 8192), generator=g, device=dev).half()
+    c0, c1 = layer.ranges["o"]
+    attn = torch.randn((1, c1 - c0), generator=g, device=dev).half()
+    layer.forward(x, attn)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    reps = 20
+    with torch.cuda.graph(graph, stream=cs, capture_error_mode="relaxed"):
+        for _ in range(reps):
+            layer.forward(x, attn)
+    torch.cuda.current_stream().wait_stream(cs)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    d.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    n = max(1, steps // reps)
+    a.record()
+    for _ in range(n):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    d.barrier()
+    us = a.elapsed_time(b) * 1e3 / (n * reps)
+    us_max = d.max(us, dev)
+    wb = layer.weight_bytes()
+    del graph
+    torch.cuda.synchronize()
+    if comm is not None:
+        comm.destroy()
+    del layer
+    torch.cuda.empty_cache()
+    peak, _ = measured_peak()
+    return {"format": "int4_g128" if fmt == 0 else "nf4_b64", "tp": d.world, "us_per_layer": round(us_max, 2),
+            "weight_bytes_per_rank": wb, "gbs_per_rank": round(wb / us_max / 1e3, 1),
+            "frac_per_rank": round(wb / us_max / 1e3 / peak, 4),
+            "allreduces_per_layer": 2 if d.world > 1 else 0}
+
+
 def run_ours(args, d):
     import torch
     import b4gemv as b4
@@ -549,9 +619,15 @@ def run_ours(args, d):
         "correctness_rel_err": gate_err,
         "clocks": clocks,
     }
+    del launcher, g_main, g_ev, g_rem
+    torch.cuda.synchronize()
     if args.detail:
         result["int4_chained"] = per_shape_chained(b4, torch, 0)
         result["nf4_chained"] = per_shape_chained(b4, torch, 1)
+    if not args.no_chain:
+        result["qwen28_int4_chain"] = chain_bench(b4, torch, dev)
+    if not args.no_tp:
+        result["l70_tp_layer"] = [tp_layer_bench(b4, torch, dev, d, fmt) for fmt in (0, 1)]
     if n == 1 and d.rank == 0 and not args.no_cpu:
         result["cpu_baseline"] = cpu_fused_baseline(sets, xs, budget_s=args.cpu_seconds)
     if d.rank == 0:
@@ -633,6 +709,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--detail", action="store_true", help="also per-shape chained us for INT4 and NF4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-chain", action="store_true", help="skip the 28-layer INT4 graph chain")
+    ap.add_argument("--no-tp", action="store_true", help="skip the Llama-3-70B tensor-parallel layer")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="untimed load before the timed region, for the clock samples")

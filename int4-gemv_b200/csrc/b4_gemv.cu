@@ -146,7 +146,7 @@ int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
     if (!fn) return cudaErrorInvalidValue;
 
     const int chunks = words / vw;
-    const int S = p.fmt == kInt4 ? vw : 2 * vw;
+    const int S = x_slots_per_chunk(vw);
     const int cols_per_chunk = 8 * vw;
     int tile_chunks;
     if (c.x_tile > 0) {

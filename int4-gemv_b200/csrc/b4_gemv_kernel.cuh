@@ -50,9 +50,12 @@ struct KParams {
 };
 
 // 16-byte shared-memory slots of staged x per chunk: 8 fp32 values per word.
+// The host launcher sizes shared memory with the same function.
+__host__ __device__ constexpr int x_slots_per_chunk(int vw) { return 2 * vw; }
+
 template <int F, int VW>
 struct XSlots {
-    static constexpr int S = 2 * VW;
+    static constexpr int S = x_slots_per_chunk(VW);
 };
 
 // Physical slot of logical slot s of tile-relative chunk c: XOR-swizzled so
