@@ -59,6 +59,8 @@ typedef struct b4_gemv_config {
     int x_tile;        /* columns of x staged in shared memory per pass, 0 = auto */
     int flags;         /* B4_FLAG_* */
     int engine;        /* B4_ENGINE_*: which pipe does the multiply-accumulates   */
+    int stages;        /* B4_ENGINE_MMA_TMA: ring stages per warp (3, 4, 6 or 8)  */
+    int stage_groups;  /* B4_ENGINE_MMA_TMA: 128-column groups per stage (2, 4, 8) */
 } b4_gemv_config;
 
 /* CUDA cores: fp32 FMA (INT4 and NF4).  rows_per_warp 1/2/4/8, batch_tile 1/2/4. */
@@ -67,6 +69,10 @@ typedef struct b4_gemv_config {
  * fp32 accumulate.  rows_per_warp 16 or 32, batch_tile 8 or 16 (the MMA's N:
  * batch rows ride along for free), vec_words 4, x_tile a multiple of 128. */
 #define B4_ENGINE_MMA 1
+/* Tensor pipe fed by a per-warp ring of bulk copies (TMA) in shared memory:
+ * rows_per_warp 16, batch_tile 8 (m <= 8) or 16 (m <= 16), vec_words 4; the
+ * whole of x must fit in shared memory next to the rings.  Persistent grid. */
+#define B4_ENGINE_MMA_TMA 2
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
  * the weight stream starts before the producer of x has finished. */
@@ -176,6 +182,12 @@ int b4_tp_gemv_allreduce(int fmt, const uint32_t* qw_shard, const void* scale_sh
 int b4_swiglu_f16(const float* gate, const float* up, void* out, long long n, b4_stream_t stream);
 int b4_cast_f16(const float* in, void* out, long long n, b4_stream_t stream);
 const char* b4_nccl_error_string(int status);
+
+/* Reads (and with clear != 0 resets) the current device's error flag: non-zero
+ * after a streaming kernel's bounded wait on its copy ring ran out (the
+ * kernel then ended early and its y is not valid).  Returns the flag, or -1
+ * if it could not be read. */
+int b4_device_error(int clear);
 
 /* ---- Misc -------------------------------------------------------------------
  * One empty kernel launch: the empty-launch floor that bench/baseline.py:71-76

@@ -19,6 +19,7 @@ NF4_BLOCK = 64
 FLAG_PDL = 1
 ENGINE_FMA = 0
 ENGINE_MMA = 1
+ENGINE_MMA_TMA = 2
 
 
 class GemvConfig(ctypes.Structure):
@@ -34,6 +35,8 @@ class GemvConfig(ctypes.Structure):
         ("x_tile", ctypes.c_int),
         ("flags", ctypes.c_int),
         ("engine", ctypes.c_int),
+        ("stages", ctypes.c_int),
+        ("stage_groups", ctypes.c_int),
     ]
 
     def as_dict(self) -> dict:
@@ -74,6 +77,7 @@ SIGNATURES = {
     "b4_swiglu_f16": (_I, [_P, _P, _P, ctypes.c_longlong, _P]),
     "b4_cast_f16": (_I, [_P, _P, ctypes.c_longlong, _P]),
     "b4_nccl_error_string": (ctypes.c_char_p, [_I]),
+    "b4_device_error": (_I, [_I]),
     "b4_status_string": (ctypes.c_char_p, [_I]),
     "b4_abi_version": (_I, []),
 }

@@ -90,7 +90,16 @@ def time_chained(torch, prob, cfg, reps=100):
     return best
 
 
+TMA_VARIANTS = [(4, 4), (3, 4), (6, 4), (4, 2), (4, 8), (8, 2)]   # (stages, stage_groups) instantiated
+
+
 def config_grid(fmt, m=1):
+    if fmt == FMT_INT4_G128 and m <= 16:
+        nt = 8 if m <= 8 else 16
+        for kw, rg, (st, kcg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), TMA_VARIANTS):
+            if kw * rg <= 8 and (nt == 8 or (st, kcg) == (4, 4)):
+                yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=nt, nf4_lut=0,
+                           x_tile=0, flags=0, engine=2, stages=st, stage_groups=kcg)
     if fmt == FMT_INT4_G128:
         for rw, kw, rg, nt in itertools.product((16, 32), (1, 2, 4, 8), (1, 2, 4, 8), (8, 16)):
             if kw * rg <= 8 and (nt == 8 or m > 8):

@@ -79,25 +79,30 @@ __device__ __forceinline__ WordVec<4> ld_stream<4>(const uint32_t* p)
 //   h[0] = (n0-8, n4-8)   h[1] = (n1-8, n5-8)
 //   h[2] = (n2-8, n6-8)   h[3] = (n3-8, n7-8)
 // as half2 (low half first).  x is staged in the matching pair order.
+// Written as plain C so the compiler can fold the masks and magic constants
+// into immediate operands (an inline-asm LOP3 would force each constant into
+// a register).
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic)
 {
-    uint32_t r;
-    asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(a), "r"(mask), "r"(magic));
-    return r;  // (a & mask) | magic
+    return (a & mask) | magic;
+}
+
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint16_t k)
+{
+    __half2_raw kr;
+    kr.x = k;
+    kr.y = k;
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), __half2(kr));
+    return *reinterpret_cast<const uint32_t*>(&r);
 }
 
 __device__ __forceinline__ void int4_word_to_half2(uint32_t w, uint32_t h[4])
 {
     const uint32_t w8 = w >> 8;
-    const uint32_t t0 = lop3_and_or(w, 0x000f000fu, 0x64006400u);
-    const uint32_t t1 = lop3_and_or(w, 0x00f000f0u, 0x54005400u);
-    const uint32_t t2 = lop3_and_or(w8, 0x000f000fu, 0x64006400u);
-    const uint32_t t3 = lop3_and_or(w8, 0x00f000f0u, 0x54005400u);
-    // 1032 = 0x6408, 72 = 0x5480 in fp16
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[0]) : "r"(t0), "r"(0x64086408u));
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[1]) : "r"(t1), "r"(0x54805480u));
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2]) : "r"(t2), "r"(0x64086408u));
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(h[3]) : "r"(t3), "r"(0x54805480u));
+    h[0] = hsub2_bits(lop3_and_or(w, 0x000f000fu, 0x64006400u), 0x6408);   // - 1032
+    h[1] = hsub2_bits(lop3_and_or(w, 0x00f000f0u, 0x54005400u), 0x5480);   // - 72
+    h[2] = hsub2_bits(lop3_and_or(w8, 0x000f000fu, 0x64006400u), 0x6408);
+    h[3] = hsub2_bits(lop3_and_or(w8, 0x00f000f0u, 0x54005400u), 0x5480);
 }
 
 // INT4 decode to fp32 for the CUDA-core kernel: OR-ing nibble j into the

@@ -8,6 +8,7 @@
 
 #include "b4_gemv_kernel.cuh"
 #include "b4_gemv_mma.cuh"
+#include "b4_gemv_tma.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -82,20 +83,30 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     cfg->nf4_lut = 0;
     cfg->x_tile = 0;
     cfg->flags = 0;
+    cfg->stages = 4;
+    cfg->stage_groups = 4;
 
-    // INT4 with 16-byte aligned codes: multiply-accumulates on the tensor pipe.
+    // INT4 with 16-byte aligned codes: multiply-accumulates on the tensor pipe,
+    // codes streamed through per-warp bulk-copy rings when x fits next to them.
     if (p.fmt == kInt4 && aligned(p.qw, 16)) {
         const int groups = p.in_f / kGroup;
         const int row_groups = (p.out_f + 15) / 16;
-        int kw = 1;
-        while (kw < 8 && (long long)row_groups * kw < sms * 16LL && groups >= 2 * (2 * kw)) kw *= 2;
-        int rg = std::max(1, std::min(8 / kw, row_groups / (2 * sms)));
-        cfg->engine = B4_ENGINE_MMA;
+        const int nb = std::min(p.m, 16);
         cfg->vec_words = 4;
         cfg->rows_per_warp = 16;
-        cfg->warps_k = kw;
-        cfg->row_groups = rg;
         cfg->batch_tile = p.m > 8 ? 16 : 8;
+        if (p.m <= 16 && (size_t)nb * groups * 256 <= 64 * 1024) {
+            const int rg = std::max(1, std::min(8, row_groups / sms));
+            cfg->engine = B4_ENGINE_MMA_TMA;
+            cfg->warps_k = std::max(1, 8 / rg);
+            cfg->row_groups = rg;
+            return;
+        }
+        int kw = 1;
+        while (kw < 8 && (long long)row_groups * kw < sms * 16LL && groups >= 2 * (2 * kw)) kw *= 2;
+        cfg->engine = B4_ENGINE_MMA;
+        cfg->warps_k = kw;
+        cfg->row_groups = std::max(1, std::min(8 / kw, row_groups / (2 * sms)));
         return;
     }
 
@@ -127,10 +138,12 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
 }
 
 int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
+int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
     if (c.engine == B4_ENGINE_MMA) return launch_gemv_mma(p, c, st);
+    if (c.engine == B4_ENGINE_MMA_TMA) return launch_gemv_tma(p, c, st);
     if (c.engine != B4_ENGINE_FMA) return cudaErrorInvalidValue;
     const int vw = c.vec_words, rw = c.rows_per_warp, kw = c.warps_k, rg = c.row_groups;
     const int mb = c.batch_tile, lut = c.nf4_lut;
@@ -284,6 +297,104 @@ int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t 
     return launch_common(fn, p, kp, grid, 32 * kw * rg, smem, c.flags, st);
 }
 
+namespace {
+
+int sm_count_cached(int dev)
+{
+    static std::atomic<int> cache[64];
+    if (dev < 0 || dev >= 64) return 148;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
+}  // namespace
+
+// Shared memory of the streaming kernel: x (whole of in_f, nb batch rows),
+// the warps_k reduction scratch, then per-warp rings and mbarriers.
+struct TmaLayout {
+    size_t ring_offset, bar_offset, total;
+};
+
+TmaLayout tma_layout(int nb, int ng, int kw, int rg, int nt, int stages, int kcg)
+{
+    const size_t x_bytes = (size_t)nb * ng * 256;
+    const size_t red_bytes = kw > 1 ? (size_t)rg * kw * nt * 4 * 32 * 4 : 0;
+    TmaLayout l;
+    l.ring_offset = (x_bytes + red_bytes + 127) / 128 * 128;
+    const size_t stage_bytes = 16 * (size_t)(kcg * 64 + 64);
+    l.bar_offset = l.ring_offset + (size_t)kw * rg * stages * stage_bytes;
+    l.total = l.bar_offset + (size_t)kw * rg * stages * 8;
+    return l;
+}
+
+int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    if (p.fmt != kInt4 || c.vec_words != 4 || c.rows_per_warp != 16) return cudaErrorInvalidValue;
+    if (c.batch_tile != 8 && c.batch_tile != 16) return cudaErrorInvalidValue;
+    if (p.m > c.batch_tile) return cudaErrorInvalidValue;
+    const int kw = c.warps_k, rg = c.row_groups;
+    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 16)) return cudaErrorInvalidValue;
+    const int nt = c.batch_tile / 8;
+    void* fn = gemv_kernel_int4_tma(nt, c.stages, c.stage_groups);
+    if (!fn) return cudaErrorInvalidValue;
+    const int ng = p.in_f / kGroup;
+    const int nb = std::min(p.m, c.batch_tile);
+    const TmaLayout l = tma_layout(nb, ng, kw, rg, nt, c.stages, c.stage_groups);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    TmaParams tp;
+    KParams& kp = tp.k;
+    kp.qw = p.qw;
+    kp.scale = p.scale;
+    kp.x = static_cast<const __half*>(p.x);
+    kp.y = p.y;
+    kp.in_f = p.in_f;
+    kp.out_f = p.out_f;
+    kp.m = p.m;
+    kp.x_ld = p.x_ld;
+    kp.y_ld = p.y_ld;
+    kp.kw = kw;
+    kp.rg = rg;
+    kp.tile_chunks = ng;
+    kp.x_vec = aligned(p.x, 16) && ((p.x_ld * 2) % 16 == 0);
+    tp.stages_dummy = c.stages;
+    tp.ring_offset = (int)l.ring_offset;
+    tp.bar_offset = (int)l.bar_offset;
+    const long long rows_per_cta = (long long)rg * 16;
+    const long long tiles = (p.out_f + rows_per_cta - 1) / rows_per_cta;
+    const int per_sm = std::max<int>(1, (int)((228 * 1024) / (l.total + 1024)));
+    const long long grid = std::min<long long>(tiles, (long long)sm_count_cached(dev) * per_sm);
+    // launch_common takes KParams; the streaming kernel's parameter block is larger
+    int smem_max = 0;
+    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (l.total > (size_t)smem_max) return cudaErrorInvalidValue;
+    if (l.total > 48 * 1024) {
+        e = ensure_smem(fn, dev, l.total);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)grid);
+    lc.blockDim = dim3(32 * kw * rg);
+    lc.dynamicSmemBytes = l.total;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (c.flags & B4_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+    }
+    void* args[] = {&tp};
+    return cudaLaunchKernelExC(&lc, fn, args);
+}
+
 }  // namespace b4
 
 using namespace b4;
@@ -343,6 +454,8 @@ int b4_gemv_nf4_b64_block_per_row(const uint32_t* qw, const float* absmax, const
     if (c.vec_words == 1) c.rows_per_warp = 1;
     return launch_gemv(p, c, reinterpret_cast<cudaStream_t>(stream));
 }
+
+int b4_device_error(int clear) { return gemv_tma_device_error(clear); }
 
 int b4_empty_launch(b4_stream_t stream)
 {

@@ -163,28 +163,37 @@ __device__ __forceinline__ void gemv_step(const Frag<VW, RW>& cur, const uint4 (
 #pragma unroll
         for (int v = 0; v < VW; ++v) {
             const uint32_t w = cur.w[i].w[v];
-            float2 d[4];
             if constexpr (F == kInt4) {
+                // decoded pairs come out of FADD2 as register pairs: FFMA2
+                float2 d[4];
                 int4_word_to_f32x2(w, d);
-            } else {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    if constexpr (LUT == 0) {
-                        d[k].x = nf4_lookup_shfl(lut, w >> (8 * k));
-                        d[k].y = nf4_lookup_shfl(lut, w >> (8 * k + 4));
-                    } else {
-                        d[k].x = lut_s[(w >> (8 * k)) & 15u];
-                        d[k].y = lut_s[(w >> (8 * k + 4)) & 15u];
+                for (int b = 0; b < MB; ++b) {
+                    const uint4 q0 = xv[b][2 * v], q1 = xv[b][2 * v + 1];
+                    pa[b] = __ffma2_rn(d[0], make_float2(__uint_as_float(q0.x), __uint_as_float(q0.y)), pa[b]);
+                    pa[b] = __ffma2_rn(d[1], make_float2(__uint_as_float(q0.z), __uint_as_float(q0.w)), pa[b]);
+                    pa[b] = __ffma2_rn(d[2], make_float2(__uint_as_float(q1.x), __uint_as_float(q1.y)), pa[b]);
+                    pa[b] = __ffma2_rn(d[3], make_float2(__uint_as_float(q1.z), __uint_as_float(q1.w)), pa[b]);
+                }
+            } else {
+                // looked-up values land in arbitrary registers: scalar FMA, two chains
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    float t;
+                    if constexpr (LUT == 0)
+                        t = nf4_lookup_shfl(lut, w >> (4 * k));
+                    else
+                        t = lut_s[(w >> (4 * k)) & 15u];
+#pragma unroll
+                    for (int b = 0; b < MB; ++b) {
+                        const uint4 q = xv[b][2 * v + (k >> 2)];
+                        const uint32_t xb = (k & 3) == 0 ? q.x : (k & 3) == 1 ? q.y : (k & 3) == 2 ? q.z : q.w;
+                        if (k & 1)
+                            pa[b].y = fmaf(t, __uint_as_float(xb), pa[b].y);
+                        else
+                            pa[b].x = fmaf(t, __uint_as_float(xb), pa[b].x);
                     }
                 }
-            }
-#pragma unroll
-            for (int b = 0; b < MB; ++b) {
-                const uint4 q0 = xv[b][2 * v], q1 = xv[b][2 * v + 1];
-                pa[b] = __ffma2_rn(d[0], make_float2(__uint_as_float(q0.x), __uint_as_float(q0.y)), pa[b]);
-                pa[b] = __ffma2_rn(d[1], make_float2(__uint_as_float(q0.z), __uint_as_float(q0.w)), pa[b]);
-                pa[b] = __ffma2_rn(d[2], make_float2(__uint_as_float(q1.x), __uint_as_float(q1.y)), pa[b]);
-                pa[b] = __ffma2_rn(d[3], make_float2(__uint_as_float(q1.z), __uint_as_float(q1.w)), pa[b]);
             }
         }
 #pragma unroll

@@ -41,10 +41,12 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_default_config_is_valid(fmt, out_f, in_f, m):
     c = b4gemv.default_config(fmt, in_f, out_f, m)
     assert c["vec_words"] in (1, 2, 4) and (in_f // 8) % c["vec_words"] == 0
-    if c["engine"] == 1:
+    if c["engine"] in (1, 2):
         assert fmt == 0 and c["vec_words"] == 4
         assert c["rows_per_warp"] in (16, 32) and c["batch_tile"] in (8, 16)
         assert 1 <= c["warps_k"] * c["row_groups"] <= 8
+        if c["engine"] == 2:
+            assert m <= c["batch_tile"] and c["rows_per_warp"] == 16
     else:
         assert c["engine"] == 0
         assert c["rows_per_warp"] in (1, 2, 4, 8)
