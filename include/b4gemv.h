@@ -59,7 +59,7 @@ typedef struct b4_gemv_config {
     int x_tile;        /* columns of x staged in shared memory per pass, 0 = auto */
     int flags;         /* B4_FLAG_* */
     int engine;        /* B4_ENGINE_*: which pipe does the multiply-accumulates   */
-    int stages;        /* B4_ENGINE_MMA_TMA: ring stages per warp (3, 4, 6 or 8)  */
+    int stages;        /* *_TMA engines: ring stages per warp (3, 4, 6 or 8)      */
     int stage_groups;  /* B4_ENGINE_MMA_TMA: 128-column groups per stage (2, 4, 8) */
 } b4_gemv_config;
 
@@ -73,6 +73,10 @@ typedef struct b4_gemv_config {
  * rows_per_warp 16, batch_tile 8 (m <= 8) or 16 (m <= 16), vec_words 4; the
  * whole of x must fit in shared memory next to the rings.  Persistent grid. */
 #define B4_ENGINE_MMA_TMA 2
+/* CUDA cores (NF4, m = 1) fed by a per-warp bulk-copy ring of codes and absmax:
+ * rows_per_warp 4, 8 or 16, vec_words 2 or 4, in_f a multiple of 256*vec_words,
+ * codes and absmax 16-byte aligned.  Persistent grid. */
+#define B4_ENGINE_FMA_TMA 3
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
  * the weight stream starts before the producer of x has finished. */

@@ -20,6 +20,7 @@ FLAG_PDL = 1
 ENGINE_FMA = 0
 ENGINE_MMA = 1
 ENGINE_MMA_TMA = 2
+ENGINE_FMA_TMA = 3
 
 
 class GemvConfig(ctypes.Structure):

@@ -91,6 +91,7 @@ def time_chained(torch, prob, cfg, reps=100):
 
 
 TMA_VARIANTS = [(4, 4), (3, 4), (6, 4), (4, 2), (4, 8), (8, 2)]   # (stages, stage_groups) instantiated
+NF4_TMA_VARIANTS = [(4, 2, 4), (4, 2, 8), (8, 2, 4), (8, 2, 6), (16, 2, 4), (4, 4, 4), (8, 4, 4)]  # (rw, vw, st)
 
 
 def config_grid(fmt, m=1):
@@ -105,6 +106,11 @@ def config_grid(fmt, m=1):
             if kw * rg <= 8 and (nt == 8 or m > 8):
                 yield dict(vec_words=4, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=nt, nf4_lut=0,
                            x_tile=0, flags=0, engine=1)
+    if fmt == FMT_NF4_B64 and m == 1:
+        for kw, rg, (rw, vw, st) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), NF4_TMA_VARIANTS):
+            if kw * rg <= 8:
+                yield dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
+                           x_tile=0, flags=0, engine=3, stages=st, stage_groups=0)
     luts = (0,) if fmt == FMT_INT4_G128 else (0, 1)
     mbs = (1,) if m == 1 else ((2,) if m == 2 else (4,))
     for vw, rw, kw, rg, mb, lut in itertools.product((2, 4), (1, 2, 4, 8), (1, 2, 4, 8), (1, 2, 4, 8), mbs, luts):

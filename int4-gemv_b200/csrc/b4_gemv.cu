@@ -9,6 +9,7 @@
 #include "b4_gemv_kernel.cuh"
 #include "b4_gemv_mma.cuh"
 #include "b4_gemv_tma.cuh"
+#include "b4_gemv_tma_nf4.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -63,6 +64,27 @@ constexpr int kSmemBudget = 96 * 1024;
 
 }  // namespace
 
+// Shared memory of the streaming kernel: x (whole of in_f, nb batch rows),
+// the warps_k reduction scratch, then per-warp rings and mbarriers.
+struct TmaLayout {
+    size_t ring_offset, bar_offset, total;
+};
+
+TmaLayout tma_layout(int nb, int ng, int kw, int rg, int nt, int stages, int kcg)
+{
+    const size_t x_bytes = (size_t)nb * ng * 256;
+    const size_t red_bytes = kw > 1 ? (size_t)rg * kw * nt * 4 * 32 * 4 : 0;
+    TmaLayout l;
+    l.ring_offset = (x_bytes + red_bytes + 127) / 128 * 128;
+    const size_t stage_bytes = 16 * (size_t)(kcg * 64 + 64);
+    l.bar_offset = l.ring_offset + (size_t)kw * rg * stages * stage_bytes;
+    l.total = l.bar_offset + (size_t)kw * rg * stages * 8;
+    return l;
+}
+
+// Opt-in shared memory per CTA on B200 (227 KB).
+constexpr size_t kTmaSmemLimit = 227 * 1024;
+
 int check_problem(const GemvProblem& p)
 {
     if (p.fmt != kInt4 && p.fmt != kNf4) return cudaErrorInvalidValue;
@@ -95,12 +117,20 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
         cfg->vec_words = 4;
         cfg->rows_per_warp = 16;
         cfg->batch_tile = p.m > 8 ? 16 : 8;
-        if (p.m <= 16 && (size_t)nb * groups * 256 <= 64 * 1024) {
+        if (p.m <= 16) {
             const int rg = std::max(1, std::min(8, row_groups / sms));
-            cfg->engine = B4_ENGINE_MMA_TMA;
-            cfg->warps_k = std::max(1, 8 / rg);
-            cfg->row_groups = rg;
-            return;
+            // largest CTA (8, 4 or 2 warps) whose x + rings fit in shared memory
+            for (int warps = 8; warps >= 2; warps /= 2) {
+                const int rgw = std::min(rg, warps);
+                const int kw = std::max(1, warps / rgw);
+                const TmaLayout l = tma_layout(nb, groups, kw, rgw, cfg->batch_tile / 8, 4, 4);
+                if (l.total <= kTmaSmemLimit) {
+                    cfg->engine = B4_ENGINE_MMA_TMA;
+                    cfg->warps_k = kw;
+                    cfg->row_groups = rgw;
+                    return;
+                }
+            }
         }
         int kw = 1;
         while (kw < 8 && (long long)row_groups * kw < sms * 16LL && groups >= 2 * (2 * kw)) kw *= 2;
@@ -139,11 +169,13 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
 
 int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
+int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
     if (c.engine == B4_ENGINE_MMA) return launch_gemv_mma(p, c, st);
     if (c.engine == B4_ENGINE_MMA_TMA) return launch_gemv_tma(p, c, st);
+    if (c.engine == B4_ENGINE_FMA_TMA) return launch_gemv_tma_nf4(p, c, st);
     if (c.engine != B4_ENGINE_FMA) return cudaErrorInvalidValue;
     const int vw = c.vec_words, rw = c.rows_per_warp, kw = c.warps_k, rg = c.row_groups;
     const int mb = c.batch_tile, lut = c.nf4_lut;
@@ -313,24 +345,6 @@ int sm_count_cached(int dev)
 
 }  // namespace
 
-// Shared memory of the streaming kernel: x (whole of in_f, nb batch rows),
-// the warps_k reduction scratch, then per-warp rings and mbarriers.
-struct TmaLayout {
-    size_t ring_offset, bar_offset, total;
-};
-
-TmaLayout tma_layout(int nb, int ng, int kw, int rg, int nt, int stages, int kcg)
-{
-    const size_t x_bytes = (size_t)nb * ng * 256;
-    const size_t red_bytes = kw > 1 ? (size_t)rg * kw * nt * 4 * 32 * 4 : 0;
-    TmaLayout l;
-    l.ring_offset = (x_bytes + red_bytes + 127) / 128 * 128;
-    const size_t stage_bytes = 16 * (size_t)(kcg * 64 + 64);
-    l.bar_offset = l.ring_offset + (size_t)kw * rg * stages * stage_bytes;
-    l.total = l.bar_offset + (size_t)kw * rg * stages * 8;
-    return l;
-}
-
 int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
     if (p.fmt != kInt4 || c.vec_words != 4 || c.rows_per_warp != 16) return cudaErrorInvalidValue;
@@ -393,6 +407,78 @@ int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t 
     }
     void* args[] = {&tp};
     return cudaLaunchKernelExC(&lc, fn, args);
+}
+
+namespace {
+
+// One launch of a streaming kernel whose parameter block is `params`.
+cudaError_t launch_persistent(void* fn, void* params, long long tiles, int threads, size_t smem, int flags,
+                              cudaStream_t st)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int smem_max = 0;
+    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (smem > (size_t)smem_max) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        e = ensure_smem(fn, dev, smem);
+        if (e != cudaSuccess) return e;
+    }
+    const int per_sm = std::max<int>(1, (int)((228 * 1024) / (smem + 1024)));
+    const long long grid = std::min<long long>(tiles, (long long)sm_count_cached(dev) * per_sm);
+    if (grid < 1) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)grid);
+    lc.blockDim = dim3(threads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (flags & B4_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+    }
+    void* args[] = {params};
+    return cudaLaunchKernelExC(&lc, fn, args);
+}
+
+}  // namespace
+
+int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    if (p.fmt != kNf4 || p.m != 1) return cudaErrorInvalidValue;
+    const int rw = c.rows_per_warp, vw = c.vec_words, kw = c.warps_k, rg = c.row_groups;
+    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
+    if (vw != 2 && vw != 4) return cudaErrorInvalidValue;
+    if (p.in_f % (256 * vw)) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 16) || !aligned(p.scale, 16)) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_nf4_tma(rw, vw, c.stages);
+    if (!fn) return cudaErrorInvalidValue;
+    const size_t stage_bytes = (size_t)rw * (128 * vw + 16 * vw);
+    const size_t x_red = (size_t)p.in_f * 4 + (size_t)rg * kw * rw * 4;
+    TmaNf4Params tp;
+    tp.ring_offset = (int)((x_red + 127) / 128 * 128);
+    tp.bar_offset = tp.ring_offset + (int)((size_t)kw * rg * c.stages * stage_bytes);
+    const size_t total = (size_t)tp.bar_offset + (size_t)kw * rg * c.stages * 8;
+    KParams& kp = tp.k;
+    kp.qw = p.qw;
+    kp.scale = p.scale;
+    kp.x = static_cast<const __half*>(p.x);
+    kp.y = p.y;
+    kp.in_f = p.in_f;
+    kp.out_f = p.out_f;
+    kp.m = p.m;
+    kp.x_ld = p.x_ld;
+    kp.y_ld = p.y_ld;
+    kp.kw = kw;
+    kp.rg = rg;
+    kp.tile_chunks = 0;
+    kp.x_vec = aligned(p.x, 8);
+    const long long rows_per_cta = (long long)rg * rw;
+    return launch_persistent(fn, &tp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, total, c.flags, st);
 }
 
 }  // namespace b4

@@ -130,6 +130,7 @@ def kernel_configs():
     """Every instantiated kernel (vec_words, rows_per_warp, batch_tile, nf4_lut)."""
     out = [(0, 4, rw, mb, 0, 1) for rw in (16, 32) for mb in (8, 16)]  # tensor-pipe INT4
     out += [(0, 4, 16, mb, 0, 2) for mb in (8, 16)]                     # tensor pipe + bulk-copy ring
+    out += [(1, vw, rw, 1, 0, 3) for rw, vw in [(4, 2), (8, 2), (16, 2), (4, 4), (8, 4)]]  # NF4 + ring
     for fmt in (0, 1):
         for lut in ((0,) if fmt == 0 else (0, 1)):
             for vw, rw in [(1, 1), (1, 4)]:
@@ -146,8 +147,11 @@ def kernel_configs():
 def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
     rng = np.random.default_rng(1000 + fmt * 100 + vw * 10 + rw + mb * 7 + lut + engine)
     cases = [(37, 1152, 1), (9, 512, 3), (70, 3584, 5)]
-    if engine >= 1:
+    if engine in (1, 2):
         cases += [(100, 1024, 11 if mb == 16 else 7), (33, 2048, mb), (48, 640, 8), (16, 128, 1)]
+    if engine == 3:   # m = 1, in_f a multiple of 256 * vec_words
+        cases = [(37, 1024, 1), (9, 2048, 1), (70, 3584, 1) if vw == 2 else (70, 4096, 1), (300, 1024, 1),
+                 (5, 18944, 1) if vw == 2 else (5, 8192, 1)]
     for out_f, in_f, m in cases:
         W, X = rand_problem(rng, out_f, in_f, m)
         qw, sc = quantised(fmt, W, cuda)
@@ -165,9 +169,16 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                     assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 assert b4gemv.load().b4_device_error(1) == 0
                 continue
+            if engine == 3:
+                for st in {(4, 2): (4, 8), (8, 2): (4, 6), (16, 2): (4,), (4, 4): (4,), (8, 4): (4,)}[(rw, vw)]:
+                    cfg.update(stages=st)
+                    y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+                    assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                assert b4gemv.load().b4_device_error(1) == 0
+                continue
             y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
             assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
-        if engine == 2:
+        if engine >= 2:
             continue   # x is staged whole: no x tiles
         # several x tiles in shared memory
         cfg = dict(vec_words=vw, rows_per_warp=rw, warps_k=2, row_groups=1, batch_tile=mb, nf4_lut=lut,
