@@ -312,6 +312,35 @@ def per_shape_chained(b4, torch, fmt, reps=200):
     return out
 
 
+def chained_us(torch, launcher, i, reps=100):
+    """us per launch of projection i over `reps` back-to-back launches in one
+    CUDA graph, rotating over the N_SETS weight copies."""
+    def body(stream):
+        for k in range(reps):
+            q, sc, x, y, a_in, a_out = launcher.calls[k % N_SETS][i]
+            st = launcher.fn(q, sc, x, y, a_in, a_out, 1, stream)
+            if st:
+                raise RuntimeError(f"GEMV launch failed with status {st}")
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(g, stream=cs, capture_error_mode="relaxed"):
+        body(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.current_stream().wait_stream(cs)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(3):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) * 1e3 / (3 * reps)
+
+
 def isolated_launches(torch, launcher, reps=100):
     """The reference's protocol (int4_gemv.cu:88-108): event-bracketed single
     launches, each followed by a synchronize; median per projection, us."""
@@ -506,14 +535,13 @@ def run_ours(args, d):
     K, W = args.steps, args.warmup
     gsteps = min(GRAPH_STEPS, K)
     g_main, _ = capture(torch, launcher, gsteps, 0, with_events=False)
-    g_ev, evs = capture(torch, launcher, gsteps, 0, with_events=True)
     rem = K % gsteps
     g_rem = capture(torch, launcher, rem, 0, with_events=False)[0] if rem else None
 
-    def run_steps(n, final_with_events):
+    def run_steps(n):
         full, r = divmod(n, gsteps)
         for j in range(full):
-            (g_ev if (final_with_events and j == full - 1 and r == 0) else g_main).replay()
+            g_main.replay()
         for _ in range(r):
             launcher.step(0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
@@ -525,7 +553,7 @@ def run_ours(args, d):
     sampler.start()
     time.sleep(0.5)
     t_soak = time.time()
-    run_steps(max(W, 3), False)
+    run_steps(max(W, 3))
     torch.cuda.synchronize()
     soak_until = time.time() + args.soak_seconds
     while time.time() < soak_until:
@@ -540,7 +568,7 @@ def run_ours(args, d):
     start.record()
     full, r = divmod(K, gsteps)
     for j in range(full):
-        (g_ev if j == full - 1 else g_main).replay()
+        g_main.replay()
     if g_rem is not None:
         g_rem.replay()
     end.record()
@@ -552,16 +580,11 @@ def run_ours(args, d):
     ms = start.elapsed_time(end)
     ms_max = d.max(ms, dev)
 
-    # per-kernel durations from the last graph replay of the timed region
-    # (gsteps steps): events before the first and after every GEMV
-    per = {name: [] for name, _, _ in SHAPES}
-    if full > 0:
-        for k in range(gsteps):
-            for i, (name, _, _) in enumerate(SHAPES):
-                a = evs[k * len(SHAPES) + i]
-                b = evs[k * len(SHAPES) + i + 1]
-                per[name].append(a.elapsed_time(b) * 1e3)
-    per_us = {n: round(statistics.mean(v), 3) for n, v in per.items() if v}
+    # per-GEMV durations: each projection launched 100 times back to back in
+    # a CUDA graph (rotating over the weight copies), events around the replay
+    # on the launching stream.  (Timing events inside the step graph would add
+    # their own gaps between kernels.)
+    per_us = {name: round(chained_us(torch, launcher, i), 3) for i, (name, _, _) in enumerate(SHAPES)}
 
     peak, peak_kind = measured_peak()
     dom = "gate_proj"
@@ -619,7 +642,7 @@ def run_ours(args, d):
         "correctness_rel_err": gate_err,
         "clocks": clocks,
     }
-    del launcher, g_main, g_ev, g_rem
+    del launcher, g_main, g_rem
     torch.cuda.synchronize()
     if args.detail:
         result["int4_chained"] = per_shape_chained(b4, torch, 0)

@@ -77,6 +77,9 @@ typedef struct b4_gemv_config {
  * rows_per_warp 4, 8 or 16, vec_words 2 or 4, in_f a multiple of 256*vec_words,
  * codes and absmax 16-byte aligned.  Persistent grid. */
 #define B4_ENGINE_FMA_TMA 3
+/* Tensor pipe, batch 1 only, lean inner loop (INT4): rows_per_warp 16,
+ * vec_words 4, `stages` = depth of the register load pipeline (2, 3, 4, 6). */
+#define B4_ENGINE_MMA_LEAN 4
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
  * the weight stream starts before the producer of x has finished. */

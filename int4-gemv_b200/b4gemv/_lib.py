@@ -21,6 +21,7 @@ ENGINE_FMA = 0
 ENGINE_MMA = 1
 ENGINE_MMA_TMA = 2
 ENGINE_FMA_TMA = 3
+ENGINE_MMA_LEAN = 4
 
 
 class GemvConfig(ctypes.Structure):

@@ -95,6 +95,11 @@ NF4_TMA_VARIANTS = [(4, 2, 4), (4, 2, 8), (8, 2, 4), (8, 2, 6), (16, 2, 4), (4, 
 
 
 def config_grid(fmt, m=1):
+    if fmt == FMT_INT4_G128 and m == 1:
+        for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (2, 3, 4, 6)):
+            if kw * rg <= 8:
+                yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
+                           x_tile=0, flags=0, engine=4, stages=st, stage_groups=0)
     if fmt == FMT_INT4_G128 and m <= 16:
         nt = 8 if m <= 8 else 16
         for kw, rg, (st, kcg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), TMA_VARIANTS):

@@ -10,6 +10,7 @@
 #include "b4_gemv_mma.cuh"
 #include "b4_gemv_tma.cuh"
 #include "b4_gemv_tma_nf4.cuh"
+#include "b4_gemv_lean.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -170,12 +171,14 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
 int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
+int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
     if (c.engine == B4_ENGINE_MMA) return launch_gemv_mma(p, c, st);
     if (c.engine == B4_ENGINE_MMA_TMA) return launch_gemv_tma(p, c, st);
     if (c.engine == B4_ENGINE_FMA_TMA) return launch_gemv_tma_nf4(p, c, st);
+    if (c.engine == B4_ENGINE_MMA_LEAN) return launch_gemv_lean(p, c, st);
     if (c.engine != B4_ENGINE_FMA) return cudaErrorInvalidValue;
     const int vw = c.vec_words, rw = c.rows_per_warp, kw = c.warps_k, rg = c.row_groups;
     const int mb = c.batch_tile, lut = c.nf4_lut;
@@ -479,6 +482,29 @@ int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStrea
     kp.x_vec = aligned(p.x, 8);
     const long long rows_per_cta = (long long)rg * rw;
     return launch_persistent(fn, &tp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, total, c.flags, st);
+}
+
+int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    if (p.fmt != kInt4 || p.m != 1 || c.vec_words != 4 || c.rows_per_warp != 16) return cudaErrorInvalidValue;
+    const int kw = c.warps_k, rg = c.row_groups;
+    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 16)) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_int4_lean(c.stages);
+    if (!fn) return cudaErrorInvalidValue;
+    LeanParams lp;
+    lp.qw = p.qw;
+    lp.scale = static_cast<const __half*>(p.scale);
+    lp.x = static_cast<const __half*>(p.x);
+    lp.y = p.y;
+    lp.in_f = p.in_f;
+    lp.out_f = p.out_f;
+    lp.kw = kw;
+    lp.rg = rg;
+    lp.x_vec = aligned(p.x, 16);
+    const size_t smem = (size_t)p.in_f * 2 + (size_t)rg * kw * 16 * 4;
+    const long long rows_per_cta = (long long)rg * 16;
+    return launch_persistent(fn, &lp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, smem, c.flags, st);
 }
 
 }  // namespace b4
