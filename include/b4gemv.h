@@ -55,7 +55,7 @@ typedef struct b4_gemv_config {
     int warps_k;       /* warps sharing one row group along in_f: 1..16        */
     int row_groups;    /* row groups per CTA; warps_k * row_groups <= 16       */
     int batch_tile;    /* batch rows per pass over the weights: 1, 2 or 4      */
-    int nf4_lut;       /* NF4 code-book lookup: 0 warp shuffle, 1 shared memory */
+    int nf4_lut;       /* NF4 code book: 0 warp shuffle, 1 shared memory, 2 pair table */
     int x_tile;        /* columns of x staged in shared memory per pass, 0 = auto */
     int flags;         /* B4_FLAG_* */
     int engine;        /* B4_ENGINE_*: which pipe does the multiply-accumulates   */
@@ -80,6 +80,13 @@ typedef struct b4_gemv_config {
 /* Tensor pipe, batch 1 only, lean inner loop (INT4): rows_per_warp 16,
  * vec_words 4, `stages` = depth of the register load pipeline (2, 3, 4, 6). */
 #define B4_ENGINE_MMA_LEAN 4
+/* As B4_ENGINE_MMA_LEAN, with the in-flight codes in a per-lane cp.async ring
+ * in shared memory instead of registers: `stages` 4, 6, 8 or 12. */
+#define B4_ENGINE_MMA_LEAN_ASYNC 5
+/* CUDA cores, NF4, batch 1, lean inner loop fed by a per-lane cp.async ring:
+ * rows_per_warp 4 or 8, vec_words 2 or 4, `stages` 4, 6 or 8, nf4_lut 0
+ * (warp-shuffle code book) or 2 (replicated pair table in shared memory). */
+#define B4_ENGINE_FMA_LEAN 6
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
  * the weight stream starts before the producer of x has finished. */

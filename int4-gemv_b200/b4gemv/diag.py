@@ -91,6 +91,8 @@ def time_chained(torch, prob, cfg, reps=100):
 
 
 TMA_VARIANTS = [(4, 4), (3, 4), (6, 4), (4, 2), (4, 8), (8, 2)]   # (stages, stage_groups) instantiated
+NF4_LEAN_VARIANTS = [(4, 4, 2, 0), (4, 8, 2, 0), (6, 4, 2, 0), (4, 4, 4, 0), (4, 4, 2, 2), (4, 8, 2, 2),
+                     (6, 4, 2, 2), (8, 4, 2, 2), (4, 4, 4, 2)]   # (stages, rw, vw, lut) instantiated
 NF4_TMA_VARIANTS = [(4, 2, 4), (4, 2, 8), (8, 2, 4), (8, 2, 6), (16, 2, 4), (4, 4, 4), (8, 4, 4)]  # (rw, vw, st)
 
 
@@ -100,6 +102,10 @@ def config_grid(fmt, m=1):
             if kw * rg <= 8:
                 yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
                            x_tile=0, flags=0, engine=4, stages=st, stage_groups=0)
+        for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (4, 6, 8, 12)):
+            if kw * rg <= 8:
+                yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
+                           x_tile=0, flags=0, engine=5, stages=st, stage_groups=0)
     if fmt == FMT_INT4_G128 and m <= 16:
         nt = 8 if m <= 8 else 16
         for kw, rg, (st, kcg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), TMA_VARIANTS):
@@ -112,6 +118,10 @@ def config_grid(fmt, m=1):
                 yield dict(vec_words=4, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=nt, nf4_lut=0,
                            x_tile=0, flags=0, engine=1)
     if fmt == FMT_NF4_B64 and m == 1:
+        for kw, rg, (st, rw, vw, lut) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), NF4_LEAN_VARIANTS):
+            if kw * rg <= 8:
+                yield dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=lut,
+                           x_tile=0, flags=0, engine=6, stages=st, stage_groups=0)
         for kw, rg, (rw, vw, st) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), NF4_TMA_VARIANTS):
             if kw * rg <= 8:
                 yield dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,

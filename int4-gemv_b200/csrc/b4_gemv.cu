@@ -11,6 +11,7 @@
 #include "b4_gemv_tma.cuh"
 #include "b4_gemv_tma_nf4.cuh"
 #include "b4_gemv_lean.cuh"
+#include "b4_gemv_lean_nf4.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -172,13 +173,15 @@ int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t 
 int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
+int launch_gemv_lean_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
     if (c.engine == B4_ENGINE_MMA) return launch_gemv_mma(p, c, st);
     if (c.engine == B4_ENGINE_MMA_TMA) return launch_gemv_tma(p, c, st);
     if (c.engine == B4_ENGINE_FMA_TMA) return launch_gemv_tma_nf4(p, c, st);
-    if (c.engine == B4_ENGINE_MMA_LEAN) return launch_gemv_lean(p, c, st);
+    if (c.engine == B4_ENGINE_MMA_LEAN || c.engine == B4_ENGINE_MMA_LEAN_ASYNC) return launch_gemv_lean(p, c, st);
+    if (c.engine == B4_ENGINE_FMA_LEAN) return launch_gemv_lean_nf4(p, c, st);
     if (c.engine != B4_ENGINE_FMA) return cudaErrorInvalidValue;
     const int vw = c.vec_words, rw = c.rows_per_warp, kw = c.warps_k, rg = c.row_groups;
     const int mb = c.batch_tile, lut = c.nf4_lut;
@@ -490,7 +493,8 @@ int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t
     const int kw = c.warps_k, rg = c.row_groups;
     if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
     if (!aligned(p.qw, 16)) return cudaErrorInvalidValue;
-    void* fn = gemv_kernel_int4_lean(c.stages);
+    const int async_ring = c.engine == B4_ENGINE_MMA_LEAN_ASYNC;
+    void* fn = gemv_kernel_int4_lean(c.stages, async_ring);
     if (!fn) return cudaErrorInvalidValue;
     LeanParams lp;
     lp.qw = p.qw;
@@ -502,8 +506,44 @@ int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t
     lp.kw = kw;
     lp.rg = rg;
     lp.x_vec = aligned(p.x, 16);
-    const size_t smem = (size_t)p.in_f * 2 + (size_t)rg * kw * 16 * 4;
+    size_t smem = (size_t)p.in_f * 2 + (size_t)(rg * kw * 16 + 3) / 4 * 16;
+    if (async_ring) smem += (size_t)kw * rg * c.stages * 64 * 16;   // per warp: stages x 2 rows x 32 lanes x 16 B
     const long long rows_per_cta = (long long)rg * 16;
+    return launch_persistent(fn, &lp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, smem, c.flags, st);
+}
+
+// Shared memory of the lean NF4 kernel: [pair table][x chunks][reduction][rings].
+size_t lean_nf4_smem(int in_f, int kw, int rg, int rw, int vw, int depth, int lut)
+{
+    const int nchunks = in_f / 8 / vw, nsteps = (nchunks + 31) / 32;
+    size_t s = lut == 2 ? 256 * 16 * 8 : 0;
+    s += (size_t)nsteps * 32 * 2 * vw * 16;
+    s += (size_t)((rg * kw * rw * 4 + 15) / 16) * 16;
+    s += (size_t)kw * rg * depth * rw * 32 * (4 * vw + 4);
+    return s;
+}
+
+int launch_gemv_lean_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    if (p.fmt != kNf4 || p.m != 1) return cudaErrorInvalidValue;
+    const int kw = c.warps_k, rg = c.row_groups, rw = c.rows_per_warp, vw = c.vec_words;
+    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
+    if ((vw != 2 && vw != 4) || (p.in_f / 8) % vw) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 4u * vw) || !aligned(p.scale, 4)) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_nf4_lean(c.stages, rw, vw, c.nf4_lut);
+    if (!fn) return cudaErrorInvalidValue;
+    LeanNf4Params lp;
+    lp.qw = p.qw;
+    lp.absmax = static_cast<const float*>(p.scale);
+    lp.x = static_cast<const __half*>(p.x);
+    lp.y = p.y;
+    lp.in_f = p.in_f;
+    lp.out_f = p.out_f;
+    lp.kw = kw;
+    lp.rg = rg;
+    lp.x_vec = aligned(p.x, 8);
+    const size_t smem = lean_nf4_smem(p.in_f, kw, rg, rw, vw, c.stages, c.nf4_lut);
+    const long long rows_per_cta = (long long)rg * rw;
     return launch_persistent(fn, &lp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, smem, c.flags, st);
 }
 

@@ -22,6 +22,14 @@
 //     equal, D[row][0] holds the row's partial sum.
 // Work split as in the other kernels: warps_k warps share a 16-row tile and
 // take groups ks, ks + warps_k, ...; CTAs loop over tiles of rg*16 rows.
+//
+// ASYNC = 1 moves the in-flight codes out of registers: each lane copies its
+// own two 16-byte pieces of every future group with cp.async into a private
+// ring slot in shared memory ((stage*2 + row)*32 + lane: a warp's copies and
+// reads of one slot are 512 contiguous bytes, conflict-free) and reads them
+// back when the group's turn comes.  Lanes only ever read what they copied
+// themselves, so the per-thread cp.async.wait_group is the only ordering
+// needed, and D stages in flight cost shared memory instead of registers.
 #pragma once
 
 #include "b4_gemv_mma.cuh"
@@ -38,7 +46,7 @@ struct LeanParams {
     int x_vec;
 };
 
-template <int D>   // D >= 2
+template <int D, int ASYNC>   // D >= 2
 __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p)
 {
     extern __shared__ __align__(16) uint4 lsm[];
@@ -53,6 +61,8 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     const int n_tiles = (p.out_f + rows_per_tile - 1) / rows_per_tile;
     uint4* xs = lsm;                                         // one slot per word
     float* red = reinterpret_cast<float*>(xs + words);      // rg*kw*16
+    // ASYNC: this warp's ring, D stages x 2 rows x 32 lanes x 16 bytes
+    uint4* ring = xs + words + (p.rg * p.kw * 16 + 3) / 4 + warp * (D * 64);
 
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -87,20 +97,27 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
 
         uint4 bufa[D], bufb[D];
         __half bsa[D], bsb[D];
-#pragma unroll
-        for (int d = 0; d < D - 1; ++d) {
-            if (d < n_it) {
+        auto fetch = [&](int slot) {
+            if constexpr (ASYNC) {
+                cp_async16(ring + (slot * 2) * 32 + lane, pa);
+                cp_async16(ring + (slot * 2 + 1) * 32 + lane, pb);
+            } else {
                 const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
                 const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
-                bufa[d] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
-                bufb[d] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
-                bsa[d] = __ldg(sa_p);
-                bsb[d] = __ldg(sb_p);
-                pa += wstep;
-                pb += wstep;
-                sa_p += p.kw;
-                sb_p += p.kw;
+                bufa[slot] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
+                bufb[slot] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
             }
+            bsa[slot] = __ldg(sa_p);
+            bsb[slot] = __ldg(sb_p);
+            pa += wstep;
+            pb += wstep;
+            sa_p += p.kw;
+            sb_p += p.kw;
+        };
+#pragma unroll
+        for (int d = 0; d < D - 1; ++d) {
+            if (d < n_it) fetch(d);
+            if constexpr (ASYNC) cp_async_commit();   // one group per stage, even if empty
         }
         float acc_a = 0.0f, acc_b = 0.0f;
         const uint4* xp = xs + ks * 16 + q * 4;              // + 16*kw per group step
@@ -110,24 +127,23 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
             for (int d = 0; d < D; ++d) {
                 const int it = it0 + d;
                 if (it < n_it) {
-                    // refill the buffer consumed in the previous step
+                    // refill the stage consumed in the previous step
                     const int nxt = (d + D - 1) % D;   // a constant once unrolled
-                    if (it + D - 1 < n_it) {
-                        const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
-                        const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
-                        bufa[nxt] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
-                        bufb[nxt] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
-                        bsa[nxt] = __ldg(sa_p);
-                        bsb[nxt] = __ldg(sb_p);
-                        pa += wstep;
-                        pb += wstep;
-                        sa_p += p.kw;
-                        sb_p += p.kw;
+                    if (it + D - 1 < n_it) fetch(nxt);
+                    uint4 wav, wbv;
+                    if constexpr (ASYNC) {
+                        cp_async_commit();
+                        cp_async_wait<D - 1>();            // this lane's copies of stage d landed
+                        wav = ring[(d * 2) * 32 + lane];
+                        wbv = ring[(d * 2 + 1) * 32 + lane];
+                    } else {
+                        wav = bufa[d];
+                        wbv = bufb[d];
                     }
                     const uint4 xv[4] = {xp[0], xp[1], xp[2], xp[3]};
                     xp += 16 * p.kw;
-                    const uint32_t wa[4] = {bufa[d].x, bufa[d].y, bufa[d].z, bufa[d].w};
-                    const uint32_t wb[4] = {bufb[d].x, bufb[d].y, bufb[d].z, bufb[d].w};
+                    const uint32_t wa[4] = {wav.x, wav.y, wav.z, wav.w};
+                    const uint32_t wb[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
                     float c0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, c1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
@@ -145,6 +161,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                 }
             }
         }
+        if constexpr (ASYNC) cp_async_wait<0>();   // nothing of this tile left in flight
 
         // rows r0+g and r0+g+8; lanes q = 0..3 hold the same values
         if (p.kw == 1) {
@@ -169,6 +186,6 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     }
 }
 
-void* gemv_kernel_int4_lean(int depth);
+void* gemv_kernel_int4_lean(int depth, int async_ring);
 
 }  // namespace b4

@@ -131,7 +131,9 @@ def kernel_configs():
     out = [(0, 4, rw, mb, 0, 1) for rw in (16, 32) for mb in (8, 16)]  # tensor-pipe INT4
     out += [(0, 4, 16, mb, 0, 2) for mb in (8, 16)]                     # tensor pipe + bulk-copy ring
     out += [(1, vw, rw, 1, 0, 3) for rw, vw in [(4, 2), (8, 2), (16, 2), (4, 4), (8, 4)]]  # NF4 + ring
-    out += [(0, 4, 16, 1, 0, 4)]                                                         # lean INT4, m = 1
+    out += [(0, 4, 16, 1, 0, 4), (0, 4, 16, 1, 0, 5)]                                    # lean INT4, m = 1
+    out += [(1, vw, rw, 1, lut, 6) for vw, rw, lut in [(2, 4, 0), (2, 8, 0), (4, 4, 0), (2, 4, 2), (2, 8, 2),
+                                                       (4, 4, 2)]]                       # lean NF4, m = 1
     for fmt in (0, 1):
         for lut in ((0,) if fmt == 0 else (0, 1)):
             for vw, rw in [(1, 1), (1, 4)]:
@@ -150,7 +152,9 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
     cases = [(37, 1152, 1), (9, 512, 3), (70, 3584, 5)]
     if engine in (1, 2):
         cases += [(100, 1024, 11 if mb == 16 else 7), (33, 2048, mb), (48, 640, 8), (16, 128, 1)]
-    if engine == 4:   # m = 1
+    if engine == 6:   # m = 1, ragged last step included
+        cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 64, 1), (5, 18944, 1), (3, 1088, 1)]
+    if engine in (4, 5):   # m = 1
         cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 128, 1), (5, 18944, 1)]
     if engine == 3:   # m = 1, in_f a multiple of 256 * vec_words
         cases = [(37, 1024, 1), (9, 2048, 1), (70, 3584, 1) if vw == 2 else (70, 4096, 1), (300, 1024, 1),
@@ -172,8 +176,16 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                     assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 assert b4gemv.load().b4_device_error(1) == 0
                 continue
-            if engine == 4:
-                for st in (2, 3, 4, 6):
+            if engine == 6:
+                sts = {(2, 4, 0): (4, 6), (2, 8, 0): (4,), (4, 4, 0): (4,), (2, 4, 2): (4, 6, 8), (2, 8, 2): (4,),
+                       (4, 4, 2): (4,)}[(vw, rw, lut)]
+                for st in sts:
+                    cfg.update(stages=st)
+                    y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+                    assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                continue
+            if engine in (4, 5):
+                for st in ((2, 3, 4, 6) if engine == 4 else (4, 6, 8, 12)):
                     cfg.update(stages=st)
                     y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
                     assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
