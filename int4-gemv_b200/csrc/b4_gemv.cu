@@ -87,6 +87,17 @@ TmaLayout tma_layout(int nb, int ng, int kw, int rg, int nt, int stages, int kcg
 // Opt-in shared memory per CTA on B200 (227 KB).
 constexpr size_t kTmaSmemLimit = 227 * 1024;
 
+// Shared memory of the lean NF4 kernel: [pair table][x chunks][reduction][rings].
+size_t lean_nf4_smem(int in_f, int kw, int rg, int rw, int vw, int depth, int lut)
+{
+    const int nchunks = in_f / 8 / vw, nsteps = (nchunks + 31) / 32;
+    size_t s = lut == 2 ? 256 * 16 * 8 : 0;
+    s += (size_t)nsteps * 32 * 2 * vw * 16;
+    s += (size_t)((rg * kw * rw * 4 + 15) / 16) * 16;
+    s += (size_t)kw * rg * depth * rw * 32 * (4 * vw + 4);
+    return s;
+}
+
 int check_problem(const GemvProblem& p)
 {
     if (p.fmt != kInt4 && p.fmt != kNf4) return cudaErrorInvalidValue;
@@ -109,6 +120,41 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     cfg->flags = 0;
     cfg->stages = 4;
     cfg->stage_groups = 4;
+
+    // Batch 1 (fitted on B200 with b4gemv.diag sweep; the reference's rule was
+    // fitted on a 36-SM part, int4_gemv.cu:52-53): the lean kernels, whose
+    // loads run ahead through per-lane cp.async rings.  CTAs of 8 warps; warps
+    // split in_f (warps_k) when there are too few rows to give every SM two
+    // CTAs of whole row tiles.
+    if (p.m == 1 && p.fmt == kInt4 && aligned(p.qw, 16) && (size_t)p.in_f * 2 + 8 * 4 * 1024 + 1024 <= kTmaSmemLimit) {
+        const int row_groups = (p.out_f + 15) / 16;
+        const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
+        cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
+        cfg->vec_words = 4;
+        cfg->rows_per_warp = 16;
+        cfg->batch_tile = 1;
+        cfg->warps_k = 8 / rg;
+        cfg->row_groups = rg;
+        cfg->stages = 4;
+        return;
+    }
+    if (p.m == 1 && p.fmt == kNf4 && aligned(p.qw, 16) && aligned(p.scale, 4) && words % 4 == 0) {
+        const int vw = (p.out_f >= 8192 || p.in_f >= 8192) ? 4 : 2;
+        const size_t smem = lean_nf4_smem(p.in_f, 1, 8, 4, vw, 4, 0);
+        if (smem <= kTmaSmemLimit) {
+            const int quads = (p.out_f + 3) / 4;
+            const int rg = std::max(1, std::min(8, quads / (sms / 2)));
+            cfg->engine = B4_ENGINE_FMA_LEAN;
+            cfg->vec_words = vw;
+            cfg->rows_per_warp = 4;
+            cfg->batch_tile = 1;
+            cfg->nf4_lut = 0;
+            cfg->warps_k = 8 / rg;
+            cfg->row_groups = rg;
+            cfg->stages = 4;
+            return;
+        }
+    }
 
     // INT4 with 16-byte aligned codes: multiply-accumulates on the tensor pipe,
     // codes streamed through per-warp bulk-copy rings when x fits next to them.
@@ -510,17 +556,6 @@ int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t
     if (async_ring) smem += (size_t)kw * rg * c.stages * 64 * 16;   // per warp: stages x 2 rows x 32 lanes x 16 B
     const long long rows_per_cta = (long long)rg * 16;
     return launch_persistent(fn, &lp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, smem, c.flags, st);
-}
-
-// Shared memory of the lean NF4 kernel: [pair table][x chunks][reduction][rings].
-size_t lean_nf4_smem(int in_f, int kw, int rg, int rw, int vw, int depth, int lut)
-{
-    const int nchunks = in_f / 8 / vw, nsteps = (nchunks + 31) / 32;
-    size_t s = lut == 2 ? 256 * 16 * 8 : 0;
-    s += (size_t)nsteps * 32 * 2 * vw * 16;
-    s += (size_t)((rg * kw * rw * 4 + 15) / 16) * 16;
-    s += (size_t)kw * rg * depth * rw * 32 * (4 * vw + 4);
-    return s;
 }
 
 int launch_gemv_lean_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)

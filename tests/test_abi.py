@@ -40,15 +40,20 @@ def test_library_loads_and_exports_every_declared_symbol():
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 8, 16])
 def test_default_config_is_valid(fmt, out_f, in_f, m):
     c = b4gemv.default_config(fmt, in_f, out_f, m)
+    e = c["engine"]
     assert c["vec_words"] in (1, 2, 4) and (in_f // 8) % c["vec_words"] == 0
-    if c["engine"] in (1, 2):
+    assert 1 <= c["warps_k"] * c["row_groups"] <= 8 or (e == 0 and c["warps_k"] * c["row_groups"] <= 16)
+    if e in (1, 2):      # tensor pipe, register-fed or bulk-copy ring
         assert fmt == 0 and c["vec_words"] == 4
         assert c["rows_per_warp"] in (16, 32) and c["batch_tile"] in (8, 16)
-        assert 1 <= c["warps_k"] * c["row_groups"] <= 8
-        if c["engine"] == 2:
+        if e == 2:
             assert m <= c["batch_tile"] and c["rows_per_warp"] == 16
+    elif e in (4, 5):    # lean batch-1 INT4
+        assert fmt == 0 and m == 1 and c["rows_per_warp"] == 16 and c["stages"] in ((2, 3, 4, 6), (4, 6, 8, 12))[e - 4]
+    elif e == 6:         # lean batch-1 NF4
+        assert fmt == 1 and m == 1 and c["rows_per_warp"] in (4, 8) and c["nf4_lut"] in (0, 2)
     else:
-        assert c["engine"] == 0
+        assert e == 0
         assert c["rows_per_warp"] in (1, 2, 4, 8)
         assert c["batch_tile"] in (1, 2, 4)
         assert 1 <= c["warps_k"] * c["row_groups"] <= (16 if c["rows_per_warp"] * c["batch_tile"] == 1 else 8)
