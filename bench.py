@@ -68,6 +68,16 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+ENGINE_KERNELS = {0: "b4_gemv_kernel", 1: "b4_gemv_mma_kernel", 2: "b4_gemv_tma_kernel", 3: "b4_gemv_tma_nf4_kernel",
+                  4: "b4_gemv_lean_kernel", 5: "b4_gemv_lean_kernel (cp.async ring)", 6: "b4_gemv_lean_nf4_kernel"}
+
+
+def engine_kernel(b4, fmt, in_f, out_f):
+    """Name of the kernel the dispatch rule picks for one batch-1 shape."""
+    cfg = b4.default_config(fmt, in_f, out_f, 1)
+    return ENGINE_KERNELS.get(cfg["engine"], f"engine {cfg['engine']}")
+
+
 def profiled_traffic(kernel_tag):
     """dram bytes per launch recorded by an ncu capture summary in profiles/."""
     pdir = os.path.join(ROOT, "profiles")
@@ -627,7 +637,7 @@ def run_ours(args, d):
                    "parallelism": f"{n} independent replicas (no data-path collective)" if n > 1 else "1 GPU"},
         "us_per_gemv": per_us,
         "gbs_per_gemv": {nm: round(nf4_bytes(o, i) / per_us[nm] / 1e3, 1) for nm, o, i in SHAPES if nm in per_us},
-        "roofline": {"bound": "hbm", "kernel": "b4_gemv_kernel (NF4, gate_proj 18944x3584)",
+        "roofline": {"bound": "hbm", "kernel": f"{engine_kernel(b4, 1, 3584, 18944)} (NF4, gate_proj 18944x3584)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
                      "bytes_per_launch": dom_bytes, "us_per_launch": dom_us,
