@@ -20,8 +20,10 @@
  *     reference silently drops a ragged tail (kernels.cuh:36,101), this ABI
  *     rejects it.
  *   - Work is enqueued on `stream` (NULL = legacy default stream) and returns
- *     without synchronising.  No host-global mutable state: any host thread
- *     may call on its own stream concurrently.
+ *     without synchronising.  The only host-global state is a mutex-guarded
+ *     cache of per-device facts (SM count, kernels whose shared-memory limit
+ *     was already raised): any host thread may call on its own stream
+ *     concurrently.
  *   - Vector paths need 16-byte (or 8-byte) aligned codes and x; other
  *     alignments fall back to 4-byte loads, never to the CPU.
  */
@@ -40,7 +42,7 @@ extern "C" {
 #define B4_FMT_INT4_G128 0
 #define B4_FMT_NF4_B64 1
 
-#define B4_ABI_VERSION 1
+#define B4_ABI_VERSION 2
 
 /* Same type as cudaStream_t, spelled without the CUDA headers. */
 typedef struct CUstream_st* b4_stream_t;
@@ -81,7 +83,9 @@ typedef struct b4_gemv_config {
  * vec_words 4, `stages` = depth of the register load pipeline (2, 3, 4, 6). */
 #define B4_ENGINE_MMA_LEAN 4
 /* As B4_ENGINE_MMA_LEAN, with the in-flight codes in a per-lane cp.async ring
- * in shared memory instead of registers: `stages` 4, 6, 8 or 12. */
+ * in shared memory instead of registers; a stage holds `stage_groups`
+ * consecutive 128-column groups ((stages, stage_groups) = (4,1), (6,1), (8,1),
+ * (3,2), (4,2), (6,2), (2,4) or (3,4); stage_groups must divide in_f/128). */
 #define B4_ENGINE_MMA_LEAN_ASYNC 5
 /* CUDA cores, NF4, batch 1, lean inner loop fed by a per-lane cp.async ring:
  * rows_per_warp 4 or 8, vec_words 2 or 4, `stages` 4, 6 or 8, nf4_lut 0
@@ -89,7 +93,10 @@ typedef struct b4_gemv_config {
 #define B4_ENGINE_FMA_LEAN 6
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
- * the weight stream starts before the producer of x has finished. */
+ * the weight stream starts before the producer of x has finished.  Only x is
+ * ordered after the previous kernel; codes and scales may be read while it
+ * still runs, so do not set the flag on a launch whose immediately preceding
+ * kernel writes this launch's weights. */
 #define B4_FLAG_PDL 1
 
 /* ---- GEMV: y[b][r] = sum_k dequant(W)[r][k] * x[b][k], b < m ----------------
@@ -119,6 +126,31 @@ int b4_gemv_default_config(int fmt, int in_f, int out_f, int m, b4_gemv_config* 
  * by hand (diag_aspect.cu:54-56,253-256,262-266). */
 int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y,
                int in_f, int out_f, int m, const b4_gemv_config* cfg, b4_stream_t stream);
+
+/* ---- Several projections that share x, as one launch ----------------------
+ * y_s[b][r] = sum_k dequant(W_s)[r][k] * x[b][k] for every segment s < nseg
+ * (1..B4_MAX_SEGMENTS), all with the same in_f: q/k/v of an attention block,
+ * or gate/up of an MLP.  At batch 1 with the lean engines this is ONE kernel
+ * launch whose row tiles span all segments, so narrow projections (k/v) ride
+ * along with a wide one instead of paying their own launch.  No counterpart
+ * in the reference, which names fused QKV as the fix for dispatch-bound k/v
+ * and leaves it unimplemented (README.md:177-179); it replaces nseg
+ * consecutive b4_gemv_int4_g128 / b4_gemv_nf4_b64 calls over the same
+ * buffers.  Other engines and m > 1 run one launch per segment.  cfg may be
+ * NULL (the dispatch rule over the segments' total rows, which
+ * b4_gemv_multi_default_config returns; it reads only qw, scale and out_f of
+ * each segment). */
+#define B4_MAX_SEGMENTS 4
+typedef struct b4_gemv_segment {
+    const uint32_t* qw;   /* uint32 [out_f][in_f/8] */
+    const void* scale;    /* INT4: fp16 [out_f][in_f/128]; NF4: fp32 [out_f][in_f/64] */
+    float* y;             /* fp32 [m][out_f] */
+    int out_f;
+} b4_gemv_segment;
+int b4_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                  const b4_gemv_config* cfg, b4_stream_t stream);
+int b4_gemv_multi_default_config(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
+                                 b4_gemv_config* cfg);
 
 /* nf4_gemv_block_per_row (kernels.cuh:211-215) with its launch geometry
  * <<<out_f, warps_per_block*32>>> (int4_gemv.cu:56-58): one CTA per row,

@@ -14,14 +14,15 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, B4Error,
-                   GemvConfig, check, load)
+from ._lib import (FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS, NF4_BLOCK, B4Error,
+                   GemvConfig, GemvSegment, check, load)
 
 __all__ = [
     "GROUP", "NF4_BLOCK", "FMT_INT4_G128", "FMT_NF4_B64", "FLAG_PDL", "B4Error",
     "GemvConfig", "load", "quantise", "quantise_nf4", "gemv_int4", "gemv_nf4", "gemv",
     "gemv_nf4_block_per_row", "dequant_int4", "dequant_nf4", "unpack_codes",
-    "quantise_device", "quantise_nf4_device", "default_config", "median",
+    "quantise_device", "quantise_nf4_device", "default_config", "median", "gemv_multi",
+    "multi_default_config", "MAX_SEGMENTS", "GemvSegment",
 ]
 
 
@@ -151,6 +152,48 @@ def gemv_nf4(qw, absmax, x, y=None, stream=None):
     check("b4_gemv_nf4_b64", load().b4_gemv_nf4_b64(_ptr(qw), _ptr(absmax), _ptr(x2), _ptr(y), in_f,
                                                     out_f, m, _stream(stream)))
     return y
+
+
+def _segments(pairs, x, ys, alloc=True):
+    import torch
+    assert 1 <= len(pairs) <= MAX_SEGMENTS
+    in_f = pairs[0][0].shape[1] * 8
+    x2 = x.reshape(-1, in_f) if x.dim() != 2 else x
+    assert x2.dtype == torch.float16 and x2.is_contiguous() and x2.shape[1] == in_f
+    m = x2.shape[0]
+    segs = (GemvSegment * len(pairs))()
+    out = []
+    for i, (qw, scale) in enumerate(pairs):
+        assert qw.is_cuda and qw.dtype in (torch.int32, torch.uint32) and qw.is_contiguous()
+        assert qw.shape[1] * 8 == in_f, "every segment shares x, so in_f must match"
+        out_f = qw.shape[0]
+        if not alloc:
+            segs[i] = GemvSegment(qw.data_ptr(), scale.data_ptr(), None, out_f)
+            continue
+        y = ys[i] if ys is not None else torch.empty((m, out_f), dtype=torch.float32, device=qw.device)
+        assert y.dtype == torch.float32 and y.is_contiguous() and y.numel() == m * out_f
+        segs[i] = GemvSegment(qw.data_ptr(), scale.data_ptr(), y.data_ptr(), out_f)
+        out.append(y)
+    return segs, x2, in_f, m, out
+
+
+def multi_default_config(fmt: int, pairs, x) -> dict:
+    """b4_gemv_multi_default_config: the dispatch rule over the segments' total rows."""
+    segs, _, in_f, m, _ = _segments(pairs, x, None, alloc=False)
+    c = GemvConfig()
+    check("b4_gemv_multi_default_config",
+          load().b4_gemv_multi_default_config(fmt, segs, len(pairs), in_f, m, ctypes.byref(c)))
+    return c.as_dict()
+
+
+def gemv_multi(fmt: int, pairs, x, ys=None, config: dict | None = None, stream=None):
+    """b4_gemv_multi: y_s = dequant(qw_s, scale_s) @ x for every (qw_s, scale_s)
+    in `pairs` (up to four matrices with the same in_f), one launch at batch 1
+    on the lean engines.  Returns the list of y_s."""
+    segs, x2, in_f, m, out = _segments(pairs, x, ys)
+    cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
+    check("b4_gemv_multi", load().b4_gemv_multi(fmt, segs, len(pairs), _ptr(x2), in_f, m, cfg, _stream(stream)))
+    return out
 
 
 def gemv_nf4_block_per_row(qw, absmax, x, warps_per_block: int, y=None, stream=None):

@@ -54,6 +54,19 @@ class GemvConfig(ctypes.Structure):
         return c
 
 
+class GemvSegment(ctypes.Structure):
+    """b4_gemv_segment (include/b4gemv.h)."""
+
+    _fields_ = [
+        ("qw", ctypes.c_void_p),
+        ("scale", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("out_f", ctypes.c_int),
+    ]
+
+
+MAX_SEGMENTS = 4
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 
@@ -64,6 +77,9 @@ SIGNATURES = {
     "b4_gemv_default_config": (_I, [_I, _I, _I, _I, ctypes.POINTER(GemvConfig)]),
     "b4_gemv_ex": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P]),
     "b4_gemv_nf4_b64_block_per_row": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "b4_gemv_multi": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _P, _I, _I, ctypes.POINTER(GemvConfig), _P]),
+    "b4_gemv_multi_default_config": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _I, _I,
+                                          ctypes.POINTER(GemvConfig)]),
     "b4_dequant_int4_g128": (_I, [_P, _P, _P, _I, _I, _P]),
     "b4_dequant_nf4_b64": (_I, [_P, _P, _P, _I, _I, _P]),
     "b4_unpack_codes": (_I, [_P, _P, _I, _I, _P]),

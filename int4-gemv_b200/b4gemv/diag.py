@@ -20,7 +20,7 @@ import itertools
 import json
 import sys
 
-from . import FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
+from . import FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
 
 SHAPES = {"q_proj": (3584, 3584), "k_proj": (512, 3584), "v_proj": (512, 3584), "o_proj": (3584, 3584),
           "gate_proj": (18944, 3584), "up_proj": (18944, 3584), "down_proj": (3584, 18944),
@@ -91,6 +91,7 @@ def time_chained(torch, prob, cfg, reps=100):
 
 
 TMA_VARIANTS = [(4, 4), (3, 4), (6, 4), (4, 2), (4, 8), (8, 2)]   # (stages, stage_groups) instantiated
+LEAN_VARIANTS = [(4, 1), (6, 1), (8, 1), (3, 2), (4, 2), (6, 2), (2, 4), (3, 4)]   # engine 5 (stages, stage_groups)
 NF4_LEAN_VARIANTS = [(4, 4, 2, 0), (4, 8, 2, 0), (6, 4, 2, 0), (4, 4, 4, 0), (4, 4, 2, 2), (4, 8, 2, 2),
                      (6, 4, 2, 2), (8, 4, 2, 2), (4, 4, 4, 2)]   # (stages, rw, vw, lut) instantiated
 NF4_TMA_VARIANTS = [(4, 2, 4), (4, 2, 8), (8, 2, 4), (8, 2, 6), (16, 2, 4), (4, 4, 4), (8, 4, 4)]  # (rw, vw, st)
@@ -101,11 +102,11 @@ def config_grid(fmt, m=1):
         for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (2, 3, 4, 6)):
             if kw * rg <= 8:
                 yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
-                           x_tile=0, flags=0, engine=4, stages=st, stage_groups=0)
-        for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (4, 6, 8, 12)):
+                           x_tile=0, flags=0, engine=4, stages=st, stage_groups=1)
+        for kw, rg, (st, sg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), LEAN_VARIANTS):
             if kw * rg <= 8:
                 yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
-                           x_tile=0, flags=0, engine=5, stages=st, stage_groups=0)
+                           x_tile=0, flags=0, engine=5, stages=st, stage_groups=sg)
     if fmt == FMT_INT4_G128 and m <= 16:
         nt = 8 if m <= 8 else 16
         for kw, rg, (st, kcg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), TMA_VARIANTS):
@@ -149,9 +150,16 @@ def cmd_sweep(args, torch):
             dflt = GemvConfig()
             check("default_config", load().b4_gemv_default_config(fmt, in_f, out_f, args.m, ctypes.byref(dflt)))
             rows = []
+            if args.pdl:
+                dflt.flags |= FLAG_PDL
             us_d = time_chained(torch, prob, dflt)
             rows.append(("default", dflt.as_dict(), us_d))
+            engines = {int(e) for e in args.engines.split(",")} if args.engines else None
             for c in config_grid(fmt, args.m):
+                if engines is not None and c.get("engine", 0) not in engines:
+                    continue
+                if args.pdl:
+                    c = dict(c, flags=c.get("flags", 0) | FLAG_PDL)
                 us = time_chained(torch, prob, GemvConfig.from_dict(c))
                 if us is not None:
                     rows.append(("grid", c, us))
@@ -219,6 +227,8 @@ def main(argv=None):
     s.add_argument("--shapes", default="")
     s.add_argument("--m", type=int, default=1)
     s.add_argument("--json", default="")
+    s.add_argument("--engines", default="", help="comma-separated engine numbers to sweep (default: all)")
+    s.add_argument("--pdl", action="store_true", help="launch every config as a programmatic dependent")
     a = sub.add_parser("aspect")
     a.add_argument("--fmt", default="nf4", choices=["nf4", "int4"])
     r = sub.add_parser("run")

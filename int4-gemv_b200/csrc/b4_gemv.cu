@@ -98,6 +98,15 @@ size_t lean_nf4_smem(int in_f, int kw, int rg, int rw, int vw, int depth, int lu
     return s;
 }
 
+// Shared memory of the lean INT4 kernel: [x][reduction][rings].
+size_t lean_int4_smem(int in_f, int kw, int rg, int stages, int groups, int async_ring)
+{
+    size_t smem = (size_t)in_f * 2 + (size_t)(rg * kw * 16 + 3) / 4 * 16;
+    // per warp: stages x groups x 2 rows x 32 lanes x 16 B
+    if (async_ring) smem += (size_t)kw * rg * stages * groups * 64 * 16;
+    return smem;
+}
+
 int check_problem(const GemvProblem& p)
 {
     if (p.fmt != kInt4 && p.fmt != kNf4) return cudaErrorInvalidValue;
@@ -121,34 +130,57 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     cfg->stages = 4;
     cfg->stage_groups = 4;
 
-    // Batch 1 (fitted on B200 with b4gemv.diag sweep; the reference's rule was
-    // fitted on a 36-SM part, int4_gemv.cu:52-53): the lean kernels, whose
-    // loads run ahead through per-lane cp.async rings.  CTAs of 8 warps; warps
-    // split in_f (warps_k) when there are too few rows to give every SM two
-    // CTAs of whole row tiles.
-    if (p.m == 1 && p.fmt == kInt4 && aligned(p.qw, 16) && (size_t)p.in_f * 2 + 8 * 4 * 1024 + 1024 <= kTmaSmemLimit) {
+    // Batch 1 (fitted on B200 with `b4gemv.diag sweep`, plain and programmatic
+    // dependent launches; the reference's rule was fitted on a 36-SM part,
+    // int4_gemv.cu:52-53): the lean kernels.  CTAs of 8 warps; warps split
+    // in_f (warps_k) when there are too few rows to give every SM two CTAs of
+    // whole row tiles.
+    if (p.m == 1 && p.fmt == kInt4 && aligned(p.qw, 16)) {
+        const int ng = p.in_f / kGroup;
         const int row_groups = (p.out_f + 15) / 16;
         const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
-        cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
         cfg->vec_words = 4;
         cfg->rows_per_warp = 16;
         cfg->batch_tile = 1;
         cfg->warps_k = 8 / rg;
         cfg->row_groups = rg;
-        cfg->stages = 4;
-        return;
+        // up to 2*148 tiles of 16 rows (q/k/v/o): the register pipeline, no ring
+        if (rg == 1 && p.in_f <= 8192) {
+            cfg->engine = B4_ENGINE_MMA_LEAN;
+            cfg->stages = 4;
+            cfg->stage_groups = 1;
+            return;
+        }
+        // larger: the cp.async ring, as many groups per stage as divide the
+        // row while two CTAs still fit in shared memory
+        const int variants[3][2] = {{2, 4}, {3, 2}, {4, 1}};   // (stages, groups per stage)
+        for (int pass = 0; pass < 2; ++pass) {
+            for (const auto& v : variants) {
+                if (ng % v[1] || (v[1] > 1 && !aligned(p.scale, 2u * v[1]))) continue;
+                const size_t smem = lean_int4_smem(p.in_f, cfg->warps_k, rg, v[0], v[1], 1);
+                if (smem > (pass == 0 ? kTmaSmemLimit / 2 - 1024 : kTmaSmemLimit)) continue;
+                cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
+                cfg->stages = v[0];
+                cfg->stage_groups = v[1];
+                return;
+            }
+        }
     }
     if (p.m == 1 && p.fmt == kNf4 && aligned(p.qw, 16) && aligned(p.scale, 4) && words % 4 == 0) {
-        const int vw = (p.out_f >= 8192 || p.in_f >= 8192) ? 4 : 2;
-        const size_t smem = lean_nf4_smem(p.in_f, 1, 8, 4, vw, 4, 0);
+        // long rows or many rows: the replicated pair-table code book; q/k/v/o:
+        // the shuffle code book with more, smaller tiles
+        const bool big = p.out_f >= 8192 || p.in_f >= 8192;
+        const int vw = p.in_f >= 8192 ? 4 : 2;
+        const int lut = big ? 2 : 0;
+        const int quads = (p.out_f + 3) / 4;
+        const int rg = std::max(1, std::min(8, quads / (big ? sms / 2 : 224)));
+        const size_t smem = lean_nf4_smem(p.in_f, 8 / rg, rg, 4, vw, 4, lut);
         if (smem <= kTmaSmemLimit) {
-            const int quads = (p.out_f + 3) / 4;
-            const int rg = std::max(1, std::min(8, quads / (sms / 2)));
             cfg->engine = B4_ENGINE_FMA_LEAN;
             cfg->vec_words = vw;
             cfg->rows_per_warp = 4;
             cfg->batch_tile = 1;
-            cfg->nf4_lut = 0;
+            cfg->nf4_lut = lut;
             cfg->warps_k = 8 / rg;
             cfg->row_groups = rg;
             cfg->stages = 4;
@@ -533,53 +565,130 @@ int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStrea
     return launch_persistent(fn, &tp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, total, c.flags, st);
 }
 
-int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+namespace {
+
+bool lean_geometry_ok(const b4_gemv_config& c) { return c.warps_k >= 1 && c.row_groups >= 1 && c.warps_k * c.row_groups <= 8; }
+
+// One launch of the lean INT4 kernel over nseg weight matrices sharing x.
+int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                          const b4_gemv_config& c, cudaStream_t st)
 {
-    if (p.fmt != kInt4 || p.m != 1 || c.vec_words != 4 || c.rows_per_warp != 16) return cudaErrorInvalidValue;
+    if (m != 1 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c)) return cudaErrorInvalidValue;
+    if (nseg < 1 || nseg > kLeanMaxSeg) return cudaErrorInvalidValue;
     const int kw = c.warps_k, rg = c.row_groups;
-    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
-    if (!aligned(p.qw, 16)) return cudaErrorInvalidValue;
     const int async_ring = c.engine == B4_ENGINE_MMA_LEAN_ASYNC;
-    void* fn = gemv_kernel_int4_lean(c.stages, async_ring);
+    const int groups = async_ring ? c.stage_groups : 1;
+    if (groups != 1 && groups != 2 && groups != 4) return cudaErrorInvalidValue;
+    if ((in_f / kGroup) % groups) return cudaErrorInvalidValue;   // a stage of `groups` groups tiles the row
+    void* fn = gemv_kernel_int4_lean(c.stages, groups, async_ring);
     if (!fn) return cudaErrorInvalidValue;
-    LeanParams lp;
-    lp.qw = p.qw;
-    lp.scale = static_cast<const __half*>(p.scale);
-    lp.x = static_cast<const __half*>(p.x);
-    lp.y = p.y;
-    lp.in_f = p.in_f;
-    lp.out_f = p.out_f;
+    LeanParams lp = {};
+    const long long rows_per_cta = (long long)rg * 16;
+    long long tiles = 0;
+    for (int s = 0; s < nseg; ++s) {
+        // a stage's scales are one load of `groups` fp16 per row
+        if (!aligned(segs[s].qw, 16) || !aligned(segs[s].scale, 2u * groups)) return cudaErrorInvalidValue;
+        tiles += (segs[s].out_f + rows_per_cta - 1) / rows_per_cta;
+        if (tiles > INT32_MAX) return cudaErrorInvalidValue;
+        lp.seg[s].qw = segs[s].qw;
+        lp.seg[s].scale = static_cast<const __half*>(segs[s].scale);
+        lp.seg[s].y = segs[s].y;
+        lp.seg[s].out_f = segs[s].out_f;
+        lp.seg[s].tile_end = (int)tiles;
+    }
+    lp.nseg = nseg;
+    lp.n_tiles = (int)tiles;
+    lp.x = static_cast<const __half*>(x);
+    lp.in_f = in_f;
     lp.kw = kw;
     lp.rg = rg;
-    lp.x_vec = aligned(p.x, 16);
-    size_t smem = (size_t)p.in_f * 2 + (size_t)(rg * kw * 16 + 3) / 4 * 16;
-    if (async_ring) smem += (size_t)kw * rg * c.stages * 64 * 16;   // per warp: stages x 2 rows x 32 lanes x 16 B
-    const long long rows_per_cta = (long long)rg * 16;
-    return launch_persistent(fn, &lp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, smem, c.flags, st);
+    lp.x_vec = aligned(x, 16);
+    const size_t smem = lean_int4_smem(in_f, kw, rg, c.stages, groups, async_ring);
+    return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
+}
+
+// One launch of the lean NF4 kernel over nseg weight matrices sharing x.
+int launch_lean_nf4_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                         const b4_gemv_config& c, cudaStream_t st)
+{
+    if (m != 1 || !lean_geometry_ok(c)) return cudaErrorInvalidValue;
+    if (nseg < 1 || nseg > kLeanMaxSeg) return cudaErrorInvalidValue;
+    const int kw = c.warps_k, rg = c.row_groups, rw = c.rows_per_warp, vw = c.vec_words;
+    if ((vw != 2 && vw != 4) || (in_f / 8) % vw) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_nf4_lean(c.stages, rw, vw, c.nf4_lut);
+    if (!fn) return cudaErrorInvalidValue;
+    LeanNf4Params lp = {};
+    const long long rows_per_cta = (long long)rg * rw;
+    long long tiles = 0;
+    for (int s = 0; s < nseg; ++s) {
+        if (!aligned(segs[s].qw, 4u * vw) || !aligned(segs[s].scale, 4)) return cudaErrorInvalidValue;
+        tiles += (segs[s].out_f + rows_per_cta - 1) / rows_per_cta;
+        if (tiles > INT32_MAX) return cudaErrorInvalidValue;
+        lp.seg[s].qw = segs[s].qw;
+        lp.seg[s].absmax = static_cast<const float*>(segs[s].scale);
+        lp.seg[s].y = segs[s].y;
+        lp.seg[s].out_f = segs[s].out_f;
+        lp.seg[s].tile_end = (int)tiles;
+    }
+    lp.nseg = nseg;
+    lp.n_tiles = (int)tiles;
+    lp.x = static_cast<const __half*>(x);
+    lp.in_f = in_f;
+    lp.kw = kw;
+    lp.rg = rg;
+    lp.x_vec = aligned(x, 8);
+    const size_t smem = lean_nf4_smem(in_f, kw, rg, rw, vw, c.stages, c.nf4_lut);
+    return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
+}
+
+}  // namespace
+
+int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    if (p.fmt != kInt4) return cudaErrorInvalidValue;
+    const b4_gemv_segment s{p.qw, p.scale, p.y, p.out_f};
+    return launch_lean_int4_segs(&s, 1, p.x, p.in_f, p.m, c, st);
 }
 
 int launch_gemv_lean_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
-    if (p.fmt != kNf4 || p.m != 1) return cudaErrorInvalidValue;
-    const int kw = c.warps_k, rg = c.row_groups, rw = c.rows_per_warp, vw = c.vec_words;
-    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
-    if ((vw != 2 && vw != 4) || (p.in_f / 8) % vw) return cudaErrorInvalidValue;
-    if (!aligned(p.qw, 4u * vw) || !aligned(p.scale, 4)) return cudaErrorInvalidValue;
-    void* fn = gemv_kernel_nf4_lean(c.stages, rw, vw, c.nf4_lut);
-    if (!fn) return cudaErrorInvalidValue;
-    LeanNf4Params lp;
-    lp.qw = p.qw;
-    lp.absmax = static_cast<const float*>(p.scale);
-    lp.x = static_cast<const __half*>(p.x);
-    lp.y = p.y;
-    lp.in_f = p.in_f;
-    lp.out_f = p.out_f;
-    lp.kw = kw;
-    lp.rg = rg;
-    lp.x_vec = aligned(p.x, 8);
-    const size_t smem = lean_nf4_smem(p.in_f, kw, rg, rw, vw, c.stages, c.nf4_lut);
-    const long long rows_per_cta = (long long)rg * rw;
-    return launch_persistent(fn, &lp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, smem, c.flags, st);
+    if (p.fmt != kNf4) return cudaErrorInvalidValue;
+    const b4_gemv_segment s{p.qw, p.scale, p.y, p.out_f};
+    return launch_lean_nf4_segs(&s, 1, p.x, p.in_f, p.m, c, st);
+}
+
+void default_config_multi(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m, b4_gemv_config* cfg)
+{
+    // the rule over the total rows, with the alignment every segment offers
+    long long rows = 0;
+    bool qw16 = true, sc4 = true;
+    for (int s = 0; s < nseg; ++s) {
+        rows += segs[s].out_f;
+        qw16 = qw16 && aligned(segs[s].qw, 16);
+        sc4 = sc4 && aligned(segs[s].scale, 4);
+    }
+    const int total = (int)std::min<long long>(rows, INT32_MAX);
+    GemvProblem p{fmt, reinterpret_cast<const uint32_t*>(qw16 ? 256 : 4),
+                  reinterpret_cast<const void*>(sc4 ? 256 : 2), reinterpret_cast<const void*>(256),
+                  reinterpret_cast<float*>(256), in_f, total, m, in_f, total};
+    default_config(p, cfg);
+}
+
+int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                      const b4_gemv_config& c, cudaStream_t st)
+{
+    if (m == 1 && fmt == kInt4 && (c.engine == B4_ENGINE_MMA_LEAN || c.engine == B4_ENGINE_MMA_LEAN_ASYNC))
+        return launch_lean_int4_segs(segs, nseg, x, in_f, m, c, st);
+    if (m == 1 && fmt == kNf4 && c.engine == B4_ENGINE_FMA_LEAN)
+        return launch_lean_nf4_segs(segs, nseg, x, in_f, m, c, st);
+    // the other engines: one launch per segment with this config
+    for (int s = 0; s < nseg; ++s) {
+        const GemvProblem p{fmt, segs[s].qw, segs[s].scale, x, segs[s].y, in_f, segs[s].out_f, m, in_f,
+                            segs[s].out_f};
+        const int e = launch_gemv(p, c, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace b4
@@ -632,14 +741,59 @@ int b4_gemv_nf4_b64_block_per_row(const uint32_t* qw, const float* absmax, const
     GemvProblem p{kNf4, qw, absmax, x, y, in_f, out_f, 1, in_f, out_f};
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
+    // the CUDA-core kernel with one row per CTA: warps_per_block warps split
+    // in_f, 16-, 8- or 4-byte loads as the alignment allows
     b4_gemv_config c;
     default_config(p, &c);
+    const int words = in_f / 8;
+    c.engine = B4_ENGINE_FMA;
+    c.vec_words = (words % 4 == 0 && aligned(qw, 16)) ? 4 : (words % 2 == 0 && aligned(qw, 8)) ? 2 : 1;
     c.rows_per_warp = 1;
     c.warps_k = warps_per_block;
     c.row_groups = 1;
     c.batch_tile = 1;
-    if (c.vec_words == 1) c.rows_per_warp = 1;
+    c.nf4_lut = 0;
+    c.x_tile = 0;
+    c.flags = 0;
     return launch_gemv(p, c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace {
+
+// Shape and pointer checks of every segment (check_problem per segment).
+int check_segments(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m, bool need_y)
+{
+    if (!segs || nseg < 1 || nseg > B4_MAX_SEGMENTS) return cudaErrorInvalidValue;
+    for (int s = 0; s < nseg; ++s) {
+        float* y = need_y ? segs[s].y : reinterpret_cast<float*>(256);
+        const GemvProblem p{fmt, segs[s].qw, segs[s].scale, x, y, in_f, segs[s].out_f, m, in_f, segs[s].out_f};
+        const int e = check_problem(p);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
+int b4_gemv_multi_default_config(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
+                                 b4_gemv_config* cfg)
+{
+    if (!cfg) return cudaErrorInvalidValue;
+    const int e = check_segments(fmt, segs, nseg, reinterpret_cast<const void*>(256), in_f, m, false);
+    if (e != cudaSuccess) return e;
+    default_config_multi(fmt, segs, nseg, in_f, m, cfg);
+    return cudaSuccess;
+}
+
+int b4_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                  const b4_gemv_config* cfg, b4_stream_t stream)
+{
+    const int e = check_segments(fmt, segs, nseg, x, in_f, m, true);
+    if (e != cudaSuccess) return e;
+    b4_gemv_config c;
+    if (cfg) c = *cfg;
+    else default_config_multi(fmt, segs, nseg, in_f, m, &c);
+    return launch_gemv_multi(fmt, segs, nseg, x, in_f, m, c, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int b4_device_error(int clear) { return gemv_tma_device_error(clear); }

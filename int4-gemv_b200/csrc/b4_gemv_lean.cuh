@@ -8,47 +8,134 @@
 // of the inner loop.  Here:
 //   * x is staged once per CTA in pair order at its natural word index: the
 //     64 bytes lane q needs for group G are words 16*G + 4q .. 16*G + 4q + 3,
-//     so one pointer bump per group and four 16-byte loads with immediate
-//     offsets fetch all B fragments (m = 1: every batch column of B holds x,
-//     all lanes read; the 8 lanes with the same q read the same address);
+//     so one pointer bump per stage and four 16-byte loads with immediate
+//     offsets per group fetch all B fragments (m = 1: every batch column of B
+//     holds x, all lanes read; the 8 lanes with the same q read the same
+//     address);
 //   * rows past out_f are clamped to a valid row for loading and never
 //     stored, so the loop has no row predicates;
 //   * codes and scales are addressed by running pointers, bumped once per
-//     group step;
-//   * a D-deep software pipeline of register buffers, unrolled so every
-//     buffer index is a compile-time constant, keeps 2*(D-1) 16-byte loads
-//     per lane in flight;
-//   * the group epilogue is two fp32 adds and two FMAs: with all B columns
-//     equal, D[row][0] holds the row's partial sum.
+//     stage; a stage is G consecutive groups of the warp's rows (G = 1, 2, 4),
+//     so the scales of a stage are one 2-, 4- or 8-byte load per row;
+//   * a D-deep software pipeline, unrolled so every buffer index is a
+//     compile-time constant, keeps D-1 stages per lane in flight;
+//   * the group epilogue is two fp32 adds and two FMAs per lane: with all B
+//     columns equal, D[row][0] holds the row's partial sum.
 // Work split as in the other kernels: warps_k warps share a 16-row tile and
-// take groups ks, ks + warps_k, ...; CTAs loop over tiles of rg*16 rows.
+// take stages ks, ks + warps_k, ...; CTAs loop over tiles of rg*16 rows.  The
+// tiles of up to four weight matrices that share x (q/k/v, gate/up) form one
+// tile space, so a fused projection is one launch.
 //
 // ASYNC = 1 moves the in-flight codes out of registers: each lane copies its
-// own two 16-byte pieces of every future group with cp.async into a private
-// ring slot in shared memory ((stage*2 + row)*32 + lane: a warp's copies and
-// reads of one slot are 512 contiguous bytes, conflict-free) and reads them
-// back when the group's turn comes.  Lanes only ever read what they copied
-// themselves, so the per-thread cp.async.wait_group is the only ordering
-// needed, and D stages in flight cost shared memory instead of registers.
+// own 16-byte pieces of every future stage with cp.async into private ring
+// slots in shared memory (((stage*G + group)*2 + row)*32 + lane: a warp's
+// copies and reads of one slot are 512 contiguous bytes, conflict-free) and
+// reads them back when the stage's turn comes.  Lanes only ever read what they
+// copied themselves, so the per-thread cp.async.wait_group is the only
+// ordering needed, and D stages in flight cost shared memory instead of
+// registers.  ASYNC = 0 keeps them in registers (G = 1 only).
+//
+// The first tile's first D-1 stages are requested before the kernel waits on
+// the grid it depends on (griddepcontrol.wait): codes and scales are inputs
+// that no preceding kernel of a decode step writes, so under programmatic
+// dependent launch the weight stream starts while the previous kernel drains;
+// only x is read after the wait.
 #pragma once
 
 #include "b4_gemv_mma.cuh"
 
 namespace b4 {
 
-struct LeanParams {
+// One weight matrix of a launch.  Several matrices that share x (q/k/v, or
+// gate/up) run as one launch: CTA tiles [tile_end[s-1], tile_end[s]) belong
+// to segment s.
+struct LeanSeg {
     const uint32_t* qw;
     const __half* scale;
-    const __half* x;
     float* y;
-    int in_f, out_f;
+    int out_f;
+    int tile_end;
+};
+
+constexpr int kLeanMaxSeg = 4;
+
+struct LeanParams {
+    LeanSeg seg[kLeanMaxSeg];
+    int nseg, n_tiles;
+    const __half* x;
+    int in_f;
     int kw, rg;
     int x_vec;
 };
 
-template <int D, int ASYNC>   // D >= 2
+// scales of one stage of G groups of one row
+template <int G> struct LeanScale;
+template <> struct LeanScale<1> { using T = unsigned short; };
+template <> struct LeanScale<2> { using T = uint32_t; };
+template <> struct LeanScale<4> { using T = uint2; };
+
+template <int G>
+__device__ __forceinline__ void lean_scales_to_f32(const typename LeanScale<G>::T& s, float (&f)[G])
+{
+    if constexpr (G == 1) {
+        f[0] = __half2float(__ushort_as_half(s));
+    } else if constexpr (G == 2) {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&s));
+        f[0] = a.x;
+        f[1] = a.y;
+    } else {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&s.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&s.y));
+        f[0] = a.x;
+        f[1] = a.y;
+        f[2] = b.x;
+        f[3] = b.y;
+    }
+}
+
+// m16n8k16 f16 x f16 -> f32 with no side effects, so the compiler may
+// schedule the MMAs of independent chains freely.
+__device__ __forceinline__ void mma_16816_pure(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                               const float (&c)[4])
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
+}
+
+// One 128-column group of rows (r0+g, r0+g+8): 8 MMAs in two interleaved
+// chains (words 0,1 and 2,3 of this lane's 16 bytes per row).
+__device__ __forceinline__ void lean_group(const uint4 wav, const uint4 wbv, const uint4 (&xv)[4], float& pa,
+                                           float& pb)
+{
+    const uint32_t wa[4] = {wav.x, wav.y, wav.z, wav.w};
+    const uint32_t wb[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
+    uint32_t ha[4][4], hb[4][4];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        int4_word_to_half2(wa[v], ha[v]);
+        int4_word_to_half2(wb[v], hb[v]);
+    }
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int v0 = j >> 1, hf = j & 1, v1 = v0 + 2;
+        const uint32_t a0[4] = {ha[v0][2 * hf], hb[v0][2 * hf], ha[v0][2 * hf + 1], hb[v0][2 * hf + 1]};
+        mma_16816_pure(c0, a0, hf ? xv[v0].z : xv[v0].x, hf ? xv[v0].w : xv[v0].y, c0);
+        const uint32_t a1[4] = {ha[v1][2 * hf], hb[v1][2 * hf], ha[v1][2 * hf + 1], hb[v1][2 * hf + 1]};
+        mma_16816_pure(c1, a1, hf ? xv[v1].z : xv[v1].x, hf ? xv[v1].w : xv[v1].y, c1);
+    }
+    pa = c0[0] + c1[0];
+    pb = c0[2] + c1[2];
+}
+
+template <int D, int G, int ASYNC>   // D >= 2; G in {1, 2, 4}; ASYNC = 0 needs G = 1
 __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p)
 {
+    static_assert(ASYNC || G == 1, "register pipeline holds one group per stage");
+    using ST = typename LeanScale<G>::T;
     extern __shared__ __align__(16) uint4 lsm[];
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
@@ -57,13 +144,82 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     const int grp = warp / p.kw;
     const int words = p.in_f >> 3;
     const int ng = p.in_f >> 7;
+    const int nst = ng / G;                                  // stages per row (the host checks ng % G == 0)
     const int rows_per_tile = p.rg * 16;
-    const int n_tiles = (p.out_f + rows_per_tile - 1) / rows_per_tile;
+    const int n_tiles = p.n_tiles;
     uint4* xs = lsm;                                         // one slot per word
     float* red = reinterpret_cast<float*>(xs + words);      // rg*kw*16
-    // ASYNC: this warp's ring, D stages x 2 rows x 32 lanes x 16 bytes
-    uint4* ring = xs + words + (p.rg * p.kw * 16 + 3) / 4 + warp * (D * 64);
+    // ASYNC: this warp's ring, D stages x G groups x 2 rows x 32 lanes x 16 bytes
+    uint4* ring = xs + words + (p.rg * p.kw * 16 + 3) / 4 + warp * (D * G * 64);
 
+    // stages of this warp: ks, ks + kw, ...; n_it is warp-uniform
+    const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
+    const int wstep = 4 * G * p.kw;                          // uint4 per stage step
+
+    const uint4 *pa = nullptr, *pb = nullptr;
+    const ST *sa_p = nullptr, *sb_p = nullptr;
+    uint4 bufa[ASYNC ? 1 : D], bufb[ASYNC ? 1 : D];
+    ST bsa[D], bsb[D];
+    int r0 = 0, out_f = 0;
+    float* y = nullptr;
+    auto setup = [&](int tile) {
+        // the segment of this tile (constant indices only: no local-memory copy of the parameters)
+        const uint32_t* qw = p.seg[0].qw;
+        const __half* sc = p.seg[0].scale;
+        y = p.seg[0].y;
+        out_f = p.seg[0].out_f;
+        int t0 = 0;
+#pragma unroll
+        for (int s = 1; s < kLeanMaxSeg; ++s) {
+            if (s < p.nseg && tile >= p.seg[s - 1].tile_end) {
+                qw = p.seg[s].qw;
+                sc = p.seg[s].scale;
+                y = p.seg[s].y;
+                out_f = p.seg[s].out_f;
+                t0 = p.seg[s - 1].tile_end;
+            }
+        }
+        r0 = (tile - t0) * rows_per_tile + grp * 16;
+        const int ra = min(r0 + g, out_f - 1);
+        const int rb = min(r0 + g + 8, out_f - 1);
+        pa = reinterpret_cast<const uint4*>(qw + (long long)ra * words) + ks * 4 * G + q;
+        pb = reinterpret_cast<const uint4*>(qw + (long long)rb * words) + ks * 4 * G + q;
+        sa_p = reinterpret_cast<const ST*>(sc + (long long)ra * ng) + ks;
+        sb_p = reinterpret_cast<const ST*>(sc + (long long)rb * ng) + ks;
+    };
+    auto fetch = [&](int slot) {
+        if constexpr (ASYNC) {
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                cp_async16(ring + ((slot * G + h) * 2) * 32 + lane, pa + 4 * h);
+                cp_async16(ring + ((slot * G + h) * 2 + 1) * 32 + lane, pb + 4 * h);
+            }
+        } else {
+            const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
+            const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
+            bufa[slot] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
+            bufb[slot] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
+        }
+        bsa[slot] = __ldg(sa_p);
+        bsb[slot] = __ldg(sb_p);
+        pa += wstep;
+        pb += wstep;
+        sa_p += p.kw;
+        sb_p += p.kw;
+    };
+    auto prologue = [&]() {
+#pragma unroll
+        for (int d = 0; d < D - 1; ++d) {
+            if (d < n_it) fetch(d);
+            if constexpr (ASYNC) cp_async_commit();   // one group per stage, even if empty
+        }
+    };
+
+    int tile = blockIdx.x;
+    if (tile < n_tiles) {   // weights first: they do not depend on the preceding grid
+        setup(tile);
+        prologue();
+    }
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int w = threadIdx.x; w < words; w += blockDim.x) {
@@ -82,45 +238,13 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     }
     __syncthreads();
 
-    // groups of this warp: ks, ks + kw, ...; n_it is warp-uniform
-    const int n_it = ng > ks ? (ng - ks + p.kw - 1) / p.kw : 0;
-    const int wstep = 4 * p.kw;                              // uint4 per group step
-
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const int r0 = tile * rows_per_tile + grp * 16;
-        const int ra = min(r0 + g, p.out_f - 1);
-        const int rb = min(r0 + g + 8, p.out_f - 1);
-        const uint4* pa = reinterpret_cast<const uint4*>(p.qw + (long long)ra * words) + ks * 4 + q;
-        const uint4* pb = reinterpret_cast<const uint4*>(p.qw + (long long)rb * words) + ks * 4 + q;
-        const __half* sa_p = p.scale + (long long)ra * ng + ks;
-        const __half* sb_p = p.scale + (long long)rb * ng + ks;
-
-        uint4 bufa[D], bufb[D];
-        __half bsa[D], bsb[D];
-        auto fetch = [&](int slot) {
-            if constexpr (ASYNC) {
-                cp_async16(ring + (slot * 2) * 32 + lane, pa);
-                cp_async16(ring + (slot * 2 + 1) * 32 + lane, pb);
-            } else {
-                const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
-                const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
-                bufa[slot] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
-                bufb[slot] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
-            }
-            bsa[slot] = __ldg(sa_p);
-            bsb[slot] = __ldg(sb_p);
-            pa += wstep;
-            pb += wstep;
-            sa_p += p.kw;
-            sb_p += p.kw;
-        };
-#pragma unroll
-        for (int d = 0; d < D - 1; ++d) {
-            if (d < n_it) fetch(d);
-            if constexpr (ASYNC) cp_async_commit();   // one group per stage, even if empty
+    for (; tile < n_tiles; tile += gridDim.x) {
+        if (tile != (int)blockIdx.x) {
+            setup(tile);
+            prologue();
         }
         float acc_a = 0.0f, acc_b = 0.0f;
-        const uint4* xp = xs + ks * 16 + q * 4;              // + 16*kw per group step
+        const uint4* xp = xs + ks * 16 * G + q * 4;          // + 16*G*kw per stage step
 
         for (int it0 = 0; it0 < n_it; it0 += D) {
 #pragma unroll
@@ -130,34 +254,30 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                     // refill the stage consumed in the previous step
                     const int nxt = (d + D - 1) % D;   // a constant once unrolled
                     if (it + D - 1 < n_it) fetch(nxt);
-                    uint4 wav, wbv;
                     if constexpr (ASYNC) {
                         cp_async_commit();
                         cp_async_wait<D - 1>();            // this lane's copies of stage d landed
-                        wav = ring[(d * 2) * 32 + lane];
-                        wbv = ring[(d * 2 + 1) * 32 + lane];
-                    } else {
-                        wav = bufa[d];
-                        wbv = bufb[d];
                     }
-                    const uint4 xv[4] = {xp[0], xp[1], xp[2], xp[3]};
-                    xp += 16 * p.kw;
-                    const uint32_t wa[4] = {wav.x, wav.y, wav.z, wav.w};
-                    const uint32_t wb[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
-                    float c0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, c1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    float sa[G], sb[G];
+                    lean_scales_to_f32<G>(bsa[d], sa);
+                    lean_scales_to_f32<G>(bsb[d], sb);
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        uint32_t ha[4], hb[4];
-                        int4_word_to_half2(wa[v], ha);
-                        int4_word_to_half2(wb[v], hb);
-                        const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
-                        const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
-                        float (&c)[4] = (v & 1) ? c1 : c0;
-                        mma_16816(c, a0, xv[v].x, xv[v].y, c);
-                        mma_16816(c, a1, xv[v].z, xv[v].w, c);
+                    for (int h = 0; h < G; ++h) {
+                        uint4 wav, wbv;
+                        if constexpr (ASYNC) {
+                            wav = ring[((d * G + h) * 2) * 32 + lane];
+                            wbv = ring[((d * G + h) * 2 + 1) * 32 + lane];
+                        } else {
+                            wav = bufa[d];
+                            wbv = bufb[d];
+                        }
+                        const uint4 xv[4] = {xp[16 * h + 0], xp[16 * h + 1], xp[16 * h + 2], xp[16 * h + 3]};
+                        float ua, ub;
+                        lean_group(wav, wbv, xv, ua, ub);
+                        acc_a = fmaf(ua, sa[h], acc_a);
+                        acc_b = fmaf(ub, sb[h], acc_b);
                     }
-                    acc_a = fmaf(c0[0] + c1[0], __half2float(bsa[d]), acc_a);
-                    acc_b = fmaf(c0[2] + c1[2], __half2float(bsb[d]), acc_b);
+                    xp += 16 * G * p.kw;
                 }
             }
         }
@@ -166,8 +286,8 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
         // rows r0+g and r0+g+8; lanes q = 0..3 hold the same values
         if (p.kw == 1) {
             if (q == 0) {
-                if (r0 + g < p.out_f) p.y[r0 + g] = acc_a;
-                if (r0 + g + 8 < p.out_f) p.y[r0 + g + 8] = acc_b;
+                if (r0 + g < out_f) y[r0 + g] = acc_a;
+                if (r0 + g + 8 < out_f) y[r0 + g + 8] = acc_b;
             }
         } else {
             float* mine = red + (grp * p.kw + ks) * 16;
@@ -179,13 +299,13 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
             if (ks == 0 && lane < 16) {
                 float t = 0.0f;
                 for (int k2 = 0; k2 < p.kw; ++k2) t += red[(grp * p.kw + k2) * 16 + lane];
-                if (r0 + lane < p.out_f) p.y[r0 + lane] = t;
+                if (r0 + lane < out_f) y[r0 + lane] = t;
             }
             __syncthreads();
         }
     }
 }
 
-void* gemv_kernel_int4_lean(int depth, int async_ring);
+void* gemv_kernel_int4_lean(int depth, int groups, int async_ring);
 
 }  // namespace b4

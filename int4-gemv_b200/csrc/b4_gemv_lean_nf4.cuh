@@ -7,6 +7,10 @@
 // (fp32, staged per CTA, XOR-swizzled so 8 consecutive lanes hit 8 distinct
 // 16-byte bank groups) and serve all RW rows.
 //
+// Up to four weight matrices that share x form one tile space (LeanNf4Seg),
+// and the first tile's first stages are requested before griddepcontrol.wait
+// (codes and absmax do not depend on the preceding grid; x does).
+//
 // In flight: each lane copies its own codes (4*VW bytes per row) and the
 // absmax of its columns (4 bytes per row) for future steps with cp.async into
 // private ring slots in shared memory, D steps deep; it reads back only what
@@ -24,16 +28,25 @@
 #pragma once
 
 #include "b4_gemv_kernel.cuh"
-#include "b4_gemv_mma.cuh"
+#include "b4_gemv_lean.cuh"
 
 namespace b4 {
 
-struct LeanNf4Params {
+// One weight matrix of a launch (see LeanSeg): tiles [tile_end[s-1],
+// tile_end[s]) belong to segment s.
+struct LeanNf4Seg {
     const uint32_t* qw;
     const float* absmax;
-    const __half* x;
     float* y;
-    int in_f, out_f;
+    int out_f;
+    int tile_end;
+};
+
+struct LeanNf4Params {
+    LeanNf4Seg seg[kLeanMaxSeg];
+    int nseg, n_tiles;
+    const __half* x;
+    int in_f;
     int kw, rg;
     int x_vec;
 };
@@ -66,7 +79,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_nf4_kernel(const LeanNf4P
     const int nchunks = words / VW;           // lane chunks per row
     const int nsteps = (nchunks + 31) / 32;
     const int rows_per_tile = p.rg * RW;
-    const int n_tiles = (p.out_f + rows_per_tile - 1) / rows_per_tile;
+    const int n_tiles = p.n_tiles;
 
     // shared memory: [pair table 32 KB if LUT=2][x][red][rings]
     unsigned char* base = reinterpret_cast<unsigned char*>(lsm);
@@ -85,6 +98,55 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_nf4_kernel(const LeanNf4P
         }
     }
     const float lut = nf4_lane_value(lane);
+    const int n_it = nsteps > ks ? (nsteps - ks + p.kw - 1) / p.kw : 0;
+
+    int r0 = 0, out_f = 0, rlast = 0;
+    const uint32_t* qw = nullptr;
+    const float* absmax = nullptr;
+    float* y = nullptr;
+    int c_next = 0;                                       // chunk of the next fetch
+    // this lane's chunk in step `it`: c = 32*(ks + it*kw) + lane
+    auto fetch = [&](int slot) {
+        const bool ok = c_next < nchunks;
+        const int cc = ok ? c_next : 0;
+#pragma unroll
+        for (int i = 0; i < RW; ++i) {
+            const long long r = min(r0 + i, rlast);
+            cp_async_bytes<CB>(ring_c + ((slot * RW + i) * 32 + lane) * CB, qw + r * words + (long long)cc * VW);
+            cp_async_bytes<4>(ring_a + (slot * RW + i) * 32 + lane, absmax + r * nblk + (cc * VW) / 8);
+        }
+        c_next += 32 * p.kw;
+    };
+    auto start_tile = [&](int tile) {
+        // the segment of this tile (constant indices only)
+        qw = p.seg[0].qw;
+        absmax = p.seg[0].absmax;
+        y = p.seg[0].y;
+        out_f = p.seg[0].out_f;
+        int t0 = 0;
+#pragma unroll
+        for (int s = 1; s < kLeanMaxSeg; ++s) {
+            if (s < p.nseg && tile >= p.seg[s - 1].tile_end) {
+                qw = p.seg[s].qw;
+                absmax = p.seg[s].absmax;
+                y = p.seg[s].y;
+                out_f = p.seg[s].out_f;
+                t0 = p.seg[s - 1].tile_end;
+            }
+        }
+        rlast = out_f - 1;
+        r0 = (tile - t0) * rows_per_tile + grp * RW;
+        c_next = 32 * ks + lane;
+#pragma unroll
+        for (int d = 0; d < D - 1; ++d) {
+            if (d < n_it) fetch(d);
+            cp_async_commit();
+        }
+    };
+
+    // codes and absmax first: they do not depend on the preceding grid
+    int tile = blockIdx.x;
+    if (tile < n_tiles) start_tile(tile);
 
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -108,31 +170,11 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_nf4_kernel(const LeanNf4P
     }
     __syncthreads();
 
-    const int n_it = nsteps > ks ? (nsteps - ks + p.kw - 1) / p.kw : 0;
     const int lx = S >= 8 ? (lane & 7) : ((lane / (8 / S)) & (S - 1));   // the swizzle of this lane's chunks
     const int tabk = (lane & 15) * 8;
 
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const int r0 = tile * rows_per_tile + grp * RW;
-        const int rlast = p.out_f - 1;
-        // this lane's chunk in step `it`: c = 32*(ks + it*kw) + lane
-        int c_next = 32 * ks + lane;                      // chunk of the next fetch
-        auto fetch = [&](int slot) {
-            const bool ok = c_next < nchunks;
-            const int cc = ok ? c_next : 0;
-#pragma unroll
-            for (int i = 0; i < RW; ++i) {
-                const long long r = min(r0 + i, rlast);
-                cp_async_bytes<CB>(ring_c + ((slot * RW + i) * 32 + lane) * CB, p.qw + r * words + (long long)cc * VW);
-                cp_async_bytes<4>(ring_a + (slot * RW + i) * 32 + lane, p.absmax + r * nblk + (cc * VW) / 8);
-            }
-            c_next += 32 * p.kw;
-        };
-#pragma unroll
-        for (int d = 0; d < D - 1; ++d) {
-            if (d < n_it) fetch(d);
-            cp_async_commit();
-        }
+    for (; tile < n_tiles; tile += gridDim.x) {
+        if (tile != (int)blockIdx.x) start_tile(tile);
         float acc[RW];
 #pragma unroll
         for (int i = 0; i < RW; ++i) acc[i] = 0.0f;
@@ -214,14 +256,14 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_nf4_kernel(const LeanNf4P
         for (int i = 1; i < RW; ++i)
             if (lane == i) mine = acc[i];
         if (p.kw == 1) {
-            if (lane < RW && r0 + lane < p.out_f) p.y[r0 + lane] = mine;
+            if (lane < RW && r0 + lane < out_f) y[r0 + lane] = mine;
         } else {
             if (lane < RW) red[(grp * p.kw + ks) * RW + lane] = mine;
             __syncthreads();
             if (ks == 0 && lane < RW) {
                 float t = 0.0f;
                 for (int k2 = 0; k2 < p.kw; ++k2) t += red[(grp * p.kw + k2) * RW + lane];
-                if (r0 + lane < p.out_f) p.y[r0 + lane] = t;
+                if (r0 + lane < out_f) y[r0 + lane] = t;
             }
             __syncthreads();
         }

@@ -29,4 +29,10 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg);
 // Validates cfg against p (and the pointer alignment it needs) and launches.
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& cfg, cudaStream_t st);
 
+// Several weight matrices over one x (b4_gemv_multi): the dispatch rule over
+// their total rows, and the launch (one kernel for the lean engines at m = 1).
+void default_config_multi(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m, b4_gemv_config* cfg);
+int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                      const b4_gemv_config& cfg, cudaStream_t st);
+
 }  // namespace b4

@@ -12,6 +12,7 @@ import pytest
 
 import b4gemv
 from b4gemv import _lib
+from b4gemv.diag import LEAN_VARIANTS
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 QWEN = [(3584, 3584), (512, 3584), (18944, 3584), (3584, 18944)]
@@ -32,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
         assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
-    assert lib.b4_abi_version() == 1
+    assert lib.b4_abi_version() == 2
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
@@ -48,8 +49,11 @@ def test_default_config_is_valid(fmt, out_f, in_f, m):
         assert c["rows_per_warp"] in (16, 32) and c["batch_tile"] in (8, 16)
         if e == 2:
             assert m <= c["batch_tile"] and c["rows_per_warp"] == 16
-    elif e in (4, 5):    # lean batch-1 INT4
-        assert fmt == 0 and m == 1 and c["rows_per_warp"] == 16 and c["stages"] in ((2, 3, 4, 6), (4, 6, 8, 12))[e - 4]
+    elif e == 4:         # lean batch-1 INT4, register pipeline
+        assert fmt == 0 and m == 1 and c["rows_per_warp"] == 16 and c["stages"] in (2, 3, 4, 6)
+    elif e == 5:         # lean batch-1 INT4, cp.async ring of `stage_groups` groups per stage
+        assert fmt == 0 and m == 1 and c["rows_per_warp"] == 16
+        assert (c["stages"], c["stage_groups"]) in LEAN_VARIANTS and (in_f // 128) % c["stage_groups"] == 0
     elif e == 6:         # lean batch-1 NF4
         assert fmt == 1 and m == 1 and c["rows_per_warp"] in (4, 8) and c["nf4_lut"] in (0, 2)
     else:
@@ -57,6 +61,45 @@ def test_default_config_is_valid(fmt, out_f, in_f, m):
         assert c["rows_per_warp"] in (1, 2, 4, 8)
         assert c["batch_tile"] in (1, 2, 4)
         assert 1 <= c["warps_k"] * c["row_groups"] <= (16 if c["rows_per_warp"] * c["batch_tile"] == 1 else 8)
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("shapes,in_f", [((3584, 512, 512), 3584), ((18944, 18944), 3584), ((8192, 1024, 1024), 8192),
+                                         ((1024, 128, 128), 8192), ((28672, 28672), 8192), ((100,), 1024)])
+def test_multi_default_config_is_one_lean_launch_at_batch_1(fmt, shapes, in_f):
+    segs = (_lib.GemvSegment * len(shapes))(*[_lib.GemvSegment(256 * (i + 1), 256, None, o)
+                                              for i, o in enumerate(shapes)])
+    c = _lib.GemvConfig()
+    assert b4gemv.load().b4_gemv_multi_default_config(fmt, segs, len(shapes), in_f, 1, ctypes.byref(c)) == 0
+    assert c.engine in ((4, 5) if fmt == 0 else (6,))
+    # the rule sees the total rows: the fused q/k/v gets the config of a 4608-row matrix
+    assert c.as_dict() == b4gemv.default_config(fmt, in_f, sum(shapes), 1)
+
+
+def test_multi_rejects_bad_segments_before_any_launch():
+    lib = b4gemv.load()
+    inv = 1
+    segs = (_lib.GemvSegment * 5)(*[_lib.GemvSegment(4096, 4096, 4096, 64) for _ in range(5)])
+    x = ctypes.c_void_p(4096)
+    assert lib.b4_gemv_multi(0, segs, 0, x, 1024, 1, None, None) == inv      # no segment
+    assert lib.b4_gemv_multi(0, segs, 5, x, 1024, 1, None, None) == inv      # more than B4_MAX_SEGMENTS
+    assert lib.b4_gemv_multi(0, segs, 2, x, 1000, 1, None, None) == inv      # in_f % 128
+    assert lib.b4_gemv_multi(1, segs, 2, x, 96, 1, None, None) == inv        # in_f % 64
+    assert lib.b4_gemv_multi(0, None, 2, x, 1024, 1, None, None) == inv
+    segs[1].out_f = 0
+    assert lib.b4_gemv_multi(0, segs, 2, x, 1024, 1, None, None) == inv      # empty segment
+    segs[1].out_f = 64
+    segs[1].y = None
+    assert lib.b4_gemv_multi(0, segs, 2, x, 1024, 1, None, None) == inv      # null y
+    c = _lib.GemvConfig()
+    assert lib.b4_gemv_multi_default_config(0, segs, 2, 1024, 1, ctypes.byref(c)) == 0   # y not read
+    segs[1].qw = 4098
+    assert lib.b4_gemv_multi_default_config(0, segs, 2, 1024, 1, ctypes.byref(c)) == inv  # misaligned codes
+    # a lean config whose stage does not tile the row: 9 groups, 2 per stage
+    segs[1].qw, segs[1].y = 4096, 4096
+    cfg = _lib.GemvConfig(vec_words=4, rows_per_warp=16, warps_k=8, row_groups=1, batch_tile=1, engine=5, stages=4,
+                          stage_groups=2)
+    assert lib.b4_gemv_multi(0, segs, 2, x, 1152, 1, ctypes.byref(cfg), None) == inv
 
 
 def test_invalid_shapes_are_rejected_before_any_launch():

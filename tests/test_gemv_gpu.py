@@ -13,6 +13,7 @@ import numpy as np
 import pytest
 
 import b4gemv
+from b4gemv.diag import LEAN_VARIANTS
 from oracle_py import rel_err
 
 TOL = 1e-3
@@ -185,8 +186,13 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                     assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 continue
             if engine in (4, 5):
-                for st in ((2, 3, 4, 6) if engine == 4 else (4, 6, 8, 12)):
-                    cfg.update(stages=st)
+                variants = [(st, 1) for st in (2, 3, 4, 6)] if engine == 4 else LEAN_VARIANTS
+                for st, sg in variants:
+                    cfg.update(stages=st, stage_groups=sg)
+                    if (in_f // 128) % sg:   # a stage of sg groups must tile the row
+                        with pytest.raises(b4gemv.B4Error):
+                            b4gemv.gemv(fmt, qw, sc, Xd, config=cfg)
+                        continue
                     y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
                     assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 continue
@@ -248,7 +254,7 @@ def test_gemv_misaligned_buffers_use_narrow_loads(cuda, oracle):
         cfg = b4gemv.default_config(fmt, 1024, 64, 1)
         y = b4gemv.gemv(fmt, qw_off, sc, x_off.view(1, 1024)).cpu().numpy()
         assert rel_err(y, f64_ref(oracle, fmt, qw, sc, X)) < TOL
-        assert cfg["vec_words"] == 4  # the rule itself prefers 16-byte loads
+        assert cfg["vec_words"] >= 2  # the rule itself prefers vector loads
 
 
 @pytest.mark.parametrize("wpb", [1, 2, 4, 8, 16])
@@ -288,3 +294,68 @@ def test_results_are_deterministic(cuda):
         a = b4gemv.gemv(fmt, qw, sc, Xd).cpu().numpy()
         b = b4gemv.gemv(fmt, qw, sc, Xd).cpu().numpy()
         assert a.tobytes() == b.tobytes()
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_gemv_multi_segments_one_launch(cuda, oracle, fmt):
+    """b4_gemv_multi: q/k/v-like segments (ragged row counts) over one x, each
+    y_s within tolerance of its double GEMV, for the default config, every
+    lean variant and the one-launch-per-segment engines; m = 2 takes the
+    per-segment path."""
+    rng = np.random.default_rng(77 + fmt)
+    in_f = 1024
+    shapes = [100, 37, 16, 250]
+    Ws = [rand_problem(rng, o, in_f)[0] for o in shapes]
+    X = rand_problem(rng, 1, in_f, 2)[1]
+    pairs = [quantised(fmt, W, cuda) for W in Ws]
+    refs = [[f64_ref(oracle, fmt, qw, sc, X[b:b + 1]) for qw, sc in pairs] for b in range(2)]
+    x1 = to_dev(X[:1], cuda)
+    for nseg in (1, 2, 3, 4):
+        cfgs = [None]
+        if fmt == 0:
+            cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=5,
+                          stages=st, stage_groups=sg) for kw, rg in [(8, 1), (2, 4), (1, 2)]
+                     for st, sg in LEAN_VARIANTS]
+            cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=4, row_groups=2, batch_tile=1, engine=4, stages=3)]
+            cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=2, row_groups=2, batch_tile=8, engine=1)]
+        else:
+            cfgs += [dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=lut,
+                          engine=6, stages=4) for vw, rw, lut in [(2, 4, 0), (4, 4, 0), (2, 8, 2)]
+                     for kw, rg in [(1, 8), (4, 2)]]
+            cfgs += [dict(vec_words=2, rows_per_warp=2, warps_k=2, row_groups=2, batch_tile=1, engine=0)]
+        for cfg in cfgs:
+            ys = b4gemv.gemv_multi(fmt, pairs[:nseg], x1, config=cfg)
+            for s in range(nseg):
+                assert rel_err(ys[s].cpu().numpy(), refs[0][s]) < TOL, (nseg, s, cfg)
+    ys = b4gemv.gemv_multi(fmt, pairs, to_dev(X, cuda))
+    for s in range(len(pairs)):
+        for b in range(2):
+            assert rel_err(ys[s][b:b + 1].cpu().numpy(), refs[b][s]) < TOL
+    # the one-launch default agrees with separate launches within the fp32 accumulation order
+    sep = [b4gemv.gemv(fmt, qw, sc, x1) for qw, sc in pairs]
+    ys = b4gemv.gemv_multi(fmt, pairs, x1)
+    for a, b in zip(ys, sep):
+        assert rel_err(a.cpu().numpy(), b.cpu().numpy().astype(np.float64)) < 1e-5
+
+
+def test_gemv_multi_rejects_bad_segments(cuda):
+    import torch
+    rng = np.random.default_rng(3)
+    W, X = rand_problem(rng, 64, 1024)
+    qw, sc = quantised(0, W, cuda)
+    x = to_dev(X, cuda)
+    with pytest.raises(AssertionError):
+        b4gemv.gemv_multi(0, [(qw, sc)] * 5, x)           # more than B4_MAX_SEGMENTS
+    qw2, sc2 = quantised(0, rand_problem(rng, 64, 512)[0], cuda)
+    with pytest.raises(AssertionError):
+        b4gemv.gemv_multi(0, [(qw, sc), (qw2, sc2)], x)   # in_f differs: x is shared
+    segs = (b4gemv.GemvSegment * 2)(b4gemv.GemvSegment(qw.data_ptr(), sc.data_ptr(), None, 64),
+                                    b4gemv.GemvSegment(qw.data_ptr(), sc.data_ptr(), None, 64))
+    y = torch.empty(64, device=cuda)
+    lib = b4gemv.load()
+    assert lib.b4_gemv_multi(0, segs, 2, x.data_ptr(), 1024, 1, None, None) == 1   # null y
+    segs[0].y = segs[1].y = y.data_ptr()
+    assert lib.b4_gemv_multi(0, segs, 0, x.data_ptr(), 1024, 1, None, None) == 1   # no segment
+    assert lib.b4_gemv_multi(0, segs, 2, x.data_ptr(), 1000, 1, None, None) == 1   # in_f % 128
+    assert lib.b4_gemv_multi(0, segs, 2, x.data_ptr(), 1024, 1, None, None) == 0
+    torch.cuda.synchronize()
