@@ -215,11 +215,22 @@ def build_weights(b4, torch, dev, fmt):
 
 
 class Launcher:
-    """Pre-bound C ABI calls: one ctypes call per GEMV, nothing else."""
+    """Pre-bound C ABI calls: one ctypes call per GEMV, nothing else.  With
+    pdl, every GEMV goes through b4_gemv_ex with the dispatch rule's config
+    plus B4_FLAG_PDL (programmatic dependent launch: the next GEMV's weight
+    stream starts while the previous kernel drains); without, through the
+    reference-shaped b4_gemv_nf4_b64 / b4_gemv_int4_g128."""
 
-    def __init__(self, b4, torch, sets, xs, ys, fmt):
+    def __init__(self, b4, torch, sets, xs, ys, fmt, pdl=False):
         lib = b4.load()
+        self.lib, self.fmt, self.pdl = lib, fmt, pdl
         self.fn = lib.b4_gemv_nf4_b64 if fmt == 1 else lib.b4_gemv_int4_g128
+        self.cfg_objs = []
+        for name, out_f, in_f in SHAPES:
+            c = b4.GemvConfig.from_dict(b4.default_config(fmt, in_f, out_f, 1))
+            c.flags = b4.FLAG_PDL
+            self.cfg_objs.append(c)
+        self.cfgs = [ctypes.byref(c) for c in self.cfg_objs]
         self.calls = []
         for s in range(len(sets)):
             row = []
@@ -229,11 +240,17 @@ class Launcher:
                             ctypes.c_void_p(xs[i].data_ptr()), ctypes.c_void_p(ys[i].data_ptr()), in_f, out_f))
             self.calls.append(row)
 
+    def call(self, i, q, sc, x, y, in_f, out_f, stream):
+        if self.pdl:
+            st = self.lib.b4_gemv_ex(self.fmt, q, sc, x, y, in_f, out_f, 1, self.cfgs[i], stream)
+        else:
+            st = self.fn(q, sc, x, y, in_f, out_f, 1, stream)
+        if st:
+            raise RuntimeError(f"GEMV launch failed with status {st}")
+
     def step(self, s, stream, events=None):
         for i, (q, sc, x, y, in_f, out_f) in enumerate(self.calls[s % len(self.calls)]):
-            st = self.fn(q, sc, x, y, in_f, out_f, 1, stream)
-            if st:
-                raise RuntimeError(f"GEMV launch failed with status {st}")
+            self.call(i, q, sc, x, y, in_f, out_f, stream)
             if events is not None:
                 events[i].record()
 
@@ -280,43 +297,16 @@ def correctness_gate(b4, torch, sets, xs, ys, fmt):
 
 def per_shape_chained(b4, torch, fmt, reps=200):
     """Per projection: `reps` back-to-back launches of that one GEMV in a
-    CUDA graph, rotating over N_SETS copies; returns us per GEMV."""
+    CUDA graph, rotating over N_SETS copies, with plain launches and as
+    programmatic dependents; us per GEMV."""
     sets, xs, ys = build_weights(b4, torch, torch.device("cuda", torch.cuda.current_device()), fmt)
-    lib = b4.load()
-    fn = lib.b4_gemv_nf4_b64 if fmt == 1 else lib.b4_gemv_int4_g128
     out = {}
-    for i, (name, out_f, in_f) in enumerate(SHAPES):
-        calls = [(ctypes.c_void_p(sets[s][i][0].data_ptr()), ctypes.c_void_p(sets[s][i][1].data_ptr()))
-                 for s in range(N_SETS)]
-        x = ctypes.c_void_p(xs[i].data_ptr())
-        y = ctypes.c_void_p(ys[i].data_ptr())
-
-        def body(stream):
-            for k in range(reps):
-                q, sc = calls[k % N_SETS]
-                fn(q, sc, x, y, in_f, out_f, 1, stream)
-
-        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-        body(stream)
-        g = torch.cuda.CUDAGraph()
-        cs = torch.cuda.Stream()
-        cs.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.graph(g, stream=cs, capture_error_mode="relaxed"):
-            body(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-        torch.cuda.current_stream().wait_stream(cs)
-        for _ in range(3):
-            g.replay()
-        torch.cuda.synchronize()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        g.replay()
-        b.record()
-        torch.cuda.synchronize()
-        us = a.elapsed_time(b) * 1e3 / reps
-        nb = nf4_bytes(out_f, in_f) if fmt == 1 else int4_bytes(out_f, in_f)
-        out[name] = {"us": round(us, 3), "gbs": round(nb / us / 1e3, 1)}
-        del g
+    for pdl in (False, True):
+        lau = Launcher(b4, torch, sets, xs, ys, fmt, pdl=pdl)
+        for i, (name, out_f, in_f) in enumerate(SHAPES):
+            us = chained_us(torch, lau, i, reps)
+            nb = nf4_bytes(out_f, in_f) if fmt == 1 else int4_bytes(out_f, in_f)
+            out.setdefault(name, {})["pdl" if pdl else "plain"] = {"us": round(us, 3), "gbs": round(nb / us / 1e3, 1)}
     del sets
     torch.cuda.synchronize()
     return out
@@ -328,9 +318,7 @@ def chained_us(torch, launcher, i, reps=100):
     def body(stream):
         for k in range(reps):
             q, sc, x, y, a_in, a_out = launcher.calls[k % N_SETS][i]
-            st = launcher.fn(q, sc, x, y, a_in, a_out, 1, stream)
-            if st:
-                raise RuntimeError(f"GEMV launch failed with status {st}")
+            launcher.call(i, q, sc, x, y, a_in, a_out, stream)
     g = torch.cuda.CUDAGraph()
     cs = torch.cuda.Stream()
     cs.wait_stream(torch.cuda.current_stream())
@@ -464,11 +452,12 @@ def chain_bench(b4, torch, dev):
     ch = DecodeChain(torch, dev, fmt=0, layers=28)
     peak, _ = measured_peak()
     out = {"config": "configs[2]: 28 layers x q/k/v/o/gate/up/down INT4 g128, batch 1, one CUDA graph",
-           "bytes_per_token": ch.bytes, "gemvs_per_token": len(ch.calls)}
-    for pdl in (False, True):
-        us = ch.time_token(pdl)
-        out["pdl" if pdl else "plain"] = {"us_per_token": round(us, 2), "gbs": round(ch.bytes / us / 1e3, 1),
-                                          "frac": round(ch.bytes / us / 1e3 / peak, 4)}
+           "bytes_per_token": ch.bytes, "gemvs_per_token": ch.launch_count(False)}
+    for key, pdl, fused in (("plain", False, False), ("pdl", True, False), ("fused_pdl", True, True)):
+        us = ch.time_token(pdl, fused)
+        out[key] = {"us_per_token": round(us, 2), "gbs": round(ch.bytes / us / 1e3, 1),
+                    "frac": round(ch.bytes / us / 1e3 / peak, 4), "launches_per_token": ch.launch_count(fused)}
+    out["fused_pdl"]["how"] = "q/k/v and gate/up as one b4_gemv_multi launch each, programmatic dependent launch"
     del ch
     torch.cuda.empty_cache()
     return out
@@ -481,7 +470,7 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
     layer is the max over ranks."""
     from b4gemv.tp import NcclComm, TPDecodeLayer
     comm = NcclComm(d.rank, d.world) if d.world > 1 else None
-    layer = TPDecodeLayer(fmt, d.rank, d.world, comm, dev, seed=5)
+    layer = TPDecodeLayer(fmt, d.rank, d.world, comm, dev, seed=5, fused=True, pdl=True)
     g = torch.Generator(device=dev)
     g.manual_seed(9)
     x = torch.randn((1, 8192), generator=g, device=dev).half()
@@ -523,7 +512,8 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
     return {"format": "int4_g128" if fmt == 0 else "nf4_b64", "tp": d.world, "us_per_layer": round(us_max, 2),
             "weight_bytes_per_rank": wb, "gbs_per_rank": round(wb / us_max / 1e3, 1),
             "frac_per_rank": round(wb / us_max / 1e3 / peak, 4),
-            "allreduces_per_layer": 2 if d.world > 1 else 0}
+            "allreduces_per_layer": 2 if d.world > 1 else 0,
+            "launches": "q/k/v and gate/up fused (b4_gemv_multi), GEMVs as programmatic dependents"}
 
 
 def run_ours(args, d):
@@ -536,7 +526,8 @@ def run_ours(args, d):
 
     sets, xs, ys = build_weights(b4, torch, dev, 1)
     gate_err = correctness_gate(b4, torch, sets, xs, ys, 1)
-    launcher = Launcher(b4, torch, sets, xs, ys, 1)
+    launcher = Launcher(b4, torch, sets, xs, ys, 1, pdl=not args.no_pdl)
+    plain = Launcher(b4, torch, sets, xs, ys, 1, pdl=False)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     for s in range(N_SETS):
         launcher.step(s, stream)  # eager first launches (attribute set-up) before capture
@@ -595,6 +586,7 @@ def run_ours(args, d):
     # on the launching stream.  (Timing events inside the step graph would add
     # their own gaps between kernels.)
     per_us = {name: round(chained_us(torch, launcher, i), 3) for i, (name, _, _) in enumerate(SHAPES)}
+    per_us_plain = {name: round(chained_us(torch, plain, i), 3) for i, (name, _, _) in enumerate(SHAPES)}
 
     peak, peak_kind = measured_peak()
     dom = "gate_proj"
@@ -636,6 +628,10 @@ def run_ours(args, d):
                    "timing": f"CUDA graphs of {gsteps} steps, events on the launching stream",
                    "parallelism": f"{n} independent replicas (no data-path collective)" if n > 1 else "1 GPU"},
         "us_per_gemv": per_us,
+        "us_per_gemv_how": ("100 launches of one projection back to back in a CUDA graph, each a programmatic "
+                            "dependent of the previous (B4_FLAG_PDL)" if not args.no_pdl else
+                            "100 launches of one projection back to back in a CUDA graph"),
+        "us_per_gemv_plain_launch": per_us_plain,
         "gbs_per_gemv": {nm: round(nf4_bytes(o, i) / per_us[nm] / 1e3, 1) for nm, o, i in SHAPES if nm in per_us},
         "roofline": {"bound": "hbm", "kernel": f"{engine_kernel(b4, 1, 3584, 18944)} (NF4, gate_proj 18944x3584)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
@@ -744,6 +740,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-chain", action="store_true", help="skip the 28-layer INT4 graph chain")
     ap.add_argument("--no-tp", action="store_true", help="skip the Llama-3-70B tensor-parallel layer")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="time the step and per-GEMV graphs with plain launches instead of programmatic dependents")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="untimed load before the timed region, for the clock samples")

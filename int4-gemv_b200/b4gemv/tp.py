@@ -23,7 +23,7 @@ from __future__ import annotations
 
 import ctypes
 
-from ._lib import FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, check, load
+from ._lib import FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, GemvConfig, GemvSegment, check, load
 
 
 def row_range(n: int, tp: int, rank: int):
@@ -111,13 +111,17 @@ class TPDecodeLayer:
     """One decoder layer's projections sharded over `tp` ranks.
 
     Shapes (Llama-3-70B defaults): hidden 8192, intermediate 28672, q 8192
-    rows (64 heads x 128), k/v 1024 rows (8 heads x 128)."""
+    rows (64 heads x 128), k/v 1024 rows (8 heads x 128).  With `fused`, this
+    rank's q/k/v shards run as one launch and gate/up as another
+    (b4_gemv_multi); with `pdl`, the GEMVs are programmatic dependents."""
 
     NAMES = ("q", "k", "v", "o", "gate", "up", "down")
 
-    def __init__(self, fmt, rank, tp, comm, device, hidden=8192, inter=28672, q_out=8192, kv_out=1024, seed=0):
+    def __init__(self, fmt, rank, tp, comm, device, hidden=8192, inter=28672, q_out=8192, kv_out=1024, seed=0,
+                 fused=True, pdl=False):
         import torch
         self.fmt, self.rank, self.tp, self.comm, self.device = fmt, rank, tp, comm, device
+        self.fused, self.pdl = fused, pdl
         self.hidden, self.inter, self.q_out, self.kv_out = hidden, inter, q_out, kv_out
         unit = fmt_unit(fmt)
         # (name, out_f, in_f, kind)
@@ -148,6 +152,27 @@ class TPDecodeLayer:
                     "up": torch.empty((1, rg), **f32), "act": torch.empty((1, rg), **f16),
                     "y": torch.empty((1, hidden), **f32)}
         torch.cuda.synchronize(device)
+        # launch configs: q/k/v and gate/up as one launch each (b4_gemv_multi)
+        # when fused, else one per projection; PDL on the GEMV launches if asked
+        lib = load()
+        self.cfg = {}
+        self.segs = {}
+        for group, names in (("qkv", ("q", "k", "v")), ("gateup", ("gate", "up"))):
+            segs = (GemvSegment * len(names))(*[GemvSegment(self.w[n][0].data_ptr(), self.w[n][1].data_ptr(),
+                                                            self.buf[n].data_ptr(), self.w[n][0].shape[0])
+                                                for n in names])
+            c = GemvConfig()
+            in_f = self.w[names[0]][0].shape[1] * 8
+            check("multi config", lib.b4_gemv_multi_default_config(fmt, segs, len(names), in_f, 1, ctypes.byref(c)))
+            c.flags = FLAG_PDL if pdl else 0
+            self.segs[group] = (segs, len(names), in_f)
+            self.cfg[group] = c
+        for name in ("q", "k", "v", "gate", "up"):
+            qw = self.w[name][0]
+            c = GemvConfig()
+            check("config", lib.b4_gemv_default_config(fmt, qw.shape[1] * 8, qw.shape[0], 1, ctypes.byref(c)))
+            c.flags = FLAG_PDL if pdl else 0
+            self.cfg[name] = c
 
     def weight_bytes(self) -> int:
         """Algorithmic bytes this rank streams per step (codes + scales)."""
@@ -156,7 +181,12 @@ class TPDecodeLayer:
     def _gemv(self, name, x, y, stream):
         qw, sc = self.w[name]
         check(f"gemv {name}", load().b4_gemv_ex(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
-                                                 qw.shape[0], 1, None, stream))
+                                                 qw.shape[0], 1, ctypes.byref(self.cfg[name]), stream))
+
+    def _multi(self, group, x, stream):
+        segs, n, in_f = self.segs[group]
+        check(f"gemv {group}", load().b4_gemv_multi(self.fmt, segs, n, _p(x), in_f, 1, ctypes.byref(self.cfg[group]),
+                                                    stream))
 
     def _rowpar(self, name, x, y, stream):
         qw, sc = self.w[name]
@@ -172,13 +202,19 @@ class TPDecodeLayer:
         st = stream if stream is not None else torch.cuda.current_stream()
         s = ctypes.c_void_p(st.cuda_stream)
         b, lib = self.buf, load()
-        self._gemv("q", x, b["q"], s)
-        self._gemv("k", x, b["k"], s)
-        self._gemv("v", x, b["v"], s)
+        if self.fused:
+            self._multi("qkv", x, s)
+        else:
+            self._gemv("q", x, b["q"], s)
+            self._gemv("k", x, b["k"], s)
+            self._gemv("v", x, b["v"], s)
         self._rowpar("o", attn, b["h"], s)
         check("cast", lib.b4_cast_f16(_p(b["h"]), _p(b["h16"]), b["h"].numel(), s))
-        self._gemv("gate", b["h16"], b["gate"], s)
-        self._gemv("up", b["h16"], b["up"], s)
+        if self.fused:
+            self._multi("gateup", b["h16"], s)
+        else:
+            self._gemv("gate", b["h16"], b["gate"], s)
+            self._gemv("up", b["h16"], b["up"], s)
         check("swiglu", lib.b4_swiglu_f16(_p(b["gate"]), _p(b["up"]), _p(b["act"]), b["act"].numel(), s))
         self._rowpar("down", b["act"], b["y"], s)
         return b["y"]

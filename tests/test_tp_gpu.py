@@ -195,3 +195,29 @@ def test_nccl_wait_host_deadline_on_a_busy_stream(cuda):
     assert lib.b4_nccl_comm_init(ctypes.byref(comm2), 1, uid, 0) == 0
     assert lib.b4_nccl_wait(comm2, ctypes.c_void_p(s.cuda_stream), 1000) == 0
     assert lib.b4_nccl_comm_destroy(comm2) == 0
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_tp1_layer_fused_and_pdl_match_separate_launches(cuda, fmt):
+    """One GPU, no collective: the layer with q/k/v and gate/up fused into one
+    launch each, and with programmatic dependent launches, gives the same
+    outputs (within the fp32 accumulation order) as seven separate plain
+    launches."""
+    import torch
+
+    from b4gemv.tp import TPDecodeLayer
+    from oracle_py import rel_err
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    x = torch.randn((1, SMALL["hidden"]), generator=g, device=cuda).half()
+    attn = torch.randn((1, SMALL["q_out"]), generator=g, device=cuda).half()
+    ref = TPDecodeLayer(fmt, 0, 1, None, cuda, seed=4, fused=False, pdl=False, **SMALL)
+    y_ref = ref.forward(x, attn).clone()
+    bufs = {n: ref.buf[n].clone() for n in ("q", "k", "v", "gate", "up")}
+    for fused, pdl in ((True, False), (True, True), (False, True)):
+        lay = TPDecodeLayer(fmt, 0, 1, None, cuda, seed=4, fused=fused, pdl=pdl, **SMALL)
+        y = lay.forward(x, attn).clone()
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), y_ref.cpu().numpy().astype(np.float64)) < 1e-5, (fused, pdl)
+        for n, b in bufs.items():
+            assert rel_err(lay.buf[n].cpu().numpy(), b.cpu().numpy().astype(np.float64)) < 1e-5, (n, fused, pdl)
