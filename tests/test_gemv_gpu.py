@@ -181,9 +181,10 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                 sts = {(2, 4, 0): (4, 6), (2, 8, 0): (4,), (4, 4, 0): (4,), (2, 4, 2): (4, 6, 8), (2, 8, 2): (4,),
                        (4, 4, 2): (4,)}[(vw, rw, lut)]
                 for st in sts:
-                    cfg.update(stages=st)
-                    y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
-                    assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                    for flags in (0, b4gemv.FLAG_PDL):
+                        cfg.update(stages=st, flags=flags)
+                        y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+                        assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 continue
             if engine in (4, 5):
                 variants = [(st, 1) for st in (2, 3, 4, 6)] if engine == 4 else LEAN_VARIANTS
@@ -193,8 +194,10 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                         with pytest.raises(b4gemv.B4Error):
                             b4gemv.gemv(fmt, qw, sc, Xd, config=cfg)
                         continue
-                    y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
-                    assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                    for flags in (0, b4gemv.FLAG_PDL):
+                        cfg.update(flags=flags)
+                        y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+                        assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 continue
             if engine == 3:
                 for st in {(4, 2): (4, 8), (8, 2): (4, 6), (16, 2): (4,), (4, 4): (4,), (8, 4): (4,)}[(rw, vw)]:
