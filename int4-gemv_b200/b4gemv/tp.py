@@ -167,7 +167,7 @@ class TPDecodeLayer:
             c.flags = FLAG_PDL if pdl else 0
             self.segs[group] = (segs, len(names), in_f)
             self.cfg[group] = c
-        for name in ("q", "k", "v", "gate", "up"):
+        for name in self.NAMES:
             qw = self.w[name][0]
             c = GemvConfig()
             check("config", lib.b4_gemv_default_config(fmt, qw.shape[1] * 8, qw.shape[0], 1, ctypes.byref(c)))
