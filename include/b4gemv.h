@@ -91,6 +91,13 @@ typedef struct b4_gemv_config {
  * rows_per_warp 4 or 8, vec_words 2 or 4, `stages` 4, 6 or 8, nf4_lut 0
  * (warp-shuffle code book) or 2 (replicated pair table in shared memory). */
 #define B4_ENGINE_FMA_LEAN 6
+/* Tensor pipe, NF4, batch 1, in_f a multiple of 128: the code book as a
+ * 32-way replicated table of byte -> (fp16 hi, fp16 lo) pairs, one PRMT and
+ * one 8-byte shared load per two codes, MMA on hi and lo into one fp32
+ * accumulator, the two NF4 blocks of a 128-column step kept apart by the
+ * MMA's N columns; codes and absmax through a register pipeline of depth
+ * `stages` (2, 3, 4).  rows_per_warp 16, vec_words 4. */
+#define B4_ENGINE_MMA_NF4 7
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
  * the weight stream starts before the producer of x has finished.  Only x is

@@ -24,6 +24,7 @@ ENGINE_FMA_TMA = 3
 ENGINE_MMA_LEAN = 4
 ENGINE_MMA_LEAN_ASYNC = 5
 ENGINE_FMA_LEAN = 6
+ENGINE_MMA_NF4 = 7
 
 
 class GemvConfig(ctypes.Structure):

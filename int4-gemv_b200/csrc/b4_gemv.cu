@@ -12,6 +12,7 @@
 #include "b4_gemv_tma_nf4.cuh"
 #include "b4_gemv_lean.cuh"
 #include "b4_gemv_lean_nf4.cuh"
+#include "b4_gemv_nf4_mma.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -105,6 +106,12 @@ size_t lean_int4_smem(int in_f, int kw, int rg, int stages, int groups, int asyn
     // per warp: stages x groups x 2 rows x 32 lanes x 16 B
     if (async_ring) smem += (size_t)kw * rg * stages * groups * 64 * 16;
     return smem;
+}
+
+// Shared memory of the NF4 tensor-pipe kernel: [pair table][x][reduction].
+size_t nf4_mma_smem(int in_f, int kw, int rg)
+{
+    return (size_t)kNf4PairTableBytes + (size_t)in_f * 2 + (size_t)(rg * kw * 16 + 3) / 4 * 16;
 }
 
 int check_problem(const GemvProblem& p)
@@ -252,6 +259,7 @@ int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t 
 int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_lean_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
+int launch_gemv_nf4_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
@@ -260,6 +268,7 @@ int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
     if (c.engine == B4_ENGINE_FMA_TMA) return launch_gemv_tma_nf4(p, c, st);
     if (c.engine == B4_ENGINE_MMA_LEAN || c.engine == B4_ENGINE_MMA_LEAN_ASYNC) return launch_gemv_lean(p, c, st);
     if (c.engine == B4_ENGINE_FMA_LEAN) return launch_gemv_lean_nf4(p, c, st);
+    if (c.engine == B4_ENGINE_MMA_NF4) return launch_gemv_nf4_mma(p, c, st);
     if (c.engine != B4_ENGINE_FMA) return cudaErrorInvalidValue;
     const int vw = c.vec_words, rw = c.rows_per_warp, kw = c.warps_k, rg = c.row_groups;
     const int mb = c.batch_tile, lut = c.nf4_lut;
@@ -641,7 +650,48 @@ int launch_lean_nf4_segs(const b4_gemv_segment* segs, int nseg, const void* x, i
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
 }
 
+// One launch of the NF4 tensor-pipe kernel over nseg weight matrices sharing x.
+int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                        const b4_gemv_config& c, cudaStream_t st)
+{
+    if (m != 1 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c)) return cudaErrorInvalidValue;
+    if (nseg < 1 || nseg > kLeanMaxSeg || in_f % 128) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_nf4_mma(c.stages);
+    if (!fn) return cudaErrorInvalidValue;
+    const int kw = c.warps_k, rg = c.row_groups;
+    LeanNf4Params lp = {};
+    const long long rows_per_cta = (long long)rg * 16;
+    long long tiles = 0;
+    for (int s = 0; s < nseg; ++s) {
+        // 16-byte code loads, 8-byte absmax loads (two blocks per step)
+        if (!aligned(segs[s].qw, 16) || !aligned(segs[s].scale, 8)) return cudaErrorInvalidValue;
+        tiles += (segs[s].out_f + rows_per_cta - 1) / rows_per_cta;
+        if (tiles > INT32_MAX) return cudaErrorInvalidValue;
+        lp.seg[s].qw = segs[s].qw;
+        lp.seg[s].absmax = static_cast<const float*>(segs[s].scale);
+        lp.seg[s].y = segs[s].y;
+        lp.seg[s].out_f = segs[s].out_f;
+        lp.seg[s].tile_end = (int)tiles;
+    }
+    lp.nseg = nseg;
+    lp.n_tiles = (int)tiles;
+    lp.x = static_cast<const __half*>(x);
+    lp.in_f = in_f;
+    lp.kw = kw;
+    lp.rg = rg;
+    lp.x_vec = aligned(x, 16);
+    const size_t smem = nf4_mma_smem(in_f, kw, rg);
+    return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
+}
+
 }  // namespace
+
+int launch_gemv_nf4_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
+{
+    if (p.fmt != kNf4) return cudaErrorInvalidValue;
+    const b4_gemv_segment s{p.qw, p.scale, p.y, p.out_f};
+    return launch_nf4_mma_segs(&s, 1, p.x, p.in_f, p.m, c, st);
+}
 
 int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
@@ -681,6 +731,8 @@ int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void
         return launch_lean_int4_segs(segs, nseg, x, in_f, m, c, st);
     if (m == 1 && fmt == kNf4 && c.engine == B4_ENGINE_FMA_LEAN)
         return launch_lean_nf4_segs(segs, nseg, x, in_f, m, c, st);
+    if (m == 1 && fmt == kNf4 && c.engine == B4_ENGINE_MMA_NF4)
+        return launch_nf4_mma_segs(segs, nseg, x, in_f, m, c, st);
     // the other engines: one launch per segment with this config
     for (int s = 0; s < nseg; ++s) {
         const GemvProblem p{fmt, segs[s].qw, segs[s].scale, x, segs[s].y, in_f, segs[s].out_f, m, in_f,

@@ -1,0 +1,251 @@
+// b4_gemv_nf4_mma.cuh -- the batch-1 NF4 b64 GEMV on the tensor pipe.
+//
+// Every NF4 code must be looked up in the 16-entry code book, and the lookups
+// are what bound the CUDA-core kernel (b4_gemv_lean_nf4.cuh): one shared load
+// or shuffle per code or code pair, plus shared-memory traffic for x and the
+// code ring, plus an FFMA per code.  Here a lookup is one PRMT and one 8-byte
+// shared load per byte (two codes), and it yields tensor-core operands:
+//
+//   * the table has an entry per byte value b (codes lo = b & 15, hi = b >> 4
+//     of two adjacent columns), 32 copies (one per lane, so a warp's loads
+//     never conflict), 256 bytes apart: entry b, copy l at byte b*256 + l*8.
+//     PRMT builds that offset from a packed word in one instruction (byte b
+//     of the word into bits 8..15, l*8 in bits 0..7).
+//   * an entry holds T[lo], T[hi] split exactly enough for fp32 work:
+//     hi part h = fp16(T) and low part fp16(T - h), as two half2 pairs.
+//     h + l represents each of the 16 fp32 code-book values (kernels.cuh:78-83)
+//     to within 2^-22 relative; the MMA multiplies both by fp16 x exactly and
+//     accumulates in fp32, so y carries fp32-level rounding, like an FMA
+//     chain over the fp32 dequantised weights.
+//   * MMA m16n8k16: lane (g, q) holds rows r0+g and r0+g+8; a 128-column step
+//     of a row is 64 bytes, lane q taking bytes 16q .. 16q+15 (columns 32q ..
+//     32q+31, NF4 block q >> 1).  MMA j uses bytes 2j and 2j+1 of each of its
+//     rows.  The two NF4 blocks of the step are kept apart by B's columns:
+//     column 0 of B holds x at block 0's positions (zero elsewhere), column 1
+//     x at block 1's, the rest zero, so D[row][0] and D[row][1] are the two
+//     blocks' partial sums and the absmax of each block scales its own sum
+//     (deq = T[c] * absmax as in kernels.cuh:331, one block at a time).  Only
+//     lanes 0, 1 (block 0) and 6, 7 (block 1) load x; the others hold zeros.
+//   * codes and absmax come straight from global memory into registers, a
+//     D-deep software pipeline, no shared-memory ring.
+//
+// Work split as in the other lean kernels: warps_k warps share a 16-row tile
+// and take steps ks, ks + warps_k, ...; CTAs loop over tiles of rg*16 rows of
+// up to four matrices that share x (LeanNf4Params).  The table and the first
+// stages' loads come before griddepcontrol.wait; x after it.
+#pragma once
+
+#include "b4_gemv_lean_nf4.cuh"
+
+namespace b4 {
+
+constexpr int kNf4PairTableBytes = 256 * 256;   // 256 byte values x 32 copies x 8 bytes
+
+// offset of (byte m of word w) in the table, for the copy at lane*8
+template <int M>
+__device__ __forceinline__ uint32_t nf4_pair_offset(uint32_t w, uint32_t lane8)
+{
+    return __byte_perm(w, lane8, 0x5504u | (M << 4));
+}
+
+template <int D>   // D >= 2
+__global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Params p)
+{
+    extern __shared__ __align__(16) uint4 lsm[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(lsm);
+    uint2* table = reinterpret_cast<uint2*>(base);                          // kNf4PairTableBytes
+    uint4* xs = reinterpret_cast<uint4*>(base + kNf4PairTableBytes);        // in_f / 8 slots of 8 halves
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    const int warp = threadIdx.x >> 5;
+    const int ks = warp % p.kw;
+    const int grp = warp / p.kw;
+    const int words = p.in_f >> 3;
+    const int nblk = p.in_f >> 6;
+    const int nst = p.in_f >> 7;                                           // 128-column steps per row
+    float* red = reinterpret_cast<float*>(xs + words);                    // rg*kw*16
+    const int rows_per_tile = p.rg * 16;
+    const int n_tiles = p.n_tiles;
+    const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
+    const uint32_t lane8 = (uint32_t)lane * 8;
+
+    const uint4 *pa = nullptr, *pb = nullptr;
+    const float2 *sa_p = nullptr, *sb_p = nullptr;
+    uint4 bufa[D], bufb[D];
+    float2 ama[D], amb[D];
+    int r0 = 0, out_f = 0;
+    float* y = nullptr;
+    const int wstep = 4 * p.kw;                                            // uint4 per step step (64 B per row)
+    auto setup = [&](int tile) {
+        const uint32_t* qw = p.seg[0].qw;
+        const float* am = p.seg[0].absmax;
+        y = p.seg[0].y;
+        out_f = p.seg[0].out_f;
+        int t0 = 0;
+#pragma unroll
+        for (int s = 1; s < kLeanMaxSeg; ++s) {
+            if (s < p.nseg && tile >= p.seg[s - 1].tile_end) {
+                qw = p.seg[s].qw;
+                am = p.seg[s].absmax;
+                y = p.seg[s].y;
+                out_f = p.seg[s].out_f;
+                t0 = p.seg[s - 1].tile_end;
+            }
+        }
+        r0 = (tile - t0) * rows_per_tile + grp * 16;
+        const int ra = min(r0 + g, out_f - 1);
+        const int rb = min(r0 + g + 8, out_f - 1);
+        pa = reinterpret_cast<const uint4*>(qw + (long long)ra * words) + ks * 4 + q;
+        pb = reinterpret_cast<const uint4*>(qw + (long long)rb * words) + ks * 4 + q;
+        sa_p = reinterpret_cast<const float2*>(am + (long long)ra * nblk) + ks;
+        sb_p = reinterpret_cast<const float2*>(am + (long long)rb * nblk) + ks;
+    };
+    auto fetch = [&](int slot) {
+        const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
+        const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
+        bufa[slot] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
+        bufb[slot] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
+        ama[slot] = __ldg(sa_p);
+        amb[slot] = __ldg(sb_p);
+        pa += wstep;
+        pb += wstep;
+        sa_p += p.kw;
+        sb_p += p.kw;
+    };
+    auto prologue = [&]() {
+#pragma unroll
+        for (int d = 0; d < D - 1; ++d)
+            if (d < n_it) fetch(d);
+    };
+
+    int tile = blockIdx.x;
+    if (tile < n_tiles) {   // weights first: they do not depend on the preceding grid
+        setup(tile);
+        prologue();
+    }
+    // the code book: entry b, copy l = (hi pair, lo pair) of (T[b & 15], T[b >> 4])
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+        const int b = i >> 5;
+        const float t0 = c_nf4_table[b & 15], t1 = c_nf4_table[b >> 4];
+        const __half h0 = __float2half_rn(t0), h1 = __float2half_rn(t1);
+        const __half l0 = __float2half_rn(t0 - __half2float(h0)), l1 = __float2half_rn(t1 - __half2float(h1));
+        const __half2 hp = __halves2half2(h0, h1), lp = __halves2half2(l0, l1);
+        table[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&hp), *reinterpret_cast<const uint32_t*>(&lp));
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int w = threadIdx.x; w < words; w += blockDim.x) {
+        const __half* src = p.x + (long long)w * 8;
+        uint4 raw;
+        if (p.x_vec) {
+            raw = __ldg(reinterpret_cast<const uint4*>(src));
+        } else {
+            const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
+            raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
+            raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
+            raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
+            raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
+        }
+        xs[w] = raw;
+    }
+    __syncthreads();
+
+    // B carries x only on lanes (g, q) with g == q >> 1 (columns 0/1 = blocks 0/1)
+    const bool x_lane = g == (q >> 1);
+    const unsigned char* tb = reinterpret_cast<const unsigned char*>(table);
+
+    for (; tile < n_tiles; tile += gridDim.x) {
+        if (tile != (int)blockIdx.x) {
+            setup(tile);
+            prologue();
+        }
+        float acc_a = 0.0f, acc_b = 0.0f;
+        const uint4* xp = xs + ks * 16 + q * 4;                            // + 16*kw per step
+        uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                       make_uint4(0, 0, 0, 0)};
+
+        for (int it0 = 0; it0 < n_it; it0 += D) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                const int it = it0 + d;
+                if (it < n_it) {
+                    const int nxt = (d + D - 1) % D;
+                    if (it + D - 1 < n_it) fetch(nxt);
+                    if (x_lane) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) xv[i] = xp[i];
+                    }
+                    xp += 16 * p.kw;
+                    const uint32_t wa[4] = {bufa[d].x, bufa[d].y, bufa[d].z, bufa[d].w};
+                    const uint32_t wb[4] = {bufb[d].x, bufb[d].y, bufb[d].z, bufb[d].w};
+                    // four chains: (j odd?, lo part?)
+                    float c[4][4];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) c[h][0] = c[h][1] = c[h][2] = c[h][3] = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        // bytes 2j, 2j+1 of this lane's 16 bytes: word j >> 1, bytes (2j) & 3 and +1
+                        const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
+                        uint32_t oa0, oa1, ob0, ob1;
+                        if (j & 1) {
+                            oa0 = nf4_pair_offset<2>(ua, lane8);
+                            oa1 = nf4_pair_offset<3>(ua, lane8);
+                            ob0 = nf4_pair_offset<2>(ub, lane8);
+                            ob1 = nf4_pair_offset<3>(ub, lane8);
+                        } else {
+                            oa0 = nf4_pair_offset<0>(ua, lane8);
+                            oa1 = nf4_pair_offset<1>(ua, lane8);
+                            ob0 = nf4_pair_offset<0>(ub, lane8);
+                            ob1 = nf4_pair_offset<1>(ub, lane8);
+                        }
+                        const uint2 ea0 = *reinterpret_cast<const uint2*>(tb + oa0);
+                        const uint2 eb0 = *reinterpret_cast<const uint2*>(tb + ob0);
+                        const uint2 ea1 = *reinterpret_cast<const uint2*>(tb + oa1);
+                        const uint2 eb1 = *reinterpret_cast<const uint2*>(tb + ob1);
+                        const uint32_t a_hi[4] = {ea0.x, eb0.x, ea1.x, eb1.x};
+                        const uint32_t a_lo[4] = {ea0.y, eb0.y, ea1.y, eb1.y};
+                        // x[32q + 4j .. +3]: halves 0..3 or 4..7 of slot j >> 1
+                        const uint4 xq = xv[j >> 1];
+                        const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
+                        const int ch = (j & 1) * 2;
+                        mma_16816_pure(c[ch], a_hi, b0, b1, c[ch]);
+                        mma_16816_pure(c[ch + 1], a_lo, b0, b1, c[ch + 1]);
+                    }
+                    const float d00 = (c[0][0] + c[1][0]) + (c[2][0] + c[3][0]);   // row g, block 0
+                    const float d01 = (c[0][1] + c[1][1]) + (c[2][1] + c[3][1]);   // row g, block 1
+                    const float d10 = (c[0][2] + c[1][2]) + (c[2][2] + c[3][2]);   // row g+8, block 0
+                    const float d11 = (c[0][3] + c[1][3]) + (c[2][3] + c[3][3]);   // row g+8, block 1
+                    acc_a = fmaf(d00, ama[d].x, acc_a);
+                    acc_a = fmaf(d01, ama[d].y, acc_a);
+                    acc_b = fmaf(d10, amb[d].x, acc_b);
+                    acc_b = fmaf(d11, amb[d].y, acc_b);
+                }
+            }
+        }
+
+        // rows r0+g and r0+g+8: lanes q = 0 hold them (columns 0 and 1 of D)
+        if (p.kw == 1) {
+            if (q == 0) {
+                if (r0 + g < out_f) y[r0 + g] = acc_a;
+                if (r0 + g + 8 < out_f) y[r0 + g + 8] = acc_b;
+            }
+        } else {
+            float* mine = red + (grp * p.kw + ks) * 16;
+            if (q == 0) {
+                mine[g] = acc_a;
+                mine[g + 8] = acc_b;
+            }
+            __syncthreads();
+            if (ks == 0 && lane < 16) {
+                float t = 0.0f;
+                for (int k2 = 0; k2 < p.kw; ++k2) t += red[(grp * p.kw + k2) * 16 + lane];
+                if (r0 + lane < out_f) y[r0 + lane] = t;
+            }
+            __syncthreads();
+        }
+    }
+}
+
+void* gemv_kernel_nf4_mma(int depth);
+
+}  // namespace b4

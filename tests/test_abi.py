@@ -54,6 +54,8 @@ def test_default_config_is_valid(fmt, out_f, in_f, m):
     elif e == 5:         # lean batch-1 INT4, cp.async ring of `stage_groups` groups per stage
         assert fmt == 0 and m == 1 and c["rows_per_warp"] == 16
         assert (c["stages"], c["stage_groups"]) in LEAN_VARIANTS and (in_f // 128) % c["stage_groups"] == 0
+    elif e == 7:         # NF4 tensor pipe, batch 1
+        assert fmt == 1 and m == 1 and in_f % 128 == 0 and c["rows_per_warp"] == 16 and c["stages"] in (2, 3, 4)
     elif e == 6:         # lean batch-1 NF4
         assert fmt == 1 and m == 1 and c["rows_per_warp"] in (4, 8) and c["nf4_lut"] in (0, 2)
     else:
@@ -71,7 +73,7 @@ def test_multi_default_config_is_one_lean_launch_at_batch_1(fmt, shapes, in_f):
                                               for i, o in enumerate(shapes)])
     c = _lib.GemvConfig()
     assert b4gemv.load().b4_gemv_multi_default_config(fmt, segs, len(shapes), in_f, 1, ctypes.byref(c)) == 0
-    assert c.engine in ((4, 5) if fmt == 0 else (6,))
+    assert c.engine in ((4, 5) if fmt == 0 else (6, 7))
     # the rule sees the total rows: the fused q/k/v gets the config of a 4608-row matrix
     assert c.as_dict() == b4gemv.default_config(fmt, in_f, sum(shapes), 1)
 

@@ -135,6 +135,7 @@ def kernel_configs():
     out += [(0, 4, 16, 1, 0, 4), (0, 4, 16, 1, 0, 5)]                                    # lean INT4, m = 1
     out += [(1, vw, rw, 1, lut, 6) for vw, rw, lut in [(2, 4, 0), (2, 8, 0), (4, 4, 0), (2, 4, 2), (2, 8, 2),
                                                        (4, 4, 2)]]                       # lean NF4, m = 1
+    out += [(1, 4, 16, 1, 0, 7)]                                                         # NF4 tensor pipe, m = 1
     for fmt in (0, 1):
         for lut in ((0,) if fmt == 0 else (0, 1)):
             for vw, rw in [(1, 1), (1, 4)]:
@@ -157,6 +158,8 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
         cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 64, 1), (5, 18944, 1), (3, 1088, 1)]
     if engine in (4, 5):   # m = 1
         cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 128, 1), (5, 18944, 1)]
+    if engine == 7:        # m = 1, in_f a multiple of 128
+        cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 128, 1), (5, 18944, 1), (33, 896, 1)]
     if engine == 3:   # m = 1, in_f a multiple of 256 * vec_words
         cases = [(37, 1024, 1), (9, 2048, 1), (70, 3584, 1) if vw == 2 else (70, 4096, 1), (300, 1024, 1),
                  (5, 18944, 1) if vw == 2 else (5, 8192, 1)]
@@ -181,6 +184,13 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                 sts = {(2, 4, 0): (4, 6), (2, 8, 0): (4,), (4, 4, 0): (4,), (2, 4, 2): (4, 6, 8), (2, 8, 2): (4,),
                        (4, 4, 2): (4,)}[(vw, rw, lut)]
                 for st in sts:
+                    for flags in (0, b4gemv.FLAG_PDL):
+                        cfg.update(stages=st, flags=flags)
+                        y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+                        assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                continue
+            if engine == 7:
+                for st in (2, 3, 4):
                     for flags in (0, b4gemv.FLAG_PDL):
                         cfg.update(stages=st, flags=flags)
                         y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
@@ -326,6 +336,8 @@ def test_gemv_multi_segments_one_launch(cuda, oracle, fmt):
                           engine=6, stages=4) for vw, rw, lut in [(2, 4, 0), (4, 4, 0), (2, 8, 2)]
                      for kw, rg in [(1, 8), (4, 2)]]
             cfgs += [dict(vec_words=2, rows_per_warp=2, warps_k=2, row_groups=2, batch_tile=1, engine=0)]
+            cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=7, stages=st)
+                     for kw, rg in [(8, 1), (2, 4), (1, 2)] for st in (2, 3, 4)]
         for cfg in cfgs:
             ys = b4gemv.gemv_multi(fmt, pairs[:nseg], x1, config=cfg)
             for s in range(nseg):
