@@ -6,13 +6,15 @@
 // code ring, plus an FFMA per code.  Here a lookup is one PRMT and one 8-byte
 // shared load per byte (two codes), and it yields tensor-core operands:
 //
-//   * the table has an entry per byte value b (codes lo = b & 15, hi = b >> 4
-//     of two adjacent columns), 32 copies (one per lane, so a warp's loads
-//     never conflict), 256 bytes apart: entry b, copy l at byte b*256 + l*8.
+//   * the table has a 256-byte row per byte value b (codes b & 15 and b >> 4
+//     of two adjacent columns): 32 copies of the pair's high parts, then 32
+//     copies of its low parts, 4 bytes each, so lane l reads its own copies at
+//     b*256 + 4l and b*256 + 128 + 4l (32 lanes, 32 banks: no conflicts).
 //     PRMT builds that offset from a packed word in one instruction (byte b
-//     of the word into bits 8..15, l*8 in bits 0..7).
-//   * an entry holds T[lo], T[hi] split exactly enough for fp32 work:
-//     hi part h = fp16(T) and low part fp16(T - h), as two half2 pairs.
+//     of the word into bits 8..15, 4l in bits 0..7); the two 4-byte loads
+//     land in independent registers that the MMA takes as they are.
+//   * the code-book values T are split exactly enough for fp32 work:
+//     high part h = fp16(T) and low part fp16(T - h), stored as half2 pairs.
 //     h + l represents each of the 16 fp32 code-book values (kernels.cuh:78-83)
 //     to within 2^-22 relative; the MMA multiplies both by fp16 x exactly and
 //     accumulates in fp32, so y carries fp32-level rounding, like an FMA
@@ -39,13 +41,13 @@
 
 namespace b4 {
 
-constexpr int kNf4PairTableBytes = 256 * 256;   // 256 byte values x 32 copies x 8 bytes
+constexpr int kNf4PairTableBytes = 256 * 256;   // 256 byte values x 32 copies x (4 + 4) bytes
 
-// offset of (byte m of word w) in the table, for the copy at lane*8
+// offset of (byte m of word w) in the table, for the copy at lane*4
 template <int M>
-__device__ __forceinline__ uint32_t nf4_pair_offset(uint32_t w, uint32_t lane8)
+__device__ __forceinline__ uint32_t nf4_pair_offset(uint32_t w, uint32_t lane4)
 {
-    return __byte_perm(w, lane8, 0x5504u | (M << 4));
+    return __byte_perm(w, lane4, 0x5504u | (M << 4));
 }
 
 template <int D>   // D >= 2
@@ -53,7 +55,6 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
 {
     extern __shared__ __align__(16) uint4 lsm[];
     unsigned char* base = reinterpret_cast<unsigned char*>(lsm);
-    uint2* table = reinterpret_cast<uint2*>(base);                          // kNf4PairTableBytes
     uint4* xs = reinterpret_cast<uint4*>(base + kNf4PairTableBytes);        // in_f / 8 slots of 8 halves
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
@@ -67,7 +68,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     const int rows_per_tile = p.rg * 16;
     const int n_tiles = p.n_tiles;
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
-    const uint32_t lane8 = (uint32_t)lane * 8;
+    const uint32_t lane4 = (uint32_t)lane * 4;
 
     const uint4 *pa = nullptr, *pb = nullptr;
     const float2 *sa_p = nullptr, *sb_p = nullptr;
@@ -123,14 +124,24 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
         setup(tile);
         prologue();
     }
-    // the code book: entry b, copy l = (hi pair, lo pair) of (T[b & 15], T[b >> 4])
-    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-        const int b = i >> 5;
+    // the code book: row b = 32 copies of the high-part pair of (T[b & 15],
+    // T[b >> 4]), then 32 copies of the low-part pair; one thread per byte
+    // value computes its pairs and writes its row
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
         const float t0 = c_nf4_table[b & 15], t1 = c_nf4_table[b >> 4];
         const __half h0 = __float2half_rn(t0), h1 = __float2half_rn(t1);
         const __half l0 = __float2half_rn(t0 - __half2float(h0)), l1 = __float2half_rn(t1 - __half2float(h1));
         const __half2 hp = __halves2half2(h0, h1), lp = __halves2half2(l0, l1);
-        table[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&hp), *reinterpret_cast<const uint32_t*>(&lp));
+        const uint32_t hw = *reinterpret_cast<const uint32_t*>(&hp), lw = *reinterpret_cast<const uint32_t*>(&lp);
+        uint4* row = reinterpret_cast<uint4*>(base + b * 256);
+        // the 16-byte chunk order rotates with b: the 8 threads of a store
+        // phase write 8 different chunks, hence 8 different bank quads
+#pragma unroll 4
+        for (int c2 = 0; c2 < 16; ++c2) {
+            const int k = (c2 + b) & 15;
+            const uint32_t v = k < 8 ? hw : lw;
+            row[k] = make_uint4(v, v, v, v);
+        }
     }
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -152,7 +163,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
 
     // B carries x only on lanes (g, q) with g == q >> 1 (columns 0/1 = blocks 0/1)
     const bool x_lane = g == (q >> 1);
-    const unsigned char* tb = reinterpret_cast<const unsigned char*>(table);
+    const unsigned char* tb = base;
 
     for (; tile < n_tiles; tile += gridDim.x) {
         if (tile != (int)blockIdx.x) {
@@ -188,22 +199,24 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
                         const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
                         uint32_t oa0, oa1, ob0, ob1;
                         if (j & 1) {
-                            oa0 = nf4_pair_offset<2>(ua, lane8);
-                            oa1 = nf4_pair_offset<3>(ua, lane8);
-                            ob0 = nf4_pair_offset<2>(ub, lane8);
-                            ob1 = nf4_pair_offset<3>(ub, lane8);
+                            oa0 = nf4_pair_offset<2>(ua, lane4);
+                            oa1 = nf4_pair_offset<3>(ua, lane4);
+                            ob0 = nf4_pair_offset<2>(ub, lane4);
+                            ob1 = nf4_pair_offset<3>(ub, lane4);
                         } else {
-                            oa0 = nf4_pair_offset<0>(ua, lane8);
-                            oa1 = nf4_pair_offset<1>(ua, lane8);
-                            ob0 = nf4_pair_offset<0>(ub, lane8);
-                            ob1 = nf4_pair_offset<1>(ub, lane8);
+                            oa0 = nf4_pair_offset<0>(ua, lane4);
+                            oa1 = nf4_pair_offset<1>(ua, lane4);
+                            ob0 = nf4_pair_offset<0>(ub, lane4);
+                            ob1 = nf4_pair_offset<1>(ub, lane4);
                         }
-                        const uint2 ea0 = *reinterpret_cast<const uint2*>(tb + oa0);
-                        const uint2 eb0 = *reinterpret_cast<const uint2*>(tb + ob0);
-                        const uint2 ea1 = *reinterpret_cast<const uint2*>(tb + oa1);
-                        const uint2 eb1 = *reinterpret_cast<const uint2*>(tb + ob1);
-                        const uint32_t a_hi[4] = {ea0.x, eb0.x, ea1.x, eb1.x};
-                        const uint32_t a_lo[4] = {ea0.y, eb0.y, ea1.y, eb1.y};
+                        const uint32_t a_hi[4] = {*reinterpret_cast<const uint32_t*>(tb + oa0),
+                                                  *reinterpret_cast<const uint32_t*>(tb + ob0),
+                                                  *reinterpret_cast<const uint32_t*>(tb + oa1),
+                                                  *reinterpret_cast<const uint32_t*>(tb + ob1)};
+                        const uint32_t a_lo[4] = {*reinterpret_cast<const uint32_t*>(tb + 128 + oa0),
+                                                  *reinterpret_cast<const uint32_t*>(tb + 128 + ob0),
+                                                  *reinterpret_cast<const uint32_t*>(tb + 128 + oa1),
+                                                  *reinterpret_cast<const uint32_t*>(tb + 128 + ob1)};
                         // x[32q + 4j .. +3]: halves 0..3 or 4..7 of slot j >> 1
                         const uint4 xq = xv[j >> 1];
                         const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
