@@ -444,6 +444,29 @@ def cpu_fused_baseline(sets, xs, budget_s=10.0):
                       f"{el:.1f} s, {threads} threads on {os.cpu_count()} host cores"}
 
 
+def small_batch_bench(b4, torch):
+    """batch M in {1, 2, 4, 8, 16} on gate_proj and
+    down_proj, INT4 and NF4, the dispatch rule's engine per (shape, M); us per
+    GEMV as 100 back-to-back programmatic-dependent launches in one graph
+    (b4gemv.diag's chained timing, 4+ weight copies > 4x L2)."""
+    from b4gemv.diag import Problem, alg_bytes, time_chained
+    out = []
+    for fmt in (0, 1):
+        for name, out_f, in_f in (("gate_proj", 18944, 3584), ("down_proj", 3584, 18944)):
+            for m in (1, 2, 4, 8, 16):
+                prob = Problem(torch, fmt, out_f, in_f, m=m)
+                cfg = b4.GemvConfig.from_dict(b4.default_config(fmt, in_f, out_f, m))
+                cfg.flags = b4.FLAG_PDL
+                us = time_chained(torch, prob, cfg)
+                nb = alg_bytes(fmt, out_f, in_f, m)
+                out.append({"format": "int4_g128" if fmt == 0 else "nf4_b64", "shape": name, "m": m,
+                            "engine": cfg.engine, "us": round(us, 3), "gbs": round(nb / us / 1e3, 1),
+                            "tflops": round(2.0 * m * out_f * in_f / us / 1e6, 2)})
+                del prob
+                torch.cuda.empty_cache()
+    return out
+
+
 def chain_bench(b4, torch, dev):
     """28 Qwen2.5-7B layers x 7 INT4 projections in one
     CUDA graph, one token; us per token with and without programmatic
@@ -653,6 +676,7 @@ def run_ours(args, d):
     if args.detail:
         result["int4_chained"] = per_shape_chained(b4, torch, 0)
         result["nf4_chained"] = per_shape_chained(b4, torch, 1)
+        result["small_batch"] = small_batch_bench(b4, torch)
     if not args.no_chain:
         result["qwen28_int4_chain"] = chain_bench(b4, torch, dev)
     if not args.no_tp:

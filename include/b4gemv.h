@@ -179,6 +179,19 @@ int b4_dequant_nf4_b64(const uint32_t* qw, const float* absmax, float* w_out,
 int b4_unpack_codes(const uint32_t* qw, uint8_t* codes, int in_f, int out_f,
                     b4_stream_t stream);
 
+/* bitsandbytes-layout NF4 codes (two per byte, the lower column in the HIGH
+ * nibble, row-major [out_f][in_f/2] bytes) -> this library's packed words
+ * (lower column in the LOW nibble, kernels.cuh:329); the swap of the two
+ * nibbles of every byte, its own inverse, so the same call converts back.
+ * No counterpart in the reference, which packs its own layout on purpose
+ * (README.md:180-181).  A non-nested bitsandbytes fp32 absmax ([out_f][in_f/64]
+ * for a row-major weight with in_f % 64 == 0) is already this library's absmax
+ * layout, and bitsandbytes' NF4 code indices are the same 16 values in the same
+ * order (kernels.cuh:64-83), so repacked codes + absmax go straight into
+ * b4_gemv_nf4_b64.  Nested (double-quantised) absmax is not handled.
+ * in_f % 64 == 0; 4-byte aligned buffers (16-byte for the vector path). */
+int b4_repack_bnb_nf4(const void* bnb_packed, uint32_t* qw, int in_f, int out_f, b4_stream_t stream);
+
 /* ---- Quantisers -------------------------------------------------------------
  * Host: quantise() (kernels.cuh:268-297) and quantise_nf4() (kernels.cuh:
  * 308-339), byte-identical output, spread over `nthreads` host threads

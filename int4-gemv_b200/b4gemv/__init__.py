@@ -22,7 +22,7 @@ __all__ = [
     "GemvConfig", "load", "quantise", "quantise_nf4", "gemv_int4", "gemv_nf4", "gemv",
     "gemv_nf4_block_per_row", "dequant_int4", "dequant_nf4", "unpack_codes",
     "quantise_device", "quantise_nf4_device", "default_config", "median", "gemv_multi",
-    "multi_default_config", "MAX_SEGMENTS", "GemvSegment",
+    "multi_default_config", "MAX_SEGMENTS", "GemvSegment", "repack_bnb_nf4",
 ]
 
 
@@ -226,6 +226,19 @@ def dequant_nf4(qw, absmax, out=None, stream=None):
         out = torch.empty((out_f, in_f), dtype=torch.float32, device=qw.device)
     check("b4_dequant_nf4_b64", load().b4_dequant_nf4_b64(_ptr(qw), _ptr(absmax), _ptr(out), in_f, out_f,
                                                           _stream(stream)))
+    return out
+
+
+def repack_bnb_nf4(bnb_packed, out=None, stream=None):
+    """b4_repack_bnb_nf4: bitsandbytes-layout NF4 bytes [out_f][in_f/2] (lower
+    column in the high nibble) -> packed words [out_f][in_f/8] of this library;
+    applied to packed words it converts back."""
+    import torch
+    out_f = bnb_packed.shape[0]
+    in_f = bnb_packed.numel() * 2 // out_f
+    if out is None:
+        out = torch.empty((out_f, in_f // 8), dtype=torch.int32, device=bnb_packed.device)
+    check("b4_repack_bnb_nf4", load().b4_repack_bnb_nf4(_ptr(bnb_packed), _ptr(out), in_f, out_f, _stream(stream)))
     return out
 
 

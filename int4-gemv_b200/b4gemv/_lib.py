@@ -84,6 +84,7 @@ SIGNATURES = {
     "b4_dequant_int4_g128": (_I, [_P, _P, _P, _I, _I, _P]),
     "b4_dequant_nf4_b64": (_I, [_P, _P, _P, _I, _I, _P]),
     "b4_unpack_codes": (_I, [_P, _P, _I, _I, _P]),
+    "b4_repack_bnb_nf4": (_I, [_P, _P, _I, _I, _P]),
     "b4_quantise_int4_g128": (_I, [_P, _I, _I, _P, _P, _P, _I]),
     "b4_quantise_nf4_b64": (_I, [_P, _I, _I, _P, _P, _P, _I]),
     "b4_quantise_int4_g128_device": (_I, [_P, _I, _I, _P, _P, _P, _P]),

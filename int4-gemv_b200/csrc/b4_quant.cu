@@ -92,6 +92,30 @@ __global__ void unpack_kernel(const uint32_t* __restrict__ qw, uint8_t* __restri
     }
 }
 
+// bitsandbytes' 4-bit packing holds two codes per byte with the lower column
+// in the HIGH nibble; this library's (the reference's, kernels.cuh:289,329)
+// holds the lower column in the LOW nibble, bytes in the same order.  The
+// repack swaps the two nibbles of every byte (its own inverse).
+__global__ void repack_nibbles_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst,
+                                      long long n_words, int vec)
+{
+    const long long n = vec ? n_words / 4 : n_words;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        if (vec) {
+            uint4 w = __ldg(reinterpret_cast<const uint4*>(src) + i);
+            w.x = ((w.x & 0x0f0f0f0fu) << 4) | ((w.x >> 4) & 0x0f0f0f0fu);
+            w.y = ((w.y & 0x0f0f0f0fu) << 4) | ((w.y >> 4) & 0x0f0f0f0fu);
+            w.z = ((w.z & 0x0f0f0f0fu) << 4) | ((w.z >> 4) & 0x0f0f0f0fu);
+            w.w = ((w.w & 0x0f0f0f0fu) << 4) | ((w.w >> 4) & 0x0f0f0f0fu);
+            reinterpret_cast<uint4*>(dst)[i] = w;
+        } else {
+            const uint32_t w = __ldg(src + i);
+            dst[i] = ((w & 0x0f0f0f0fu) << 4) | ((w >> 4) & 0x0f0f0f0fu);
+        }
+    }
+}
+
 // INT4 g128 (kernels.cuh:268-297): one warp per (row, group); lane l holds
 // columns 4l..4l+3 of the group.
 __global__ void quant_int4_kernel(const float* __restrict__ W, int out_f, int in_f,
@@ -212,6 +236,17 @@ int b4_unpack_codes(const uint32_t* qw, uint8_t* codes, int in_f, int out_f, b4_
     const long long n = (long long)out_f * (in_f / 8);
     unpack_kernel<<<grid_for(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         qw, codes, n, aligned(codes, 8));
+    return cudaGetLastError();
+}
+
+int b4_repack_bnb_nf4(const void* bnb_packed, uint32_t* qw, int in_f, int out_f, b4_stream_t stream)
+{
+    if (!bnb_packed || !qw || in_f <= 0 || out_f <= 0 || in_f % 64) return cudaErrorInvalidValue;
+    if (!aligned(bnb_packed, 4) || !aligned(qw, 4)) return cudaErrorInvalidValue;
+    const long long n = (long long)out_f * (in_f / 8);
+    const int vec = aligned(bnb_packed, 16) && aligned(qw, 16) && n % 4 == 0;
+    repack_nibbles_kernel<<<grid_for(vec ? n / 4 : n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint32_t*>(bnb_packed), qw, n, vec);
     return cudaGetLastError();
 }
 

@@ -126,3 +126,15 @@ def rel_err(got, ref) -> float:
     err = np.max(np.abs(got - ref)) if got.size else 0.0
     scale = np.max(np.abs(ref)) if ref.size else 0.0
     return float(err / scale) if scale > 0 else float(err)
+
+
+def bnb_pack_nf4(codes):
+    """bitsandbytes' 4-bit packing of a row-major code matrix [out][in]
+    (uint8 values 0..15): byte j of a row = (code[2j] << 4) | code[2j+1], the
+    lower column in the high nibble (bitsandbytes' blockwise 4-bit quantiser
+    packs pairs this way; bitsandbytes itself is not installed here, so this
+    restatement is unpinned).  Test helper for b4_repack_bnb_nf4."""
+    import numpy as np
+    c = np.asarray(codes, np.uint8)
+    return ((c[:, 0::2] << 4) | c[:, 1::2]).astype(np.uint8)
+

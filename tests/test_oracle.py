@@ -140,3 +140,9 @@ def test_reference_cpu_loop_matches_f64(golden, oracle):
     y32 = oracle.gemv_deq_f32(g["int4_deq"], x)
     y64 = oracle.gemv_f64(False, g["int4_packed"], g["int4_scales"], g["x"])[0]
     assert rel_err(y32, y64) < 1e-5
+
+
+def test_bnb_packing_helper_puts_the_lower_column_in_the_high_nibble():
+    from oracle_py import bnb_pack_nf4
+    codes = np.array([[1, 2, 3, 4, 15, 0, 7, 8]], np.uint8)
+    assert bnb_pack_nf4(codes).tolist() == [[0x12, 0x34, 0xF0, 0x78]]
