@@ -145,7 +145,7 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     if (p.m == 1 && p.fmt == kInt4 && aligned(p.qw, 16)) {
         const int ng = p.in_f / kGroup;
         const int row_groups = (p.out_f + 15) / 16;
-        const int rg = std::max(1, std::min(4, row_groups / (2 * sms)));
+        const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
         cfg->vec_words = 4;
         cfg->rows_per_warp = 16;
         cfg->batch_tile = 1;
@@ -179,7 +179,7 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     if (p.m == 1 && p.fmt == kNf4 && p.in_f % 128 == 0 && p.in_f < 8192 && p.out_f >= 2048 && aligned(p.qw, 16) &&
         aligned(p.scale, 8) && nf4_mma_smem(p.in_f, 8, 1) <= kTmaSmemLimit) {
         const int row_groups = (p.out_f + 15) / 16;
-        const int rg = std::max(1, std::min(4, row_groups / (2 * sms)));
+        const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
         cfg->engine = B4_ENGINE_MMA_NF4;
         cfg->vec_words = 4;
         cfg->rows_per_warp = 16;
