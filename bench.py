@@ -26,6 +26,10 @@ import argparse
 import ctypes
 import json
 import os
+
+# NCCL prints its version banner on stdout unless told otherwise; the contract
+# line must be the only line this script prints (a caller's setting wins).
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 import re
 import statistics
 import subprocess
@@ -526,6 +530,23 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
     us = a.elapsed_time(b) * 1e3 / (n * reps)
     us_max = d.max(us, dev)
     wb = layer.weight_bytes()
+    # the layer's two fp32 all-reduces alone (32 KB each), eager NCCL through
+    # torch.distributed on the same ranks: the collective share of the layer
+    ar_us = None
+    if d.world > 1:
+        import torch.distributed as dist
+        buf = torch.zeros(8192, dtype=torch.float32, device=dev)
+        for _ in range(20):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        d.barrier()
+        a.record()
+        for _ in range(200):
+            dist.all_reduce(buf)
+            dist.all_reduce(buf)
+        b.record()
+        torch.cuda.synchronize()
+        ar_us = d.max(a.elapsed_time(b) * 1e3 / 200, dev)
     del graph
     torch.cuda.synchronize()
     if comm is not None:
@@ -537,6 +558,7 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
             "weight_bytes_per_rank": wb, "gbs_per_rank": round(wb / us_max / 1e3, 1),
             "frac_per_rank": round(wb / us_max / 1e3 / peak, 4),
             "allreduces_per_layer": 2 if d.world > 1 else 0,
+            "two_allreduces_us": round(ar_us, 2) if ar_us is not None else None,
             "launches": "q/k/v and gate/up fused (b4_gemv_multi), GEMVs as programmatic dependents"}
 
 

@@ -42,7 +42,7 @@ extern "C" {
 #define B4_FMT_INT4_G128 0
 #define B4_FMT_NF4_B64 1
 
-#define B4_ABI_VERSION 2
+#define B4_ABI_VERSION 3
 
 /* Same type as cudaStream_t, spelled without the CUDA headers. */
 typedef struct CUstream_st* b4_stream_t;
@@ -63,6 +63,9 @@ typedef struct b4_gemv_config {
     int engine;        /* B4_ENGINE_*: which pipe does the multiply-accumulates   */
     int stages;        /* *_TMA engines: ring stages per warp (3, 4, 6 or 8)      */
     int stage_groups;  /* B4_ENGINE_MMA_TMA: 128-column groups per stage (2, 4, 8) */
+    int tile_rows;     /* engines 4, 5, 7: rows of each warp's 16-row MMA block that
+                        * carry weights (1..16, 0 = 16); fewer rows per CTA spread
+                        * a matrix of few rows evenly over the SMs */
 } b4_gemv_config;
 
 /* CUDA cores: fp32 FMA (INT4 and NF4).  rows_per_warp 1/2/4/8, batch_tile 1/2/4. */

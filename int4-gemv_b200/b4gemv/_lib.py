@@ -42,6 +42,7 @@ class GemvConfig(ctypes.Structure):
         ("engine", ctypes.c_int),
         ("stages", ctypes.c_int),
         ("stage_groups", ctypes.c_int),
+        ("tile_rows", ctypes.c_int),
     ]
 
     def as_dict(self) -> dict:

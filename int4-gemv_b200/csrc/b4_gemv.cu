@@ -114,6 +114,17 @@ size_t nf4_mma_smem(int in_f, int kw, int rg)
     return (size_t)kNf4PairTableBytes + (size_t)in_f * 2 + (size_t)(rg * kw * 16 + 3) / 4 * 16;
 }
 
+// Rows per 16-row MMA block for the tensor-pipe batch-1 engines: when a
+// matrix has fewer than 2*SMs full tiles (rg = 1), spread its rows over just
+// under 2*SMs tiles, so no SM carries two tiles while another has one; k/v-
+// sized matrices (< 2048 rows) keep full blocks (they are launch-bound).
+int even_tile_rows(int out_f, int rg, int sms)
+{
+    if (rg != 1 || out_f < 2048) return 0;
+    const int tr = (out_f + 2 * sms - 1) / (2 * sms);
+    return tr >= 16 ? 0 : tr;
+}
+
 int check_problem(const GemvProblem& p)
 {
     if (p.fmt != kInt4 && p.fmt != kNf4) return cudaErrorInvalidValue;
@@ -136,6 +147,7 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     cfg->flags = 0;
     cfg->stages = 4;
     cfg->stage_groups = 4;
+    cfg->tile_rows = 0;
 
     // Batch 1 (fitted on B200 with `b4gemv.diag sweep`, plain and programmatic
     // dependent launches; the reference's rule was fitted on a 36-SM part,
@@ -151,6 +163,7 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
         cfg->batch_tile = 1;
         cfg->warps_k = 8 / rg;
         cfg->row_groups = rg;
+        cfg->tile_rows = even_tile_rows(p.out_f, rg, sms);
         // up to 2*148 tiles of 16 rows (q/k/v/o): the register pipeline, no ring
         if (rg == 1 && p.in_f <= 8192) {
             cfg->engine = B4_ENGINE_MMA_LEAN;
@@ -186,6 +199,7 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
         cfg->batch_tile = 1;
         cfg->warps_k = 8 / rg;
         cfg->row_groups = rg;
+        cfg->tile_rows = even_tile_rows(p.out_f, rg, sms);
         cfg->stages = 3;
         return;
     }
@@ -607,8 +621,10 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
     if ((in_f / kGroup) % groups) return cudaErrorInvalidValue;   // a stage of `groups` groups tiles the row
     void* fn = gemv_kernel_int4_lean(c.stages, groups, async_ring);
     if (!fn) return cudaErrorInvalidValue;
+    const int tr = c.tile_rows ? c.tile_rows : 16;
+    if (tr < 1 || tr > 16) return cudaErrorInvalidValue;
     LeanParams lp = {};
-    const long long rows_per_cta = (long long)rg * 16;
+    const long long rows_per_cta = (long long)rg * tr;
     long long tiles = 0;
     for (int s = 0; s < nseg; ++s) {
         // a stage's scales are one load of `groups` fp16 per row
@@ -627,6 +643,7 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
     lp.in_f = in_f;
     lp.kw = kw;
     lp.rg = rg;
+    lp.tr = tr;
     lp.x_vec = aligned(x, 16);
     const size_t smem = lean_int4_smem(in_f, kw, rg, c.stages, groups, async_ring);
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
@@ -675,8 +692,10 @@ int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, in
     void* fn = gemv_kernel_nf4_mma(c.stages);
     if (!fn) return cudaErrorInvalidValue;
     const int kw = c.warps_k, rg = c.row_groups;
+    const int tr = c.tile_rows ? c.tile_rows : 16;
+    if (tr < 1 || tr > 16) return cudaErrorInvalidValue;
     LeanNf4Params lp = {};
-    const long long rows_per_cta = (long long)rg * 16;
+    const long long rows_per_cta = (long long)rg * tr;
     long long tiles = 0;
     for (int s = 0; s < nseg; ++s) {
         // 16-byte code loads, 8-byte absmax loads (two blocks per step)
@@ -695,6 +714,7 @@ int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, in
     lp.in_f = in_f;
     lp.kw = kw;
     lp.rg = rg;
+    lp.tr = tr;
     lp.x_vec = aligned(x, 16);
     const size_t smem = nf4_mma_smem(in_f, kw, rg);
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);

@@ -21,8 +21,11 @@
 //     compile-time constant, keeps D-1 stages per lane in flight;
 //   * the group epilogue is two fp32 adds and two FMAs per lane: with all B
 //     columns equal, D[row][0] holds the row's partial sum.
-// Work split as in the other kernels: warps_k warps share a 16-row tile and
-// take stages ks, ks + warps_k, ...; CTAs loop over tiles of rg*16 rows.  The
+// Work split as in the other kernels: warps_k warps share a 16-row MMA block
+// and take stages ks, ks + warps_k, ...; CTAs loop over tiles of rg blocks.
+// Only the first tr rows of a block carry weights (tr = 16 unless a matrix
+// of few rows is spread thinner to give every SM the same number of rows);
+// the other MMA rows load nothing and are never stored.  The
 // tiles of up to four weight matrices that share x (q/k/v, gate/up) form one
 // tile space, so a fused projection is one launch.
 //
@@ -65,6 +68,7 @@ struct LeanParams {
     const __half* x;
     int in_f;
     int kw, rg;
+    int tr;      // rows of each warp's 16-row block that carry weights (1..16)
     int x_vec;
 };
 
@@ -145,7 +149,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     const int words = p.in_f >> 3;
     const int ng = p.in_f >> 7;
     const int nst = ng / G;                                  // stages per row (the host checks ng % G == 0)
-    const int rows_per_tile = p.rg * 16;
+    const int rows_per_tile = p.rg * p.tr;
     const int n_tiles = p.n_tiles;
     uint4* xs = lsm;                                         // one slot per word
     float* red = reinterpret_cast<float*>(xs + words);      // rg*kw*16
@@ -158,9 +162,10 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
 
     const uint4 *pa = nullptr, *pb = nullptr;
     const ST *sa_p = nullptr, *sb_p = nullptr;
-    uint4 bufa[ASYNC ? 1 : D], bufb[ASYNC ? 1 : D];
-    ST bsa[D], bsb[D];
+    uint4 bufa[ASYNC ? 1 : D] = {}, bufb[ASYNC ? 1 : D] = {};
+    ST bsa[D] = {}, bsb[D] = {};
     int r0 = 0, out_f = 0;
+    bool va = false, vb = false;   // this lane's rows r0+g, r0+g+8 carry weights
     float* y = nullptr;
     auto setup = [&](int tile) {
         // the segment of this tile (constant indices only: no local-memory copy of the parameters)
@@ -179,7 +184,9 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                 t0 = p.seg[s - 1].tile_end;
             }
         }
-        r0 = (tile - t0) * rows_per_tile + grp * 16;
+        r0 = (tile - t0) * rows_per_tile + grp * p.tr;
+        va = g < p.tr && r0 + g < out_f;
+        vb = g + 8 < p.tr && r0 + g + 8 < out_f;
         const int ra = min(r0 + g, out_f - 1);
         const int rb = min(r0 + g + 8, out_f - 1);
         pa = reinterpret_cast<const uint4*>(qw + (long long)ra * words) + ks * 4 * G + q;
@@ -188,20 +195,25 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
         sb_p = reinterpret_cast<const ST*>(sc + (long long)rb * ng) + ks;
     };
     auto fetch = [&](int slot) {
+        // rows that carry no weights load nothing (their MMA rows are never stored)
         if constexpr (ASYNC) {
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-                cp_async16(ring + ((slot * G + h) * 2) * 32 + lane, pa + 4 * h);
-                cp_async16(ring + ((slot * G + h) * 2 + 1) * 32 + lane, pb + 4 * h);
+                if (va) cp_async16(ring + ((slot * G + h) * 2) * 32 + lane, pa + 4 * h);
+                if (vb) cp_async16(ring + ((slot * G + h) * 2 + 1) * 32 + lane, pb + 4 * h);
             }
         } else {
-            const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
-            const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
-            bufa[slot] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
-            bufb[slot] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
+            if (va) {
+                const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
+                bufa[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+            }
+            if (vb) {
+                const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
+                bufb[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+            }
         }
-        bsa[slot] = __ldg(sa_p);
-        bsb[slot] = __ldg(sb_p);
+        if (va) bsa[slot] = __ldg(sa_p);
+        if (vb) bsb[slot] = __ldg(sb_p);
         pa += wstep;
         pb += wstep;
         sa_p += p.kw;
@@ -286,8 +298,8 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
         // rows r0+g and r0+g+8; lanes q = 0..3 hold the same values
         if (p.kw == 1) {
             if (q == 0) {
-                if (r0 + g < out_f) y[r0 + g] = acc_a;
-                if (r0 + g + 8 < out_f) y[r0 + g + 8] = acc_b;
+                if (va) y[r0 + g] = acc_a;
+                if (vb) y[r0 + g + 8] = acc_b;
             }
         } else {
             float* mine = red + (grp * p.kw + ks) * 16;
@@ -296,7 +308,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                 mine[g + 8] = acc_b;
             }
             __syncthreads();
-            if (ks == 0 && lane < 16) {
+            if (ks == 0 && lane < p.tr) {
                 float t = 0.0f;
                 for (int k2 = 0; k2 < p.kw; ++k2) t += red[(grp * p.kw + k2) * 16 + lane];
                 if (r0 + lane < out_f) y[r0 + lane] = t;

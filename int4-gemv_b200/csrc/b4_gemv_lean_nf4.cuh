@@ -48,6 +48,7 @@ struct LeanNf4Params {
     const __half* x;
     int in_f;
     int kw, rg;
+    int tr;      // engine 7: rows of each warp's 16-row block that carry weights (1..16)
     int x_vec;
 };
 

@@ -31,9 +31,10 @@
 //   * codes and absmax come straight from global memory into registers, a
 //     D-deep software pipeline, no shared-memory ring.
 //
-// Work split as in the other lean kernels: warps_k warps share a 16-row tile
-// and take steps ks, ks + warps_k, ...; CTAs loop over tiles of rg*16 rows of
-// up to four matrices that share x (LeanNf4Params).  The table and the first
+// Work split as in the other lean kernels: warps_k warps share a 16-row MMA
+// block and take steps ks, ks + warps_k, ...; CTAs loop over tiles of rg
+// blocks of up to four matrices that share x (LeanNf4Params); only the first
+// tr rows of a block carry weights (see b4_gemv_lean.cuh).  The table and the first
 // stages' loads come before griddepcontrol.wait; x after it.
 #pragma once
 
@@ -65,16 +66,17 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     const int nblk = p.in_f >> 6;
     const int nst = p.in_f >> 7;                                           // 128-column steps per row
     float* red = reinterpret_cast<float*>(xs + words);                    // rg*kw*16
-    const int rows_per_tile = p.rg * 16;
+    const int rows_per_tile = p.rg * p.tr;
     const int n_tiles = p.n_tiles;
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
     const uint32_t lane4 = (uint32_t)lane * 4;
 
     const uint4 *pa = nullptr, *pb = nullptr;
     const float2 *sa_p = nullptr, *sb_p = nullptr;
-    uint4 bufa[D], bufb[D];
-    float2 ama[D], amb[D];
+    uint4 bufa[D] = {}, bufb[D] = {};
+    float2 ama[D] = {}, amb[D] = {};
     int r0 = 0, out_f = 0;
+    bool va = false, vb = false;   // this lane's rows r0+g, r0+g+8 carry weights
     float* y = nullptr;
     const int wstep = 4 * p.kw;                                            // uint4 per step step (64 B per row)
     auto setup = [&](int tile) {
@@ -93,7 +95,9 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
                 t0 = p.seg[s - 1].tile_end;
             }
         }
-        r0 = (tile - t0) * rows_per_tile + grp * 16;
+        r0 = (tile - t0) * rows_per_tile + grp * p.tr;
+        va = g < p.tr && r0 + g < out_f;
+        vb = g + 8 < p.tr && r0 + g + 8 < out_f;
         const int ra = min(r0 + g, out_f - 1);
         const int rb = min(r0 + g + 8, out_f - 1);
         pa = reinterpret_cast<const uint4*>(qw + (long long)ra * words) + ks * 4 + q;
@@ -102,12 +106,17 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
         sb_p = reinterpret_cast<const float2*>(am + (long long)rb * nblk) + ks;
     };
     auto fetch = [&](int slot) {
-        const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
-        const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
-        bufa[slot] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
-        bufb[slot] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
-        ama[slot] = __ldg(sa_p);
-        amb[slot] = __ldg(sb_p);
+        // rows that carry no weights load nothing (their MMA rows are never stored)
+        if (va) {
+            const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
+            bufa[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+            ama[slot] = __ldg(sa_p);
+        }
+        if (vb) {
+            const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
+            bufb[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+            amb[slot] = __ldg(sb_p);
+        }
         pa += wstep;
         pb += wstep;
         sa_p += p.kw;
@@ -239,8 +248,8 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
         // rows r0+g and r0+g+8: lanes q = 0 hold them (columns 0 and 1 of D)
         if (p.kw == 1) {
             if (q == 0) {
-                if (r0 + g < out_f) y[r0 + g] = acc_a;
-                if (r0 + g + 8 < out_f) y[r0 + g + 8] = acc_b;
+                if (va) y[r0 + g] = acc_a;
+                if (vb) y[r0 + g + 8] = acc_b;
             }
         } else {
             float* mine = red + (grp * p.kw + ks) * 16;
@@ -249,7 +258,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
                 mine[g + 8] = acc_b;
             }
             __syncthreads();
-            if (ks == 0 && lane < 16) {
+            if (ks == 0 && lane < p.tr) {
                 float t = 0.0f;
                 for (int k2 = 0; k2 < p.kw; ++k2) t += red[(grp * p.kw + k2) * 16 + lane];
                 if (r0 + lane < out_f) y[r0 + lane] = t;

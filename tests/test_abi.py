@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
         assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
-    assert lib.b4_abi_version() == 2
+    assert lib.b4_abi_version() == 3
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
@@ -102,6 +102,16 @@ def test_multi_rejects_bad_segments_before_any_launch():
     cfg = _lib.GemvConfig(vec_words=4, rows_per_warp=16, warps_k=8, row_groups=1, batch_tile=1, engine=5, stages=4,
                           stage_groups=2)
     assert lib.b4_gemv_multi(0, segs, 2, x, 1152, 1, ctypes.byref(cfg), None) == inv
+
+
+def test_tile_rows_out_of_range_is_rejected():
+    lib = b4gemv.load()
+    bogus = ctypes.c_void_p(4096)
+    for e, fmt, st, sg in [(4, 0, 4, 1), (5, 0, 2, 4), (7, 1, 3, 0)]:
+        for tr in (-1, 17):
+            cfg = _lib.GemvConfig(vec_words=4, rows_per_warp=16, warps_k=8, row_groups=1, batch_tile=1, engine=e,
+                                  stages=st, stage_groups=sg, tile_rows=tr)
+            assert lib.b4_gemv_ex(fmt, bogus, bogus, bogus, bogus, 1024, 64, 1, ctypes.byref(cfg), None) == 1
 
 
 def test_invalid_shapes_are_rejected_before_any_launch():

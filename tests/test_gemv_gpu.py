@@ -195,6 +195,11 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                         cfg.update(stages=st, flags=flags)
                         y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
                         assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                for tr in (1, 5, 13):   # rows per 16-row MMA block that carry weights
+                    cfg.update(stages=3, flags=0, tile_rows=tr)
+                    y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+                    assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                cfg.update(tile_rows=0)
                 continue
             if engine in (4, 5):
                 variants = [(st, 1) for st in (2, 3, 4, 6)] if engine == 4 else LEAN_VARIANTS
@@ -208,6 +213,11 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                         cfg.update(flags=flags)
                         y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
                         assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                for tr in (1, 5, 13):   # rows per 16-row MMA block that carry weights
+                    cfg.update(stages=variants[0][0], stage_groups=variants[0][1], flags=0, tile_rows=tr)
+                    y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
+                    assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+                cfg.update(tile_rows=0)
                 continue
             if engine == 3:
                 for st in {(4, 2): (4, 8), (8, 2): (4, 6), (16, 2): (4,), (4, 4): (4,), (8, 4): (4,)}[(rw, vw)]:
@@ -331,6 +341,9 @@ def test_gemv_multi_segments_one_launch(cuda, oracle, fmt):
                      for st, sg in LEAN_VARIANTS]
             cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=4, row_groups=2, batch_tile=1, engine=4, stages=3)]
             cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=2, row_groups=2, batch_tile=8, engine=1)]
+            cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=e, stages=st,
+                          stage_groups=sg, tile_rows=tr) for kw, rg in [(8, 1), (2, 2)] for tr in (3, 13)
+                     for e, st, sg in [(4, 4, 1), (5, 2, 4)]]
         else:
             cfgs += [dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=lut,
                           engine=6, stages=4) for vw, rw, lut in [(2, 4, 0), (4, 4, 0), (2, 8, 2)]
@@ -338,6 +351,8 @@ def test_gemv_multi_segments_one_launch(cuda, oracle, fmt):
             cfgs += [dict(vec_words=2, rows_per_warp=2, warps_k=2, row_groups=2, batch_tile=1, engine=0)]
             cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=7, stages=st)
                      for kw, rg in [(8, 1), (2, 4), (1, 2)] for st in (2, 3, 4)]
+            cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=7, stages=3,
+                          tile_rows=tr) for kw, rg in [(8, 1), (2, 2)] for tr in (3, 13)]
         for cfg in cfgs:
             ys = b4gemv.gemv_multi(fmt, pairs[:nseg], x1, config=cfg)
             for s in range(nseg):
