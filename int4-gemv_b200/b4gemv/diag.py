@@ -107,6 +107,11 @@ def config_grid(fmt, m=1):
             if kw * rg <= 8:
                 yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
                            x_tile=0, flags=0, engine=5, stages=st, stage_groups=sg)
+    if fmt == FMT_INT4_G128 and 2 <= m <= 16:   # lean kernel with the batch rows in the MMA's N
+        for kw, rg, (st, sg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), [(2, 4), (3, 2), (4, 1)]):
+            if kw * rg <= 8:
+                yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
+                           x_tile=0, flags=0, engine=5, stages=st, stage_groups=sg)
     if fmt == FMT_INT4_G128 and m <= 16:
         nt = 8 if m <= 8 else 16
         for kw, rg, (st, kcg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), TMA_VARIANTS):

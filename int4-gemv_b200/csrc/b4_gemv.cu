@@ -11,6 +11,7 @@
 #include "b4_gemv_tma.cuh"
 #include "b4_gemv_tma_nf4.cuh"
 #include "b4_gemv_lean.cuh"
+#include "b4_gemv_lean_mb.cuh"
 #include "b4_gemv_lean_nf4.cuh"
 #include "b4_gemv_nf4_mma.cuh"
 #include "b4_internal.h"
@@ -108,6 +109,13 @@ size_t lean_int4_smem(int in_f, int kw, int rg, int stages, int groups, int asyn
     return smem;
 }
 
+// Shared memory of the small-batch lean INT4 kernel: [x, m rows][reduction][rings].
+size_t lean_int4_mb_smem(int in_f, int m, int kw, int rg, int stages, int groups)
+{
+    const int nc = m > 8 ? 16 : 8;
+    return (size_t)m * in_f * 2 + (size_t)rg * kw * 16 * nc * 4 + (size_t)kw * rg * stages * groups * 64 * 16;
+}
+
 // Shared memory of the NF4 tensor-pipe kernel: [pair table][x][reduction].
 size_t nf4_mma_smem(int in_f, int kw, int rg)
 {
@@ -184,6 +192,28 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
                 cfg->stage_groups = v[1];
                 return;
             }
+        }
+    }
+    // INT4 at small batch (2..16 rows): the same lean kernel with the batch rows
+    // in the MMA's N columns, when x for all rows fits next to the rings.
+    if (p.m >= 2 && p.m <= 16 && p.fmt == kInt4 && aligned(p.qw, 16)) {
+        const int ng = p.in_f / kGroup;
+        const int row_groups = (p.out_f + 15) / 16;
+        const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
+        const int variants[3][2] = {{2, 4}, {3, 2}, {4, 1}};
+        for (const auto& v : variants) {
+            if (ng % v[1] || (v[1] > 1 && !aligned(p.scale, 2u * v[1]))) continue;
+            if (lean_int4_mb_smem(p.in_f, p.m, 8 / rg, rg, v[0], v[1]) > kTmaSmemLimit) continue;
+            cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
+            cfg->vec_words = 4;
+            cfg->rows_per_warp = 16;
+            cfg->batch_tile = 1;
+            cfg->warps_k = 8 / rg;
+            cfg->row_groups = rg;
+            cfg->tile_rows = even_tile_rows(p.out_f, rg, sms);
+            cfg->stages = v[0];
+            cfg->stage_groups = v[1];
+            return;
         }
     }
     // NF4 at batch 1, q/o/gate/up-like (in_f < 8192, at least 2048 rows): the
@@ -608,18 +638,23 @@ namespace {
 
 bool lean_geometry_ok(const b4_gemv_config& c) { return c.warps_k >= 1 && c.row_groups >= 1 && c.warps_k * c.row_groups <= 8; }
 
-// One launch of the lean INT4 kernel over nseg weight matrices sharing x.
+// One launch of the lean INT4 kernel over nseg weight matrices sharing x
+// (m = 1; m = 2..16 with the cp.async ring: the small-batch kernel).
 int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
                           const b4_gemv_config& c, cudaStream_t st)
 {
-    if (m != 1 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c)) return cudaErrorInvalidValue;
+    if (m < 1 || m > 16 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c))
+        return cudaErrorInvalidValue;
+    if (m > 1 && c.engine != B4_ENGINE_MMA_LEAN_ASYNC) return cudaErrorInvalidValue;
     if (nseg < 1 || nseg > kLeanMaxSeg) return cudaErrorInvalidValue;
     const int kw = c.warps_k, rg = c.row_groups;
     const int async_ring = c.engine == B4_ENGINE_MMA_LEAN_ASYNC;
     const int groups = async_ring ? c.stage_groups : 1;
     if (groups != 1 && groups != 2 && groups != 4) return cudaErrorInvalidValue;
     if ((in_f / kGroup) % groups) return cudaErrorInvalidValue;   // a stage of `groups` groups tiles the row
-    void* fn = gemv_kernel_int4_lean(c.stages, groups, async_ring);
+    const int nb = m > 8 ? 2 : 1;
+    void* fn = m == 1 ? gemv_kernel_int4_lean(c.stages, groups, async_ring)
+                      : gemv_kernel_int4_lean_mb(c.stages, groups, nb);
     if (!fn) return cudaErrorInvalidValue;
     const int tr = c.tile_rows ? c.tile_rows : 16;
     if (tr < 1 || tr > 16) return cudaErrorInvalidValue;
@@ -645,6 +680,13 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
     lp.rg = rg;
     lp.tr = tr;
     lp.x_vec = aligned(x, 16);
+    if (m > 1) {
+        LeanMbParams mp;
+        mp.base = lp;
+        mp.m = m;
+        const size_t smem = lean_int4_mb_smem(in_f, m, kw, rg, c.stages, groups);
+        return launch_persistent(fn, &mp, tiles, 32 * kw * rg, smem, c.flags, st);
+    }
     const size_t smem = lean_int4_smem(in_f, kw, rg, c.stages, groups, async_ring);
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
 }
@@ -763,7 +805,7 @@ void default_config_multi(int fmt, const b4_gemv_segment* segs, int nseg, int in
 int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
                       const b4_gemv_config& c, cudaStream_t st)
 {
-    if (m == 1 && fmt == kInt4 && (c.engine == B4_ENGINE_MMA_LEAN || c.engine == B4_ENGINE_MMA_LEAN_ASYNC))
+    if (fmt == kInt4 && ((m == 1 && c.engine == B4_ENGINE_MMA_LEAN) || (m <= 16 && c.engine == B4_ENGINE_MMA_LEAN_ASYNC)))
         return launch_lean_int4_segs(segs, nseg, x, in_f, m, c, st);
     if (m == 1 && fmt == kNf4 && c.engine == B4_ENGINE_FMA_LEAN)
         return launch_lean_nf4_segs(segs, nseg, x, in_f, m, c, st);

@@ -51,8 +51,8 @@ def test_default_config_is_valid(fmt, out_f, in_f, m):
             assert m <= c["batch_tile"] and c["rows_per_warp"] == 16
     elif e == 4:         # lean batch-1 INT4, register pipeline
         assert fmt == 0 and m == 1 and c["rows_per_warp"] == 16 and c["stages"] in (2, 3, 4, 6)
-    elif e == 5:         # lean batch-1 INT4, cp.async ring of `stage_groups` groups per stage
-        assert fmt == 0 and m == 1 and c["rows_per_warp"] == 16
+    elif e == 5:         # lean INT4 (m <= 16: batch rows in the MMA's N), cp.async ring of `stage_groups` groups
+        assert fmt == 0 and m <= 16 and c["rows_per_warp"] == 16
         assert (c["stages"], c["stage_groups"]) in LEAN_VARIANTS and (in_f // 128) % c["stage_groups"] == 0
     elif e == 7:         # NF4 tensor pipe, batch 1
         assert fmt == 1 and m == 1 and in_f % 128 == 0 and c["rows_per_warp"] == 16 and c["stages"] in (2, 3, 4)

@@ -413,3 +413,24 @@ def test_repack_bnb_nf4_matches_reference_packing(cuda, oracle):
         y1 = b4gemv.gemv_nf4(qw, am, x).cpu().numpy()
         y2 = b4gemv.gemv_nf4(torch.from_numpy(p.view(np.int32)).to(cuda), am, x).cpu().numpy()
         assert y1.tobytes() == y2.tobytes()
+
+
+@pytest.mark.parametrize("m", [2, 3, 5, 8, 9, 16])
+def test_int4_small_batch_lean_kernel(cuda, oracle, m):
+    """The lean INT4 kernel with batch rows in the MMA's N columns (engine 5,
+    m = 2..16): every (stages, groups) variant, several warp splits and
+    weight-carrying rows per MMA block, against the double GEMV per batch row."""
+    rng = np.random.default_rng(300 + m)
+    for out_f, in_f in [(70, 1024), (37, 3584), (300, 512)]:
+        W, X = rand_problem(rng, out_f, in_f, m)
+        qw, sc = quantised(0, W, cuda)
+        ref = f64_ref(oracle, 0, qw, sc, X)
+        Xd = to_dev(X, cuda)
+        for (st, sg), (kw, rg), tr in itertools.product([(2, 4), (3, 2), (4, 1)], [(8, 1), (2, 2), (1, 4)], (0, 5)):
+            if (in_f // 128) % sg:
+                continue
+            cfg = dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=5, stages=st,
+                       stage_groups=sg, tile_rows=tr)
+            y = b4gemv.gemv(0, qw, sc, Xd, config=cfg).cpu().numpy()
+            assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+    assert b4gemv.default_config(0, 3584, 18944, m)["engine"] == 5
