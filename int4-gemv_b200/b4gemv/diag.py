@@ -123,8 +123,8 @@ def config_grid(fmt, m=1):
             if kw * rg <= 8 and (nt == 8 or m > 8):
                 yield dict(vec_words=4, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=nt, nf4_lut=0,
                            x_tile=0, flags=0, engine=1)
-    if fmt == FMT_NF4_B64 and m == 1:
-        for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (2, 3, 4)):
+    if fmt == FMT_NF4_B64 and m <= 16:
+        for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (2, 3, 4) if m == 1 else (2, 3)):
             if kw * rg <= 8:
                 yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
                            x_tile=0, flags=0, engine=7, stages=st, stage_groups=0)

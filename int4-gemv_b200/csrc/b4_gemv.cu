@@ -14,6 +14,7 @@
 #include "b4_gemv_lean_mb.cuh"
 #include "b4_gemv_lean_nf4.cuh"
 #include "b4_gemv_nf4_mma.cuh"
+#include "b4_gemv_nf4_mma_mb.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -122,6 +123,13 @@ size_t nf4_mma_smem(int in_f, int kw, int rg)
     return (size_t)kNf4PairTableBytes + (size_t)in_f * 2 + (size_t)(rg * kw * 16 + 3) / 4 * 16;
 }
 
+// ... and of its small-batch form: [pair table][x, m rows][reduction].
+size_t nf4_mma_mb_smem(int in_f, int m, int kw, int rg)
+{
+    const int nr = (m + 3) / 4 > 2 ? 16 : ((m + 3) / 4) * 4;
+    return (size_t)kNf4PairTableBytes + (size_t)m * in_f * 2 + (size_t)rg * kw * 16 * nr * 4;
+}
+
 // Rows per 16-row MMA block for the tensor-pipe batch-1 engines: when a
 // matrix has fewer than 2*SMs full tiles (rg = 1), spread its rows over just
 // under 2*SMs tiles, so no SM carries two tiles while another has one; k/v-
@@ -196,11 +204,13 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     }
     // INT4 at small batch (2..16 rows): the same lean kernel with the batch rows
     // in the MMA's N columns, when x for all rows fits next to the rings.
+    // (fitted on B200 for m = 2..16 on gate/down: one CTA per SM's worth of
+    // rows per tile, 2 stages of 4 groups up to m = 4, 3 of 2 beyond)
     if (p.m >= 2 && p.m <= 16 && p.fmt == kInt4 && aligned(p.qw, 16)) {
         const int ng = p.in_f / kGroup;
         const int row_groups = (p.out_f + 15) / 16;
-        const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
-        const int variants[3][2] = {{2, 4}, {3, 2}, {4, 1}};
+        const int rg = std::max(1, std::min(8, (row_groups + sms - 1) / sms));
+        const int variants[3][2] = {{p.m <= 4 ? 2 : 3, p.m <= 4 ? 4 : 2}, {3, 2}, {4, 1}};
         for (const auto& v : variants) {
             if (ng % v[1] || (v[1] > 1 && !aligned(p.scale, 2u * v[1]))) continue;
             if (lean_int4_mb_smem(p.in_f, p.m, 8 / rg, rg, v[0], v[1]) > kTmaSmemLimit) continue;
@@ -213,6 +223,24 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
             cfg->tile_rows = even_tile_rows(p.out_f, rg, sms);
             cfg->stages = v[0];
             cfg->stage_groups = v[1];
+            return;
+        }
+    }
+    // NF4 at small batch (2..16 rows): the tensor-pipe engine with the batch
+    // rows in the MMA's N columns, when x for all rows fits next to the table.
+    if (p.m >= 2 && p.m <= 16 && p.fmt == kNf4 && p.in_f % 128 == 0 && aligned(p.qw, 16) && aligned(p.scale, 8)) {
+        const int row_groups = (p.out_f + 15) / 16;
+        int rg = std::max(1, std::min(8, (row_groups + sms - 1) / sms));
+        if (p.m <= 4 && rg == 8) rg = 4;
+        if (nf4_mma_mb_smem(p.in_f, p.m, 8 / rg, rg) <= kTmaSmemLimit) {
+            cfg->engine = B4_ENGINE_MMA_NF4;
+            cfg->vec_words = 4;
+            cfg->rows_per_warp = 16;
+            cfg->batch_tile = 1;
+            cfg->warps_k = 8 / rg;
+            cfg->row_groups = rg;
+            cfg->tile_rows = 0;
+            cfg->stages = p.m <= 4 ? 2 : 3;
             return;
         }
     }
@@ -729,9 +757,11 @@ int launch_lean_nf4_segs(const b4_gemv_segment* segs, int nseg, const void* x, i
 int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
                         const b4_gemv_config& c, cudaStream_t st)
 {
-    if (m != 1 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c)) return cudaErrorInvalidValue;
+    if (m < 1 || m > 16 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c))
+        return cudaErrorInvalidValue;
     if (nseg < 1 || nseg > kLeanMaxSeg || in_f % 128) return cudaErrorInvalidValue;
-    void* fn = gemv_kernel_nf4_mma(c.stages);
+    const int nb = (m + 3) / 4 > 2 ? 4 : (m + 3) / 4;   // 8-column MMA blocks of 4 batch rows
+    void* fn = m == 1 ? gemv_kernel_nf4_mma(c.stages) : gemv_kernel_nf4_mma_mb(c.stages, nb);
     if (!fn) return cudaErrorInvalidValue;
     const int kw = c.warps_k, rg = c.row_groups;
     const int tr = c.tile_rows ? c.tile_rows : 16;
@@ -758,6 +788,13 @@ int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, in
     lp.rg = rg;
     lp.tr = tr;
     lp.x_vec = aligned(x, 16);
+    if (m > 1) {
+        Nf4MmaMbParams mp;
+        mp.base = lp;
+        mp.m = m;
+        const size_t smem = nf4_mma_mb_smem(in_f, m, kw, rg);
+        return launch_persistent(fn, &mp, tiles, 32 * kw * rg, smem, c.flags, st);
+    }
     const size_t smem = nf4_mma_smem(in_f, kw, rg);
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
 }
@@ -809,7 +846,7 @@ int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void
         return launch_lean_int4_segs(segs, nseg, x, in_f, m, c, st);
     if (m == 1 && fmt == kNf4 && c.engine == B4_ENGINE_FMA_LEAN)
         return launch_lean_nf4_segs(segs, nseg, x, in_f, m, c, st);
-    if (m == 1 && fmt == kNf4 && c.engine == B4_ENGINE_MMA_NF4)
+    if (m <= 16 && fmt == kNf4 && c.engine == B4_ENGINE_MMA_NF4)
         return launch_nf4_mma_segs(segs, nseg, x, in_f, m, c, st);
     // the other engines: one launch per segment with this config
     for (int s = 0; s < nseg; ++s) {

@@ -51,6 +51,30 @@ __device__ __forceinline__ uint32_t nf4_pair_offset(uint32_t w, uint32_t lane4)
     return __byte_perm(w, lane4, 0x5504u | (M << 4));
 }
 
+// The code book: row b = 32 copies of the high-part pair of (T[b & 15],
+// T[b >> 4]), then 32 copies of the low-part pair; one thread per byte value
+// computes its pairs and writes its row.  Called by all threads of a CTA;
+// the caller synchronises before reading.
+__device__ __forceinline__ void nf4_pair_table_fill(unsigned char* base)
+{
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+        const float t0 = c_nf4_table[b & 15], t1 = c_nf4_table[b >> 4];
+        const __half h0 = __float2half_rn(t0), h1 = __float2half_rn(t1);
+        const __half l0 = __float2half_rn(t0 - __half2float(h0)), l1 = __float2half_rn(t1 - __half2float(h1));
+        const __half2 hp = __halves2half2(h0, h1), lp = __halves2half2(l0, l1);
+        const uint32_t hw = *reinterpret_cast<const uint32_t*>(&hp), lw = *reinterpret_cast<const uint32_t*>(&lp);
+        uint4* row = reinterpret_cast<uint4*>(base + b * 256);
+        // the 16-byte chunk order rotates with b: the 8 threads of a store
+        // phase write 8 different chunks, hence 8 different bank quads
+#pragma unroll 4
+        for (int c2 = 0; c2 < 16; ++c2) {
+            const int k = (c2 + b) & 15;
+            const uint32_t v = k < 8 ? hw : lw;
+            row[k] = make_uint4(v, v, v, v);
+        }
+    }
+}
+
 template <int D>   // D >= 2
 __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Params p)
 {
@@ -133,25 +157,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
         setup(tile);
         prologue();
     }
-    // the code book: row b = 32 copies of the high-part pair of (T[b & 15],
-    // T[b >> 4]), then 32 copies of the low-part pair; one thread per byte
-    // value computes its pairs and writes its row
-    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
-        const float t0 = c_nf4_table[b & 15], t1 = c_nf4_table[b >> 4];
-        const __half h0 = __float2half_rn(t0), h1 = __float2half_rn(t1);
-        const __half l0 = __float2half_rn(t0 - __half2float(h0)), l1 = __float2half_rn(t1 - __half2float(h1));
-        const __half2 hp = __halves2half2(h0, h1), lp = __halves2half2(l0, l1);
-        const uint32_t hw = *reinterpret_cast<const uint32_t*>(&hp), lw = *reinterpret_cast<const uint32_t*>(&lp);
-        uint4* row = reinterpret_cast<uint4*>(base + b * 256);
-        // the 16-byte chunk order rotates with b: the 8 threads of a store
-        // phase write 8 different chunks, hence 8 different bank quads
-#pragma unroll 4
-        for (int c2 = 0; c2 < 16; ++c2) {
-            const int k = (c2 + b) & 15;
-            const uint32_t v = k < 8 ? hw : lw;
-            row[k] = make_uint4(v, v, v, v);
-        }
-    }
+    nf4_pair_table_fill(base);
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int w = threadIdx.x; w < words; w += blockDim.x) {

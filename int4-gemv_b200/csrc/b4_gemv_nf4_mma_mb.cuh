@@ -1,0 +1,271 @@
+// b4_gemv_nf4_mma_mb.cuh -- the NF4 b64 tensor-pipe GEMV for small batches
+// (m = 2..16).
+//
+// The batch-1 kernel (b4_gemv_nf4_mma.cuh) uses two of the MMA's eight N
+// columns: column 0 carries x at the positions of the step's first NF4 block,
+// column 1 at the second's.  Here each 8-column MMA block carries four batch
+// rows for both NF4 blocks: column c is NF4 block c >> 2 of batch row
+// 4*nb + (c & 3), and NB = ceil(m / 4) blocks cover the batch.  The code-book
+// lookups (PRMT + two 4-byte shared loads per byte) are done once per lane and
+// shared by every batch row; only the MMAs and the x fragments grow with m.
+//
+// B fragments: lane (g, q) supplies column g at the k-slots of lanes q, whose
+// codes lie in NF4 block q >> 1, so it carries x of batch row 4*nb + (g & 3)
+// when (g >> 2) == (q >> 1) and zero otherwise (16 of 32 lanes load x).
+// D: lane (g, q) holds columns 2q, 2q+1 = NF4 block q >> 1 of batch rows
+// 4*nb + 2(q & 1) and +1, for weight rows g and g+8; it scales them by that
+// block's absmax, and lanes q and q ^ 2 (the two blocks) are added with one
+// shuffle at the end.  x is staged per CTA for all m rows in natural order.
+#pragma once
+
+#include "b4_gemv_nf4_mma.cuh"
+
+namespace b4 {
+
+struct Nf4MmaMbParams {
+    LeanNf4Params base;   // seg[].y is [m][out_f_s]
+    int m;                // batch rows, 2..4*NB
+};
+
+template <int D, int NB>
+__global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4MmaMbParams pm)
+{
+    const LeanNf4Params& p = pm.base;
+    const int m = pm.m;
+    extern __shared__ __align__(16) uint4 lsm[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(lsm);
+    uint4* xs = reinterpret_cast<uint4*>(base + kNf4PairTableBytes);        // [m][in_f / 8] slots
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    const int warp = threadIdx.x >> 5;
+    const int ks = warp % p.kw;
+    const int grp = warp / p.kw;
+    const int words = p.in_f >> 3;
+    const int nblk = p.in_f >> 6;
+    const int nst = p.in_f >> 7;
+    constexpr int NR = 4 * NB;                                             // batch rows per pass
+    float* red = reinterpret_cast<float*>(xs + (size_t)m * words);        // rg*kw*16*NR
+    const int rows_per_tile = p.rg * p.tr;
+    const int n_tiles = p.n_tiles;
+    const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
+    const uint32_t lane4 = (uint32_t)lane * 4;
+
+    const uint4 *pa = nullptr, *pb = nullptr;
+    const float2 *sa_p = nullptr, *sb_p = nullptr;
+    uint4 bufa[D] = {}, bufb[D] = {};
+    float2 ama[D] = {}, amb[D] = {};
+    int r0 = 0, out_f = 0;
+    bool va = false, vb = false;
+    float* y = nullptr;
+    const int wstep = 4 * p.kw;
+    auto setup = [&](int tile) {
+        const uint32_t* qw = p.seg[0].qw;
+        const float* am = p.seg[0].absmax;
+        y = p.seg[0].y;
+        out_f = p.seg[0].out_f;
+        int t0 = 0;
+#pragma unroll
+        for (int s = 1; s < kLeanMaxSeg; ++s) {
+            if (s < p.nseg && tile >= p.seg[s - 1].tile_end) {
+                qw = p.seg[s].qw;
+                am = p.seg[s].absmax;
+                y = p.seg[s].y;
+                out_f = p.seg[s].out_f;
+                t0 = p.seg[s - 1].tile_end;
+            }
+        }
+        r0 = (tile - t0) * rows_per_tile + grp * p.tr;
+        va = g < p.tr && r0 + g < out_f;
+        vb = g + 8 < p.tr && r0 + g + 8 < out_f;
+        const int ra = min(r0 + g, out_f - 1);
+        const int rb = min(r0 + g + 8, out_f - 1);
+        pa = reinterpret_cast<const uint4*>(qw + (long long)ra * words) + ks * 4 + q;
+        pb = reinterpret_cast<const uint4*>(qw + (long long)rb * words) + ks * 4 + q;
+        sa_p = reinterpret_cast<const float2*>(am + (long long)ra * nblk) + ks;
+        sb_p = reinterpret_cast<const float2*>(am + (long long)rb * nblk) + ks;
+    };
+    auto fetch = [&](int slot) {
+        if (va) {
+            const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
+            bufa[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+            ama[slot] = __ldg(sa_p);
+        }
+        if (vb) {
+            const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
+            bufb[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+            amb[slot] = __ldg(sb_p);
+        }
+        pa += wstep;
+        pb += wstep;
+        sa_p += p.kw;
+        sb_p += p.kw;
+    };
+    auto prologue = [&]() {
+#pragma unroll
+        for (int d = 0; d < D - 1; ++d)
+            if (d < n_it) fetch(d);
+    };
+
+    int tile = blockIdx.x;
+    if (tile < n_tiles) {
+        setup(tile);
+        prologue();
+    }
+    nf4_pair_table_fill(base);
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int i = threadIdx.x; i < m * words; i += blockDim.x) {
+        const __half* src = p.x + (long long)i * 8;   // x is [m][in_f], contiguous
+        uint4 raw;
+        if (p.x_vec) {
+            raw = __ldg(reinterpret_cast<const uint4*>(src));
+        } else {
+            const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
+            raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
+            raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
+            raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
+            raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
+        }
+        xs[i] = raw;
+    }
+    __syncthreads();
+
+    // B: this lane carries batch row 4*nb + (g & 3) when (g >> 2) == (q >> 1)
+    const bool x_lane = (g >> 2) == (q >> 1);
+    const uint4* xrow[NB];
+    bool x_on[NB];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+        const int b = 4 * nb + (g & 3);
+        x_on[nb] = x_lane && b < m;
+        xrow[nb] = xs + (size_t)min(b, m - 1) * words + ks * 16 + q * 4;
+    }
+    const unsigned char* tb = base;
+    const bool hi_blk = q >= 2;   // the NF4 block of this lane's D columns
+
+    for (; tile < n_tiles; tile += gridDim.x) {
+        if (tile != (int)blockIdx.x) {
+            setup(tile);
+            prologue();
+        }
+        float acc[NB][4];
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) acc[nb][0] = acc[nb][1] = acc[nb][2] = acc[nb][3] = 0.0f;
+        int xoff = 0;
+
+        for (int it0 = 0; it0 < n_it; it0 += D) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                const int it = it0 + d;
+                if (it < n_it) {
+                    const int nxt = (d + D - 1) % D;
+                    if (it + D - 1 < n_it) fetch(nxt);
+                    const uint32_t wa[4] = {bufa[d].x, bufa[d].y, bufa[d].z, bufa[d].w};
+                    const uint32_t wb[4] = {bufb[d].x, bufb[d].y, bufb[d].z, bufb[d].w};
+                    // the A operands of the step's 8 MMAs: high and low parts
+                    uint32_t a_hi[8][4], a_lo[8][4];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
+                        uint32_t oa0, oa1, ob0, ob1;
+                        if (j & 1) {
+                            oa0 = nf4_pair_offset<2>(ua, lane4);
+                            oa1 = nf4_pair_offset<3>(ua, lane4);
+                            ob0 = nf4_pair_offset<2>(ub, lane4);
+                            ob1 = nf4_pair_offset<3>(ub, lane4);
+                        } else {
+                            oa0 = nf4_pair_offset<0>(ua, lane4);
+                            oa1 = nf4_pair_offset<1>(ua, lane4);
+                            ob0 = nf4_pair_offset<0>(ub, lane4);
+                            ob1 = nf4_pair_offset<1>(ub, lane4);
+                        }
+                        a_hi[j][0] = *reinterpret_cast<const uint32_t*>(tb + oa0);
+                        a_hi[j][1] = *reinterpret_cast<const uint32_t*>(tb + ob0);
+                        a_hi[j][2] = *reinterpret_cast<const uint32_t*>(tb + oa1);
+                        a_hi[j][3] = *reinterpret_cast<const uint32_t*>(tb + ob1);
+                        a_lo[j][0] = *reinterpret_cast<const uint32_t*>(tb + 128 + oa0);
+                        a_lo[j][1] = *reinterpret_cast<const uint32_t*>(tb + 128 + ob0);
+                        a_lo[j][2] = *reinterpret_cast<const uint32_t*>(tb + 128 + oa1);
+                        a_lo[j][3] = *reinterpret_cast<const uint32_t*>(tb + 128 + ob1);
+                    }
+                    const float am_a = hi_blk ? ama[d].y : ama[d].x;
+                    const float am_b = hi_blk ? amb[d].y : amb[d].x;
+#pragma unroll
+                    for (int nb = 0; nb < NB; ++nb) {
+                        uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                                       make_uint4(0, 0, 0, 0)};
+                        if (x_on[nb]) {
+                            const uint4* xp = xrow[nb] + xoff;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) xv[i] = xp[i];
+                        }
+                        float c[4][4];
+#pragma unroll
+                        for (int h2 = 0; h2 < 4; ++h2) c[h2][0] = c[h2][1] = c[h2][2] = c[h2][3] = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint4 xq = xv[j >> 1];
+                            const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
+                            const int ch = (j & 1) * 2;
+                            mma_16816_pure(c[ch], a_hi[j], b0, b1, c[ch]);
+                            mma_16816_pure(c[ch + 1], a_lo[j], b0, b1, c[ch + 1]);
+                        }
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float s = (c[0][e] + c[1][e]) + (c[2][e] + c[3][e]);
+                            acc[nb][e] = fmaf(s, e < 2 ? am_a : am_b, acc[nb][e]);
+                        }
+                    }
+                    xoff += 16 * p.kw;
+                }
+            }
+        }
+
+        // add the two NF4 blocks' sums (lanes q and q ^ 2); lanes q < 2 then hold
+        // rows g, g+8 of batch rows 4*nb + 2q, +1
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[nb][e] += __shfl_xor_sync(0xffffffffu, acc[nb][e], 2);
+        if (p.kw == 1) {
+            if (q < 2) {
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const int b = 4 * nb + 2 * q;
+                    if (va && b < m) y[(long long)b * out_f + r0 + g] = acc[nb][0];
+                    if (va && b + 1 < m) y[(long long)(b + 1) * out_f + r0 + g] = acc[nb][1];
+                    if (vb && b < m) y[(long long)b * out_f + r0 + g + 8] = acc[nb][2];
+                    if (vb && b + 1 < m) y[(long long)(b + 1) * out_f + r0 + g + 8] = acc[nb][3];
+                }
+            }
+        } else {
+            float* mine = red + (size_t)(grp * p.kw + ks) * 16 * NR;   // [16 rows][NR batch rows]
+            if (q < 2) {
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const int b = 4 * nb + 2 * q;
+                    mine[g * NR + b] = acc[nb][0];
+                    mine[g * NR + b + 1] = acc[nb][1];
+                    mine[(g + 8) * NR + b] = acc[nb][2];
+                    mine[(g + 8) * NR + b + 1] = acc[nb][3];
+                }
+            }
+            __syncthreads();
+            if (ks == 0) {
+                for (int e = lane; e < 16 * NR; e += 32) {
+                    const int row = e / NR, b = e - row * NR;
+                    if (row < p.tr && b < m && r0 + row < out_f) {
+                        float t = 0.0f;
+                        for (int k2 = 0; k2 < p.kw; ++k2) t += red[(size_t)(grp * p.kw + k2) * 16 * NR + e];
+                        y[(long long)b * out_f + r0 + row] = t;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+void* gemv_kernel_nf4_mma_mb(int depth, int nb);
+
+}  // namespace b4

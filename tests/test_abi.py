@@ -54,8 +54,8 @@ def test_default_config_is_valid(fmt, out_f, in_f, m):
     elif e == 5:         # lean INT4 (m <= 16: batch rows in the MMA's N), cp.async ring of `stage_groups` groups
         assert fmt == 0 and m <= 16 and c["rows_per_warp"] == 16
         assert (c["stages"], c["stage_groups"]) in LEAN_VARIANTS and (in_f // 128) % c["stage_groups"] == 0
-    elif e == 7:         # NF4 tensor pipe, batch 1
-        assert fmt == 1 and m == 1 and in_f % 128 == 0 and c["rows_per_warp"] == 16 and c["stages"] in (2, 3, 4)
+    elif e == 7:         # NF4 tensor pipe (m <= 16: batch rows in the MMA's N)
+        assert fmt == 1 and m <= 16 and in_f % 128 == 0 and c["rows_per_warp"] == 16 and c["stages"] in (2, 3, 4)
     elif e == 6:         # lean batch-1 NF4
         assert fmt == 1 and m == 1 and c["rows_per_warp"] in (4, 8) and c["nf4_lut"] in (0, 2)
     else:

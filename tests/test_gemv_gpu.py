@@ -434,3 +434,22 @@ def test_int4_small_batch_lean_kernel(cuda, oracle, m):
             y = b4gemv.gemv(0, qw, sc, Xd, config=cfg).cpu().numpy()
             assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
     assert b4gemv.default_config(0, 3584, 18944, m)["engine"] == 5
+
+
+@pytest.mark.parametrize("m", [2, 3, 5, 8, 9, 16])
+def test_nf4_small_batch_tensor_pipe_kernel(cuda, oracle, m):
+    """The NF4 tensor-pipe kernel with four batch rows per 8-column MMA block
+    (engine 7, m = 2..16): both pipeline depths, several warp splits and
+    weight-carrying rows per MMA block, against the double GEMV per batch row."""
+    rng = np.random.default_rng(400 + m)
+    for out_f, in_f in [(70, 1024), (37, 3584), (300, 512)]:
+        W, X = rand_problem(rng, out_f, in_f, m)
+        qw, sc = quantised(1, W, cuda)
+        ref = f64_ref(oracle, 1, qw, sc, X)
+        Xd = to_dev(X, cuda)
+        for st, (kw, rg), tr in itertools.product((2, 3), [(8, 1), (2, 2), (1, 4)], (0, 5)):
+            cfg = dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=7, stages=st,
+                       tile_rows=tr)
+            y = b4gemv.gemv(1, qw, sc, Xd, config=cfg).cpu().numpy()
+            assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
+    assert b4gemv.default_config(1, 3584, 18944, m)["engine"] == 7
