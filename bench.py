@@ -496,7 +496,7 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
     over the N ranks of this run (column-parallel q/k/v/gate/up, row-parallel
     o/down + NCCL all-reduce of fp32 y), replayed from a CUDA graph; us per
     layer is the max over ranks."""
-    from b4gemv.tp import NcclComm, TPDecodeLayer
+    from b4gemv.tp import NcclComm, P2pComm, TPDecodeLayer
     comm = NcclComm(d.rank, d.world) if d.world > 1 else None
     layer = TPDecodeLayer(fmt, d.rank, d.world, comm, dev, seed=5, fused=True, pdl=True)
     g = torch.Generator(device=dev)
@@ -504,31 +504,49 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
     x = torch.randn((1, 8192), generator=g, device=dev).half()
     c0, c1 = layer.ranges["o"]
     attn = torch.randn((1, c1 - c0), generator=g, device=dev).half()
-    layer.forward(x, attn)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    cs = torch.cuda.Stream()
-    cs.wait_stream(torch.cuda.current_stream())
-    reps = 20
-    with torch.cuda.graph(graph, stream=cs, capture_error_mode="relaxed"):
-        for _ in range(reps):
-            layer.forward(x, attn)
-    torch.cuda.current_stream().wait_stream(cs)
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    d.barrier()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
-    n = max(1, steps // reps)
-    a.record()
-    for _ in range(n):
-        graph.replay()
-    b.record()
-    torch.cuda.synchronize()
-    d.barrier()
-    us = a.elapsed_time(b) * 1e3 / (n * reps)
-    us_max = d.max(us, dev)
+
+    def time_layer():
+        layer.forward(x, attn)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(torch.cuda.current_stream())
+        reps = 20
+        with torch.cuda.graph(graph, stream=cs, capture_error_mode="relaxed"):
+            for _ in range(reps):
+                layer.forward(x, attn)
+        torch.cuda.current_stream().wait_stream(cs)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        d.barrier()
+        n = max(1, steps // reps)
+        a.record()
+        for _ in range(n):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        d.barrier()
+        del graph
+        torch.cuda.synchronize()
+        return d.max(a.elapsed_time(b) * 1e3 / (n * reps), dev)
+
+    us_max = time_layer()
+    # INT4 at N > 1: o/down with the all-reduce fused into the GEMV over peer
+    # memory (b4_tp_gemv_p2p) instead of the NCCL all-reduce
+    us_p2p = None
+    p2p_status = None
+    if d.world > 1 and fmt == 0:
+        p2p = P2pComm(d.rank, d.world, max_rows=8192)
+        layer.p2p = p2p
+        us_p2p = time_layer()
+        p2p_status = p2p.status()
+        layer.p2p = None
+        torch.cuda.synchronize()
+        d.barrier()
+        p2p.destroy()
     wb = layer.weight_bytes()
     # the layer's two fp32 all-reduces alone (32 KB each), eager NCCL through
     # torch.distributed on the same ranks: the collective share of the layer
@@ -547,8 +565,6 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
         b.record()
         torch.cuda.synchronize()
         ar_us = d.max(a.elapsed_time(b) * 1e3 / 200, dev)
-    del graph
-    torch.cuda.synchronize()
     if comm is not None:
         comm.destroy()
     del layer
@@ -559,7 +575,11 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
             "frac_per_rank": round(wb / us_max / 1e3 / peak, 4),
             "allreduces_per_layer": 2 if d.world > 1 else 0,
             "two_allreduces_us": round(ar_us, 2) if ar_us is not None else None,
-            "launches": "q/k/v and gate/up fused (b4_gemv_multi), GEMVs as programmatic dependents"}
+            "us_per_layer_p2p": round(us_p2p, 2) if us_p2p is not None else None,
+            "p2p_status": p2p_status,
+            "launches": "q/k/v and gate/up fused (b4_gemv_multi), GEMVs as programmatic dependents; "
+                        "us_per_layer: o/down + NCCL all-reduce; us_per_layer_p2p: o/down with the "
+                        "all-reduce fused into the GEMV over peer memory"}
 
 
 def run_ours(args, d):

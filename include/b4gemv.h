@@ -221,7 +221,7 @@ int b4_quantise_nf4_b64_device(const float* W, int out_f, int in_f, uint32_t* pa
  * Statuses >= B4_STATUS_NCCL_BASE are NCCL results (base + ncclResult_t). */
 #define B4_STATUS_NCCL_BASE 10000
 #define B4_STATUS_NCCL_MISSING 10900 /* no libnccl.so.2 in the process or on the path */
-#define B4_STATUS_TIMEOUT 10901      /* b4_nccl_wait deadline passed; communicator aborted */
+#define B4_STATUS_TIMEOUT 10901      /* b4_nccl_wait deadline passed (communicator aborted), or a b4_p2p wait gave up */
 
 typedef struct b4_nccl_id { char internal[128]; } b4_nccl_id; /* = ncclUniqueId */
 
@@ -245,6 +245,29 @@ int b4_shard_columns(int fmt, const uint32_t* qw, const void* scale, int in_f, i
  * ncclAllReduce(y, y, m*out_f, fp32, sum) on the same stream. */
 int b4_tp_gemv_allreduce(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard,
                          float* y, int in_shard, int out_f, int m, void* nccl_comm, b4_stream_t stream);
+
+/* Row-parallel GEMV with the all-reduce fused into its epilogue over NVLink
+ * peer memory, no collective library: each warp block of rows is stored into
+ * every rank's receive slots as soon as it is done, flagged, and summed in rank
+ * order once every rank's copy has arrived (bounded waits: a rank that never
+ * arrives makes the call time out, b4_p2p_status reports it, and the GPU stays
+ * usable).  y is bit-identical on every rank.  Set-up, once per rank and
+ * device: b4_p2p_create (one device allocation, max_rows >= the out_f of every
+ * call), b4_p2p_ipc_handle -> send the 64-byte handle to every peer ->
+ * b4_p2p_open_peer for each peer's handle.  Every rank must make the same
+ * sequence of calls (the call counter lives on the device, so calls captured
+ * in a CUDA graph may be replayed).  After a timeout the ranks' call counters
+ * disagree: destroy and re-create the b4_p2p on every rank.  flags:
+ * B4_FLAG_PDL (or 0).  INT4, batch 1.  No counterpart in the reference (it has
+ * no multi-GPU code). */
+typedef struct b4_p2p b4_p2p;
+int b4_p2p_create(int rank, int world, int max_rows, b4_p2p** out);
+int b4_p2p_ipc_handle(const b4_p2p* p2p, void* handle64);
+int b4_p2p_open_peer(b4_p2p* p2p, int peer, const void* handle64);
+int b4_p2p_status(b4_p2p* p2p, int clear);   /* B4_STATUS_TIMEOUT if a wait gave up */
+int b4_p2p_destroy(b4_p2p* p2p);
+int b4_tp_gemv_p2p(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard, float* y,
+                   int in_shard, int out_f, b4_p2p* p2p, int flags, b4_stream_t stream);
 
 /* Elementwise glue of the decode layer: out = fp16(silu(gate) * up) (the MLP
  * activation between gate/up and down) and out = fp16(in). */

@@ -97,6 +97,12 @@ SIGNATURES = {
     "b4_nccl_wait": (_I, [_P, _P, _I]),
     "b4_shard_columns": (_I, [_I, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "b4_tp_gemv_allreduce": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "b4_p2p_create": (_I, [_I, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
+    "b4_p2p_ipc_handle": (_I, [_P, _P]),
+    "b4_p2p_open_peer": (_I, [_P, _I, _P]),
+    "b4_p2p_status": (_I, [_P, _I]),
+    "b4_p2p_destroy": (_I, [_P]),
+    "b4_tp_gemv_p2p": (_I, [_I, _P, _P, _P, _P, _I, _I, _P, _I, _P]),
     "b4_swiglu_f16": (_I, [_P, _P, _P, ctypes.c_longlong, _P]),
     "b4_cast_f16": (_I, [_P, _P, ctypes.c_longlong, _P]),
     "b4_nccl_error_string": (ctypes.c_char_p, [_I]),

@@ -76,6 +76,35 @@ class NcclComm:
             self.ptr = ctypes.c_void_p()
 
 
+class P2pComm:
+    """The peer-memory all-reduce of b4_tp_gemv_p2p: one device allocation per
+    rank, its CUDA IPC handle sent to every peer over torch.distributed (any
+    backend), every peer's allocation mapped here."""
+
+    def __init__(self, rank: int, world: int, max_rows: int, group=None):
+        import torch.distributed as dist
+        lib = load()
+        self.ptr = ctypes.c_void_p()
+        check("b4_p2p_create", lib.b4_p2p_create(rank, world, max_rows, ctypes.byref(self.ptr)))
+        h = ctypes.create_string_buffer(64)
+        check("b4_p2p_ipc_handle", lib.b4_p2p_ipc_handle(self.ptr, h))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(h.raw), group=group)
+        for r in range(world):
+            if r != rank:
+                check("b4_p2p_open_peer", lib.b4_p2p_open_peer(self.ptr, r, ctypes.create_string_buffer(handles[r], 64)))
+        self.rank, self.world, self.max_rows = rank, world, max_rows
+
+    def status(self, clear: bool = False) -> int:
+        """0, or B4_STATUS_TIMEOUT if a wait in a kernel gave up (a peer did not arrive)."""
+        return load().b4_p2p_status(self.ptr, 1 if clear else 0)
+
+    def destroy(self):
+        if self.ptr:
+            load().b4_p2p_destroy(self.ptr)
+            self.ptr = ctypes.c_void_p()
+
+
 def _p(t):
     return ctypes.c_void_p(t.data_ptr())
 
@@ -118,10 +147,11 @@ class TPDecodeLayer:
     NAMES = ("q", "k", "v", "o", "gate", "up", "down")
 
     def __init__(self, fmt, rank, tp, comm, device, hidden=8192, inter=28672, q_out=8192, kv_out=1024, seed=0,
-                 fused=True, pdl=False):
+                 fused=True, pdl=False, p2p=None):
         import torch
         self.fmt, self.rank, self.tp, self.comm, self.device = fmt, rank, tp, comm, device
         self.fused, self.pdl = fused, pdl
+        self.p2p = p2p   # a P2pComm: row-parallel INT4 GEMVs all-reduce over peer memory instead of NCCL
         self.hidden, self.inter, self.q_out, self.kv_out = hidden, inter, q_out, kv_out
         unit = fmt_unit(fmt)
         # (name, out_f, in_f, kind)
@@ -192,6 +222,11 @@ class TPDecodeLayer:
         qw, sc = self.w[name]
         if self.tp == 1:
             return self._gemv(name, x, y, stream)
+        if self.p2p is not None and self.fmt == FMT_INT4_G128:
+            check(f"tp p2p {name}", load().b4_tp_gemv_p2p(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
+                                                          qw.shape[0], self.p2p.ptr,
+                                                          FLAG_PDL if self.pdl else 0, stream))
+            return
         check(f"tp {name}", load().b4_tp_gemv_allreduce(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
                                                          qw.shape[0], 1, self.comm.ptr, stream))
 

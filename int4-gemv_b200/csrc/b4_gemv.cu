@@ -594,7 +594,7 @@ namespace {
 
 // One launch of a streaming kernel whose parameter block is `params`.
 cudaError_t launch_persistent(void* fn, void* params, long long tiles, int threads, size_t smem, int flags,
-                              cudaStream_t st)
+                              cudaStream_t st, bool resident_only = false)
 {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -608,7 +608,14 @@ cudaError_t launch_persistent(void* fn, void* params, long long tiles, int threa
         if (e != cudaSuccess) return e;
     }
     const int per_sm = std::max<int>(1, (int)((228 * 1024) / (smem + 1024)));
-    const long long grid = std::min<long long>(tiles, (long long)sm_count_cached(dev) * per_sm);
+    long long grid = std::min<long long>(tiles, (long long)sm_count_cached(dev) * per_sm);
+    if (resident_only) {
+        // every CTA resident at once (registers and threads counted too)
+        int occ = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem);
+        if (e != cudaSuccess) return e;
+        grid = std::min<long long>(grid, (long long)sm_count_cached(dev) * occ);
+    }
     if (grid < 1) return cudaErrorInvalidValue;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3((unsigned)grid);
@@ -800,6 +807,47 @@ int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, in
 }
 
 }  // namespace
+
+// A row-parallel INT4 shard at batch 1 with the peer-memory all-reduce fused
+// into the epilogue (b4_p2p.cuh): the lean kernel's P2P variant.
+int launch_lean_int4_p2p(const GemvProblem& p, const b4_gemv_config& c, const P2pArgs& a, cudaStream_t st)
+{
+    if (p.fmt != kInt4 || p.m != 1 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c))
+        return cudaErrorInvalidValue;
+    if (c.engine != B4_ENGINE_MMA_LEAN && c.engine != B4_ENGINE_MMA_LEAN_ASYNC) return cudaErrorInvalidValue;
+    const int kw = c.warps_k, rg = c.row_groups;
+    const int async_ring = c.engine == B4_ENGINE_MMA_LEAN_ASYNC;
+    const int groups = async_ring ? c.stage_groups : 1;
+    if (groups != 1 && groups != 2 && groups != 4) return cudaErrorInvalidValue;
+    if ((p.in_f / kGroup) % groups) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 16) || !aligned(p.scale, 2u * groups)) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_int4_lean_p2p(c.stages, groups, async_ring);
+    if (!fn) return cudaErrorInvalidValue;
+    const int tr = c.tile_rows ? c.tile_rows : 16;
+    if (tr < 1 || tr > 16) return cudaErrorInvalidValue;
+    const long long rows_per_cta = (long long)rg * tr;
+    const long long tiles = (p.out_f + rows_per_cta - 1) / rows_per_cta;
+    if (p.out_f > a.max_rows) return cudaErrorInvalidValue;
+    LeanParams lp = {};
+    lp.seg[0].qw = p.qw;
+    lp.seg[0].scale = static_cast<const __half*>(p.scale);
+    lp.seg[0].y = p.y;
+    lp.seg[0].out_f = p.out_f;
+    lp.seg[0].tile_end = (int)tiles;
+    lp.nseg = 1;
+    lp.n_tiles = (int)tiles;
+    lp.x = static_cast<const __half*>(p.x);
+    lp.in_f = p.in_f;
+    lp.kw = kw;
+    lp.rg = rg;
+    lp.tr = tr;
+    lp.x_vec = aligned(p.x, 16);
+    lp.p2p = a;
+    const size_t smem = lean_int4_smem(p.in_f, kw, rg, c.stages, groups, async_ring);
+    // a CTA waits only for the CTA of the same index on every peer, so with
+    // every CTA resident no wait can depend on a CTA that is not running
+    return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st, true);
+}
 
 int launch_gemv_nf4_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {

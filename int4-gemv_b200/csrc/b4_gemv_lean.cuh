@@ -46,6 +46,7 @@
 #pragma once
 
 #include "b4_gemv_mma.cuh"
+#include "b4_p2p.cuh"
 
 namespace b4 {
 
@@ -70,6 +71,7 @@ struct LeanParams {
     int kw, rg;
     int tr;      // rows of each warp's 16-row block that carry weights (1..16)
     int x_vec;
+    P2pArgs p2p; // P2P kernels: the all-reduce of y over peer memory (b4_p2p.cuh)
 };
 
 // scales of one stage of G groups of one row
@@ -135,7 +137,11 @@ __device__ __forceinline__ void lean_group(const uint4 wav, const uint4 wbv, con
     pb = c0[2] + c1[2];
 }
 
-template <int D, int G, int ASYNC>   // D >= 2; G in {1, 2, 4}; ASYNC = 0 needs G = 1
+// P2P = 1: a row-parallel shard of a tensor-parallel GEMV; y is all-reduced
+// over the ranks through peer memory in the epilogue (b4_p2p.cuh), one warp
+// block at a time, so the transfer of early blocks overlaps the math of later
+// ones.  One segment only.
+template <int D, int G, int ASYNC, int P2P = 0>   // D >= 2; G in {1, 2, 4}; ASYNC = 0 needs G = 1
 __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p)
 {
     static_assert(ASYNC || G == 1, "register pipeline holds one group per stage");
@@ -249,6 +255,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
         xs[w] = int4_pair_order(raw);
     }
     __syncthreads();
+    const uint32_t epoch = P2P ? p2p_epoch(p.p2p) : 0u;
 
     for (; tile < n_tiles; tile += gridDim.x) {
         if (tile != (int)blockIdx.x) {
@@ -296,7 +303,30 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
         if constexpr (ASYNC) cp_async_wait<0>();   // nothing of this tile left in flight
 
         // rows r0+g and r0+g+8; lanes q = 0..3 hold the same values
-        if (p.kw == 1) {
+        if constexpr (P2P) {
+            // push this block's partial rows to every rank; summed after the last block
+            const int nrows = max(0, min(p.tr, out_f - r0));
+            if (p.kw == 1) {
+                // lane i < tr: row r0 + i
+                const float va_i = __shfl_sync(0xffffffffu, acc_a, (lane & 7) * 4);
+                const float vb_i = __shfl_sync(0xffffffffu, acc_b, (lane & 7) * 4);
+                p2p_push(p.p2p, epoch, r0, nrows, lane < 8 ? va_i : vb_i);
+            } else {
+                float* mine = red + (grp * p.kw + ks) * 16;
+                if (q == 0) {
+                    mine[g] = acc_a;
+                    mine[g + 8] = acc_b;
+                }
+                __syncthreads();
+                if (ks == 0) {
+                    float t = 0.0f;
+                    if (lane < 16)
+                        for (int k2 = 0; k2 < p.kw; ++k2) t += red[(grp * p.kw + k2) * 16 + lane];
+                    p2p_push(p.p2p, epoch, r0, nrows, t);
+                }
+                __syncthreads();
+            }
+        } else if (p.kw == 1) {
             if (q == 0) {
                 if (va) y[r0 + g] = acc_a;
                 if (vb) y[r0 + g + 8] = acc_b;
@@ -316,8 +346,20 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
             __syncthreads();
         }
     }
+    if constexpr (P2P) {
+        // every rank's copy of this warp's blocks, summed in rank order (one segment)
+        if (ks == 0) {
+            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+                const int rr = t * rows_per_tile + grp * p.tr;
+                p2p_reduce(p.p2p, epoch, rr, max(0, min(p.tr, p.seg[0].out_f - rr)), p.seg[0].y);
+            }
+        }
+        __syncthreads();   // every warp of the CTA has read the epoch
+        if (threadIdx.x == 0) p2p_finish(p.p2p, epoch);
+    }
 }
 
 void* gemv_kernel_int4_lean(int depth, int groups, int async_ring);
+void* gemv_kernel_int4_lean_p2p(int depth, int groups, int async_ring);
 
 }  // namespace b4

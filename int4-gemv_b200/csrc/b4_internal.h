@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/b4gemv.h"
+#include "b4_p2p.cuh"
 
 namespace b4 {
 
@@ -28,6 +29,10 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg);
 
 // Validates cfg against p (and the pointer alignment it needs) and launches.
 int launch_gemv(const GemvProblem& p, const b4_gemv_config& cfg, cudaStream_t st);
+
+// A row-parallel INT4 shard at batch 1 whose epilogue all-reduces y over the
+// ranks' peer memory (b4_p2p.cuh); cfg must be a lean INT4 config.
+int launch_lean_int4_p2p(const GemvProblem& p, const b4_gemv_config& cfg, const P2pArgs& a, cudaStream_t st);
 
 // Several weight matrices over one x (b4_gemv_multi): the dispatch rule over
 // their total rows, and the launch (one kernel for the lean engines at m = 1).

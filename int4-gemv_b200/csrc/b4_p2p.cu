@@ -1,0 +1,143 @@
+// b4_p2p.cu -- host side of the peer-memory all-reduce fused into the
+// row-parallel GEMV (device side: b4_p2p.cuh, b4_gemv_lean.cuh P2P = 1).
+//
+// One cudaMalloc per rank holds the receive slots and the call counter; its CUDA IPC handle travels to the peers over whatever channel
+// the caller has (the Python layer uses torch.distributed), and each peer
+// maps it with cudaIpcOpenMemHandle.  Kernels only ever store to peers and
+// read their own memory; every wait in them is bounded.
+#include <cstring>
+#include <new>
+
+#include "b4_internal.h"
+
+using namespace b4;
+
+struct b4_p2p {
+    int device = 0;
+    int rank = 0, world = 0;
+    int max_rows = 0;
+    char* base = nullptr;                 // this rank's allocation
+    char* peers[kP2pMaxRanks] = {};      // every rank's allocation as mapped here (own at [rank])
+    size_t recv_bytes = 0, bytes = 0;
+};
+
+namespace {
+
+P2pArgs args_of(const b4_p2p* h)
+{
+    P2pArgs a = {};
+    for (int r = 0; r < h->world; ++r) a.recv[r] = reinterpret_cast<unsigned long long*>(h->peers[r]);
+    uint32_t* tail = reinterpret_cast<uint32_t*>(h->base + h->recv_bytes);
+    a.epoch = tail;
+    a.done = tail + 1;
+    a.error = tail + 2;
+    a.rank = h->rank;
+    a.world = h->world;
+    a.max_rows = h->max_rows;
+    return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b4_p2p_create(int rank, int world, int max_rows, b4_p2p** out)
+{
+    if (!out || world < 1 || world > kP2pMaxRanks || rank < 0 || rank >= world || max_rows < 1)
+        return cudaErrorInvalidValue;
+    b4_p2p* h = new (std::nothrow) b4_p2p;
+    if (!h) return cudaErrorMemoryAllocation;
+    cudaError_t e = cudaGetDevice(&h->device);
+    if (e != cudaSuccess) {
+        delete h;
+        return e;
+    }
+    h->rank = rank;
+    h->world = world;
+    h->max_rows = max_rows;
+    h->recv_bytes = (size_t)2 * world * max_rows * sizeof(unsigned long long);
+    h->bytes = h->recv_bytes + 256;
+    e = cudaMalloc(&h->base, h->bytes);
+    if (e == cudaSuccess) e = cudaMemset(h->base, 0, h->bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        if (h->base) cudaFree(h->base);
+        delete h;
+        return e;
+    }
+    h->peers[rank] = h->base;
+    *out = h;
+    return cudaSuccess;
+}
+
+int b4_p2p_ipc_handle(const b4_p2p* h, void* handle64)
+{
+    if (!h || !handle64) return cudaErrorInvalidValue;
+    cudaIpcMemHandle_t ipc;
+    const cudaError_t e = cudaIpcGetMemHandle(&ipc, h->base);
+    if (e != cudaSuccess) return e;
+    static_assert(sizeof(ipc) == 64, "CUDA IPC handles are 64 bytes");
+    std::memcpy(handle64, &ipc, sizeof(ipc));
+    return cudaSuccess;
+}
+
+int b4_p2p_open_peer(b4_p2p* h, int peer, const void* handle64)
+{
+    if (!h || !handle64 || peer < 0 || peer >= h->world || peer == h->rank || h->peers[peer])
+        return cudaErrorInvalidValue;
+    cudaIpcMemHandle_t ipc;
+    std::memcpy(&ipc, handle64, sizeof(ipc));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, ipc, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return e;
+    h->peers[peer] = static_cast<char*>(p);
+    return cudaSuccess;
+}
+
+int b4_p2p_status(b4_p2p* h, int clear)
+{
+    if (!h) return cudaErrorInvalidValue;
+    uint32_t* err = reinterpret_cast<uint32_t*>(h->base + h->recv_bytes) + 2;
+    uint32_t v = 0;
+    cudaError_t e = cudaMemcpy(&v, err, sizeof(v), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return e;
+    if (clear && v) {
+        e = cudaMemset(err, 0, sizeof(v));
+        if (e != cudaSuccess) return e;
+    }
+    return v ? B4_STATUS_TIMEOUT : cudaSuccess;
+}
+
+int b4_p2p_destroy(b4_p2p* h)
+{
+    if (!h) return cudaErrorInvalidValue;
+    cudaError_t first = cudaSuccess;
+    for (int r = 0; r < h->world; ++r) {
+        if (r != h->rank && h->peers[r]) {
+            const cudaError_t e = cudaIpcCloseMemHandle(h->peers[r]);
+            if (first == cudaSuccess) first = e;
+        }
+    }
+    const cudaError_t e = cudaFree(h->base);
+    if (first == cudaSuccess) first = e;
+    delete h;
+    return first;
+}
+
+int b4_tp_gemv_p2p(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard, float* y,
+                   int in_shard, int out_f, b4_p2p* h, int flags, b4_stream_t stream)
+{
+    if (!h) return cudaErrorInvalidValue;
+    for (int r = 0; r < h->world; ++r)
+        if (!h->peers[r]) return cudaErrorInvalidValue;   // every peer must be mapped first
+    const GemvProblem p{fmt, qw_shard, scale_shard, x_shard, y, in_shard, out_f, 1, in_shard, out_f};
+    int e = check_problem(p);
+    if (e != cudaSuccess) return e;
+    if (fmt != B4_FMT_INT4_G128 || (flags & ~B4_FLAG_PDL)) return cudaErrorInvalidValue;
+    b4_gemv_config c;
+    default_config(p, &c);
+    c.flags = flags;
+    return launch_lean_int4_p2p(p, c, args_of(h), reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,132 @@
+// b4_p2p.cuh -- the all-reduce of a row-parallel GEMV over NVLink peer
+// memory, fused into the GEMV's epilogue.
+//
+// Each rank holds one device allocation (exported through CUDA IPC and mapped
+// by every peer):
+//   recv  uint64 [2][world][max_rows]   (epoch << 32) | fp32 bits of a partial row
+//   epoch uint32, done uint32, error uint32
+// indexed first by the call's parity (epoch & 1), so a rank may start call
+// e+1 while a peer still reads call e's slots (call e+2 can only start after
+// every peer has finished call e: it needs their call e+1 rows, which they
+// store after their call e kernel has completed).
+//
+// The value and the call's epoch travel in ONE naturally aligned 64-bit store,
+// which is single-copy atomic: a reader that sees the epoch also sees the
+// value, with no flag, no fence and no second round trip.  Stale slots hold
+// an older epoch (e - 2 or earlier), so they never match.
+//
+// A warp that has finished a block of rows stores them into slot
+// [parity][rank] of every rank's recv (peer stores over NVLink, its own by a
+// local store) and goes on to its next block; only after its last block does
+// it read back, for each of its blocks, every rank's copy from its own memory
+// (bounded polls: after kP2pMaxSpins polls, or as soon as another wait of the
+// call has given up, it records kP2pErrTimeout in the error word and moves
+// on), sums the ranks in rank order and stores y.  Every rank adds the same
+// numbers in the same order: y is bit-identical on all ranks.  The epoch lives
+// in device memory: every CTA reads it after griddepcontrol.wait (the
+// previous call has completed) and the last CTA to finish advances it, so a
+// call captured in a CUDA graph stays correct when the graph is replayed.
+#pragma once
+
+#include <cstdint>
+
+namespace b4 {
+
+constexpr int kP2pMaxRanks = 8;
+constexpr uint32_t kP2pErrTimeout = 1u;
+constexpr long long kP2pMaxSpins = 1ll << 22;   // x ~0.2-1 us per poll: one to a few seconds
+
+struct P2pArgs {
+    unsigned long long* recv[kP2pMaxRanks];   // every rank's slots (this rank's own at [rank])
+    uint32_t* epoch;                          // this rank's call counter
+    uint32_t* done;                           // CTAs of this call that have finished
+    uint32_t* error;                          // this rank's error word
+    int rank, world;
+    int max_rows;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v)
+{
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// The epoch of this call (read once per CTA, after griddepcontrol.wait).
+__device__ __forceinline__ uint32_t p2p_epoch(const P2pArgs& a)
+{
+    return ld_acquire_sys(a.epoch) + 1u;
+}
+
+// Lane i < nrows holds row r0 + i of this rank's partial y in v: store it into
+// slot [parity][rank][r0 + i] of every rank.  Called by a whole warp.
+__device__ __forceinline__ void p2p_push(const P2pArgs& a, uint32_t epoch, int r0, int nrows, float v)
+{
+    const int lane = threadIdx.x & 31;
+    if (lane < nrows) {
+        const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+        const size_t off = ((size_t)(epoch & 1u) * a.world + a.rank) * a.max_rows + r0 + lane;
+        for (int k = 1; k <= a.world; ++k) {
+            const int r = (a.rank + k) % a.world;   // peers first, this rank's own slot last
+            st_relaxed_sys_u64(a.recv[r] + off, w);
+        }
+    }
+}
+
+// Lane i < nrows waits for row r0 + i from every rank in this rank's own slots
+// and stores their sum, in rank order, into y[r0 + i].  Called by a whole warp.
+__device__ __forceinline__ void p2p_reduce(const P2pArgs& a, uint32_t epoch, int r0, int nrows, float* y)
+{
+    const int lane = threadIdx.x & 31;
+    if (lane < nrows) {
+        const unsigned long long* mine = a.recv[a.rank] + (size_t)(epoch & 1u) * a.world * a.max_rows + r0 + lane;
+        float s = 0.0f;
+        for (int r = 0; r < a.world; ++r) {
+            const unsigned long long* slot = mine + (size_t)r * a.max_rows;
+            unsigned long long w = ld_relaxed_sys_u64(slot);
+            long long n = 0;
+            while ((uint32_t)(w >> 32) != epoch) {
+                // give up after kP2pMaxSpins polls, or at once when another wait
+                // of this call already gave up (a missing peer costs one timeout)
+                if (++n >= kP2pMaxSpins || ((n & 63) == 0 && *(volatile const uint32_t*)a.error)) {
+                    atomicOr(a.error, kP2pErrTimeout);
+                    break;
+                }
+                __nanosleep(64);
+                w = ld_relaxed_sys_u64(slot);
+            }
+            s += __uint_as_float((uint32_t)w);
+        }
+        y[r0 + lane] = s;
+    }
+}
+
+// The last CTA of the call to finish advances the epoch (called by thread 0 of
+// every CTA after its last block).
+__device__ __forceinline__ void p2p_finish(const P2pArgs& a, uint32_t epoch)
+{
+    __threadfence();
+    if (atomicAdd(a.done, 1u) == gridDim.x - 1) {
+        *a.done = 0;
+        st_release_sys(a.epoch, epoch);
+    }
+}
+
+}  // namespace b4

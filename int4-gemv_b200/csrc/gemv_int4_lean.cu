@@ -27,3 +27,16 @@ void* b4::gemv_kernel_int4_lean(int depth, int groups, int async_ring)
     }
     return nullptr;
 }
+
+// Row-parallel tensor-parallel shards with the peer-memory all-reduce in the
+// epilogue (the batch-1 dispatch's variants).
+void* b4::gemv_kernel_int4_lean_p2p(int depth, int groups, int async_ring)
+{
+    if (!async_ring) return groups == 1 && depth == 4 ? (void*)&b4::b4_gemv_lean_kernel<4, 1, 0, 1> : nullptr;
+    switch (groups * 100 + depth) {
+        case 104: return (void*)&b4::b4_gemv_lean_kernel<4, 1, 1, 1>;
+        case 203: return (void*)&b4::b4_gemv_lean_kernel<3, 2, 1, 1>;
+        case 402: return (void*)&b4::b4_gemv_lean_kernel<2, 4, 1, 1>;
+    }
+    return nullptr;
+}

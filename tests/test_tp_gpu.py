@@ -221,3 +221,143 @@ def test_tp1_layer_fused_and_pdl_match_separate_launches(cuda, fmt):
         assert rel_err(y.cpu().numpy(), y_ref.cpu().numpy().astype(np.float64)) < 1e-5, (fused, pdl)
         for n, b in bufs.items():
             assert rel_err(lay.buf[n].cpu().numpy(), b.cpu().numpy().astype(np.float64)) < 1e-5, (n, fused, pdl)
+
+
+def _p2p_worker(rank, world, port, mode, results):
+    import sys
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.join(os.path.dirname(here), "int4-gemv_b200"))
+    import ctypes
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import b4gemv
+    from b4gemv.tp import NcclComm, P2pComm, TPDecodeLayer, col_range, quantise_full, shard_columns
+    from oracle_py import Oracle, rel_err
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    out_f, in_f = 1000, 2048
+    p2p = P2pComm(rank, world, max_rows=4096)
+    lib = b4gemv.load()
+    out = {}
+    try:
+        qw, sc = quantise_full(0, out_f, in_f, 7, dev)
+        c0, c1 = col_range(in_f, 128, world, rank)
+        qs, ss = shard_columns(0, qw, sc, c0, c1)
+        g = torch.Generator(device=dev)
+        g.manual_seed(3)
+        x = torch.randn((1, in_f), generator=g, device=dev).half()
+        xs = x[:, c0:c1].contiguous()
+        y = torch.zeros((1, out_f), device=dev)
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        flags = 0
+        if mode == "timeout":
+            if rank == 0:   # the peer never makes this call: every wait must give up by itself
+                assert lib.b4_tp_gemv_p2p(0, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, st) == 0
+                torch.cuda.synchronize()
+                out["status"] = p2p.status(clear=True)
+                y2 = b4gemv.gemv(0, qw, sc, x)      # the GPU is still usable
+                torch.cuda.synchronize()
+                out["after"] = bool(torch.isfinite(y2).all().item())
+            dist.barrier()
+            results[rank] = out
+            return
+        ys = []
+        for i in range(4):   # successive calls: the call counter advances on the device
+            flags = b4gemv.FLAG_PDL if i >= 2 else 0
+            y.fill_(float("nan"))
+            assert lib.b4_tp_gemv_p2p(0, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, st) == 0
+            torch.cuda.synchronize()
+            ys.append(y.clone())
+        # captured once, replayed: still a fresh epoch every replay
+        graph = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(graph, stream=cs, capture_error_mode="relaxed"):
+            s2 = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            lib.b4_tp_gemv_p2p(0, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, s2)
+        torch.cuda.current_stream().wait_stream(cs)
+        for _ in range(3):
+            y.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize()
+            ys.append(y.clone())
+        del graph
+        out["status"] = p2p.status()
+        out["same_calls"] = all(torch.equal(ys[0], t) for t in ys)
+        ref = Oracle().gemv_f64(False, qw.cpu().numpy().view(np.uint32), sc.cpu().numpy().view(np.uint16),
+                                x.cpu().numpy())
+        out["err"] = rel_err(ys[0].cpu().numpy(), ref)
+        comm = NcclComm(rank, world)
+        yn = torch.zeros((1, out_f), device=dev)
+        assert lib.b4_tp_gemv_allreduce(0, P(qs), P(ss), P(xs), P(yn), c1 - c0, out_f, 1, comm.ptr, st) == 0
+        torch.cuda.synchronize()
+        comm.destroy()
+        out["vs_nccl"] = rel_err(ys[0].cpu().numpy(), yn.cpu().numpy().astype(np.float64))
+        gathered = [None] * world
+        dist.all_gather_object(gathered, ys[0].cpu().numpy().tobytes())
+        out["same_ranks"] = all(b == gathered[0] for b in gathered)
+        # the decode layer with both row-parallel projections on the P2P path
+        # against the same layer on NCCL (world 2: a + b either way, bit for bit)
+        comm = NcclComm(rank, world)
+        lp = TPDecodeLayer(0, rank, world, comm, dev, seed=3, pdl=True, p2p=p2p, **SMALL)
+        ln = TPDecodeLayer(0, rank, world, comm, dev, seed=3, pdl=True, **SMALL)
+        xl = torch.randn((1, SMALL["hidden"]), generator=g, device=dev).half()
+        a0, a1 = lp.ranges["o"]
+        attn = torch.randn((1, SMALL["q_out"]), generator=g, device=dev).half()[:, a0:a1].contiguous()
+        y_p = lp.forward(xl, attn).clone()
+        y_n = ln.forward(xl, attn).clone()
+        torch.cuda.synchronize()
+        comm.destroy()
+        out["layer_equal"] = torch.equal(y_p, y_n)
+        out["layer_status"] = p2p.status()
+        results[rank] = out
+    finally:
+        dist.barrier()
+        p2p.destroy()
+        dist.destroy_process_group()
+
+
+def _run_p2p(world, mode):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    res = ctx.Manager().dict()
+    port = _port()
+    ps = [ctx.Process(target=_p2p_worker, args=(r, world, port, mode, res)) for r in range(world)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=300)
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+    return dict(res)
+
+
+@pytest.mark.skipif(_n_gpus() < 2, reason="needs 2 GPUs")
+def test_p2p_rowparallel_gemv_matches_nccl_and_is_identical_on_every_rank():
+    res = _run_p2p(2, "parity")
+    for r in (0, 1):
+        assert res[r]["status"] == 0, res
+        assert res[r]["same_calls"], res       # 4 calls + 3 graph replays, bit for bit
+        assert res[r]["err"] < 1e-3, res       # against the double GEMV of the full matrix
+        assert res[r]["vs_nccl"] < 1e-5, res   # against the NCCL all-reduce of the same partials
+        assert res[r]["same_ranks"], res       # every rank sums in rank order
+        assert res[r]["layer_equal"], res      # TPDecodeLayer(p2p=...) against TPDecodeLayer on NCCL
+        assert res[r]["layer_status"] == 0, res
+
+
+@pytest.mark.skipif(_n_gpus() < 2, reason="needs 2 GPUs")
+def test_p2p_wait_for_a_peer_that_never_arrives_times_out_and_the_gpu_stays_usable():
+    res = _run_p2p(2, "timeout")
+    assert res[0]["status"] == 10901, res      # B4_STATUS_TIMEOUT
+    assert res[0]["after"], res
