@@ -184,7 +184,7 @@ int b4_cast_f16(const float* in, void* out, long long n, b4_stream_t stream)
 const char* b4_nccl_error_string(int status)
 {
     if (status == B4_STATUS_NCCL_MISSING) return "libnccl.so.2 not found";
-    if (status == B4_STATUS_TIMEOUT) return "timed out; communicator aborted";
+    if (status == B4_STATUS_TIMEOUT) return "timed out (b4_nccl_wait: communicator aborted; b4_p2p: a peer did not arrive)";
     const NcclApi& n = nccl();
     if (status > B4_STATUS_NCCL_BASE && status < B4_STATUS_NCCL_BASE + 100 && n.ok)
         return n.GetErrorString((ncclResult_t)(status - B4_STATUS_NCCL_BASE));
