@@ -247,19 +247,21 @@ int b4_tp_gemv_allreduce(int fmt, const uint32_t* qw_shard, const void* scale_sh
                          float* y, int in_shard, int out_f, int m, void* nccl_comm, b4_stream_t stream);
 
 /* Row-parallel GEMV with the all-reduce fused into its epilogue over NVLink
- * peer memory, no collective library: each warp block of rows is stored into
- * every rank's receive slots as soon as it is done, flagged, and summed in rank
- * order once every rank's copy has arrived (bounded waits: a rank that never
- * arrives makes the call time out, b4_p2p_status reports it, and the GPU stays
- * usable).  y is bit-identical on every rank.  Set-up, once per rank and
- * device: b4_p2p_create (one device allocation, max_rows >= the out_f of every
- * call), b4_p2p_ipc_handle -> send the 64-byte handle to every peer ->
- * b4_p2p_open_peer for each peer's handle.  Every rank must make the same
- * sequence of calls (the call counter lives on the device, so calls captured
- * in a CUDA graph may be replayed).  After a timeout the ranks' call counters
- * disagree: destroy and re-create the b4_p2p on every rank.  flags:
- * B4_FLAG_PDL (or 0).  INT4, batch 1.  No counterpart in the reference (it has
- * no multi-GPU code). */
+ * peer memory, no collective library: each warp stores its finished rows into
+ * every rank's receive slots (one 64-bit word per row: the call's epoch and
+ * the fp32 partial), goes on to its next rows, and after its last rows sums
+ * every rank's copy in rank order.  y is bit-identical on every rank.  Waits
+ * are bounded: a rank that never arrives makes the others' calls time out,
+ * their rows of y are NaN, b4_p2p_status reports B4_STATUS_TIMEOUT, and the
+ * GPU stays usable (then destroy and re-create the b4_p2p on every rank: the
+ * call counters disagree).  Set-up, once per rank and device: b4_p2p_create
+ * (one device allocation of 16 * world * max_rows + 256 bytes, max_rows >=
+ * the out_f of every call), b4_p2p_ipc_handle -> send the 64-byte handle to
+ * every peer -> b4_p2p_open_peer for each peer's handle.  One process per GPU
+ * (CUDA IPC).  Every rank must make the same sequence of calls; the call
+ * counter lives on the device, so calls captured in a CUDA graph may be
+ * replayed.  flags: B4_FLAG_PDL (or 0).  INT4, batch 1.  No counterpart in
+ * the reference (it has no multi-GPU code). */
 typedef struct b4_p2p b4_p2p;
 int b4_p2p_create(int rank, int world, int max_rows, b4_p2p** out);
 int b4_p2p_ipc_handle(const b4_p2p* p2p, void* handle64);

@@ -20,12 +20,13 @@
 // local store) and goes on to its next block; only after its last block does
 // it read back, for each of its blocks, every rank's copy from its own memory
 // (bounded polls: after kP2pMaxSpins polls, or as soon as another wait of the
-// call has given up, it records kP2pErrTimeout in the error word and moves
-// on), sums the ranks in rank order and stores y.  Every rank adds the same
-// numbers in the same order: y is bit-identical on all ranks.  The epoch lives
-// in device memory: every CTA reads it after griddepcontrol.wait (the
-// previous call has completed) and the last CTA to finish advances it, so a
-// call captured in a CUDA graph stays correct when the graph is replayed.
+// call has given up, it records kP2pErrTimeout in the error word and stores
+// NaN for that row), sums the ranks in rank order and stores y.  Every rank
+// adds the same numbers in the same order: y is bit-identical on all ranks.
+// The epoch lives in device memory: every CTA reads it after
+// griddepcontrol.wait (the previous call has completed) and the last CTA to
+// finish advances it, so a call captured in a CUDA graph stays correct when
+// the graph is replayed.
 #pragma once
 
 #include <cstdint>
@@ -102,15 +103,21 @@ __device__ __forceinline__ void p2p_reduce(const P2pArgs& a, uint32_t epoch, int
             const unsigned long long* slot = mine + (size_t)r * a.max_rows;
             unsigned long long w = ld_relaxed_sys_u64(slot);
             long long n = 0;
+            bool arrived = true;
             while ((uint32_t)(w >> 32) != epoch) {
                 // give up after kP2pMaxSpins polls, or at once when another wait
                 // of this call already gave up (a missing peer costs one timeout)
                 if (++n >= kP2pMaxSpins || ((n & 63) == 0 && *(volatile const uint32_t*)a.error)) {
                     atomicOr(a.error, kP2pErrTimeout);
+                    arrived = false;
                     break;
                 }
                 __nanosleep(64);
                 w = ld_relaxed_sys_u64(slot);
+            }
+            if (!arrived) {
+                s = __int_as_float(0x7fffffff);   // a row with a missing rank is NaN, never a partial sum
+                break;
             }
             s += __uint_as_float((uint32_t)w);
         }

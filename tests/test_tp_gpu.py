@@ -264,6 +264,7 @@ def _p2p_worker(rank, world, port, mode, results):
                 assert lib.b4_tp_gemv_p2p(0, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, st) == 0
                 torch.cuda.synchronize()
                 out["status"] = p2p.status(clear=True)
+                out["rows_nan"] = bool(torch.isnan(y).all().item())   # no partial sums pass as results
                 y2 = b4gemv.gemv(0, qw, sc, x)      # the GPU is still usable
                 torch.cuda.synchronize()
                 out["after"] = bool(torch.isfinite(y2).all().item())
@@ -360,4 +361,5 @@ def test_p2p_rowparallel_gemv_matches_nccl_and_is_identical_on_every_rank():
 def test_p2p_wait_for_a_peer_that_never_arrives_times_out_and_the_gpu_stays_usable():
     res = _run_p2p(2, "timeout")
     assert res[0]["status"] == 10901, res      # B4_STATUS_TIMEOUT
+    assert res[0]["rows_nan"], res
     assert res[0]["after"], res
