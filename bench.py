@@ -78,8 +78,10 @@ ENGINE_KERNELS = {0: "b4_gemv_kernel", 1: "b4_gemv_mma_kernel", 2: "b4_gemv_tma_
 
 
 def engine_kernel(b4, fmt, in_f, out_f):
-    """Name of the kernel the dispatch rule picks for one batch-1 shape."""
-    cfg = b4.default_config(fmt, in_f, out_f, 1)
+    """Name of the kernel the dispatch rule (of b4_gemv_ws) picks for one batch-1 shape."""
+    cfg = b4.default_config_ws(fmt, in_f, out_f, 1)
+    if cfg["flags"] & b4.FLAG_SPLIT:
+        return "b4_gemv_split_int4_kernel" if fmt == 0 else "b4_gemv_split_nf4_kernel"
     return ENGINE_KERNELS.get(cfg["engine"], f"engine {cfg['engine']}")
 
 
@@ -220,22 +222,27 @@ def build_weights(b4, torch, dev, fmt):
 
 
 class Launcher:
-    """Pre-bound C ABI calls: one ctypes call per GEMV, nothing else.  With
-    pdl, every GEMV goes through b4_gemv_ex with the dispatch rule's config
-    plus B4_FLAG_PDL (programmatic dependent launch: the next GEMV's weight
-    stream starts while the previous kernel drains); without, through the
-    reference-shaped b4_gemv_nf4_b64 / b4_gemv_int4_g128."""
+    """Pre-bound C ABI calls: one ctypes call per GEMV, nothing else.  Every
+    GEMV goes through b4_gemv_ws with one zero-filled workspace (the split
+    kernels of the few-row shapes use it; the GEMVs run one after another on
+    one stream, so they may share it).  With pdl, the config is the dispatch
+    rule's (b4_gemv_default_config_ws) plus B4_FLAG_PDL (programmatic dependent
+    launch: the next GEMV's weight stream starts while the previous kernel
+    drains); without, the rule's own (cfg NULL)."""
 
     def __init__(self, b4, torch, sets, xs, ys, fmt, pdl=False):
         lib = b4.load()
         self.lib, self.fmt, self.pdl = lib, fmt, pdl
-        self.fn = lib.b4_gemv_nf4_b64 if fmt == 1 else lib.b4_gemv_int4_g128
         self.cfg_objs = []
+        need = 0
         for name, out_f, in_f in SHAPES:
-            c = b4.GemvConfig.from_dict(b4.default_config(fmt, in_f, out_f, 1))
-            c.flags = b4.FLAG_PDL
+            c = b4.GemvConfig.from_dict(b4.default_config_ws(fmt, in_f, out_f, 1))
+            c.flags |= b4.FLAG_PDL
             self.cfg_objs.append(c)
+            need = max(need, b4.workspace_size(fmt, in_f, out_f, 1, c.as_dict()))
         self.cfgs = [ctypes.byref(c) for c in self.cfg_objs]
+        self.ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=xs[0].device)
+        self.ws_ptr, self.ws_len = ctypes.c_void_p(self.ws.data_ptr()), self.ws.numel()
         self.calls = []
         for s in range(len(sets)):
             row = []
@@ -246,10 +253,8 @@ class Launcher:
             self.calls.append(row)
 
     def call(self, i, q, sc, x, y, in_f, out_f, stream):
-        if self.pdl:
-            st = self.lib.b4_gemv_ex(self.fmt, q, sc, x, y, in_f, out_f, 1, self.cfgs[i], stream)
-        else:
-            st = self.fn(q, sc, x, y, in_f, out_f, 1, stream)
+        st = self.lib.b4_gemv_ws(self.fmt, q, sc, x, y, in_f, out_f, 1, self.cfgs[i] if self.pdl else None,
+                                 self.ws_ptr, self.ws_len, stream)
         if st:
             raise RuntimeError(f"GEMV launch failed with status {st}")
 
@@ -289,7 +294,7 @@ def correctness_gate(b4, torch, sets, xs, ys, fmt):
     worst = 0.0
     for i, (name, out_f, in_f) in enumerate(SHAPES):
         qw, sc = sets[0][i]
-        y = b4.gemv(fmt, qw, sc, xs[i])
+        y = b4.gemv_ws(fmt, qw, sc, xs[i])
         deq = b4.dequant_nf4(qw, sc) if fmt == 1 else b4.dequant_int4(qw, sc)
         ref = (deq.double() @ xs[i].double().t()).t()
         err = float((y.double() - ref).abs().max() / ref.abs().max())

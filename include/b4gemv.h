@@ -42,7 +42,7 @@ extern "C" {
 #define B4_FMT_INT4_G128 0
 #define B4_FMT_NF4_B64 1
 
-#define B4_ABI_VERSION 3
+#define B4_ABI_VERSION 4
 
 /* Same type as cudaStream_t, spelled without the CUDA headers. */
 typedef struct CUstream_st* b4_stream_t;
@@ -108,6 +108,12 @@ typedef struct b4_gemv_config {
  * still runs, so do not set the flag on a launch whose immediately preceding
  * kernel writes this launch's weights. */
 #define B4_FLAG_PDL 1
+/* Split the work into equal runs of (16-row block, k-step) units per warp,
+ * with a deterministic cross-CTA reduction through a workspace; engines
+ * B4_ENGINE_MMA_LEAN_ASYNC (INT4: stages x stage_groups ring) and
+ * B4_ENGINE_MMA_NF4 (NF4: register pipeline of `stages`), batch 1.  Only
+ * b4_gemv_ws takes it (the other entry points reject it). */
+#define B4_FLAG_SPLIT 2
 
 /* ---- GEMV: y[b][r] = sum_k dequant(W)[r][k] * x[b][k], b < m ----------------
  * qw     : uint32 [out_f][in_f/8] packed codes
@@ -136,6 +142,35 @@ int b4_gemv_default_config(int fmt, int in_f, int out_f, int m, b4_gemv_config* 
  * by hand (diag_aspect.cu:54-56,253-256,262-266). */
 int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y,
                int in_f, int out_f, int m, const b4_gemv_config* cfg, b4_stream_t stream);
+
+/* ---- GEMV with a caller-owned workspace --------------------------------------
+ * A matrix whose 16-row blocks do not divide evenly over the resident CTAs
+ * leaves SMs idle in its last wave; the split path (B4_FLAG_SPLIT) instead
+ * gives every warp of the grid an equal run of (block, k-step) units and adds
+ * a block's pieces through `ws`: per 16-row block, one arrival counter and
+ * the pieces' partial sums.  The warp that completes a block sums its pieces
+ * in k order, so y is deterministic.  The cross-CTA sum costs ~2 us, so the
+ * rule (b4_gemv_default_config_ws) splits only at batch 1 where whole-row
+ * tiles run between one and two waves on rows of at most 8192 columns (INT4
+ * 8192x8192: 14.9 -> 12.5 us on B200); any split config can be passed
+ * explicitly.  Same operands and semantics as b4_gemv_ex; a replacement for
+ * b4_gemv_int4_g128 / b4_gemv_nf4_b64 (kernels.cuh:26-30, 87-91) that runs
+ * split where the rule says so and identically elsewhere.
+ *
+ * b4_gemv_workspace_size: bytes of workspace the call with these arguments
+ * needs on the current device (0 when the config does not split; cfg NULL =
+ * the dispatch rule).  ws: device memory, 16-byte aligned, at least that
+ * size, ZERO-FILLED before its first use (cudaMemset); every call leaves it
+ * zeroed again, so it can be reused by later calls and by CUDA-graph
+ * replays.  Calls that may run at the same time (different streams) need
+ * different workspaces.  A workspace that is too small returns
+ * cudaErrorInvalidValue before anything is launched. */
+int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_config* cfg, size_t* bytes);
+/* The dispatch rule of b4_gemv_ws (cfg NULL): b4_gemv_default_config's choice,
+ * or a B4_FLAG_SPLIT config where the split pays (see above). */
+int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg);
+int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f, int out_f,
+               int m, const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream);
 
 /* ---- Several projections that share x, as one launch ----------------------
  * y_s[b][r] = sum_k dequant(W_s)[r][k] * x[b][k] for every segment s < nseg

@@ -14,7 +14,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS, NF4_BLOCK, B4Error,
+from ._lib import (FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS, NF4_BLOCK, B4Error,
                    GemvConfig, GemvSegment, check, load)
 
 __all__ = [
@@ -22,7 +22,8 @@ __all__ = [
     "GemvConfig", "load", "quantise", "quantise_nf4", "gemv_int4", "gemv_nf4", "gemv",
     "gemv_nf4_block_per_row", "dequant_int4", "dequant_nf4", "unpack_codes",
     "quantise_device", "quantise_nf4_device", "default_config", "median", "gemv_multi",
-    "multi_default_config", "MAX_SEGMENTS", "GemvSegment", "repack_bnb_nf4",
+    "multi_default_config", "MAX_SEGMENTS", "GemvSegment", "repack_bnb_nf4", "FLAG_SPLIT",
+    "gemv_ws", "workspace_size", "workspace", "default_config_ws",
 ]
 
 
@@ -115,6 +116,14 @@ def default_config(fmt: int, in_f: int, out_f: int, m: int = 1) -> dict:
     return c.as_dict()
 
 
+def default_config_ws(fmt: int, in_f: int, out_f: int, m: int = 1) -> dict:
+    """b4_gemv_default_config_ws: the config b4_gemv_ws uses (split for few-row
+    shapes at batch 1, b4_gemv_default_config's choice otherwise)."""
+    c = GemvConfig()
+    check("b4_gemv_default_config_ws", load().b4_gemv_default_config_ws(fmt, in_f, out_f, m, ctypes.byref(c)))
+    return c.as_dict()
+
+
 def _gemv_args(qw, scale, x, y):
     import torch
     assert qw.is_cuda and qw.dtype in (torch.int32, torch.uint32) and qw.is_contiguous()
@@ -138,16 +147,74 @@ def gemv(fmt: int, qw, scale, x, y=None, config: dict | None = None, stream=None
     return y
 
 
-def gemv_int4(qw, scales, x, y=None, stream=None):
-    """b4_gemv_int4_g128: the INT4 g128 GEMV with the dispatch rule's config."""
+_WS_SIZE = {}
+_WS = {}
+
+
+def workspace_size(fmt: int, in_f: int, out_f: int, m: int = 1, config: dict | None = None) -> int:
+    """b4_gemv_workspace_size on the current device: bytes of workspace
+    b4_gemv_ws needs for this shape (0 when the config does not split)."""
+    import torch
+    key = (fmt, in_f, out_f, m, torch.cuda.current_device()) if config is None else None
+    if key is not None and key in _WS_SIZE:
+        return _WS_SIZE[key]
+    cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
+    n = ctypes.c_size_t(0)
+    check("b4_gemv_workspace_size", load().b4_gemv_workspace_size(fmt, in_f, out_f, m, cfg, ctypes.byref(n)))
+    if key is not None:
+        _WS_SIZE[key] = n.value
+    return n.value
+
+
+def workspace(device, nbytes: int):
+    """The package's workspace for b4_gemv_ws on `device`: one zero-filled
+    uint8 tensor per device, grown on demand (at least 1 MiB).  Every call
+    leaves it zeroed.  Calls on different streams that may overlap must not
+    share it: pass them their own (torch.zeros(n, dtype=torch.uint8))."""
+    import torch
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _WS.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=f"cuda:{idx}")
+        _WS[idx] = ws
+    return ws
+
+
+def gemv_ws(fmt: int, qw, scale, x, y=None, config: dict | None = None, ws=None, stream=None):
+    """b4_gemv_ws: the GEMV with a workspace (the split path for few-row
+    matrices at batch 1; config None = the dispatch rule).  ws: a zero-filled
+    CUDA uint8 tensor of at least workspace_size() bytes, or None for the
+    package's per-device workspace."""
+    out_f, in_f, m, x2, y = _gemv_args(qw, scale, x, y)
+    need = workspace_size(fmt, in_f, out_f, m, config)
+    if ws is None and need:
+        ws = workspace(qw.device, need)
+    cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
+    check("b4_gemv_ws", load().b4_gemv_ws(fmt, _ptr(qw), _ptr(scale), _ptr(x2), _ptr(y), in_f, out_f, m, cfg,
+                                          _ptr(ws) if ws is not None else None,
+                                          ws.numel() if ws is not None else 0, _stream(stream)))
+    return y
+
+
+def gemv_int4(qw, scales, x, y=None, stream=None, split: bool = True):
+    """The INT4 g128 GEMV with the dispatch rule's config: b4_gemv_ws with the
+    package's workspace (split: True), or b4_gemv_int4_g128, which needs no
+    workspace and never splits (split: False)."""
+    if split:
+        return gemv_ws(FMT_INT4_G128, qw, scales, x, y, stream=stream)
     out_f, in_f, m, x2, y = _gemv_args(qw, scales, x, y)
     check("b4_gemv_int4_g128", load().b4_gemv_int4_g128(_ptr(qw), _ptr(scales), _ptr(x2), _ptr(y), in_f,
                                                         out_f, m, _stream(stream)))
     return y
 
 
-def gemv_nf4(qw, absmax, x, y=None, stream=None):
-    """b4_gemv_nf4_b64: the NF4 b64 GEMV with the dispatch rule's config."""
+def gemv_nf4(qw, absmax, x, y=None, stream=None, split: bool = True):
+    """The NF4 b64 GEMV with the dispatch rule's config: b4_gemv_ws with the
+    package's workspace (split: True), or b4_gemv_nf4_b64, which needs no
+    workspace and never splits (split: False)."""
+    if split:
+        return gemv_ws(FMT_NF4_B64, qw, absmax, x, y, stream=stream)
     out_f, in_f, m, x2, y = _gemv_args(qw, absmax, x, y)
     check("b4_gemv_nf4_b64", load().b4_gemv_nf4_b64(_ptr(qw), _ptr(absmax), _ptr(x2), _ptr(y), in_f,
                                                     out_f, m, _stream(stream)))

@@ -17,6 +17,7 @@ FMT_NF4_B64 = 1
 GROUP = 128
 NF4_BLOCK = 64
 FLAG_PDL = 1
+FLAG_SPLIT = 2
 ENGINE_FMA = 0
 ENGINE_MMA = 1
 ENGINE_MMA_TMA = 2
@@ -78,6 +79,9 @@ SIGNATURES = {
     "b4_gemv_nf4_b64": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "b4_gemv_default_config": (_I, [_I, _I, _I, _I, ctypes.POINTER(GemvConfig)]),
     "b4_gemv_ex": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P]),
+    "b4_gemv_workspace_size": (_I, [_I, _I, _I, _I, ctypes.POINTER(GemvConfig), ctypes.POINTER(ctypes.c_size_t)]),
+    "b4_gemv_default_config_ws": (_I, [_I, _I, _I, _I, ctypes.POINTER(GemvConfig)]),
+    "b4_gemv_ws": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P, ctypes.c_size_t, _P]),
     "b4_gemv_nf4_b64_block_per_row": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "b4_gemv_multi": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _P, _I, _I, ctypes.POINTER(GemvConfig), _P]),
     "b4_gemv_multi_default_config": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _I, _I,

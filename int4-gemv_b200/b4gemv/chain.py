@@ -5,13 +5,16 @@ all 196 GEMVs captured in one CUDA graph on one GPU.  It exposes the launch
 overhead the isolated-launch numbers hide; with programmatic dependent launch
 each GEMV streams its first weights while the previous one finishes, and with
 `fused` the q/k/v and gate/up projections of a layer run as one launch each
-(b4_gemv_multi), 112 launches per token instead of 196.
+(b4_gemv_multi), 112 launches per token instead of 196.  The other GEMVs go
+through b4_gemv_ws with the chain's workspace, so the few-row o/down
+projections run split (B4_FLAG_SPLIT); the GEMVs run one after another on one
+stream, so they share it.
 """
 from __future__ import annotations
 
 import ctypes
 
-from ._lib import FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, GemvSegment, check, load
+from ._lib import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, GemvSegment, check, load
 
 QWEN_LAYER = [("q", 3584, 3584), ("k", 512, 3584), ("v", 512, 3584), ("o", 3584, 3584),
               ("gate", 18944, 3584), ("up", 18944, 3584), ("down", 3584, 18944)]
@@ -48,6 +51,12 @@ class DecodeChain:
         torch.cuda.synchronize(device)
         self.cfg_single = {}
         self.cfg_multi = {}
+        need = 0
+        for name, out_f, in_f in QWEN_LAYER:
+            n = ctypes.c_size_t(0)
+            check("b4_gemv_workspace_size", load().b4_gemv_workspace_size(fmt, in_f, out_f, 1, None, ctypes.byref(n)))
+            need = max(need, n.value)
+        self.ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
 
     def launches(self, fused: bool):
         """(kind, args) per launch of one token, configs resolved."""
@@ -75,7 +84,8 @@ class DecodeChain:
                     in_f, out_f = qw.shape[1] * 8, qw.shape[0]
                     if (in_f, out_f) not in self.cfg_single:
                         c = GemvConfig()
-                        check("default_config", lib.b4_gemv_default_config(self.fmt, in_f, out_f, 1, ctypes.byref(c)))
+                        check("default_config", lib.b4_gemv_default_config_ws(self.fmt, in_f, out_f, 1,
+                                                                              ctypes.byref(c)))
                         self.cfg_single[(in_f, out_f)] = c
                     out.append(("single", (qw, sc, x, y, in_f, out_f, self.cfg_single[(in_f, out_f)])))
         return out
@@ -90,11 +100,11 @@ class DecodeChain:
                                                          ctypes.byref(c), stream))
             else:
                 qw, sc, x, y, in_f, out_f, c = a
-                c.flags = FLAG_PDL if pdl else 0
-                check("b4_gemv_ex", lib.b4_gemv_ex(self.fmt, ctypes.c_void_p(qw.data_ptr()),
+                c.flags = (c.flags & FLAG_SPLIT) | (FLAG_PDL if pdl else 0)
+                check("b4_gemv_ws", lib.b4_gemv_ws(self.fmt, ctypes.c_void_p(qw.data_ptr()),
                                                    ctypes.c_void_p(sc.data_ptr()), ctypes.c_void_p(x.data_ptr()),
                                                    ctypes.c_void_p(y.data_ptr()), in_f, out_f, 1, ctypes.byref(c),
-                                                   stream))
+                                                   ctypes.c_void_p(self.ws.data_ptr()), self.ws.numel(), stream))
 
     def launch_count(self, fused: bool) -> int:
         return len(self.launches(fused))

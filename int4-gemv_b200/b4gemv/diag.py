@@ -20,13 +20,14 @@ import itertools
 import json
 import sys
 
-from . import FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
+from . import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
 
 SHAPES = {"q_proj": (3584, 3584), "k_proj": (512, 3584), "v_proj": (512, 3584), "o_proj": (3584, 3584),
           "gate_proj": (18944, 3584), "up_proj": (18944, 3584), "down_proj": (3584, 18944),
           # Llama-3-70B layer and its tensor-parallel shards
           "l70_qo": (8192, 8192), "l70_kv": (1024, 8192), "l70_gu": (28672, 8192), "l70_down": (8192, 28672)}
 L2_BYTES = 126 * 1024 * 1024
+WS_BYTES = 8 << 20   # workspace for the split configs (the largest shape here needs < 1 MiB)
 
 
 def alg_bytes(fmt, out_f, in_f, m=1):
@@ -52,12 +53,16 @@ class Problem:
         self.y = torch.empty((m, out_f), device=dev)
         self.fmt, self.out_f, self.in_f, self.m = fmt, out_f, in_f, m
         self.ptrs = [(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(s.data_ptr())) for q, s in self.copies]
+        # one zero-filled workspace for the split configs (every call leaves it zeroed)
+        self.ws = torch.zeros(WS_BYTES, dtype=torch.uint8, device=dev)
 
     def launch(self, k, cfg, stream):
+        """One GEMV through b4_gemv_ws (cfg None: the rule of b4_gemv_ws)."""
         q, s = self.ptrs[k % len(self.ptrs)]
-        return load().b4_gemv_ex(self.fmt, q, s, ctypes.c_void_p(self.x.data_ptr()),
+        return load().b4_gemv_ws(self.fmt, q, s, ctypes.c_void_p(self.x.data_ptr()),
                                  ctypes.c_void_p(self.y.data_ptr()), self.in_f, self.out_f, self.m,
-                                 ctypes.byref(cfg) if cfg is not None else None, stream)
+                                 ctypes.byref(cfg) if cfg is not None else None,
+                                 ctypes.c_void_p(self.ws.data_ptr()), self.ws.numel(), stream)
 
 
 def time_chained(torch, prob, cfg, reps=100):
@@ -97,7 +102,24 @@ NF4_LEAN_VARIANTS = [(4, 4, 2, 0), (4, 8, 2, 0), (6, 4, 2, 0), (4, 4, 4, 0), (4,
 NF4_TMA_VARIANTS = [(4, 2, 4), (4, 2, 8), (8, 2, 4), (8, 2, 6), (16, 2, 4), (4, 4, 4), (8, 4, 4)]  # (rw, vw, st)
 
 
+SPLIT_INT4_VARIANTS = [(4, 1), (6, 1), (3, 2), (4, 2), (2, 4), (3, 4)]   # split INT4 (stages, stage_groups)
+
+
+def split_grid(fmt):
+    """The split configs (B4_FLAG_SPLIT, batch 1)."""
+    base = dict(vec_words=4, rows_per_warp=16, warps_k=1, row_groups=8, batch_tile=1, nf4_lut=0, x_tile=0,
+                flags=FLAG_SPLIT)
+    if fmt == FMT_INT4_G128:
+        for st, sg in SPLIT_INT4_VARIANTS:
+            yield dict(base, engine=5, stages=st, stage_groups=sg)
+    else:
+        for st in (2, 3, 4):
+            yield dict(base, engine=7, stages=st, stage_groups=0)
+
+
 def config_grid(fmt, m=1):
+    if m == 1:
+        yield from split_grid(fmt)
     if fmt == FMT_INT4_G128 and m == 1:
         for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (2, 3, 4, 6)):
             if kw * rg <= 8:
@@ -157,14 +179,21 @@ def cmd_sweep(args, torch):
             prob = Problem(torch, fmt, out_f, in_f, m=args.m)
             nb = alg_bytes(fmt, out_f, in_f, args.m)
             dflt = GemvConfig()
-            check("default_config", load().b4_gemv_default_config(fmt, in_f, out_f, args.m, ctypes.byref(dflt)))
+            check("default_config", load().b4_gemv_default_config_ws(fmt, in_f, out_f, args.m, ctypes.byref(dflt)))
+            tile = GemvConfig()
+            check("default_config", load().b4_gemv_default_config(fmt, in_f, out_f, args.m, ctypes.byref(tile)))
             rows = []
             if args.pdl:
                 dflt.flags |= FLAG_PDL
+                tile.flags |= FLAG_PDL
             us_d = time_chained(torch, prob, dflt)
             rows.append(("default", dflt.as_dict(), us_d))
+            us_t = time_chained(torch, prob, tile)
+            rows.append(("default_unsplit", tile.as_dict(), us_t))
+            print(f"  rule (b4_gemv_ws) {us_d:.3f} us, unsplit rule (b4_gemv_default_config) {us_t:.3f} us", flush=True)
             engines = {int(e) for e in args.engines.split(",")} if args.engines else None
-            for c in config_grid(fmt, args.m):
+            grid = split_grid(fmt) if args.split_only else config_grid(fmt, args.m)
+            for c in grid:
                 if engines is not None and c.get("engine", 0) not in engines:
                     continue
                 if args.pdl:
@@ -181,7 +210,8 @@ def cmd_sweep(args, torch):
                         "bytes": nb, "default": {"cfg": dflt.as_dict(), "us": us_d},
                         "top": [{"cfg": c, "us": us} for _, c, us in rows[:12]],
                         "all": [[c.get("engine", 0), c["vec_words"], c["rows_per_warp"], c["warps_k"], c["row_groups"],
-                                 c["batch_tile"], c["nf4_lut"], round(us, 3)] for _, c, us in rows]})
+                                 c["batch_tile"], c["nf4_lut"], c.get("flags", 0), c.get("stages", 0),
+                                 c.get("stage_groups", 0), round(us, 3)] for _, c, us in rows]})
             del prob
             torch.cuda.empty_cache()
     if args.json:
@@ -215,7 +245,7 @@ def cmd_run(args, torch):
     cfg = None
     if args.config:
         d = GemvConfig()
-        check("default_config", load().b4_gemv_default_config(fmt, in_f, out_f, args.m, ctypes.byref(d)))
+        check("default_config", load().b4_gemv_default_config_ws(fmt, in_f, out_f, args.m, ctypes.byref(d)))
         c = d.as_dict()
         for kv in args.config.split(","):
             k, v = kv.split("=")
@@ -223,7 +253,7 @@ def cmd_run(args, torch):
         cfg = GemvConfig.from_dict(c)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     for k in range(args.launches):
-        check("b4_gemv_ex", prob.launch(k, cfg, stream))
+        check("b4_gemv_ws", prob.launch(k, cfg, stream))
     torch.cuda.synchronize()
     print(f"ran {args.launches} launches of {args.fmt} {args.shape} {out_f}x{in_f} m={args.m}")
 
@@ -238,6 +268,7 @@ def main(argv=None):
     s.add_argument("--json", default="")
     s.add_argument("--engines", default="", help="comma-separated engine numbers to sweep (default: all)")
     s.add_argument("--pdl", action="store_true", help="launch every config as a programmatic dependent")
+    s.add_argument("--split-only", action="store_true", help="sweep only the split configs (B4_FLAG_SPLIT)")
     a = sub.add_parser("aspect")
     a.add_argument("--fmt", default="nf4", choices=["nf4", "int4"])
     r = sub.add_parser("run")

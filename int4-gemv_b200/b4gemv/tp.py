@@ -23,7 +23,7 @@ from __future__ import annotations
 
 import ctypes
 
-from ._lib import FLAG_PDL, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, GemvConfig, GemvSegment, check, load
+from ._lib import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, GemvConfig, GemvSegment, check, load
 
 
 def row_range(n: int, tp: int, rank: int):
@@ -197,12 +197,20 @@ class TPDecodeLayer:
             c.flags = FLAG_PDL if pdl else 0
             self.segs[group] = (segs, len(names), in_f)
             self.cfg[group] = c
+        # single GEMVs through b4_gemv_ws: the few-row ones run split with this
+        # layer's workspace (its GEMVs run one after another on one stream)
+        need = 0
         for name in self.NAMES:
             qw = self.w[name][0]
             c = GemvConfig()
-            check("config", lib.b4_gemv_default_config(fmt, qw.shape[1] * 8, qw.shape[0], 1, ctypes.byref(c)))
-            c.flags = FLAG_PDL if pdl else 0
+            check("config", lib.b4_gemv_default_config_ws(fmt, qw.shape[1] * 8, qw.shape[0], 1, ctypes.byref(c)))
+            c.flags = (c.flags & FLAG_SPLIT) | (FLAG_PDL if pdl else 0)
             self.cfg[name] = c
+            n = ctypes.c_size_t(0)
+            check("workspace", lib.b4_gemv_workspace_size(fmt, qw.shape[1] * 8, qw.shape[0], 1, ctypes.byref(c),
+                                                          ctypes.byref(n)))
+            need = max(need, n.value)
+        self.ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
 
     def weight_bytes(self) -> int:
         """Algorithmic bytes this rank streams per step (codes + scales)."""
@@ -210,8 +218,9 @@ class TPDecodeLayer:
 
     def _gemv(self, name, x, y, stream):
         qw, sc = self.w[name]
-        check(f"gemv {name}", load().b4_gemv_ex(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
-                                                 qw.shape[0], 1, ctypes.byref(self.cfg[name]), stream))
+        check(f"gemv {name}", load().b4_gemv_ws(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
+                                                 qw.shape[0], 1, ctypes.byref(self.cfg[name]), _p(self.ws),
+                                                 self.ws.numel(), stream))
 
     def _multi(self, group, x, stream):
         segs, n, in_f = self.segs[group]

@@ -15,6 +15,7 @@
 #include "b4_gemv_lean_nf4.cuh"
 #include "b4_gemv_nf4_mma.cuh"
 #include "b4_gemv_nf4_mma_mb.cuh"
+#include "b4_gemv_split.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -512,6 +513,28 @@ int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t 
 
 namespace {
 
+// Resident CTAs per SM of a kernel at a block size and shared-memory size,
+// queried once per (kernel, device, size) under a mutex (the split launches
+// size their grid with it on every call).
+cudaError_t occupancy_cached(const void* fn, int dev, int threads, size_t smem, int* occ)
+{
+    static std::mutex mu;
+    static std::map<std::pair<std::pair<const void*, int>, std::pair<int, size_t>>, int> done;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(std::make_pair(fn, dev), std::make_pair(threads, smem));
+    const auto it = done.find(key);
+    if (it != done.end()) {
+        *occ = it->second;
+        return cudaSuccess;
+    }
+    int n = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem);
+    if (e != cudaSuccess) return e;
+    done[key] = n;
+    *occ = n;
+    return cudaSuccess;
+}
+
 int sm_count_cached(int dev)
 {
     static std::atomic<int> cache[64];
@@ -906,6 +929,120 @@ int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void
     return cudaSuccess;
 }
 
+// ---- split launches (b4_gemv_split.cuh) ---------------------------------------
+
+int split_plan(const GemvProblem& p, const b4_gemv_config& c, SplitPlan* plan)
+{
+    if (p.m != 1 || !(c.flags & B4_FLAG_SPLIT)) return cudaErrorInvalidValue;
+    SplitPlan s = {};
+    if (p.fmt == kInt4) {
+        const int G = c.stage_groups, ng = p.in_f / kGroup;
+        if (c.engine != B4_ENGINE_MMA_LEAN_ASYNC || (G != 1 && G != 2 && G != 4) || ng % G) return cudaErrorInvalidValue;
+        if (!aligned(p.qw, 16) || !aligned(p.scale, 2u * G)) return cudaErrorInvalidValue;
+        s.fn = gemv_kernel_split_int4(c.stages, G);
+        s.nst = ng / G;
+        s.smem = (size_t)p.in_f * 2 + (size_t)8 * c.stages * G * 64 * 16;
+    } else {
+        if (c.engine != B4_ENGINE_MMA_NF4 || p.in_f % 128) return cudaErrorInvalidValue;
+        if (!aligned(p.qw, 16) || !aligned(p.scale, 8)) return cudaErrorInvalidValue;
+        s.fn = gemv_kernel_split_nf4(c.stages);
+        s.nst = p.in_f / 128;
+        s.smem = (size_t)kNf4PairTableBytes + (size_t)p.in_f * 2;
+    }
+    if (!s.fn) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int smem_max = 0;
+    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (s.smem > (size_t)smem_max) return cudaErrorInvalidValue;
+    if (s.smem > 48 * 1024) {
+        e = ensure_smem(s.fn, dev, s.smem);
+        if (e != cudaSuccess) return e;
+    }
+    int occ = 0;
+    e = occupancy_cached(s.fn, dev, 256, s.smem, &occ);
+    if (e != cudaSuccess) return e;
+    if (occ < 1) return cudaErrorInvalidValue;
+    s.nblocks = (p.out_f + 15) / 16;
+    s.total = s.nblocks * s.nst;
+    // every resident warp takes an equal run of k-steps; CTAs left without
+    // work are not launched
+    const long long warps = (long long)sm_count_cached(dev) * occ * 8;
+    s.per = (int)std::min<long long>((s.total + warps - 1) / warps, INT32_MAX);
+    const long long used = (s.total + s.per - 1) / s.per;
+    s.grid = (int)((used + 7) / 8);
+    s.maxp = (s.nst - 1) / s.per + 2;
+    s.cnt_bytes = ((size_t)s.nblocks * 4 + 255) / 256 * 256;
+    s.ws_bytes = s.cnt_bytes + (size_t)s.nblocks * s.maxp * 16 * sizeof(float);
+    *plan = s;
+    return cudaSuccess;
+}
+
+int launch_split(const GemvProblem& p, const b4_gemv_config& c, void* ws, size_t ws_bytes, cudaStream_t st)
+{
+    SplitPlan s;
+    int e = split_plan(p, c, &s);
+    if (e != cudaSuccess) return e;
+    if (!ws || !aligned(ws, 16) || ws_bytes < s.ws_bytes) return cudaErrorInvalidValue;
+    SplitParams sp;
+    sp.qw = p.qw;
+    sp.scale = p.scale;
+    sp.x = static_cast<const __half*>(p.x);
+    sp.y = p.y;
+    sp.cnt = static_cast<unsigned*>(ws);
+    sp.part = reinterpret_cast<float*>(static_cast<char*>(ws) + s.cnt_bytes);
+    sp.total = s.total;
+    sp.in_f = p.in_f;
+    sp.out_f = p.out_f;
+    sp.nst = s.nst;
+    sp.per = s.per;
+    sp.maxp = s.maxp;
+    sp.x_vec = aligned(p.x, 16);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)s.grid);
+    lc.blockDim = dim3(256);
+    lc.dynamicSmemBytes = s.smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (c.flags & B4_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+    }
+    void* args[] = {&sp};
+    return cudaLaunchKernelExC(&lc, s.fn, args);
+}
+
+void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
+{
+    default_config(p, cfg);
+    // Fitted on B200 (`b4gemv.diag sweep --split-only --pdl`): the split's
+    // cross-CTA sum costs ~2 us at the kernel's end (fence, atomic, L2 reads),
+    // so it pays only where whole-row tiles run between one and two waves
+    // (296 < 16-row blocks < 592) on rows short enough that the second wave
+    // is a large share of the time: INT4 8192x8192 (Llama-3-70B q/o) 14.9 ->
+    // 12.5 us.  Qwen q/o (224 blocks) ran 3.8 -> 6.5 us split, down_proj and
+    // 8192x28672 no faster, and NF4 never faster.
+    const int sms = 148;
+    const long long blocks = (p.out_f + 15) / 16;
+    if (p.m != 1 || p.fmt != kInt4 || blocks <= 2LL * sms || blocks >= 4LL * sms || p.in_f > 8192) return;
+    const int ng = p.in_f / kGroup;
+    if (!aligned(p.qw, 16) || ng % 4 || !aligned(p.scale, 8)) return;
+    cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
+    cfg->stage_groups = 4;
+    cfg->stages = 2;
+    cfg->vec_words = 4;
+    cfg->rows_per_warp = 16;
+    cfg->batch_tile = 1;
+    cfg->warps_k = 1;
+    cfg->row_groups = 8;
+    cfg->tile_rows = 0;
+    cfg->flags |= B4_FLAG_SPLIT;
+}
+
 }  // namespace b4
 
 using namespace b4;
@@ -933,7 +1070,53 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     b4_gemv_config c;
     if (cfg) c = *cfg;
     else default_config(p, &c);
+    if (c.flags & B4_FLAG_SPLIT) return cudaErrorInvalidValue;   // needs a workspace: b4_gemv_ws
     return launch_gemv(p, c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg)
+{
+    if (!cfg) return cudaErrorInvalidValue;
+    GemvProblem p{fmt, reinterpret_cast<const uint32_t*>(256), reinterpret_cast<const void*>(256),
+                  reinterpret_cast<const void*>(256), reinterpret_cast<float*>(256), in_f, out_f, m, in_f, out_f};
+    const int e = check_problem(p);
+    if (e != cudaSuccess) return e;
+    default_config_ws(p, cfg);
+    return cudaSuccess;
+}
+
+int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_config* cfg, size_t* bytes)
+{
+    if (!bytes) return cudaErrorInvalidValue;
+    // the rule sees 256-byte aligned buffers, as every cudaMalloc gives
+    GemvProblem p{fmt, reinterpret_cast<const uint32_t*>(256), reinterpret_cast<const void*>(256),
+                  reinterpret_cast<const void*>(256), reinterpret_cast<float*>(256), in_f, out_f, m, in_f, out_f};
+    int e = check_problem(p);
+    if (e != cudaSuccess) return e;
+    b4_gemv_config c;
+    if (cfg) c = *cfg;
+    else default_config_ws(p, &c);
+    *bytes = 0;
+    if (!(c.flags & B4_FLAG_SPLIT)) return cudaSuccess;
+    SplitPlan s;
+    e = split_plan(p, c, &s);
+    if (e != cudaSuccess) return e;
+    *bytes = s.ws_bytes;
+    return cudaSuccess;
+}
+
+int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f, int out_f,
+               int m, const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream)
+{
+    GemvProblem p{fmt, qw, scale, x, y, in_f, out_f, m, in_f, out_f};
+    int e = check_problem(p);
+    if (e != cudaSuccess) return e;
+    b4_gemv_config c;
+    if (cfg) c = *cfg;
+    else default_config_ws(p, &c);
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (c.flags & B4_FLAG_SPLIT) return launch_split(p, c, ws, ws_bytes, st);
+    return launch_gemv(p, c, st);
 }
 
 int b4_gemv_int4_g128(const uint32_t* qw, const void* scales, const void* x, float* y,

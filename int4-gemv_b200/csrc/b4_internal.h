@@ -40,4 +40,23 @@ void default_config_multi(int fmt, const b4_gemv_segment* segs, int nseg, int in
 int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
                       const b4_gemv_config& cfg, cudaStream_t st);
 
+// A split launch (b4_gemv_split.cuh) on the current device: kernel, grid,
+// k-steps per row and per warp, piece slots per 16-row block, shared memory
+// and the workspace it needs ([cnt_bytes of counters][partial sums]).
+struct SplitPlan {
+    void* fn;
+    long long nblocks, total;
+    int nst, per, maxp, grid;
+    size_t smem, cnt_bytes, ws_bytes;
+};
+int split_plan(const GemvProblem& p, const b4_gemv_config& cfg, SplitPlan* plan);
+
+// Launches the split kernel of cfg (B4_FLAG_SPLIT) with the caller's workspace
+// (16-byte aligned, at least the plan's ws_bytes, counters zero).
+int launch_split(const GemvProblem& p, const b4_gemv_config& cfg, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// The workspace rule: default_config, switched to a split config (B4_FLAG_SPLIT)
+// for batch-1 matrices with too few rows to balance whole-row tiles.
+void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg);
+
 }  // namespace b4

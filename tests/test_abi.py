@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
         assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
-    assert lib.b4_abi_version() == 3
+    assert lib.b4_abi_version() == 4
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
@@ -171,3 +171,28 @@ def test_host_quantisers_match_oracle_random(oracle):
 def test_median_is_the_reference_upper_median():
     assert b4gemv.median([3.0, 1.0, 2.0, 4.0]) == 3.0
     assert b4gemv.median([5.0]) == 5.0
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("out_f,in_f", QWEN + LLAMA_TP)
+@pytest.mark.parametrize("m", [1, 2, 16])
+def test_workspace_rule_splits_only_where_fitted(fmt, out_f, in_f, m):
+    """b4_gemv_default_config_ws: b4_gemv_default_config's choice, or a split
+    INT4 config for batch-1 matrices of 297..591 row blocks and in_f <= 8192."""
+    c = b4gemv.default_config_ws(fmt, in_f, out_f, m)
+    blocks = (out_f + 15) // 16
+    split = bool(c["flags"] & b4gemv.FLAG_SPLIT)
+    assert split == (fmt == 0 and m == 1 and 296 < blocks < 592 and in_f <= 8192 and (in_f // 128) % 4 == 0)
+    if split:
+        assert c["engine"] == 5 and (c["stages"], c["stage_groups"]) == (2, 4)
+    else:
+        assert c == b4gemv.default_config(fmt, in_f, out_f, m)
+
+
+def test_split_flag_needs_the_workspace_entry_point():
+    """b4_gemv_ex has no workspace: a split config is rejected before any device call."""
+    lib = b4gemv.load()
+    c = _lib.GemvConfig.from_dict(b4gemv.default_config_ws(0, 8192, 8192, 1))
+    assert c.flags & b4gemv.FLAG_SPLIT
+    p = ctypes.c_void_p(4096)
+    assert lib.b4_gemv_ex(0, p, p, p, p, 8192, 8192, 1, ctypes.byref(c), None) == 1
