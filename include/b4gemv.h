@@ -172,6 +172,29 @@ int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_confi
 int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f, int out_f,
                int m, const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream);
 
+/* ---- Split GEMV without allocation -------------------------------------------
+ * No counterpart in the reference (its kernels need no scratch).  For callers
+ * that cannot allocate device memory -- a plugin given only its input and
+ * output buffers by a framework that owns every allocation, or code whose
+ * memory budget is fixed before its first call -- this is b4_gemv_ws's split
+ * path (B4_FLAG_SPLIT, batch 1) with the workspace held in the library's own
+ * static device array of B4_STATIC_SCRATCH_BYTES (1 MiB), which every GPU that
+ * loads the library keeps until the process exits.  It calls no cudaMalloc or
+ * cudaFree.  cfg NULL = a split config for the format (INT4: stages x groups
+ * chosen by divisibility; NF4: depth 3); a cfg without B4_FLAG_SPLIT is
+ * rejected.  A shape whose split needs more than the array holds returns
+ * B4_STATUS_SCRATCH_TOO_SMALL before anything is launched (b4_gemv_ws and a
+ * workspace of b4_gemv_workspace_size bytes handle it).  The first call on a
+ * device looks up the array's device address and clears it (synchronously):
+ * make it before any stream capture.  Every call clears the counters it uses
+ * on `stream` before its kernel.  All calls on a device share the one array:
+ * calls that may overlap on the GPU (different streams, unordered threads)
+ * race, so serialise them. */
+#define B4_STATIC_SCRATCH_BYTES (1u << 20)
+#define B4_STATUS_SCRATCH_TOO_SMALL 10902
+int b4_gemv_split_noalloc(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f,
+                          int out_f, const b4_gemv_config* cfg, b4_stream_t stream);
+
 /* ---- Several projections that share x, as one launch ----------------------
  * y_s[b][r] = sum_k dequant(W_s)[r][k] * x[b][k] for every segment s < nseg
  * (1..B4_MAX_SEGMENTS), all with the same in_f: q/k/v of an attention block,

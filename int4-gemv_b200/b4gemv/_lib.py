@@ -82,6 +82,7 @@ SIGNATURES = {
     "b4_gemv_workspace_size": (_I, [_I, _I, _I, _I, ctypes.POINTER(GemvConfig), ctypes.POINTER(ctypes.c_size_t)]),
     "b4_gemv_default_config_ws": (_I, [_I, _I, _I, _I, ctypes.POINTER(GemvConfig)]),
     "b4_gemv_ws": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, ctypes.POINTER(GemvConfig), _P, ctypes.c_size_t, _P]),
+    "b4_gemv_split_noalloc": (_I, [_I, _P, _P, _P, _P, _I, _I, ctypes.POINTER(GemvConfig), _P]),
     "b4_gemv_nf4_b64_block_per_row": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "b4_gemv_multi": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _P, _I, _I, ctypes.POINTER(GemvConfig), _P]),
     "b4_gemv_multi_default_config": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _I, _I,

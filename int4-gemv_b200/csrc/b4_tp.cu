@@ -185,6 +185,8 @@ const char* b4_nccl_error_string(int status)
 {
     if (status == B4_STATUS_NCCL_MISSING) return "libnccl.so.2 not found";
     if (status == B4_STATUS_TIMEOUT) return "timed out (b4_nccl_wait: communicator aborted; b4_p2p: a peer did not arrive)";
+    if (status == B4_STATUS_SCRATCH_TOO_SMALL)
+        return "the split needs more scratch than the static array holds (B4_STATIC_SCRATCH_BYTES): use b4_gemv_ws";
     const NcclApi& n = nccl();
     if (status > B4_STATUS_NCCL_BASE && status < B4_STATUS_NCCL_BASE + 100 && n.ok)
         return n.GetErrorString((ncclResult_t)(status - B4_STATUS_NCCL_BASE));
