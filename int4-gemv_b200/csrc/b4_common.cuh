@@ -158,6 +158,46 @@ __device__ __forceinline__ uint4 int4_pair_order(uint4 v)
     return r;
 }
 
+// One 16-byte word of x (8 fp16 values at src): a single 16-byte load when x is
+// 16-byte aligned, else eight 2-byte loads.
+__device__ __forceinline__ uint4 ld_x_word(const __half* src, bool vec)
+{
+    if (vec) return __ldg(reinterpret_cast<const uint4*>(src));
+    const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
+    uint4 raw;
+    raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
+    raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
+    raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
+    raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
+    return raw;
+}
+
+// Stages n 16-byte words of x (word i at x + 8i) into shared memory through
+// store(i, word).  Each thread loads XU of its words (i = tid, tid + blockDim,
+// ...) into registers before it stores any, so it waits for one memory round
+// trip per XU words instead of one per word: x is read after the
+// grid-dependency wait, on the kernel's critical path, and a long row (down_proj:
+// 2368 words for 256 threads) would otherwise cost ten round trips.
+template <int XU, typename Store>
+__device__ __forceinline__ void stage_x_words(const __half* x, int n, bool vec, Store store)
+{
+    for (int i0 = threadIdx.x; i0 < n; i0 += XU * blockDim.x) {
+        uint4 r[XU];
+#pragma unroll
+        for (int u = 0; u < XU; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            r[u] = i < n ? ld_x_word(x + (long long)i * 8, vec) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < XU; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            if (i < n) store(i, r[u]);
+        }
+    }
+}
+
+constexpr int kXUnroll = 8;   // x words in flight per thread while staging
+
 // ---- NF4 decode ---------------------------------------------------------------
 // Warp-register code book: lane L holds NF4[L & 15]; a shuffle with the packed
 // word shifted right by 4k as the source lane reads NF4[nibble k], since the

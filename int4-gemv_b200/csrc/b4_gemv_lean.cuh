@@ -240,20 +240,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     }
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int w = threadIdx.x; w < words; w += blockDim.x) {
-        const __half* src = p.x + (long long)w * 8;
-        uint4 raw;
-        if (p.x_vec) {
-            raw = __ldg(reinterpret_cast<const uint4*>(src));
-        } else {
-            const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
-            raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
-            raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
-            raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
-            raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
-        }
-        xs[w] = int4_pair_order(raw);
-    }
+    stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = int4_pair_order(v); });
     __syncthreads();
     const uint32_t epoch = P2P ? p2p_epoch(p.p2p) : 0u;
 

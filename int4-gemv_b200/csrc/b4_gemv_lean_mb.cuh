@@ -113,21 +113,8 @@ __global__ void __launch_bounds__(256, 3 - NB) b4_gemv_lean_mb_kernel(const Lean
     }
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int i = threadIdx.x; i < m * words; i += blockDim.x) {
-        const int b = i / words, w = i - b * words;
-        const __half* src = p.x + (long long)b * p.in_f + (long long)w * 8;
-        uint4 raw;
-        if (p.x_vec) {
-            raw = __ldg(reinterpret_cast<const uint4*>(src));
-        } else {
-            const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
-            raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
-            raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
-            raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
-            raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
-        }
-        xs[i] = int4_pair_order(raw);
-    }
+    // x is [m][in_f], contiguous: word i of the whole batch is at x + 8i
+    stage_x_words<kXUnroll>(p.x, m * words, p.x_vec, [&](int i, uint4 v) { xs[i] = int4_pair_order(v); });
     __syncthreads();
 
     // the batch rows this lane feeds into B (columns g of each block)

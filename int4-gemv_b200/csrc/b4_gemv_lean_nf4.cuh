@@ -151,23 +151,36 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_nf4_kernel(const LeanNf4P
 
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // x: lane chunk c (VW words, 8*VW columns) -> S swizzled 16-byte slots
-    for (int i = threadIdx.x; i < nsteps * 32 * S; i += blockDim.x) {
-        const int c = i / S, sl = i - c * S;
-        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (c < nchunks) {
-            const long long col = (long long)c * VW * 8 + sl * 4;
-            if (p.x_vec) {
-                const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p.x + col));
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-                const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-                v = make_float4(a.x, a.y, d.x, d.y);
-            } else {
-                v = make_float4(__half2float(p.x[col]), __half2float(p.x[col + 1]), __half2float(p.x[col + 2]),
-                                __half2float(p.x[col + 3]));
+    // x: lane chunk c (VW words, 8*VW columns) -> S swizzled 16-byte slots;
+    // kXUnroll slots' loads in flight per thread before any is stored (one
+    // memory round trip per kXUnroll slots on this critical path)
+    const int nslots = nsteps * 32 * S;
+    for (int i0 = threadIdx.x; i0 < nslots; i0 += kXUnroll * blockDim.x) {
+        float4 v[kXUnroll];
+#pragma unroll
+        for (int u = 0; u < kXUnroll; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            const int c = i / S, sl = i - c * S;
+            v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (i < nslots && c < nchunks) {
+                const long long col = (long long)c * VW * 8 + sl * 4;
+                if (p.x_vec) {
+                    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p.x + col));
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                    v[u] = make_float4(a.x, a.y, d.x, d.y);
+                } else {
+                    v[u] = make_float4(__half2float(p.x[col]), __half2float(p.x[col + 1]),
+                                       __half2float(p.x[col + 2]), __half2float(p.x[col + 3]));
+                }
             }
         }
-        reinterpret_cast<float4*>(xs)[swz<S>(c, sl)] = v;
+#pragma unroll
+        for (int u = 0; u < kXUnroll; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            const int c = i / S, sl = i - c * S;
+            if (i < nslots) reinterpret_cast<float4*>(xs)[swz<S>(c, sl)] = v[u];
+        }
     }
     __syncthreads();
 

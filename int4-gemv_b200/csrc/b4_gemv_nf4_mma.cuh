@@ -160,20 +160,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     nf4_pair_table_fill(base);
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int w = threadIdx.x; w < words; w += blockDim.x) {
-        const __half* src = p.x + (long long)w * 8;
-        uint4 raw;
-        if (p.x_vec) {
-            raw = __ldg(reinterpret_cast<const uint4*>(src));
-        } else {
-            const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
-            raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
-            raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
-            raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
-            raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
-        }
-        xs[w] = raw;
-    }
+    stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = v; });
     __syncthreads();
 
     // B carries x only on lanes (g, q) with g == q >> 1 (columns 0/1 = blocks 0/1)

@@ -114,20 +114,8 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     nf4_pair_table_fill(base);
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int i = threadIdx.x; i < m * words; i += blockDim.x) {
-        const __half* src = p.x + (long long)i * 8;   // x is [m][in_f], contiguous
-        uint4 raw;
-        if (p.x_vec) {
-            raw = __ldg(reinterpret_cast<const uint4*>(src));
-        } else {
-            const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
-            raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
-            raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
-            raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
-            raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
-        }
-        xs[i] = raw;
-    }
+    // x is [m][in_f], contiguous: word i of the whole batch is at x + 8i
+    stage_x_words<kXUnroll>(p.x, m * words, p.x_vec, [&](int i, uint4 v) { xs[i] = v; });
     __syncthreads();
 
     // B: this lane carries batch row 4*nb + (g & 3) when (g >> 2) == (q >> 1)

@@ -105,21 +105,7 @@ __device__ __forceinline__ void split_emit(const SplitParams& p, long long b, in
 template <bool PAIR>
 __device__ __forceinline__ void split_stage_x(const SplitParams& p, uint4* xs)
 {
-    const int words = p.in_f >> 3;
-    for (int w = threadIdx.x; w < words; w += blockDim.x) {
-        const __half* src = p.x + (long long)w * 8;
-        uint4 raw;
-        if (p.x_vec) {
-            raw = __ldg(reinterpret_cast<const uint4*>(src));
-        } else {
-            const unsigned short* h = reinterpret_cast<const unsigned short*>(src);
-            raw.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
-            raw.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
-            raw.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
-            raw.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
-        }
-        xs[w] = PAIR ? int4_pair_order(raw) : raw;
-    }
+    stage_x_words<kXUnroll>(p.x, p.in_f >> 3, p.x_vec, [&](int w, uint4 v) { xs[w] = PAIR ? int4_pair_order(v) : v; });
 }
 
 // INT4 g128: a step is G consecutive 128-column groups (G divides in_f/128);
