@@ -7,12 +7,13 @@
 // shared load per byte (two codes), and it yields tensor-core operands:
 //
 //   * the table has a 256-byte row per byte value b (codes b & 15 and b >> 4
-//     of two adjacent columns): 32 copies of the pair's high parts, then 32
-//     copies of its low parts, 4 bytes each, so lane l reads its own copies at
-//     b*256 + 4l and b*256 + 128 + 4l (32 lanes, 32 banks: no conflicts).
-//     PRMT builds that offset from a packed word in one instruction (byte b
-//     of the word into bits 8..15, 4l in bits 0..7); the two 4-byte loads
-//     land in independent registers that the MMA takes as they are.
+//     of two adjacent columns): 32 copies of the 8-byte entry (the pair's
+//     high parts, then its low parts), so lane l reads its own copy at
+//     b*256 + 8l with one 8-byte load (each half-warp covers the 32 banks
+//     once: the two shared-memory wavefronts an 8-byte load takes anyway, no
+//     conflicts).  PRMT builds that offset from a packed word in one
+//     instruction (byte b of the word into bits 8..15, 8l in bits 0..7); the
+//     load's two words are MMA operands as they are.
 //   * the code-book values T are split exactly enough for fp32 work:
 //     high part h = fp16(T) and low part fp16(T - h), stored as half2 pairs.
 //     h + l represents each of the 16 fp32 code-book values (kernels.cuh:78-83)
@@ -44,17 +45,23 @@ namespace b4 {
 
 constexpr int kNf4PairTableBytes = 256 * 256;   // 256 byte values x 32 copies x (4 + 4) bytes
 
-// offset of (byte m of word w) in the table, for the copy at lane*4
+// offset of (byte m of word w) in the table, for the copy at lane*8
 template <int M>
-__device__ __forceinline__ uint32_t nf4_pair_offset(uint32_t w, uint32_t lane4)
+__device__ __forceinline__ uint32_t nf4_pair_offset(uint32_t w, uint32_t lane8)
 {
-    return __byte_perm(w, lane4, 0x5504u | (M << 4));
+    return __byte_perm(w, lane8, 0x5504u | (M << 4));
 }
 
-// The code book: row b = 32 copies of the high-part pair of (T[b & 15],
-// T[b >> 4]), then 32 copies of the low-part pair; one thread per byte value
-// computes its pairs and writes its row.  Called by all threads of a CTA;
-// the caller synchronises before reading.
+// The table entry at `off`: .x = the high-part pair, .y = the low-part pair.
+__device__ __forceinline__ uint2 nf4_pair_lookup(const unsigned char* tb, uint32_t off)
+{
+    return *reinterpret_cast<const uint2*>(tb + off);
+}
+
+// The code book: row b = 32 copies of (high-part pair, low-part pair) of
+// (T[b & 15], T[b >> 4]); one thread per byte value computes its pairs and
+// writes its row.  Called by all threads of a CTA; the caller synchronises
+// before reading.
 __device__ __forceinline__ void nf4_pair_table_fill(unsigned char* base)
 {
     for (int b = threadIdx.x; b < 256; b += blockDim.x) {
@@ -67,11 +74,7 @@ __device__ __forceinline__ void nf4_pair_table_fill(unsigned char* base)
         // the 16-byte chunk order rotates with b: the 8 threads of a store
         // phase write 8 different chunks, hence 8 different bank quads
 #pragma unroll 4
-        for (int c2 = 0; c2 < 16; ++c2) {
-            const int k = (c2 + b) & 15;
-            const uint32_t v = k < 8 ? hw : lw;
-            row[k] = make_uint4(v, v, v, v);
-        }
+        for (int c2 = 0; c2 < 16; ++c2) row[(c2 + b) & 15] = make_uint4(hw, lw, hw, lw);
     }
 }
 
@@ -93,7 +96,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     const int rows_per_tile = p.rg * p.tr;
     const int n_tiles = p.n_tiles;
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
-    const uint32_t lane4 = (uint32_t)lane * 4;
+    const uint32_t lane8 = (uint32_t)lane * 8;
 
     const uint4 *pa = nullptr, *pb = nullptr;
     const float2 *sa_p = nullptr, *sb_p = nullptr;
@@ -201,24 +204,20 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
                         const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
                         uint32_t oa0, oa1, ob0, ob1;
                         if (j & 1) {
-                            oa0 = nf4_pair_offset<2>(ua, lane4);
-                            oa1 = nf4_pair_offset<3>(ua, lane4);
-                            ob0 = nf4_pair_offset<2>(ub, lane4);
-                            ob1 = nf4_pair_offset<3>(ub, lane4);
+                            oa0 = nf4_pair_offset<2>(ua, lane8);
+                            oa1 = nf4_pair_offset<3>(ua, lane8);
+                            ob0 = nf4_pair_offset<2>(ub, lane8);
+                            ob1 = nf4_pair_offset<3>(ub, lane8);
                         } else {
-                            oa0 = nf4_pair_offset<0>(ua, lane4);
-                            oa1 = nf4_pair_offset<1>(ua, lane4);
-                            ob0 = nf4_pair_offset<0>(ub, lane4);
-                            ob1 = nf4_pair_offset<1>(ub, lane4);
+                            oa0 = nf4_pair_offset<0>(ua, lane8);
+                            oa1 = nf4_pair_offset<1>(ua, lane8);
+                            ob0 = nf4_pair_offset<0>(ub, lane8);
+                            ob1 = nf4_pair_offset<1>(ub, lane8);
                         }
-                        const uint32_t a_hi[4] = {*reinterpret_cast<const uint32_t*>(tb + oa0),
-                                                  *reinterpret_cast<const uint32_t*>(tb + ob0),
-                                                  *reinterpret_cast<const uint32_t*>(tb + oa1),
-                                                  *reinterpret_cast<const uint32_t*>(tb + ob1)};
-                        const uint32_t a_lo[4] = {*reinterpret_cast<const uint32_t*>(tb + 128 + oa0),
-                                                  *reinterpret_cast<const uint32_t*>(tb + 128 + ob0),
-                                                  *reinterpret_cast<const uint32_t*>(tb + 128 + oa1),
-                                                  *reinterpret_cast<const uint32_t*>(tb + 128 + ob1)};
+                        const uint2 ea0 = nf4_pair_lookup(tb, oa0), eb0 = nf4_pair_lookup(tb, ob0);
+                        const uint2 ea1 = nf4_pair_lookup(tb, oa1), eb1 = nf4_pair_lookup(tb, ob1);
+                        const uint32_t a_hi[4] = {ea0.x, eb0.x, ea1.x, eb1.x};
+                        const uint32_t a_lo[4] = {ea0.y, eb0.y, ea1.y, eb1.y};
                         // x[32q + 4j .. +3]: halves 0..3 or 4..7 of slot j >> 1
                         const uint4 xq = xv[j >> 1];
                         const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;

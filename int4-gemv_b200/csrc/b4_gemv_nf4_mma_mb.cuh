@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     const int rows_per_tile = p.rg * p.tr;
     const int n_tiles = p.n_tiles;
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
-    const uint32_t lane4 = (uint32_t)lane * 4;
+    const uint32_t lane8 = (uint32_t)lane * 8;
 
     const uint4 *pa = nullptr, *pb = nullptr;
     const float2 *sa_p = nullptr, *sb_p = nullptr;
@@ -157,24 +157,26 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
                         const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
                         uint32_t oa0, oa1, ob0, ob1;
                         if (j & 1) {
-                            oa0 = nf4_pair_offset<2>(ua, lane4);
-                            oa1 = nf4_pair_offset<3>(ua, lane4);
-                            ob0 = nf4_pair_offset<2>(ub, lane4);
-                            ob1 = nf4_pair_offset<3>(ub, lane4);
+                            oa0 = nf4_pair_offset<2>(ua, lane8);
+                            oa1 = nf4_pair_offset<3>(ua, lane8);
+                            ob0 = nf4_pair_offset<2>(ub, lane8);
+                            ob1 = nf4_pair_offset<3>(ub, lane8);
                         } else {
-                            oa0 = nf4_pair_offset<0>(ua, lane4);
-                            oa1 = nf4_pair_offset<1>(ua, lane4);
-                            ob0 = nf4_pair_offset<0>(ub, lane4);
-                            ob1 = nf4_pair_offset<1>(ub, lane4);
+                            oa0 = nf4_pair_offset<0>(ua, lane8);
+                            oa1 = nf4_pair_offset<1>(ua, lane8);
+                            ob0 = nf4_pair_offset<0>(ub, lane8);
+                            ob1 = nf4_pair_offset<1>(ub, lane8);
                         }
-                        a_hi[j][0] = *reinterpret_cast<const uint32_t*>(tb + oa0);
-                        a_hi[j][1] = *reinterpret_cast<const uint32_t*>(tb + ob0);
-                        a_hi[j][2] = *reinterpret_cast<const uint32_t*>(tb + oa1);
-                        a_hi[j][3] = *reinterpret_cast<const uint32_t*>(tb + ob1);
-                        a_lo[j][0] = *reinterpret_cast<const uint32_t*>(tb + 128 + oa0);
-                        a_lo[j][1] = *reinterpret_cast<const uint32_t*>(tb + 128 + ob0);
-                        a_lo[j][2] = *reinterpret_cast<const uint32_t*>(tb + 128 + oa1);
-                        a_lo[j][3] = *reinterpret_cast<const uint32_t*>(tb + 128 + ob1);
+                        const uint2 ea0 = nf4_pair_lookup(tb, oa0), eb0 = nf4_pair_lookup(tb, ob0);
+                        const uint2 ea1 = nf4_pair_lookup(tb, oa1), eb1 = nf4_pair_lookup(tb, ob1);
+                        a_hi[j][0] = ea0.x;
+                        a_hi[j][1] = eb0.x;
+                        a_hi[j][2] = ea1.x;
+                        a_hi[j][3] = eb1.x;
+                        a_lo[j][0] = ea0.y;
+                        a_lo[j][1] = eb0.y;
+                        a_lo[j][2] = ea1.y;
+                        a_lo[j][3] = eb1.y;
                     }
                     const float am_a = hi_blk ? ama[d].y : ama[d].x;
                     const float am_b = hi_blk ? amb[d].y : amb[d].x;

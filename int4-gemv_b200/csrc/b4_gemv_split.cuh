@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_split_nf4_kernel(const SplitPa
     const int warp = threadIdx.x >> 5;
     const int words = p.in_f >> 3;
     const int nblk = p.in_f >> 6;
-    const uint32_t lane4 = (uint32_t)lane * 4;
+    const uint32_t lane8 = (uint32_t)lane * 8;
     const int warp_id = blockIdx.x * 8 + warp;
     const long long u0 = (long long)warp_id * p.per;
     const long long u1 = min(u0 + p.per, p.total);
@@ -314,24 +314,20 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_split_nf4_kernel(const SplitPa
                     const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
                     uint32_t oa0, oa1, ob0, ob1;
                     if (j & 1) {
-                        oa0 = nf4_pair_offset<2>(ua, lane4);
-                        oa1 = nf4_pair_offset<3>(ua, lane4);
-                        ob0 = nf4_pair_offset<2>(ub, lane4);
-                        ob1 = nf4_pair_offset<3>(ub, lane4);
+                        oa0 = nf4_pair_offset<2>(ua, lane8);
+                        oa1 = nf4_pair_offset<3>(ua, lane8);
+                        ob0 = nf4_pair_offset<2>(ub, lane8);
+                        ob1 = nf4_pair_offset<3>(ub, lane8);
                     } else {
-                        oa0 = nf4_pair_offset<0>(ua, lane4);
-                        oa1 = nf4_pair_offset<1>(ua, lane4);
-                        ob0 = nf4_pair_offset<0>(ub, lane4);
-                        ob1 = nf4_pair_offset<1>(ub, lane4);
+                        oa0 = nf4_pair_offset<0>(ua, lane8);
+                        oa1 = nf4_pair_offset<1>(ua, lane8);
+                        ob0 = nf4_pair_offset<0>(ub, lane8);
+                        ob1 = nf4_pair_offset<1>(ub, lane8);
                     }
-                    const uint32_t a_hi[4] = {*reinterpret_cast<const uint32_t*>(tb + oa0),
-                                              *reinterpret_cast<const uint32_t*>(tb + ob0),
-                                              *reinterpret_cast<const uint32_t*>(tb + oa1),
-                                              *reinterpret_cast<const uint32_t*>(tb + ob1)};
-                    const uint32_t a_lo[4] = {*reinterpret_cast<const uint32_t*>(tb + 128 + oa0),
-                                              *reinterpret_cast<const uint32_t*>(tb + 128 + ob0),
-                                              *reinterpret_cast<const uint32_t*>(tb + 128 + oa1),
-                                              *reinterpret_cast<const uint32_t*>(tb + 128 + ob1)};
+                    const uint2 ea0 = nf4_pair_lookup(tb, oa0), eb0 = nf4_pair_lookup(tb, ob0);
+                    const uint2 ea1 = nf4_pair_lookup(tb, oa1), eb1 = nf4_pair_lookup(tb, ob1);
+                    const uint32_t a_hi[4] = {ea0.x, eb0.x, ea1.x, eb1.x};
+                    const uint32_t a_lo[4] = {ea0.y, eb0.y, ea1.y, eb1.y};
                     const uint4 xq = xv[j >> 1];
                     const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
                     const int ch = (j & 1) * 2;
