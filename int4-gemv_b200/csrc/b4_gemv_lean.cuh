@@ -9,9 +9,11 @@
 //   * x is staged once per CTA in pair order at its natural word index: the
 //     64 bytes lane q needs for group G are words 16*G + 4q .. 16*G + 4q + 3,
 //     so one pointer bump per stage and four 16-byte loads with immediate
-//     offsets per group fetch all B fragments (m = 1: every batch column of B
-//     holds x, all lanes read; the 8 lanes with the same q read the same
-//     address);
+//     offsets per group fetch the B fragments.  m = 1: only column 0 of B
+//     holds x (lanes g = 0 load it, the others hold zeros), since only
+//     D[row][0] is used: a 16-byte x load then costs one shared-memory
+//     wavefront instead of four, which took x from half of the kernel's
+//     shared-memory traffic to a sixth;
 //   * rows past out_f are clamped to a valid row for loading and never
 //     stored, so the loop has no row predicates;
 //   * codes and scales are addressed by running pointers, bumped once per
@@ -19,8 +21,8 @@
 //     so the scales of a stage are one 2-, 4- or 8-byte load per row;
 //   * a D-deep software pipeline, unrolled so every buffer index is a
 //     compile-time constant, keeps D-1 stages per lane in flight;
-//   * the group epilogue is two fp32 adds and two FMAs per lane: with all B
-//     columns equal, D[row][0] holds the row's partial sum.
+//   * the group epilogue is two fp32 adds and two FMAs per lane: D[row][0]
+//     (lanes q = 0) holds the row's partial sum.
 // Work split as in the other kernels: warps_k warps share a 16-row MMA block
 // and take stages ks, ks + warps_k, ...; CTAs loop over tiles of rg blocks.
 // Only the first tr rows of a block carry weights (tr = 16 unless a matrix
@@ -277,7 +279,13 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                             wav = bufa[d];
                             wbv = bufb[d];
                         }
-                        const uint4 xv[4] = {xp[16 * h + 0], xp[16 * h + 1], xp[16 * h + 2], xp[16 * h + 3]};
+                        // B column 0 = x (lanes g = 0), columns 1..7 zero
+                        uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                                       make_uint4(0, 0, 0, 0)};
+                        if (g == 0) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) xv[i] = xp[16 * h + i];
+                        }
                         float ua, ub;
                         lean_group(wav, wbv, xv, ua, ub);
                         acc_a = fmaf(ua, sa[h], acc_a);

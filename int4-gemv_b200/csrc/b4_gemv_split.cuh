@@ -195,7 +195,13 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_split_int4_kernel(const SplitP
                 for (int h = 0; h < G; ++h) {
                     const uint4 wav = ring[((d * G + h) * 2) * 32 + lane];
                     const uint4 wbv = ring[((d * G + h) * 2 + 1) * 32 + lane];
-                    const uint4 xv[4] = {xp[16 * h + 0], xp[16 * h + 1], xp[16 * h + 2], xp[16 * h + 3]};
+                    // B column 0 = x (lanes g = 0), columns 1..7 zero
+                    uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                                   make_uint4(0, 0, 0, 0)};
+                    if (g == 0) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) xv[i] = xp[16 * h + i];
+                    }
                     float ua, ub;
                     lean_group(wav, wbv, xv, ua, ub);
                     acc_a = fmaf(ua, sa[h], acc_a);
