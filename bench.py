@@ -385,10 +385,14 @@ def empty_launch_floor(b4, torch, reps=200):
     return round(sorted(t)[len(t) // 2], 3)
 
 
-def e2e_steps(b4, torch, sets, xs, ys, n_steps):
+def e2e_steps(b4, torch, sets, xs, ys, n_steps, graph=True):
     """End to end through the public API with host buffers: every step copies
     its x (all seven projections, pinned host) to the device, runs the seven
-    GEMVs through b4gemv.gemv_nf4 (the C ABI), copies y back and reads it."""
+    GEMVs through b4gemv.gemv_nf4 (the C ABI), copies y back and reads it.
+    With `graph`, the seven b4gemv.gemv_nf4 calls of each weight set are
+    captured once in a CUDA graph (as a decode loop runs them) and every step
+    replays one between its copies; without, every step calls the Python API
+    seven times (its host cost included)."""
     in_sizes = [in_f for _, _, in_f in SHAPES]
     out_sizes = [out_f for _, out_f, _ in SHAPES]
     hx = torch.empty(sum(in_sizes), dtype=torch.float16).pin_memory()
@@ -406,12 +410,32 @@ def e2e_steps(b4, torch, sets, xs, ys, n_steps):
         o += n
     checksum = 0.0
 
+    def gemvs(s, stream=None):
+        for i in range(len(SHAPES)):
+            qw, sc = sets[s % N_SETS][i]
+            b4.gemv_nf4(qw, sc, xv[i], yv[i], stream=stream)
+
+    graphs = []
+    if graph:
+        for k in range(N_SETS):
+            gemvs(k)                      # eager first: configs and caches settle outside capture
+        torch.cuda.synchronize()
+        for k in range(N_SETS):
+            g = torch.cuda.CUDAGraph()
+            cs = torch.cuda.Stream()
+            cs.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(g, stream=cs):
+                gemvs(k, cs)
+            torch.cuda.current_stream().wait_stream(cs)
+            graphs.append(g)
+
     def one(s):
         nonlocal checksum
         dx.copy_(hx, non_blocking=True)
-        for i in range(len(SHAPES)):
-            qw, sc = sets[s % N_SETS][i]
-            b4.gemv_nf4(qw, sc, xv[i], yv[i])
+        if graph:
+            graphs[s % N_SETS].replay()
+        else:
+            gemvs(s)
         hy.copy_(dy, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         checksum += float(hy[0])
@@ -673,6 +697,8 @@ def run_ours(args, d):
     e2e_n = max(3, min(K, 200))
     e2e_ms, h2d, d2h = e2e_steps(b4, torch, sets, xs, ys, e2e_n)
     e2e_ms_max = d.max(e2e_ms, dev)
+    e2e_eager_ms, _, _ = e2e_steps(b4, torch, sets, xs, ys, e2e_n, graph=False)
+    e2e_eager_ms_max = d.max(e2e_eager_ms, dev)
 
     # detail: the reference's isolated-launch protocol and the launch floor
     iso = isolated_launches(torch, plain)
@@ -711,8 +737,11 @@ def run_ours(args, d):
                      "traffic": traffic},
         "e2e": {"value": round(n * e2e_n * STEP_BYTES / (e2e_ms_max / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "how": "public API b4gemv.gemv_nf4 -> C ABI per GEMV; pinned x copied in and y copied out "
-                       "and read on the host every step", "steps": e2e_n},
+                "how": "public API b4gemv.gemv_nf4 -> C ABI per GEMV, the seven calls of a step captured once "
+                       "in a CUDA graph and replayed; pinned x copied in and y copied out and read on the host "
+                       "every step", "steps": e2e_n,
+                "eager_value": round(n * e2e_n * STEP_BYTES / (e2e_eager_ms_max / 1e3) / 1e9, 2),
+                "eager_how": "the same with the seven b4gemv.gemv_nf4 Python calls made every step"},
         "isolated_launch_us": iso,
         "empty_launch_floor_us": floor,
         "gpu_launches": K * len(SHAPES),

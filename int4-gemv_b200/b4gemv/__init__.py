@@ -151,13 +151,18 @@ _WS_SIZE = {}
 _WS = {}
 
 
-def workspace_size(fmt: int, in_f: int, out_f: int, m: int = 1, config: dict | None = None) -> int:
-    """b4_gemv_workspace_size on the current device: bytes of workspace
-    b4_gemv_ws needs for this shape (0 when the config does not split)."""
+def workspace_size(fmt: int, in_f: int, out_f: int, m: int = 1, config: dict | None = None, device=None) -> int:
+    """b4_gemv_workspace_size on the current device (or `device`, an index):
+    bytes of workspace b4_gemv_ws needs for this shape (0 when the config does
+    not split).  Rule answers are cached per (shape, device)."""
     import torch
-    key = (fmt, in_f, out_f, m, torch.cuda.current_device()) if config is None else None
-    if key is not None and key in _WS_SIZE:
-        return _WS_SIZE[key]
+    if config is None:
+        key = (fmt, in_f, out_f, m, torch.cuda.current_device() if device is None else device)
+        n = _WS_SIZE.get(key)
+        if n is not None:
+            return n
+    else:
+        key = None
     cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
     n = ctypes.c_size_t(0)
     check("b4_gemv_workspace_size", load().b4_gemv_workspace_size(fmt, in_f, out_f, m, cfg, ctypes.byref(n)))
@@ -187,7 +192,7 @@ def gemv_ws(fmt: int, qw, scale, x, y=None, config: dict | None = None, ws=None,
     CUDA uint8 tensor of at least workspace_size() bytes, or None for the
     package's per-device workspace."""
     out_f, in_f, m, x2, y = _gemv_args(qw, scale, x, y)
-    need = workspace_size(fmt, in_f, out_f, m, config)
+    need = workspace_size(fmt, in_f, out_f, m, config, qw.device.index)
     if ws is None and need:
         ws = workspace(qw.device, need)
     cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None

@@ -263,11 +263,14 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
         return;
     }
     if (p.m == 1 && p.fmt == kNf4 && aligned(p.qw, 16) && aligned(p.scale, 4) && words % 4 == 0) {
-        // long rows or many rows: the replicated pair-table code book; q/k/v/o:
-        // the shuffle code book with more, smaller tiles
-        const bool big = p.out_f >= 8192 || p.in_f >= 8192;
+        // many rows or rows longer than 8192 columns: bigger tiles; rows longer
+        // than 8192 columns: the replicated pair-table code book, else the
+        // shuffle code book (refitted on B200 PDL chains: Llama-3-70B k/v
+        // 1024x8192 7.1 -> 5.2 us and q/o 8192x8192 18.0 -> 17.0 us; Qwen down
+        // 3584x18944 and 8192x28672 keep the pair table)
+        const bool big = p.out_f >= 8192 || p.in_f > 8192;
         const int vw = p.in_f >= 8192 ? 4 : 2;
-        const int lut = big ? 2 : 0;
+        const int lut = p.in_f > 8192 ? 2 : 0;
         const int quads = (p.out_f + 3) / 4;
         const int rg = std::max(1, std::min(8, quads / (big ? sms / 2 : 224)));
         const size_t smem = lean_nf4_smem(p.in_f, 8 / rg, rg, 4, vw, 4, lut);
