@@ -24,8 +24,12 @@ from . import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, chec
 
 SHAPES = {"q_proj": (3584, 3584), "k_proj": (512, 3584), "v_proj": (512, 3584), "o_proj": (3584, 3584),
           "gate_proj": (18944, 3584), "up_proj": (18944, 3584), "down_proj": (3584, 18944),
-          # Llama-3-70B layer and its tensor-parallel shards
-          "l70_qo": (8192, 8192), "l70_kv": (1024, 8192), "l70_gu": (28672, 8192), "l70_down": (8192, 28672)}
+          # Llama-3-70B layer and its tensor-parallel shards (column-parallel rows, row-parallel columns)
+          "l70_qo": (8192, 8192), "l70_kv": (1024, 8192), "l70_gu": (28672, 8192), "l70_down": (8192, 28672),
+          "tp2_q": (4096, 8192), "tp2_kv": (512, 8192), "tp2_gu": (14336, 8192), "tp2_o": (8192, 4096),
+          "tp2_down": (8192, 14336), "tp4_q": (2048, 8192), "tp4_gu": (7168, 8192), "tp4_o": (8192, 2048),
+          "tp4_down": (8192, 7168), "tp8_q": (1024, 8192), "tp8_gu": (3584, 8192), "tp8_o": (8192, 1024),
+          "tp8_down": (8192, 3584)}
 L2_BYTES = 126 * 1024 * 1024
 WS_BYTES = 8 << 20   # workspace for the split configs (the largest shape here needs < 1 MiB)
 

@@ -166,30 +166,29 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     cfg->stage_groups = 4;
     cfg->tile_rows = 0;
 
-    // Batch 1 (fitted on B200 with `b4gemv.diag sweep`, plain and programmatic
-    // dependent launches; the reference's rule was fitted on a 36-SM part,
-    // int4_gemv.cu:52-53): the lean kernels.  CTAs of 8 warps; warps split
-    // in_f (warps_k) when there are too few rows to give every SM two CTAs of
-    // whole row tiles.
+    // Batch 1 (fitted on B200 with `b4gemv.diag sweep --pdl` over the Qwen2.5-7B,
+    // Llama-3-70B and tensor-parallel shard shapes; the reference's rule was
+    // fitted on a 36-SM part, int4_gemv.cu:52-53): the lean kernel with the
+    // cp.async ring, CTAs of 8 warps, and the fewest row groups per CTA (a
+    // power of two, so warps_k * row_groups = 8) that still gives one tile per
+    // CTA with every CTA resident at once (2 per SM).  A tile count just above
+    // the resident CTAs costs a second wave for a handful of tiles (Llama-3-70B
+    // gate/up had 299 tiles: 34.9 us, now 27.6 us), and several tiles per CTA
+    // restart the ring per tile.  Rows longer than 8192 columns on fewer 16-row
+    // blocks than resident CTAs use thinner tiles instead (down_proj).
     if (p.m == 1 && p.fmt == kInt4 && aligned(p.qw, 16)) {
         const int ng = p.in_f / kGroup;
-        const int row_groups = (p.out_f + 15) / 16;
-        const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
+        const long long blocks = (p.out_f + 15) / 16;
+        int rg = 1;
+        while (rg < 8 && (blocks + rg - 1) / rg > 2LL * sms) rg *= 2;
         cfg->vec_words = 4;
         cfg->rows_per_warp = 16;
         cfg->batch_tile = 1;
         cfg->warps_k = 8 / rg;
         cfg->row_groups = rg;
-        cfg->tile_rows = even_tile_rows(p.out_f, rg, sms);
-        // up to 2*148 tiles of 16 rows (q/k/v/o): the register pipeline, no ring
-        if (rg == 1 && p.in_f <= 8192) {
-            cfg->engine = B4_ENGINE_MMA_LEAN;
-            cfg->stages = 4;
-            cfg->stage_groups = 1;
-            return;
-        }
-        // larger: the cp.async ring, as many groups per stage as divide the
-        // row while two CTAs still fit in shared memory
+        cfg->tile_rows = p.in_f > 8192 ? even_tile_rows(p.out_f, rg, sms) : 0;
+        // two stages of four groups where two CTAs still fit in shared memory
+        // (within 2 % of the best ring on every swept shape), else fewer groups
         const int variants[3][2] = {{2, 4}, {3, 2}, {4, 1}};   // (stages, groups per stage)
         for (int pass = 0; pass < 2; ++pass) {
             for (const auto& v : variants) {
@@ -245,13 +244,18 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
             return;
         }
     }
-    // NF4 at batch 1, q/o/gate/up-like (in_f < 8192, at least 2048 rows): the
-    // tensor-pipe engine; its 64 KB code-book table costs more than it saves
-    // on narrow (k/v) or long-row (down) matrices.
-    if (p.m == 1 && p.fmt == kNf4 && p.in_f % 128 == 0 && p.in_f < 8192 && p.out_f >= 2048 && aligned(p.qw, 16) &&
+    // NF4 at batch 1, q/o/gate/up-like (in_f < 8192, or 8192 on at most one
+    // resident tile per CTA: the tensor-parallel q and gate/up shards, 5 %
+    // faster there; at least 2048 rows): the tensor-pipe engine; its 64 KB
+    // code-book table costs more than it saves on narrow (k/v) or long-row
+    // (down) matrices.
+    const bool nf4_mma_shape = p.in_f < 8192 || (p.in_f == 8192 && (p.out_f + 15) / 16 <= 2 * sms);
+    if (p.m == 1 && p.fmt == kNf4 && p.in_f % 128 == 0 && nf4_mma_shape && p.out_f >= 2048 && aligned(p.qw, 16) &&
         aligned(p.scale, 8) && nf4_mma_smem(p.in_f, 8, 1) <= kTmaSmemLimit) {
-        const int row_groups = (p.out_f + 15) / 16;
-        const int rg = std::max(1, std::min(8, row_groups / (2 * sms)));
+        // the fewest row groups (a power of two) that give one resident tile per CTA
+        const long long blocks = (p.out_f + 15) / 16;
+        int rg = 1;
+        while (rg < 8 && (blocks + rg - 1) / rg > 2LL * sms) rg *= 2;
         cfg->engine = B4_ENGINE_MMA_NF4;
         cfg->vec_words = 4;
         cfg->rows_per_warp = 16;
@@ -1021,29 +1025,15 @@ int launch_split(const GemvProblem& p, const b4_gemv_config& c, void* ws, size_t
 
 void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
 {
+    // Measured on B200 (`b4gemv.diag sweep --split-only --pdl`): the split's
+    // cross-CTA sum costs ~2 us at the kernel's end (store, fence, atomic, then
+    // the last arriver's L2 reads), and once the tile rule gives every CTA one
+    // resident tile no batch-1 shape ran faster split (INT4 8192x8192: 11.3 us
+    // split, 8.8 us with two 16-row blocks per CTA; Qwen q/o 6.4 vs 3.4 us,
+    // down 13.2 vs 10.5 us; NF4 gate 16.8 vs 14.2 us).  The rule of b4_gemv_ws
+    // is therefore b4_gemv_default_config's; split configs are taken when
+    // passed explicitly.
     default_config(p, cfg);
-    // Fitted on B200 (`b4gemv.diag sweep --split-only --pdl`): the split's
-    // cross-CTA sum costs ~2 us at the kernel's end (fence, atomic, L2 reads),
-    // so it pays only where whole-row tiles run between one and two waves
-    // (296 < 16-row blocks < 592) on rows short enough that the second wave
-    // is a large share of the time: INT4 8192x8192 (Llama-3-70B q/o) 14.9 ->
-    // 12.5 us.  Qwen q/o (224 blocks) ran 3.8 -> 6.5 us split, down_proj and
-    // 8192x28672 no faster, and NF4 never faster.
-    const int sms = 148;
-    const long long blocks = (p.out_f + 15) / 16;
-    if (p.m != 1 || p.fmt != kInt4 || blocks <= 2LL * sms || blocks >= 4LL * sms || p.in_f > 8192) return;
-    const int ng = p.in_f / kGroup;
-    if (!aligned(p.qw, 16) || ng % 4 || !aligned(p.scale, 8)) return;
-    cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
-    cfg->stage_groups = 4;
-    cfg->stages = 2;
-    cfg->vec_words = 4;
-    cfg->rows_per_warp = 16;
-    cfg->batch_tile = 1;
-    cfg->warps_k = 1;
-    cfg->row_groups = 8;
-    cfg->tile_rows = 0;
-    cfg->flags |= B4_FLAG_SPLIT;
 }
 
 }  // namespace b4

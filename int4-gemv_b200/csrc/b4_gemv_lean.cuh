@@ -168,10 +168,14 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
     const int wstep = 4 * G * p.kw;                          // uint4 per stage step
 
+    // ASYNC: scales run SD - 1 stages ahead of their use (codes D - 1): a
+    // scale is one small global load whose latency the codes' cp.async ring
+    // does not hide, and a stage of 4 groups is only ~0.3 us of work
+    constexpr int SD = ASYNC ? 2 * D : D;
     const uint4 *pa = nullptr, *pb = nullptr;
     const ST *sa_p = nullptr, *sb_p = nullptr;
     uint4 bufa[ASYNC ? 1 : D] = {}, bufb[ASYNC ? 1 : D] = {};
-    ST bsa[D] = {}, bsb[D] = {};
+    ST bsa[SD] = {}, bsb[SD] = {};
     int r0 = 0, out_f = 0;
     bool va = false, vb = false;   // this lane's rows r0+g, r0+g+8 carry weights
     float* y = nullptr;
@@ -220,14 +224,19 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                 bufb[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
             }
         }
-        if (va) bsa[slot] = __ldg(sa_p);
-        if (vb) bsb[slot] = __ldg(sb_p);
         pa += wstep;
         pb += wstep;
+    };
+    auto fetch_scales = [&](int slot) {
+        if (va) bsa[slot] = __ldg(sa_p);
+        if (vb) bsb[slot] = __ldg(sb_p);
         sa_p += p.kw;
         sb_p += p.kw;
     };
     auto prologue = [&]() {
+#pragma unroll
+        for (int d = 0; d < SD - 1; ++d)
+            if (d < n_it) fetch_scales(d);
 #pragma unroll
         for (int d = 0; d < D - 1; ++d) {
             if (d < n_it) fetch(d);
@@ -254,17 +263,18 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
         float acc_a = 0.0f, acc_b = 0.0f;
         const uint4* xp = xs + ks * 16 * G + q * 4;          // + 16*G*kw per stage step
 
-        for (int it0 = 0; it0 < n_it; it0 += D) {
+        for (int it0 = 0; it0 < n_it; it0 += SD) {   // SD is a multiple of D
 #pragma unroll
-            for (int d = 0; d < D; ++d) {
+            for (int d = 0; d < SD; ++d) {
                 const int it = it0 + d;
                 if (it < n_it) {
-                    // refill the stage consumed in the previous step
-                    const int nxt = (d + D - 1) % D;   // a constant once unrolled
+                    // refill the stage consumed in the previous step (constant slots once unrolled)
+                    const int cs = d % D, nxt = (d + D - 1) % D;
                     if (it + D - 1 < n_it) fetch(nxt);
+                    if (it + SD - 1 < n_it) fetch_scales((d + SD - 1) % SD);
                     if constexpr (ASYNC) {
                         cp_async_commit();
-                        cp_async_wait<D - 1>();            // this lane's copies of stage d landed
+                        cp_async_wait<D - 1>();            // this lane's copies of stage it landed
                     }
                     float sa[G], sb[G];
                     lean_scales_to_f32<G>(bsa[d], sa);
@@ -273,11 +283,11 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                     for (int h = 0; h < G; ++h) {
                         uint4 wav, wbv;
                         if constexpr (ASYNC) {
-                            wav = ring[((d * G + h) * 2) * 32 + lane];
-                            wbv = ring[((d * G + h) * 2 + 1) * 32 + lane];
+                            wav = ring[((cs * G + h) * 2) * 32 + lane];
+                            wbv = ring[((cs * G + h) * 2 + 1) * 32 + lane];
                         } else {
-                            wav = bufa[d];
-                            wbv = bufb[d];
+                            wav = bufa[cs];
+                            wbv = bufb[cs];
                         }
                         // B column 0 = x (lanes g = 0), columns 1..7 zero
                         uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),

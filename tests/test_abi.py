@@ -176,23 +176,30 @@ def test_median_is_the_reference_upper_median():
 @pytest.mark.parametrize("fmt", [0, 1])
 @pytest.mark.parametrize("out_f,in_f", QWEN + LLAMA_TP)
 @pytest.mark.parametrize("m", [1, 2, 16])
-def test_workspace_rule_splits_only_where_fitted(fmt, out_f, in_f, m):
-    """b4_gemv_default_config_ws: b4_gemv_default_config's choice, or a split
-    INT4 config for batch-1 matrices of 297..591 row blocks and in_f <= 8192."""
+def test_workspace_rule_is_the_plain_rule(fmt, out_f, in_f, m):
+    """b4_gemv_default_config_ws: no measured shape ran faster split, so the
+    rule of b4_gemv_ws is b4_gemv_default_config's (split only when asked)."""
     c = b4gemv.default_config_ws(fmt, in_f, out_f, m)
+    assert not c["flags"] & b4gemv.FLAG_SPLIT
+    assert c == b4gemv.default_config(fmt, in_f, out_f, m)
+
+
+@pytest.mark.parametrize("out_f,in_f", QWEN + LLAMA_TP)
+def test_batch1_int4_rule_gives_one_resident_tile_per_cta(out_f, in_f):
+    """Batch-1 INT4: the cp.async-ring engine with 8-warp CTAs and the fewest
+    power-of-two row groups whose tiles fit the 2 x 148 resident CTAs."""
+    c = b4gemv.default_config(0, in_f, out_f, 1)
     blocks = (out_f + 15) // 16
-    split = bool(c["flags"] & b4gemv.FLAG_SPLIT)
-    assert split == (fmt == 0 and m == 1 and 296 < blocks < 592 and in_f <= 8192 and (in_f // 128) % 4 == 0)
-    if split:
-        assert c["engine"] == 5 and (c["stages"], c["stage_groups"]) == (2, 4)
-    else:
-        assert c == b4gemv.default_config(fmt, in_f, out_f, m)
+    assert c["engine"] == 5 and c["warps_k"] * c["row_groups"] == 8 and c["row_groups"] in (1, 2, 4, 8)
+    rg = c["row_groups"]
+    tiles = -(-blocks // rg)
+    assert tiles <= 296 or rg == 8
+    assert rg == 1 or -(-blocks // (rg // 2)) > 296
 
 
 def test_split_flag_needs_the_workspace_entry_point():
     """b4_gemv_ex has no workspace: a split config is rejected before any device call."""
     lib = b4gemv.load()
-    c = _lib.GemvConfig.from_dict(b4gemv.default_config_ws(0, 8192, 8192, 1))
-    assert c.flags & b4gemv.FLAG_SPLIT
+    c = _lib.GemvConfig.from_dict(dict(b4gemv.default_config(0, 8192, 8192, 1), flags=b4gemv.FLAG_SPLIT))
     p = ctypes.c_void_p(4096)
     assert lib.b4_gemv_ex(0, p, p, p, p, 8192, 8192, 1, ctypes.byref(c), None) == 1

@@ -41,15 +41,14 @@ def fresh_ws(cuda, fmt, in_f, out_f, cfg=None):
     return torch.zeros(n, dtype=torch.uint8, device=cuda)
 
 
-def test_rule_splits_one_to_two_wave_int4_shapes(cuda, oracle):
-    fmt, out_f, in_f = 0, 8192, 8192      # Llama-3-70B q/o: 512 blocks, 1.7 waves of whole-row tiles
-    assert b4gemv.workspace_size(fmt, in_f, out_f) > 0
-    assert b4gemv.default_config_ws(fmt, in_f, out_f)["flags"] & b4gemv.FLAG_SPLIT
-    rng = np.random.default_rng(300)
+@pytest.mark.parametrize("fmt,out_f,in_f", [(0, 8192, 8192), (0, 3584, 3584), (1, 3584, 18944)])
+def test_explicit_split_matches_the_rule_and_oracle(cuda, oracle, fmt, out_f, in_f):
+    rng = np.random.default_rng(300 + fmt + out_f)
     W, X = rand_problem(rng, out_f, in_f)
     qw, sc = quantised(fmt, W, cuda)
-    ws = fresh_ws(cuda, fmt, in_f, out_f)
-    y = b4gemv.gemv_ws(fmt, qw, sc, to_dev(X, cuda), ws=ws).cpu().numpy()
+    cfg = split_config(fmt, 2 if fmt == 0 else 3, 4 if fmt == 0 else 1)
+    ws = fresh_ws(cuda, fmt, in_f, out_f, cfg)
+    y = b4gemv.gemv_ws(fmt, qw, sc, to_dev(X, cuda), config=cfg, ws=ws).cpu().numpy()
     ref = f64_ref(oracle, fmt, qw, sc, X)
     assert rel_err(y, ref) < TOL
     y0 = (b4gemv.gemv_int4 if fmt == 0 else b4gemv.gemv_nf4)(qw, sc, to_dev(X, cuda), split=False).cpu().numpy()
@@ -60,11 +59,12 @@ def test_rule_splits_one_to_two_wave_int4_shapes(cuda, oracle):
 
 @pytest.mark.parametrize("name", list(QWEN))
 def test_rule_does_not_split_where_it_does_not_pay(cuda, name):
+    """No batch-1 shape measured faster split once every CTA has one resident tile."""
     out_f, in_f = QWEN[name]
     for fmt in (0, 1):
         assert b4gemv.workspace_size(fmt, in_f, out_f) == 0
-    assert b4gemv.workspace_size(1, 8192, 8192) == 0       # NF4: never faster split
-    assert b4gemv.workspace_size(0, 28672, 8192) == 0      # long rows: no faster split
+        assert b4gemv.workspace_size(fmt, 8192, 8192) == 0
+        assert b4gemv.workspace_size(fmt, 28672, 8192) == 0
 
 
 @pytest.mark.parametrize("stages,groups", INT4_VARIANTS)
@@ -153,19 +153,22 @@ def test_split_argument_checks(cuda):
     Xd = to_dev(X, cuda)
     y = torch.empty((1, out_f), dtype=torch.float32, device=cuda)
     lib = load()
-    need = b4gemv.workspace_size(0, in_f, out_f)
+    cfg_d = split_config(0, 2, 4)
+    cfg = GemvConfig.from_dict(cfg_d)
+    need = b4gemv.workspace_size(0, in_f, out_f, 1, cfg_d)
+    assert need > 0
     ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
     p = ctypes.c_void_p
     args = (0, p(qw.data_ptr()), p(sc.data_ptr()), p(Xd.data_ptr()), p(y.data_ptr()), in_f, out_f, 1)
     st = p(torch.cuda.current_stream().cuda_stream)
     # too small, missing or misaligned workspace: rejected before any launch
-    assert lib.b4_gemv_ws(*args, None, p(ws.data_ptr()), need - 1, st) == 1
-    assert lib.b4_gemv_ws(*args, None, None, 0, st) == 1
-    assert lib.b4_gemv_ws(*args, None, p(ws.data_ptr() + 4), need - 4, st) == 1
+    assert lib.b4_gemv_ws(*args, ctypes.byref(cfg), p(ws.data_ptr()), need - 1, st) == 1
+    assert lib.b4_gemv_ws(*args, ctypes.byref(cfg), None, 0, st) == 1
+    assert lib.b4_gemv_ws(*args, ctypes.byref(cfg), p(ws.data_ptr() + 4), need - 4, st) == 1
     # the split flag needs the workspace entry point
-    cfg = GemvConfig.from_dict(split_config(0, 4, 2))
     assert lib.b4_gemv_ex(*args, ctypes.byref(cfg), st) == 1
-    # batch > 1 never splits: no workspace needed
+    # batch > 1 never splits, nor does the rule: no workspace needed
     assert b4gemv.workspace_size(0, in_f, out_f, 2) == 0
-    assert lib.b4_gemv_ws(*args, None, p(ws.data_ptr()), need, st) == 0
+    assert lib.b4_gemv_ws(*args, None, None, 0, st) == 0
+    assert lib.b4_gemv_ws(*args, ctypes.byref(cfg), p(ws.data_ptr()), need, st) == 0
     torch.cuda.synchronize()
