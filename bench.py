@@ -489,13 +489,22 @@ def small_batch_bench(b4, torch):
         for name, out_f, in_f in (("gate_proj", 18944, 3584), ("down_proj", 3584, 18944)):
             for m in (1, 2, 4, 8, 16):
                 prob = Problem(torch, fmt, out_f, in_f, m=m)
-                cfg = b4.GemvConfig.from_dict(b4.default_config(fmt, in_f, out_f, m))
-                cfg.flags = b4.FLAG_PDL
+                rule = b4.default_config(fmt, in_f, out_f, m)
+                # the rule as the entry points run it (B4_ENGINE_AUTO: batch chunks where x
+                # does not fit the tensor-pipe engines), each launch a programmatic dependent
+                cfg = b4.GemvConfig.from_dict(dict(rule, engine=-1, flags=b4.FLAG_PDL))
                 us = time_chained(torch, prob, cfg)
+                engine, launches = rule["engine"], 1
+                if m > 1 and engine not in (5, 7):   # the entry points' batch chunks
+                    for mc in (8, 4, 2):
+                        e = b4.default_config(fmt, in_f, out_f, mc)["engine"] if mc < m else -1
+                        if e in (5, 7):
+                            engine, launches = e, -(-m // mc)
+                            break
                 nb = alg_bytes(fmt, out_f, in_f, m)
                 out.append({"format": "int4_g128" if fmt == 0 else "nf4_b64", "shape": name, "m": m,
-                            "engine": cfg.engine, "us": round(us, 3), "gbs": round(nb / us / 1e3, 1),
-                            "tflops": round(2.0 * m * out_f * in_f / us / 1e6, 2)})
+                            "engine": engine, "launches": launches, "us": round(us, 3),
+                            "gbs": round(nb / us / 1e3, 1), "tflops": round(2.0 * m * out_f * in_f / us / 1e6, 2)})
                 del prob
                 torch.cuda.empty_cache()
     return out

@@ -68,6 +68,13 @@ typedef struct b4_gemv_config {
                         * a matrix of few rows evenly over the SMs */
 } b4_gemv_config;
 
+/* The dispatch rule picks the launch, as with cfg NULL; only `flags` is read
+ * (so a caller can ask for B4_FLAG_PDL without choosing a geometry).  With the
+ * rule, a batch whose x does not fit next to the tensor-pipe engines' buffers
+ * in shared memory (m * in_f too large, e.g. 18944 columns at m >= 8) runs as
+ * launches over chunks of 8, 4 or 2 batch rows, each a full pass over the
+ * weights, instead of on the engines that re-read them per batch row. */
+#define B4_ENGINE_AUTO (-1)
 /* CUDA cores: fp32 FMA (INT4 and NF4).  rows_per_warp 1/2/4/8, batch_tile 1/2/4. */
 #define B4_ENGINE_FMA 0
 /* Tensor pipe (INT4 only): register-operand MMA, exact fp16 (code-8) and x,

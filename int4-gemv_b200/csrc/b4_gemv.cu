@@ -262,7 +262,7 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
         cfg->batch_tile = 1;
         cfg->warps_k = 8 / rg;
         cfg->row_groups = rg;
-        cfg->tile_rows = even_tile_rows(p.out_f, rg, sms);
+        cfg->tile_rows = 0;   // full 16-row blocks (q_proj 5.3 us with 13-row tiles, 5.2 us without)
         cfg->stages = 3;
         return;
     }
@@ -1023,6 +1023,45 @@ int launch_split(const GemvProblem& p, const b4_gemv_config& c, void* ws, size_t
     return cudaLaunchKernelExC(&lc, s.fn, args);
 }
 
+// The dispatch rule's launch for cfg NULL.  A batch whose x does not fit
+// next to the tensor-pipe engines' buffers in shared memory (m * in_f too
+// large: down_proj at m >= 8) would fall back to the generic CUDA-core or
+// register-operand engines, which re-read or re-decode the weights per batch
+// row (NF4 down_proj, m = 8: 292 us).  It runs instead as launches of the
+// largest chunk of batch rows that the tensor-pipe engines take (8, 4 or 2
+// rows), each a full pass over the weights (m = 8 as two passes of 4 rows:
+// 2 x 31 us).
+int launch_default(const GemvProblem& p, int flags, cudaStream_t st)
+{
+    b4_gemv_config c;
+    default_config(p, &c);
+    c.flags = flags;
+    const bool tensor_pipe = c.engine == B4_ENGINE_MMA_LEAN_ASYNC || c.engine == B4_ENGINE_MMA_NF4;
+    if (p.m > 1 && !tensor_pipe) {
+        for (int mc = 8; mc >= 2; mc /= 2) {
+            if (mc >= p.m) continue;
+            GemvProblem q = p;
+            q.m = mc;
+            b4_gemv_config cc;
+            default_config(q, &cc);
+            if (cc.engine != B4_ENGINE_MMA_LEAN_ASYNC && cc.engine != B4_ENGINE_MMA_NF4) continue;
+            for (int b0 = 0; b0 < p.m; b0 += mc) {
+                GemvProblem part = p;
+                part.m = std::min(mc, p.m - b0);
+                part.x = static_cast<const __half*>(p.x) + (long long)b0 * p.x_ld;
+                part.y = p.y + (long long)b0 * p.y_ld;
+                b4_gemv_config pc;
+                default_config(part, &pc);
+                pc.flags = flags;
+                const int e = launch_gemv(part, pc, st);
+                if (e != cudaSuccess) return e;
+            }
+            return cudaSuccess;
+        }
+    }
+    return launch_gemv(p, c, st);
+}
+
 void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
 {
     // Measured on B200 (`b4gemv.diag sweep --split-only --pdl`): the split's
@@ -1060,11 +1099,10 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     GemvProblem p{fmt, qw, scale, x, y, in_f, out_f, m, in_f, out_f};
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
-    b4_gemv_config c;
-    if (cfg) c = *cfg;
-    else default_config(p, &c);
-    if (c.flags & B4_FLAG_SPLIT) return cudaErrorInvalidValue;   // needs a workspace: b4_gemv_ws
-    return launch_gemv(p, c, reinterpret_cast<cudaStream_t>(stream));
+    if (!cfg || cfg->engine == B4_ENGINE_AUTO)
+        return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, reinterpret_cast<cudaStream_t>(stream));
+    if (cfg->flags & B4_FLAG_SPLIT) return cudaErrorInvalidValue;   // needs a workspace: b4_gemv_ws
+    return launch_gemv(p, *cfg, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg)
@@ -1104,12 +1142,11 @@ int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     GemvProblem p{fmt, qw, scale, x, y, in_f, out_f, m, in_f, out_f};
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
-    b4_gemv_config c;
-    if (cfg) c = *cfg;
-    else default_config_ws(p, &c);
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (c.flags & B4_FLAG_SPLIT) return launch_split(p, c, ws, ws_bytes, st);
-    return launch_gemv(p, c, st);
+    if (!cfg || cfg->engine == B4_ENGINE_AUTO)   // the rule of b4_gemv_ws never splits
+        return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, st);
+    if (cfg->flags & B4_FLAG_SPLIT) return launch_split(p, *cfg, ws, ws_bytes, st);
+    return launch_gemv(p, *cfg, st);
 }
 
 int b4_gemv_int4_g128(const uint32_t* qw, const void* scales, const void* x, float* y,

@@ -453,3 +453,30 @@ def test_nf4_small_batch_tensor_pipe_kernel(cuda, oracle, m):
             y = b4gemv.gemv(1, qw, sc, Xd, config=cfg).cpu().numpy()
             assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
     assert b4gemv.default_config(1, 3584, 18944, m)["engine"] == 7
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("m", [8, 9, 16])
+def test_long_rows_large_batch_run_as_tensor_pipe_chunks(cuda, oracle, fmt, m):
+    """x for 8+ rows of 18944 columns does not fit next to the tensor-pipe
+    engines' buffers: with the dispatch rule (cfg NULL, or B4_ENGINE_AUTO with
+    the PDL flag) the entry points run batch chunks through them."""
+    import ctypes
+    import torch
+    out_f, in_f = 640, 18944
+    rng = np.random.default_rng(70 + m + fmt)
+    W, X = rand_problem(rng, out_f, in_f, m)
+    qw, sc = quantised(fmt, W, cuda)
+    assert b4gemv.default_config(fmt, in_f, out_f, m)["engine"] not in (5, 7)
+    ref = f64_ref(oracle, fmt, qw, sc, X)
+    Xd = to_dev(X, cuda)
+    y = (b4gemv.gemv_int4 if fmt == 0 else b4gemv.gemv_nf4)(qw, sc, Xd).cpu().numpy()
+    assert rel_err(y, ref) < TOL
+    y2 = torch.full((m, out_f), float("nan"), dtype=torch.float32, device=cuda)
+    cfg = b4gemv.GemvConfig.from_dict({"engine": b4gemv._lib.ENGINE_AUTO, "flags": b4gemv.FLAG_PDL})
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = ctypes.c_void_p
+    assert b4gemv.load().b4_gemv_ex(fmt, p(qw.data_ptr()), p(sc.data_ptr()), p(Xd.data_ptr()), p(y2.data_ptr()),
+                                    in_f, out_f, m, ctypes.byref(cfg), st) == 0
+    torch.cuda.synchronize()
+    assert rel_err(y2.cpu().numpy(), ref) < TOL
