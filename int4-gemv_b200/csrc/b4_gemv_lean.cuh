@@ -262,6 +262,9 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
         }
         float acc_a = 0.0f, acc_b = 0.0f;
         const uint4* xp = xs + ks * 16 * G + q * 4;          // + 16*G*kw per stage step
+        // B fragments: column 0 holds x (lanes g = 0 load it per group), columns 1..7 zero
+        uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                       make_uint4(0, 0, 0, 0)};
 
         for (int it0 = 0; it0 < n_it; it0 += SD) {   // SD is a multiple of D
 #pragma unroll
@@ -289,10 +292,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                             wav = bufa[cs];
                             wbv = bufb[cs];
                         }
-                        // B column 0 = x (lanes g = 0), columns 1..7 zero
-                        uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                                       make_uint4(0, 0, 0, 0)};
-                        if (g == 0) {
+                        if (g == 0) {   // B column 0 = x; the other lanes keep their zeros
 #pragma unroll
                             for (int i = 0; i < 4; ++i) xv[i] = xp[16 * h + i];
                         }

@@ -179,6 +179,8 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_split_int4_kernel(const SplitP
     int cs = (int)(u0 % p.nst);
     const uint4* xp = xs + cs * 16 * G + q * 4;
     float acc_a = 0.0f, acc_b = 0.0f;
+    // B fragments: column 0 holds x (lanes g = 0 load it per group), columns 1..7 zero
+    uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
     for (int it0 = 0; it0 < n_it; it0 += D) {
 #pragma unroll
         for (int d = 0; d < D; ++d) {
@@ -195,10 +197,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_split_int4_kernel(const SplitP
                 for (int h = 0; h < G; ++h) {
                     const uint4 wav = ring[((d * G + h) * 2) * 32 + lane];
                     const uint4 wbv = ring[((d * G + h) * 2 + 1) * 32 + lane];
-                    // B column 0 = x (lanes g = 0), columns 1..7 zero
-                    uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                                   make_uint4(0, 0, 0, 0)};
-                    if (g == 0) {
+                    if (g == 0) {   // B column 0 = x; the other lanes keep their zeros
 #pragma unroll
                         for (int i = 0; i < 4; ++i) xv[i] = xp[16 * h + i];
                     }
