@@ -5,8 +5,12 @@ Metric: us/GEMV and achieved HBM GB/s, batch-1 INT4/NF4 GEMV.
 Workload: NF4 b64 GEMV at batch 1 over the seven
 Qwen2.5-7B projections q/k/v/o (3584x3584, 512x3584 x2, 3584x3584), gate/up
 (18944x3584) and down (3584x18944).  A step is one GEMV of each projection,
-issued through the C ABI (b4_gemv_nf4_b64).  value = algorithmic bytes of the
-step (packed codes + absmax + x) x steps / device time, summed over ranks.
+issued through the C ABI as decode issues them: q/k/v read one x and gate/up
+another (as in the model), and each of those groups is one b4_gemv_multi
+launch; o and down are b4_gemv_ws launches (4 launches per step, programmatic
+dependents).  value = algorithmic bytes of the step (packed codes + absmax +
+x) x steps / device time, summed over ranks; `separate_launches` reports the
+same step as seven launches.
 
 Timing: W warm-up steps, then exactly K steps bracketed by a barrier and
 torch.cuda.synchronize on both sides, timed with CUDA events on the launching
@@ -197,9 +201,17 @@ class ClockSampler:
 
 # ---- the measured arm -----------------------------------------------------------
 
+# the input each projection reads, as in the model: q/k/v share the attention
+# block's input, gate/up the MLP's
+X_GROUP = {"q_proj": 0, "k_proj": 0, "v_proj": 0, "o_proj": 3, "gate_proj": 4, "up_proj": 4, "down_proj": 6}
+# the step's launches: (projections, one b4_gemv_multi launch if several)
+FUSED_STEP = [(0, 1, 2), (3,), (4, 5), (6,)]
+
+
 def build_weights(b4, torch, dev, fmt):
     """Per shape: N_SETS copies of (qw, scale) quantised on the device from
-    W ~ N(0, 0.02) (seed = shape index), one x ~ N(0, 1) fp16 and one y."""
+    W ~ N(0, 0.02) (seed = shape index) and one y; x ~ N(0, 1) fp16 per input
+    (q/k/v share one, gate/up another, X_GROUP)."""
     sets = [[] for _ in range(N_SETS)]
     xs, ys = [], []
     for idx, (name, out_f, in_f) in enumerate(SHAPES):
@@ -213,9 +225,13 @@ def build_weights(b4, torch, dev, fmt):
         del W
         for s in range(N_SETS):
             sets[s].append((qw.clone(), sc.clone()) if s else (qw, sc))
-        gx = torch.Generator(device=dev)
-        gx.manual_seed(1000 + idx)
-        xs.append(torch.randn((1, in_f), generator=gx, device=dev, dtype=torch.float32).half())
+        src = X_GROUP[name]
+        if src == idx:
+            gx = torch.Generator(device=dev)
+            gx.manual_seed(1000 + idx)
+            xs.append(torch.randn((1, in_f), generator=gx, device=dev, dtype=torch.float32).half())
+        else:
+            xs.append(xs[src])
         ys.append(torch.empty((1, out_f), dtype=torch.float32, device=dev))
     torch.cuda.synchronize()
     return sets, xs, ys
@@ -230,9 +246,9 @@ class Launcher:
     launch: the next GEMV's weight stream starts while the previous kernel
     drains); without, the rule's own (cfg NULL)."""
 
-    def __init__(self, b4, torch, sets, xs, ys, fmt, pdl=False):
+    def __init__(self, b4, torch, sets, xs, ys, fmt, pdl=False, fused=False):
         lib = b4.load()
-        self.lib, self.fmt, self.pdl = lib, fmt, pdl
+        self.lib, self.fmt, self.pdl, self.fused = lib, fmt, pdl, fused
         self.cfg_objs = []
         need = 0
         for name, out_f, in_f in SHAPES:
@@ -251,6 +267,25 @@ class Launcher:
                 row.append((ctypes.c_void_p(qw.data_ptr()), ctypes.c_void_p(sc.data_ptr()),
                             ctypes.c_void_p(xs[i].data_ptr()), ctypes.c_void_p(ys[i].data_ptr()), in_f, out_f))
             self.calls.append(row)
+        # fused step: q/k/v and gate/up as one b4_gemv_multi launch each (they share x)
+        self.multi = []
+        for s in range(len(sets)):
+            row = []
+            for group in FUSED_STEP:
+                if len(group) == 1:
+                    row.append(("single", group[0]))
+                    continue
+                segs = (b4.GemvSegment * len(group))(*[
+                    b4.GemvSegment(sets[s][i][0].data_ptr(), sets[s][i][1].data_ptr(), ys[i].data_ptr(), SHAPES[i][1])
+                    for i in group])
+                in_f = SHAPES[group[0]][2]
+                c = b4.GemvConfig()
+                st = lib.b4_gemv_multi_default_config(fmt, segs, len(group), in_f, 1, ctypes.byref(c))
+                if st:
+                    raise RuntimeError(f"multi config failed with status {st}")
+                c.flags |= b4.FLAG_PDL if pdl else 0
+                row.append(("multi", (segs, len(group), ctypes.c_void_p(xs[group[0]].data_ptr()), in_f, c)))
+            self.multi.append(row)
 
     def call(self, i, q, sc, x, y, in_f, out_f, stream):
         st = self.lib.b4_gemv_ws(self.fmt, q, sc, x, y, in_f, out_f, 1, self.cfgs[i] if self.pdl else None,
@@ -258,7 +293,23 @@ class Launcher:
         if st:
             raise RuntimeError(f"GEMV launch failed with status {st}")
 
+    def launches_per_step(self):
+        return len(FUSED_STEP) if self.fused else len(SHAPES)
+
     def step(self, s, stream, events=None):
+        if self.fused:
+            calls = self.calls[s % len(self.calls)]
+            for j, (kind, a) in enumerate(self.multi[s % len(self.multi)]):
+                if kind == "single":
+                    self.call(a, *calls[a], stream)
+                else:
+                    segs, n, x, in_f, c = a
+                    st = self.lib.b4_gemv_multi(self.fmt, segs, n, x, in_f, 1, ctypes.byref(c), stream)
+                    if st:
+                        raise RuntimeError(f"GEMV launch failed with status {st}")
+                if events is not None:
+                    events[j].record()
+            return
         for i, (q, sc, x, y, in_f, out_f) in enumerate(self.calls[s % len(self.calls)]):
             self.call(i, q, sc, x, y, in_f, out_f, stream)
             if events is not None:
@@ -320,6 +371,26 @@ def per_shape_chained(b4, torch, fmt, reps=200):
     del sets
     torch.cuda.synchronize()
     return out
+
+
+def step_graph_ms(torch, launcher, n_steps):
+    """ms for n_steps steps of `launcher` captured in one CUDA graph (best of 3
+    replays after 2 untimed ones), events on the launching stream."""
+    g, _ = capture(torch, launcher, n_steps, 0, with_events=False)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(3):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        best = a.elapsed_time(b) if best is None else min(best, a.elapsed_time(b))
+    del g
+    return best
 
 
 def chained_us(torch, launcher, i, reps=100):
@@ -393,17 +464,19 @@ def e2e_steps(b4, torch, sets, xs, ys, n_steps, graph=True):
     captured once in a CUDA graph (as a decode loop runs them) and every step
     replays one between its copies; without, every step calls the Python API
     seven times (its host cost included)."""
-    in_sizes = [in_f for _, _, in_f in SHAPES]
+    inputs = sorted(set(X_GROUP.values()))                # one x per input group
+    in_sizes = [SHAPES[i][2] for i in inputs]
     out_sizes = [out_f for _, out_f, _ in SHAPES]
     hx = torch.empty(sum(in_sizes), dtype=torch.float16).pin_memory()
-    hx.copy_(torch.cat([x.reshape(-1).cpu() for x in xs]))
+    hx.copy_(torch.cat([xs[i].reshape(-1).cpu() for i in inputs]))
     hy = torch.empty(sum(out_sizes), dtype=torch.float32).pin_memory()
     dx = torch.empty_like(hx, device=xs[0].device)
     dy = torch.empty_like(hy, device=xs[0].device)
-    xv, yv, o = [], [], 0
-    for n in in_sizes:
-        xv.append(dx[o:o + n].view(1, n))
+    xg, yv, o = {}, [], 0
+    for i, n in zip(inputs, in_sizes):
+        xg[i] = dx[o:o + n].view(1, n)
         o += n
+    xv = [xg[X_GROUP[name]] for name, _, _ in SHAPES]
     o = 0
     for n in out_sizes:
         yv.append(dy[o:o + n].view(1, n))
@@ -411,9 +484,15 @@ def e2e_steps(b4, torch, sets, xs, ys, n_steps, graph=True):
     checksum = 0.0
 
     def gemvs(s, stream=None):
-        for i in range(len(SHAPES)):
-            qw, sc = sets[s % N_SETS][i]
-            b4.gemv_nf4(qw, sc, xv[i], yv[i], stream=stream)
+        # as decode runs them: q/k/v and gate/up (one x each) as one launch each
+        for group in FUSED_STEP:
+            if len(group) == 1:
+                i = group[0]
+                qw, sc = sets[s % N_SETS][i]
+                b4.gemv_nf4(qw, sc, xv[i], yv[i], stream=stream, pdl=True)
+            else:
+                b4.gemv_multi(1, [sets[s % N_SETS][i] for i in group], xv[group[0]], [yv[i] for i in group],
+                              stream=stream, pdl=True)
 
     graphs = []
     if graph:
@@ -630,11 +709,15 @@ def run_ours(args, d):
 
     sets, xs, ys = build_weights(b4, torch, dev, 1)
     gate_err = correctness_gate(b4, torch, sets, xs, ys, 1)
-    launcher = Launcher(b4, torch, sets, xs, ys, 1, pdl=not args.no_pdl)
+    # the timed step as decode runs it: q/k/v and gate/up (one x each) as one
+    # b4_gemv_multi launch each; `separate`: the seven GEMVs as seven launches
+    launcher = Launcher(b4, torch, sets, xs, ys, 1, pdl=not args.no_pdl, fused=True)
+    separate = Launcher(b4, torch, sets, xs, ys, 1, pdl=not args.no_pdl)
     plain = Launcher(b4, torch, sets, xs, ys, 1, pdl=False)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     for s in range(N_SETS):
         launcher.step(s, stream)  # eager first launches (attribute set-up) before capture
+        separate.step(s, stream)
     torch.cuda.synchronize()
 
     K, W = args.steps, args.warmup
@@ -690,6 +773,7 @@ def run_ours(args, d):
     # on the launching stream.  (Timing events inside the step graph would add
     # their own gaps between kernels.)
     per_us = {name: round(chained_us(torch, launcher, i), 3) for i, (name, _, _) in enumerate(SHAPES)}
+    sep_ms = d.max(step_graph_ms(torch, separate, min(K, 500)), dev)
     per_us_plain = {name: round(chained_us(torch, plain, i), 3) for i, (name, _, _) in enumerate(SHAPES)}
 
     peak, peak_kind = measured_peak()
@@ -732,6 +816,8 @@ def run_ours(args, d):
                    "bytes_per_step": STEP_BYTES,
                    "l2": f"{N_SETS} rotating weight copies, {N_SETS * STEP_BYTES / 1e6:.0f} MB (> 4x the 126 MB L2)",
                    "timing": f"CUDA graphs of {gsteps} steps, events on the launching stream",
+                   "launches": "q/k/v read one x and gate/up another (as in the model) and run as one "
+                               "b4_gemv_multi launch each: 4 launches per step, programmatic dependents",
                    "parallelism": f"{n} independent replicas (no data-path collective)" if n > 1 else "1 GPU"},
         "us_per_gemv": per_us,
         "us_per_gemv_how": ("100 launches of one projection back to back in a CUDA graph, each a programmatic "
@@ -746,14 +832,18 @@ def run_ours(args, d):
                      "traffic": traffic},
         "e2e": {"value": round(n * e2e_n * STEP_BYTES / (e2e_ms_max / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "how": "public API b4gemv.gemv_nf4 -> C ABI per GEMV, the seven calls of a step captured once "
-                       "in a CUDA graph and replayed; pinned x copied in and y copied out and read on the host "
-                       "every step", "steps": e2e_n,
+                "how": "public API b4gemv.gemv_nf4(pdl=True) -> C ABI per GEMV, the seven calls of a step "
+                       "captured once in a CUDA graph and replayed; pinned x copied in and y copied out and read "
+                       "on the host every step", "steps": e2e_n,
                 "eager_value": round(n * e2e_n * STEP_BYTES / (e2e_eager_ms_max / 1e3) / 1e9, 2),
                 "eager_how": "the same with the seven b4gemv.gemv_nf4 Python calls made every step"},
         "isolated_launch_us": iso,
         "empty_launch_floor_us": floor,
-        "gpu_launches": K * len(SHAPES),
+        "gpu_launches": K * launcher.launches_per_step(),
+        "separate_launches": {"value": round(n * min(K, 500) * STEP_BYTES / (sep_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                              "ms_per_step": round(sep_ms / min(K, 500), 5), "launches_per_step": len(SHAPES),
+                              "how": "the same step as seven launches, one per projection (programmatic "
+                                     "dependents)"},
         "correctness_rel_err": gate_err,
         "clocks": clocks,
     }

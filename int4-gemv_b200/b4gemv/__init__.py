@@ -186,11 +186,18 @@ def workspace(device, nbytes: int):
     return ws
 
 
-def gemv_ws(fmt: int, qw, scale, x, y=None, config: dict | None = None, ws=None, stream=None):
-    """b4_gemv_ws: the GEMV with a workspace (the split path for few-row
-    matrices at batch 1; config None = the dispatch rule).  ws: a zero-filled
-    CUDA uint8 tensor of at least workspace_size() bytes, or None for the
-    package's per-device workspace."""
+_AUTO_PDL = {"engine": -1, "flags": FLAG_PDL}
+
+
+def gemv_ws(fmt: int, qw, scale, x, y=None, config: dict | None = None, ws=None, stream=None, pdl: bool = False):
+    """b4_gemv_ws: the GEMV with a workspace (the split kernels when a split
+    config is passed; config None = the dispatch rule, which never splits).
+    ws: a zero-filled CUDA uint8 tensor of at least workspace_size() bytes, or
+    None for the package's per-device workspace.  pdl (with config None): the
+    dispatch rule's launch as a programmatic dependent of the previous kernel
+    on the stream (B4_ENGINE_AUTO + B4_FLAG_PDL)."""
+    if pdl and config is None:
+        config = _AUTO_PDL
     out_f, in_f, m, x2, y = _gemv_args(qw, scale, x, y)
     need = workspace_size(fmt, in_f, out_f, m, config, qw.device.index)
     if ws is None and need:
@@ -202,24 +209,24 @@ def gemv_ws(fmt: int, qw, scale, x, y=None, config: dict | None = None, ws=None,
     return y
 
 
-def gemv_int4(qw, scales, x, y=None, stream=None, split: bool = True):
+def gemv_int4(qw, scales, x, y=None, stream=None, split: bool = True, pdl: bool = False):
     """The INT4 g128 GEMV with the dispatch rule's config: b4_gemv_ws with the
-    package's workspace (split: True), or b4_gemv_int4_g128, which needs no
-    workspace and never splits (split: False)."""
+    package's workspace (split: True; pdl: as a programmatic dependent of the
+    previous kernel), or b4_gemv_int4_g128 (split: False)."""
     if split:
-        return gemv_ws(FMT_INT4_G128, qw, scales, x, y, stream=stream)
+        return gemv_ws(FMT_INT4_G128, qw, scales, x, y, stream=stream, pdl=pdl)
     out_f, in_f, m, x2, y = _gemv_args(qw, scales, x, y)
     check("b4_gemv_int4_g128", load().b4_gemv_int4_g128(_ptr(qw), _ptr(scales), _ptr(x2), _ptr(y), in_f,
                                                         out_f, m, _stream(stream)))
     return y
 
 
-def gemv_nf4(qw, absmax, x, y=None, stream=None, split: bool = True):
+def gemv_nf4(qw, absmax, x, y=None, stream=None, split: bool = True, pdl: bool = False):
     """The NF4 b64 GEMV with the dispatch rule's config: b4_gemv_ws with the
-    package's workspace (split: True), or b4_gemv_nf4_b64, which needs no
-    workspace and never splits (split: False)."""
+    package's workspace (split: True; pdl: as a programmatic dependent of the
+    previous kernel), or b4_gemv_nf4_b64 (split: False)."""
     if split:
-        return gemv_ws(FMT_NF4_B64, qw, absmax, x, y, stream=stream)
+        return gemv_ws(FMT_NF4_B64, qw, absmax, x, y, stream=stream, pdl=pdl)
     out_f, in_f, m, x2, y = _gemv_args(qw, absmax, x, y)
     check("b4_gemv_nf4_b64", load().b4_gemv_nf4_b64(_ptr(qw), _ptr(absmax), _ptr(x2), _ptr(y), in_f,
                                                     out_f, m, _stream(stream)))
@@ -258,10 +265,13 @@ def multi_default_config(fmt: int, pairs, x) -> dict:
     return c.as_dict()
 
 
-def gemv_multi(fmt: int, pairs, x, ys=None, config: dict | None = None, stream=None):
+def gemv_multi(fmt: int, pairs, x, ys=None, config: dict | None = None, stream=None, pdl: bool = False):
     """b4_gemv_multi: y_s = dequant(qw_s, scale_s) @ x for every (qw_s, scale_s)
     in `pairs` (up to four matrices with the same in_f), one launch at batch 1
-    on the lean engines.  Returns the list of y_s."""
+    on the lean engines.  pdl (with config None): the dispatch rule's config as
+    a programmatic dependent of the previous kernel.  Returns the list of y_s."""
+    if pdl and config is None:
+        config = dict(multi_default_config(fmt, pairs, x), flags=FLAG_PDL)
     segs, x2, in_f, m, out = _segments(pairs, x, ys)
     cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
     check("b4_gemv_multi", load().b4_gemv_multi(fmt, segs, len(pairs), _ptr(x2), in_f, m, cfg, _stream(stream)))

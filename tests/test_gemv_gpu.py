@@ -480,3 +480,21 @@ def test_long_rows_large_batch_run_as_tensor_pipe_chunks(cuda, oracle, fmt, m):
                                     in_f, out_f, m, ctypes.byref(cfg), st) == 0
     torch.cuda.synchronize()
     assert rel_err(y2.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_python_api_pdl_matches_oracle(cuda, oracle, fmt):
+    """gemv_int4 / gemv_nf4 with pdl=True: the dispatch rule's launch as a
+    programmatic dependent (B4_ENGINE_AUTO + B4_FLAG_PDL) after a producer of x."""
+    import torch
+    rng = np.random.default_rng(808 + fmt)
+    W, X = rand_problem(rng, 3584, 3584)
+    qw, sc = quantised(fmt, W, cuda)
+    xsrc = to_dev(X, cuda)
+    x = torch.zeros_like(xsrc)
+    fn = b4gemv.gemv_int4 if fmt == 0 else b4gemv.gemv_nf4
+    for _ in range(3):
+        x.zero_()
+        x.copy_(xsrc)
+        y = fn(qw, sc, x, pdl=True)
+    assert rel_err(y.cpu().numpy(), f64_ref(oracle, fmt, qw, sc, X)) < TOL
