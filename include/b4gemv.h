@@ -20,10 +20,12 @@
  *     reference silently drops a ragged tail (kernels.cuh:36,101), this ABI
  *     rejects it.
  *   - Work is enqueued on `stream` (NULL = legacy default stream) and returns
- *     without synchronising.  The only host-global state is a mutex-guarded
- *     cache of per-device facts (SM count, kernels whose shared-memory limit
- *     was already raised): any host thread may call on its own stream
- *     concurrently.
+ *     without synchronising.  The only host-global state is mutex-guarded
+ *     caches of per-device facts (SM count, kernels whose shared-memory limit
+ *     was already raised, resident CTAs per kernel, the device address of the
+ *     static scratch array of b4_gemv_split_noalloc): any host thread may call
+ *     on its own stream concurrently (b4_gemv_split_noalloc's scratch and a
+ *     b4_gemv_ws workspace excepted: calls sharing them must not overlap).
  *   - Vector paths need 16-byte (or 8-byte) aligned codes and x; other
  *     alignments fall back to 4-byte loads, never to the CPU.
  */
