@@ -206,6 +206,25 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     // in the MMA's N columns, when x for all rows fits next to the rings.
     // (fitted on B200 for m = 2..16 on gate/down: one CTA per SM's worth of
     // rows per tile, 2 stages of 4 groups up to m = 4, 3 of 2 beyond)
+    // 9..16 rows: one CTA of 16 warps per SM sharing one copy of x, the fewest
+    // power-of-two row groups that give one tile per CTA, 4 stages of 1 group
+    if (p.m >= 9 && p.m <= 16 && p.fmt == kInt4 && aligned(p.qw, 16)) {
+        const long long blocks = (p.out_f + 15) / 16;
+        int rg = 1;
+        while (rg < 8 && (blocks + rg - 1) / rg > sms) rg *= 2;
+        if (lean_int4_mb_smem(p.in_f, p.m, 16 / rg, rg, 4, 1) <= kTmaSmemLimit) {
+            cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
+            cfg->vec_words = 4;
+            cfg->rows_per_warp = 16;
+            cfg->batch_tile = 1;
+            cfg->warps_k = 16 / rg;
+            cfg->row_groups = rg;
+            cfg->tile_rows = 0;
+            cfg->stages = 4;
+            cfg->stage_groups = 1;
+            return;
+        }
+    }
     if (p.m >= 2 && p.m <= 16 && p.fmt == kInt4 && aligned(p.qw, 16)) {
         const int ng = p.in_f / kGroup;
         const int row_groups = (p.out_f + 15) / 16;
@@ -708,7 +727,10 @@ bool lean_geometry_ok(const b4_gemv_config& c) { return c.warps_k >= 1 && c.row_
 int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
                           const b4_gemv_config& c, cudaStream_t st)
 {
-    if (m < 1 || m > 16 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c))
+    // CTAs of 16 warps: batches of 9..16 rows on the 4-stage single-group ring
+    const bool wide = c.warps_k >= 1 && c.row_groups >= 1 && c.warps_k * c.row_groups == 16;
+    if (wide && (m < 9 || c.stages != 4 || c.stage_groups != 1)) return cudaErrorInvalidValue;
+    if (m < 1 || m > 16 || c.vec_words != 4 || c.rows_per_warp != 16 || (!wide && !lean_geometry_ok(c)))
         return cudaErrorInvalidValue;
     if (m > 1 && c.engine != B4_ENGINE_MMA_LEAN_ASYNC) return cudaErrorInvalidValue;
     if (nseg < 1 || nseg > kLeanMaxSeg) return cudaErrorInvalidValue;
@@ -719,7 +741,7 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
     if ((in_f / kGroup) % groups) return cudaErrorInvalidValue;   // a stage of `groups` groups tiles the row
     const int nb = m > 8 ? 2 : 1;
     void* fn = m == 1 ? gemv_kernel_int4_lean(c.stages, groups, async_ring)
-                      : gemv_kernel_int4_lean_mb(c.stages, groups, nb);
+                      : gemv_kernel_int4_lean_mb(c.stages, groups, nb, wide);
     if (!fn) return cudaErrorInvalidValue;
     const int tr = c.tile_rows ? c.tile_rows : 16;
     if (tr < 1 || tr > 16) return cudaErrorInvalidValue;

@@ -28,8 +28,11 @@ struct LeanMbParams {
     int m;             // batch rows, 2..8*NB
 };
 
-template <int D, int G, int NB>
-__global__ void __launch_bounds__(256, 3 - NB) b4_gemv_lean_mb_kernel(const LeanMbParams pm)
+// MAXT = 512: CTAs of 16 warps, one per SM, for batches of 9..16 rows, whose x
+// fills most of the shared memory: the 16 warps share one copy of x where two
+// CTAs of 8 warps would not fit.
+template <int D, int G, int NB, int MAXT = 256>
+__global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_mb_kernel(const LeanMbParams pm)
 {
     using ST = typename LeanScale<G>::T;
     const LeanParams& p = pm.base;
@@ -220,6 +223,6 @@ __global__ void __launch_bounds__(256, 3 - NB) b4_gemv_lean_mb_kernel(const Lean
     }
 }
 
-void* gemv_kernel_int4_lean_mb(int depth, int groups, int nb);
+void* gemv_kernel_int4_lean_mb(int depth, int groups, int nb, int wide = 0);
 
 }  // namespace b4

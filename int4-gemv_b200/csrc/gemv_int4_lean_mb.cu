@@ -1,9 +1,11 @@
 // Instantiations of the small-batch lean INT4 kernel: (stages, groups per
-// stage) x (one or two 8-column blocks of batch rows).
+// stage) x (one or two 8-column blocks of batch rows); `wide`: the 16-warp
+// CTA for two blocks (9..16 batch rows).
 #include "b4_gemv_lean_mb.cuh"
 
-void* b4::gemv_kernel_int4_lean_mb(int depth, int groups, int nb)
+void* b4::gemv_kernel_int4_lean_mb(int depth, int groups, int nb, int wide)
 {
+    if (wide) return nb == 2 && groups == 1 && depth == 4 ? (void*)&b4::b4_gemv_lean_mb_kernel<4, 1, 2, 512> : nullptr;
     switch (nb * 1000 + groups * 100 + depth) {
         case 1402: return (void*)&b4::b4_gemv_lean_mb_kernel<2, 4, 1>;
         case 1203: return (void*)&b4::b4_gemv_lean_mb_kernel<3, 2, 1>;

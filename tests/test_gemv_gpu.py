@@ -498,3 +498,33 @@ def test_python_api_pdl_matches_oracle(cuda, oracle, fmt):
         x.copy_(xsrc)
         y = fn(qw, sc, x, pdl=True)
     assert rel_err(y.cpu().numpy(), f64_ref(oracle, fmt, qw, sc, X)) < TOL
+
+
+@pytest.mark.parametrize("m", [9, 12, 16])
+def test_int4_small_batch_sixteen_warp_ctas(cuda, oracle, m):
+    """Batches of 9..16 rows on CTAs of 16 warps sharing one copy of x (engine 5,
+    4 stages of 1 group): several warp splits, against the double GEMV."""
+    rng = np.random.default_rng(900 + m)
+    for out_f, in_f in [(70, 1024), (300, 3584), (2049, 512)]:
+        W, X = rand_problem(rng, out_f, in_f, m)
+        qw, sc = quantised(0, W, cuda)
+        ref = f64_ref(oracle, 0, qw, sc, X)
+        Xd = to_dev(X, cuda)
+        for kw, rg in [(16, 1), (8, 2), (2, 8)]:
+            cfg = dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=5, stages=4,
+                       stage_groups=1)
+            y = b4gemv.gemv(0, qw, sc, Xd, config=cfg).cpu().numpy()
+            assert rel_err(y, ref) < TOL, (out_f, in_f, m, kw, rg)
+    c = b4gemv.default_config(0, 3584, 18944, m)
+    assert c["warps_k"] * c["row_groups"] == 16
+
+
+def test_int4_sixteen_warp_ctas_need_nine_rows(cuda):
+    import torch
+    qw = torch.zeros((64, 128), dtype=torch.int32, device=cuda)
+    sc = torch.zeros((64, 8), dtype=torch.float16, device=cuda)
+    x = torch.zeros((8, 1024), dtype=torch.float16, device=cuda)
+    cfg = dict(vec_words=4, rows_per_warp=16, warps_k=16, row_groups=1, batch_tile=1, engine=5, stages=4,
+               stage_groups=1)
+    with pytest.raises(b4gemv.B4Error):
+        b4gemv.gemv(0, qw, sc, x, config=cfg)
