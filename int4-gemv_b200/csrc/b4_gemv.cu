@@ -206,25 +206,6 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
     // in the MMA's N columns, when x for all rows fits next to the rings.
     // (fitted on B200 for m = 2..16 on gate/down: one CTA per SM's worth of
     // rows per tile, 2 stages of 4 groups up to m = 4, 3 of 2 beyond)
-    // 9..16 rows: one CTA of 16 warps per SM sharing one copy of x, the fewest
-    // power-of-two row groups that give one tile per CTA, 4 stages of 1 group
-    if (p.m >= 9 && p.m <= 16 && p.fmt == kInt4 && aligned(p.qw, 16)) {
-        const long long blocks = (p.out_f + 15) / 16;
-        int rg = 1;
-        while (rg < 8 && (blocks + rg - 1) / rg > sms) rg *= 2;
-        if (lean_int4_mb_smem(p.in_f, p.m, 16 / rg, rg, 4, 1) <= kTmaSmemLimit) {
-            cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
-            cfg->vec_words = 4;
-            cfg->rows_per_warp = 16;
-            cfg->batch_tile = 1;
-            cfg->warps_k = 16 / rg;
-            cfg->row_groups = rg;
-            cfg->tile_rows = 0;
-            cfg->stages = 4;
-            cfg->stage_groups = 1;
-            return;
-        }
-    }
     if (p.m >= 2 && p.m <= 16 && p.fmt == kInt4 && aligned(p.qw, 16)) {
         const int ng = p.in_f / kGroup;
         const int row_groups = (p.out_f + 15) / 16;

@@ -503,7 +503,8 @@ def test_python_api_pdl_matches_oracle(cuda, oracle, fmt):
 @pytest.mark.parametrize("m", [9, 12, 16])
 def test_int4_small_batch_sixteen_warp_ctas(cuda, oracle, m):
     """Batches of 9..16 rows on CTAs of 16 warps sharing one copy of x (engine 5,
-    4 stages of 1 group): several warp splits, against the double GEMV."""
+    4 stages of 1 group; an explicit config): several warp splits, against the
+    double GEMV."""
     rng = np.random.default_rng(900 + m)
     for out_f, in_f in [(70, 1024), (300, 3584), (2049, 512)]:
         W, X = rand_problem(rng, out_f, in_f, m)
@@ -515,8 +516,6 @@ def test_int4_small_batch_sixteen_warp_ctas(cuda, oracle, m):
                        stage_groups=1)
             y = b4gemv.gemv(0, qw, sc, Xd, config=cfg).cpu().numpy()
             assert rel_err(y, ref) < TOL, (out_f, in_f, m, kw, rg)
-    c = b4gemv.default_config(0, 3584, 18944, m)
-    assert c["warps_k"] * c["row_groups"] == 16
 
 
 def test_int4_sixteen_warp_ctas_need_nine_rows(cuda):
@@ -528,3 +527,46 @@ def test_int4_sixteen_warp_ctas_need_nine_rows(cuda):
                stage_groups=1)
     with pytest.raises(b4gemv.B4Error):
         b4gemv.gemv(0, qw, sc, x, config=cfg)
+
+
+# ---- full-size properties (Llama-3-70B shapes, too large for a full CPU reference) ----
+
+L70 = {"qo": (8192, 8192), "gate_up": (28672, 8192), "down": (8192, 28672)}
+
+
+def device_quantised(fmt, out_f, in_f, seed, cuda):
+    import torch
+    g = torch.Generator(device=cuda)
+    g.manual_seed(seed)
+    W = torch.randn((out_f, in_f), generator=g, device=cuda) * 0.02
+    qw, sc, _ = (b4gemv.quantise_device if fmt == 0 else b4gemv.quantise_nf4_device)(W)
+    del W
+    return qw, sc
+
+
+@pytest.mark.parametrize("name", list(L70))
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_full_size_doubling_row_permutation_and_sampled_rows(cuda, oracle, name, fmt):
+    """At the full Llama-3-70B shapes: y(2x) == 2 y(x) bit for bit (scaling x by
+    2 is exact in fp16 and doubles every product and partial sum exactly);
+    permuting the weight rows permutes y bit for bit (rows are independent);
+    64 sampled rows within TOL of the double GEMV over their dequantised
+    weights."""
+    import torch
+    out_f, in_f = L70[name]
+    qw, sc = device_quantised(fmt, out_f, in_f, 40 + fmt, cuda)
+    rng = np.random.default_rng(41 + fmt)
+    X = rng.standard_normal((1, in_f)).astype(np.float16)
+    x = to_dev(X, cuda)
+    fn = b4gemv.gemv_int4 if fmt == 0 else b4gemv.gemv_nf4
+    y1 = fn(qw, sc, x)
+    y2 = fn(qw, sc, x * 2)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y1).all()
+    assert torch.equal(y2, y1 * 2)
+    perm = torch.randperm(out_f, generator=torch.Generator().manual_seed(7)).to(cuda)
+    yp = fn(qw[perm].contiguous(), sc[perm].contiguous(), x)
+    assert torch.equal(yp, y1[:, perm])
+    rows = np.sort(rng.choice(out_f, 64, replace=False))
+    ref = f64_ref(oracle, fmt, qw[rows].contiguous(), sc[rows].contiguous(), X)
+    assert rel_err(y1.cpu().numpy()[:, rows], ref) < TOL
