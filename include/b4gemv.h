@@ -123,14 +123,6 @@ typedef struct b4_gemv_config {
  * B4_ENGINE_MMA_NF4 (NF4: register pipeline of `stages`), batch 1.  Only
  * b4_gemv_ws takes it (the other entry points reject it). */
 #define B4_FLAG_SPLIT 2
-/* One CTA of 16 warps per SM: the first f * SMs row blocks are whole blocks, f
- * per CTA, and the remaining blocks are cut along in_f into one equal run per
- * CTA; each CTA works through its run first, hands its piece of those blocks
- * to the workspace (summed in CTA order by the last CTA to arrive) and then
- * its whole blocks, so every SM does the same work and the cross-CTA sum is
- * not on the critical path.  Engine B4_ENGINE_MMA_NF4 (stages 2 or 3), batch
- * 1.  Only b4_gemv_ws takes it. */
-#define B4_FLAG_HYBRID 4
 
 /* ---- GEMV: y[b][r] = sum_k dequant(W)[r][k] * x[b][k], b < m ----------------
  * qw     : uint32 [out_f][in_f/8] packed codes

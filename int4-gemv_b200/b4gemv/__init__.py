@@ -14,7 +14,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (FLAG_HYBRID, FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS, NF4_BLOCK, B4Error,
+from ._lib import (FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS, NF4_BLOCK, B4Error,
                    GemvConfig, GemvSegment, check, load)
 
 __all__ = [
@@ -23,7 +23,7 @@ __all__ = [
     "gemv_nf4_block_per_row", "dequant_int4", "dequant_nf4", "unpack_codes",
     "quantise_device", "quantise_nf4_device", "default_config", "median", "gemv_multi",
     "multi_default_config", "MAX_SEGMENTS", "GemvSegment", "repack_bnb_nf4", "FLAG_SPLIT",
-    "gemv_ws", "workspace_size", "workspace", "default_config_ws", "FLAG_HYBRID",
+    "gemv_ws", "workspace_size", "workspace", "default_config_ws",
 ]
 
 

@@ -18,7 +18,6 @@ GROUP = 128
 NF4_BLOCK = 64
 FLAG_PDL = 1
 FLAG_SPLIT = 2
-FLAG_HYBRID = 4
 ENGINE_AUTO = -1
 ENGINE_FMA = 0
 ENGINE_MMA = 1

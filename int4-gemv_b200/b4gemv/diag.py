@@ -20,7 +20,7 @@ import itertools
 import json
 import sys
 
-from . import FLAG_HYBRID, FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
+from . import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
 
 SHAPES = {"q_proj": (3584, 3584), "k_proj": (512, 3584), "v_proj": (512, 3584), "o_proj": (3584, 3584),
           "gate_proj": (18944, 3584), "up_proj": (18944, 3584), "down_proj": (3584, 18944),
@@ -119,8 +119,6 @@ def split_grid(fmt):
     else:
         for st in (2, 3, 4):
             yield dict(base, engine=7, stages=st, stage_groups=0)
-        for st in (2, 3):   # the hybrid split: 16-warp CTAs, whole blocks plus a run of split ones
-            yield dict(base, engine=7, stages=st, stage_groups=0, warps_k=16, row_groups=1, flags=FLAG_HYBRID)
 
 
 def config_grid(fmt, m=1):

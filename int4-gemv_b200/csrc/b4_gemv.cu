@@ -1026,78 +1026,6 @@ int launch_split(const GemvProblem& p, const b4_gemv_config& c, void* ws, size_t
     return cudaLaunchKernelExC(&lc, s.fn, args);
 }
 
-int hybrid_plan(const GemvProblem& p, const b4_gemv_config& c, HybridPlan* plan)
-{
-    if (p.m != 1 || !(c.flags & B4_FLAG_HYBRID) || (c.flags & B4_FLAG_SPLIT)) return cudaErrorInvalidValue;
-    if (p.fmt != kNf4 || c.engine != B4_ENGINE_MMA_NF4 || p.in_f % 128) return cudaErrorInvalidValue;
-    if (!aligned(p.qw, 16) || !aligned(p.scale, 8)) return cudaErrorInvalidValue;
-    HybridPlan h = {};
-    h.fn = gemv_kernel_hybrid_nf4(c.stages);
-    if (!h.fn) return cudaErrorInvalidValue;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    h.grid = sm_count_cached(dev);
-    h.nst = p.in_f / 128;
-    const long long nblocks = (p.out_f + 15) / 16;
-    h.f = (int)(nblocks / h.grid);
-    h.R = (int)(nblocks - (long long)h.f * h.grid);
-    const long long split_steps = (long long)h.R * h.nst;
-    h.chunk = h.R ? (int)((split_steps + h.grid - 1) / h.grid) : 1;
-    h.maxp = h.R ? (h.nst - 1) / h.chunk + 2 : 1;
-    const int nsb_max = h.R ? (h.chunk + h.nst - 1) / h.nst + 1 : 0;
-    h.lbmax = nsb_max + h.f;
-    h.smem = (size_t)kNf4PairTableBytes + (size_t)p.in_f * 2 + (size_t)h.lbmax * 16 * 16 * 4 + 16;
-    int smem_max = 0;
-    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (e != cudaSuccess) return e;
-    if (h.smem > (size_t)smem_max) return cudaErrorInvalidValue;
-    e = ensure_smem(h.fn, dev, h.smem);
-    if (e != cudaSuccess) return e;
-    h.cnt_bytes = ((size_t)h.R * 4 + 255) / 256 * 256;
-    h.ws_bytes = h.R ? h.cnt_bytes + (size_t)h.R * h.maxp * 16 * sizeof(float) : 0;
-    *plan = h;
-    return cudaSuccess;
-}
-
-int launch_hybrid(const GemvProblem& p, const b4_gemv_config& c, void* ws, size_t ws_bytes, cudaStream_t st)
-{
-    HybridPlan h;
-    int e = hybrid_plan(p, c, &h);
-    if (e != cudaSuccess) return e;
-    if (h.ws_bytes && (!ws || !aligned(ws, 16) || ws_bytes < h.ws_bytes)) return cudaErrorInvalidValue;
-    HybridParams hp;
-    hp.qw = p.qw;
-    hp.scale = p.scale;
-    hp.x = static_cast<const __half*>(p.x);
-    hp.y = p.y;
-    hp.cnt = static_cast<unsigned*>(ws);
-    hp.part = ws ? reinterpret_cast<float*>(static_cast<char*>(ws) + h.cnt_bytes) : nullptr;
-    hp.in_f = p.in_f;
-    hp.out_f = p.out_f;
-    hp.nst = h.nst;
-    hp.f = h.f;
-    hp.R = h.R;
-    hp.chunk = h.chunk;
-    hp.maxp = h.maxp;
-    hp.lbmax = h.lbmax;
-    hp.x_vec = aligned(p.x, 16);
-    cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3((unsigned)h.grid);
-    lc.blockDim = dim3(32 * kHybridWarps);
-    lc.dynamicSmemBytes = h.smem;
-    lc.stream = st;
-    cudaLaunchAttribute attr[1];
-    if (c.flags & B4_FLAG_PDL) {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        lc.attrs = attr;
-        lc.numAttrs = 1;
-    }
-    void* args[] = {&hp};
-    return cudaLaunchKernelExC(&lc, h.fn, args);
-}
-
 // The dispatch rule's launch for cfg NULL.  A batch whose x does not fit
 // next to the tensor-pipe engines' buffers in shared memory (m * in_f too
 // large: down_proj at m >= 8) would fall back to the generic CUDA-core or
@@ -1176,7 +1104,7 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     if (e != cudaSuccess) return e;
     if (!cfg || cfg->engine == B4_ENGINE_AUTO)
         return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, reinterpret_cast<cudaStream_t>(stream));
-    if (cfg->flags & (B4_FLAG_SPLIT | B4_FLAG_HYBRID)) return cudaErrorInvalidValue;   // need a workspace: b4_gemv_ws
+    if (cfg->flags & B4_FLAG_SPLIT) return cudaErrorInvalidValue;   // needs a workspace: b4_gemv_ws
     return launch_gemv(p, *cfg, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -1203,13 +1131,6 @@ int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_co
     if (cfg) c = *cfg;
     else default_config_ws(p, &c);
     *bytes = 0;
-    if (c.flags & B4_FLAG_HYBRID) {
-        HybridPlan h;
-        e = hybrid_plan(p, c, &h);
-        if (e != cudaSuccess) return e;
-        *bytes = h.ws_bytes;
-        return cudaSuccess;
-    }
     if (!(c.flags & B4_FLAG_SPLIT)) return cudaSuccess;
     SplitPlan s;
     e = split_plan(p, c, &s);
@@ -1228,7 +1149,6 @@ int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     if (!cfg || cfg->engine == B4_ENGINE_AUTO)   // the rule of b4_gemv_ws never splits
         return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, st);
     if (cfg->flags & B4_FLAG_SPLIT) return launch_split(p, *cfg, ws, ws_bytes, st);
-    if (cfg->flags & B4_FLAG_HYBRID) return launch_hybrid(p, *cfg, ws, ws_bytes, st);
     return launch_gemv(p, *cfg, st);
 }
 

@@ -364,285 +364,4 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_split_nf4_kernel(const SplitPa
 void* gemv_kernel_split_int4(int depth, int groups);
 void* gemv_kernel_split_nf4(int depth);
 
-// ---- hybrid split: whole blocks per CTA plus an equal share of the rest --------
-//
-// One CTA of 16 warps per SM (C CTAs).  The first f * C row blocks are whole
-// blocks, f per CTA; the last R = nblocks - f * C blocks ("split blocks") are
-// cut along k into C equal runs of `chunk` k-steps, one per CTA.  A CTA's
-// k-step sequence is its split run FIRST, then its f whole blocks, and its 16
-// warps take equal consecutive ranges of that sequence.  So every CTA does
-// the same work (+-1 step), and the cross-CTA sum of a split block happens
-// early: the warps covering the CTA's split run count themselves in on a
-// shared-memory counter, the last of them adds the run's pieces per block and
-// hands the CTA's piece of each split block to the workspace protocol of
-// split_emit (store, fence, atomicAdd; the last CTA to arrive sums the
-// pieces in CTA order and stores y) while the other warps are still on the
-// whole blocks.  Whole blocks are summed over their warps in shared memory
-// at the end.  Deterministic; no spin, no named barrier.
-struct HybridParams {
-    const uint32_t* qw;
-    const void* scale;
-    const __half* x;
-    float* y;
-    float* part;          // [R][maxp][16]
-    unsigned* cnt;        // [R]
-    int in_f, out_f;
-    int nst;              // k-steps per row
-    int f;                // whole blocks per CTA
-    int R;                // split blocks (the last R)
-    int chunk;            // split-run k-steps per CTA
-    int maxp;             // piece slots per split block
-    int lbmax;            // local blocks per CTA (shared-memory partial slots)
-    int x_vec;
-};
-
-constexpr int kHybridWarps = 16;
-
-// Rows 16b + i (lane i < 16 holds row i's value v): the CTA's piece of split
-// block b (split index bl = b - f*C) into the workspace; the last CTA to
-// arrive sums the pieces and stores y.  Called by one whole warp.
-__device__ __forceinline__ void hybrid_split_store(const HybridParams& p, int b, float v)
-{
-    const int lane = threadIdx.x & 31;
-    const int C = gridDim.x;
-    const int bl = b - p.f * C;
-    const int first = (int)(((long long)bl * p.nst) / p.chunk);
-    const int last = (int)((((long long)bl + 1) * p.nst - 1) / p.chunk);
-    const int np = last - first + 1;
-    const long long r0 = (long long)b * 16;
-    if (np == 1) {
-        if (lane < 16 && r0 + lane < p.out_f) p.y[r0 + lane] = v;
-        return;
-    }
-    const int piece = (int)blockIdx.x - first;
-    if (lane < 16) __stcg(p.part + ((size_t)bl * p.maxp + piece) * 16 + lane, v);
-    __threadfence();
-    __syncwarp();
-    unsigned old = 0;
-    if (lane == 0) old = atomicAdd(p.cnt + bl, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != (unsigned)(np - 1)) return;
-    __threadfence();
-    if (lane < 16) {
-        const float* col = p.part + (size_t)bl * p.maxp * 16 + lane;
-        float t = 0.0f;
-        for (int k = 0; k < np; ++k) t += __ldcg(col + k * 16);
-        if (r0 + lane < p.out_f) p.y[r0 + lane] = t;
-    }
-    if (lane == 0) p.cnt[bl] = 0u;
-}
-
-// NF4 b64, the tensor-pipe decode of b4_gemv_split_nf4_kernel.
-template <int D>
-__global__ void __launch_bounds__(512, 1) b4_gemv_hybrid_nf4_kernel(const HybridParams p)
-{
-    extern __shared__ __align__(16) uint4 lsm[];
-    unsigned char* base = reinterpret_cast<unsigned char*>(lsm);
-    uint4* xs = reinterpret_cast<uint4*>(base + kNf4PairTableBytes);       // in_f / 8 slots
-    const int words = p.in_f >> 3;
-    float* red = reinterpret_cast<float*>(xs + words);                     // [lbmax][16 warps][16]
-    unsigned* split_done = reinterpret_cast<unsigned*>(red + p.lbmax * kHybridWarps * 16);
-    const int lane = threadIdx.x & 31;
-    const int g = lane >> 2, q = lane & 3;
-    const int warp = threadIdx.x >> 5;
-    const int nblk = p.in_f >> 6;
-    const uint32_t lane8 = (uint32_t)lane * 8;
-    const int C = gridDim.x, c = blockIdx.x;
-    const float* absmax = static_cast<const float*>(p.scale);
-
-    // this CTA's sequence: split run [s0, s0 + S) of the split region, then f whole blocks
-    const long long split_steps = (long long)p.R * p.nst;
-    const long long s0 = min((long long)c * p.chunk, split_steps);
-    const int S = (int)(min(s0 + p.chunk, split_steps) - s0);
-    const int T = S + p.f * p.nst;
-    const int per = (T + kHybridWarps - 1) / kHybridWarps;
-    const int t0 = min(warp * per, T);
-    const int n_it = min(t0 + per, T) - t0;
-    const int nsb = S ? (int)((s0 + S - 1) / p.nst - s0 / p.nst + 1) : 0;   // split blocks in the run
-    const int split_warps = S ? (S + per - 1) / per : 0;                    // warps 0 .. split_warps-1
-
-    // block, step and local block index of sequence position t
-    auto locate = [&](int t, int& blk, int& stp, int& lb) {
-        if (t < S) {
-            const long long u = s0 + t;
-            blk = p.f * C + (int)(u / p.nst);
-            stp = (int)(u % p.nst);
-            lb = (int)(u / p.nst - s0 / p.nst);
-        } else {
-            blk = c * p.f + (t - S) / p.nst;
-            stp = (t - S) % p.nst;
-            lb = nsb + (t - S) / p.nst;
-        }
-    };
-
-    int fb = 0, fs = 0, flb = 0, ft = t0;
-    if (n_it) locate(t0, fb, fs, flb);
-    const uint4 *pa = nullptr, *pb = nullptr;
-    const float2 *sa_p = nullptr, *sb_p = nullptr;
-    uint4 bufa[D] = {}, bufb[D] = {};
-    float2 ama[D] = {}, amb[D] = {};
-    auto aim = [&]() {
-        const long long last_row = p.out_f - 1;
-        const long long ra = min((long long)fb * 16 + g, last_row), rb = min((long long)fb * 16 + g + 8, last_row);
-        pa = reinterpret_cast<const uint4*>(p.qw + ra * words) + fs * 4 + q;
-        pb = reinterpret_cast<const uint4*>(p.qw + rb * words) + fs * 4 + q;
-        sa_p = reinterpret_cast<const float2*>(absmax + ra * nblk) + fs;
-        sb_p = reinterpret_cast<const float2*>(absmax + rb * nblk) + fs;
-    };
-    auto fetch = [&](int slot) {
-        const WordVec<4> va = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
-        const WordVec<4> vb = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
-        bufa[slot] = make_uint4(va.w[0], va.w[1], va.w[2], va.w[3]);
-        bufb[slot] = make_uint4(vb.w[0], vb.w[1], vb.w[2], vb.w[3]);
-        ama[slot] = __ldg(sa_p);
-        amb[slot] = __ldg(sb_p);
-        pa += 4;
-        pb += 4;
-        ++sa_p;
-        ++sb_p;
-        ++ft;
-        if (ft == S) {             // the split run ends: the whole blocks start at step 0
-            fb = c * p.f;
-            fs = 0;
-            aim();
-        } else if (++fs == p.nst) {
-            ++fb;
-            fs = 0;
-            aim();
-        }
-    };
-
-    if (n_it) {   // weights first: they do not depend on the preceding grid
-        aim();
-#pragma unroll
-        for (int d = 0; d < D - 1; ++d)
-            if (d < n_it) fetch(d);
-    }
-    nf4_pair_table_fill(base);
-    if (threadIdx.x == 0) *split_done = 0u;
-    asm volatile("griddepcontrol.launch_dependents;");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = v; });
-    __syncthreads();
-
-    // the warp whose count completes the split run adds the run's pieces per
-    // block (over the warps that cover it, in warp order) and stores the CTA's
-    // piece of each split block
-    auto split_run_done = [&]() {
-        __threadfence_block();
-        __syncwarp();
-        unsigned old = 0;
-        if (lane == 0) old = atomicAdd(split_done, 1u);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old != (unsigned)(split_warps - 1)) return;
-        __threadfence_block();
-        for (int j = 0; j < nsb; ++j) {
-            // sequence range of local split block j, and the warps covering it
-            const long long u0 = max(s0, (s0 / p.nst + j) * p.nst), u1 = min(s0 + S, (s0 / p.nst + j + 1) * p.nst);
-            const int w0 = (int)((u0 - s0) / per), w1 = (int)((u1 - 1 - s0) / per);
-            float v = 0.0f;
-            if (lane < 16)
-                for (int w = w0; w <= w1; ++w) v += red[(j * kHybridWarps + w) * 16 + lane];
-            hybrid_split_store(p, p.f * C + (int)(s0 / p.nst) + j, v);
-        }
-    };
-
-    if (n_it) {
-        const bool x_lane = g == (q >> 1);
-        const unsigned char* tb = base;
-        int cb, cs, clb, ct = t0;
-        locate(t0, cb, cs, clb);
-        const uint4* xp = xs + cs * 16 + q * 4;
-        float acc_a = 0.0f, acc_b = 0.0f;
-        uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                       make_uint4(0, 0, 0, 0)};
-        for (int it0 = 0; it0 < n_it; it0 += D) {
-#pragma unroll
-            for (int d = 0; d < D; ++d) {
-                const int it = it0 + d;
-                if (it < n_it) {
-                    const int nxt = (d + D - 1) % D;
-                    if (it + D - 1 < n_it) fetch(nxt);
-                    if (x_lane) {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) xv[i] = xp[i];
-                    }
-                    xp += 16;
-                    const uint32_t wa[4] = {bufa[d].x, bufa[d].y, bufa[d].z, bufa[d].w};
-                    const uint32_t wb[4] = {bufb[d].x, bufb[d].y, bufb[d].z, bufb[d].w};
-                    float cc[4][4];
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) cc[h][0] = cc[h][1] = cc[h][2] = cc[h][3] = 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
-                        uint32_t oa0, oa1, ob0, ob1;
-                        if (j & 1) {
-                            oa0 = nf4_pair_offset<2>(ua, lane8);
-                            oa1 = nf4_pair_offset<3>(ua, lane8);
-                            ob0 = nf4_pair_offset<2>(ub, lane8);
-                            ob1 = nf4_pair_offset<3>(ub, lane8);
-                        } else {
-                            oa0 = nf4_pair_offset<0>(ua, lane8);
-                            oa1 = nf4_pair_offset<1>(ua, lane8);
-                            ob0 = nf4_pair_offset<0>(ub, lane8);
-                            ob1 = nf4_pair_offset<1>(ub, lane8);
-                        }
-                        const uint2 ea0 = nf4_pair_lookup(tb, oa0), eb0 = nf4_pair_lookup(tb, ob0);
-                        const uint2 ea1 = nf4_pair_lookup(tb, oa1), eb1 = nf4_pair_lookup(tb, ob1);
-                        const uint32_t a_hi[4] = {ea0.x, eb0.x, ea1.x, eb1.x};
-                        const uint32_t a_lo[4] = {ea0.y, eb0.y, ea1.y, eb1.y};
-                        const uint4 xq = xv[j >> 1];
-                        const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
-                        const int ch = (j & 1) * 2;
-                        mma_16816_pure(cc[ch], a_hi, b0, b1, cc[ch]);
-                        mma_16816_pure(cc[ch + 1], a_lo, b0, b1, cc[ch + 1]);
-                    }
-                    const float d00 = (cc[0][0] + cc[1][0]) + (cc[2][0] + cc[3][0]);   // row g, NF4 block 0
-                    const float d01 = (cc[0][1] + cc[1][1]) + (cc[2][1] + cc[3][1]);   // row g, NF4 block 1
-                    const float d10 = (cc[0][2] + cc[1][2]) + (cc[2][2] + cc[3][2]);   // row g+8, NF4 block 0
-                    const float d11 = (cc[0][3] + cc[1][3]) + (cc[2][3] + cc[3][3]);   // row g+8, NF4 block 1
-                    acc_a = fmaf(d00, ama[d].x, acc_a);
-                    acc_a = fmaf(d01, ama[d].y, acc_a);
-                    acc_b = fmaf(d10, amb[d].x, acc_b);
-                    acc_b = fmaf(d11, amb[d].y, acc_b);
-                    ++ct;
-                    const bool run_end = ct == S;                 // the split run ends here
-                    const bool blk_end = run_end || ++cs == p.nst;
-                    if (blk_end || it == n_it - 1) {
-                        // this warp's piece of local block clb (rows g, g+8 on lanes q = 0)
-                        if (q == 0) {
-                            red[(clb * kHybridWarps + warp) * 16 + g] = acc_a;
-                            red[(clb * kHybridWarps + warp) * 16 + g + 8] = acc_b;
-                        }
-                        acc_a = acc_b = 0.0f;
-                        if (ct <= S && (run_end || it == n_it - 1)) split_run_done();
-                        if (blk_end) {
-                            if (run_end) cb = c * p.f;
-                            else ++cb;
-                            cs = 0;
-                            ++clb;
-                            xp = xs + q * 4;
-                        }
-                    }
-                }
-            }
-        }
-    }
-    __syncthreads();
-    // whole blocks: warp j adds block nsb + j over the warps that cover it
-    for (int j = warp; j < p.f; j += kHybridWarps) {
-        const int u0 = S + j * p.nst, u1 = u0 + p.nst;          // sequence range of the block
-        const int w0 = u0 / per, w1 = (u1 - 1) / per;
-        const long long r0 = ((long long)c * p.f + j) * 16;
-        if (lane < 16) {
-            float v = 0.0f;
-            for (int w = w0; w <= w1; ++w) v += red[((nsb + j) * kHybridWarps + w) * 16 + lane];
-            if (r0 + lane < p.out_f) p.y[r0 + lane] = v;
-        }
-    }
-}
-
-void* gemv_kernel_hybrid_nf4(int depth);
-
 }  // namespace b4

@@ -55,16 +55,6 @@ int split_plan(const GemvProblem& p, const b4_gemv_config& cfg, SplitPlan* plan)
 // (16-byte aligned, at least the plan's ws_bytes, counters zero).
 int launch_split(const GemvProblem& p, const b4_gemv_config& cfg, void* ws, size_t ws_bytes, cudaStream_t st);
 
-// The hybrid split (b4_gemv_split.cuh, B4_FLAG_HYBRID): kernel, the split
-// geometry, shared memory and workspace on the current device.
-struct HybridPlan {
-    void* fn;
-    int grid, nst, f, R, chunk, maxp, lbmax;
-    size_t smem, cnt_bytes, ws_bytes;
-};
-int hybrid_plan(const GemvProblem& p, const b4_gemv_config& cfg, HybridPlan* plan);
-int launch_hybrid(const GemvProblem& p, const b4_gemv_config& cfg, void* ws, size_t ws_bytes, cudaStream_t st);
-
 // The workspace rule: default_config, switched to a split config (B4_FLAG_SPLIT)
 // for batch-1 matrices with too few rows to balance whole-row tiles.
 void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg);

@@ -24,12 +24,3 @@ void* b4::gemv_kernel_split_nf4(int depth)
     }
     return nullptr;
 }
-
-void* b4::gemv_kernel_hybrid_nf4(int depth)
-{
-    switch (depth) {
-        case 2: return (void*)&b4::b4_gemv_hybrid_nf4_kernel<2>;
-        case 3: return (void*)&b4::b4_gemv_hybrid_nf4_kernel<3>;
-    }
-    return nullptr;
-}

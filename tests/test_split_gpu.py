@@ -172,36 +172,3 @@ def test_split_argument_checks(cuda):
     assert lib.b4_gemv_ws(*args, None, None, 0, st) == 0
     assert lib.b4_gemv_ws(*args, ctypes.byref(cfg), p(ws.data_ptr()), need, st) == 0
     torch.cuda.synchronize()
-
-
-def hybrid_config(stages):
-    return {"vec_words": 4, "rows_per_warp": 16, "batch_tile": 1, "warps_k": 16, "row_groups": 1,
-            "stages": stages, "stage_groups": 0, "engine": b4gemv._lib.ENGINE_MMA_NF4, "flags": b4gemv.FLAG_HYBRID}
-
-
-@pytest.mark.parametrize("stages", [2, 3])
-@pytest.mark.parametrize("shape", [(3584, 18944), (3584, 3584), (2049, 1024), (8192, 8192), (300, 4096),
-                                   (18944, 3584), (16, 256)])
-def test_nf4_hybrid_split(cuda, oracle, stages, shape):
-    """NF4 hybrid split (B4_FLAG_HYBRID): 16-warp CTAs with whole blocks plus an
-    equal run of split blocks; against the double GEMV, bit-identical repeats,
-    counters zero afterwards; shapes with and without whole blocks or split
-    blocks."""
-    import torch
-    out_f, in_f = shape
-    rng = np.random.default_rng(out_f * 7 + in_f + stages)
-    W, X = rand_problem(rng, out_f, in_f)
-    qw, sc = quantised(1, W, cuda)
-    cfg = hybrid_config(stages)
-    n = b4gemv.workspace_size(1, in_f, out_f, 1, cfg)
-    ws = torch.zeros(max(n, 16), dtype=torch.uint8, device=cuda)
-    Xd = to_dev(X, cuda)
-    ys = [b4gemv.gemv_ws(1, qw, sc, Xd, config=cfg, ws=ws).clone() for _ in range(2)]
-    torch.cuda.synchronize()
-    assert torch.equal(ys[0], ys[1])
-    assert rel_err(ys[0].cpu().numpy(), f64_ref(oracle, 1, qw, sc, X)) < TOL, (shape, stages)
-    # the split blocks' counters (the workspace's first 4 * R bytes) are zero again
-    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
-    nblocks = (out_f + 15) // 16
-    R = nblocks - (nblocks // sms) * sms
-    assert int(ws[: 4 * R].count_nonzero()) == 0
