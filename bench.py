@@ -651,11 +651,11 @@ def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
         return d.max(a.elapsed_time(b) * 1e3 / (n * reps), dev)
 
     us_max = time_layer()
-    # INT4 at N > 1: o/down with the all-reduce fused into the GEMV over peer
-    # memory (b4_tp_gemv_p2p) instead of the NCCL all-reduce
+    # N > 1: o/down with the all-reduce fused into the GEMV over peer memory
+    # (b4_tp_gemv_p2p) instead of the NCCL all-reduce
     us_p2p = None
     p2p_status = None
-    if d.world > 1 and fmt == 0:
+    if d.world > 1:
         p2p = P2pComm(d.rank, d.world, max_rows=8192)
         layer.p2p = p2p
         us_p2p = time_layer()

@@ -327,8 +327,9 @@ int b4_tp_gemv_allreduce(int fmt, const uint32_t* qw_shard, const void* scale_sh
  * every peer -> b4_p2p_open_peer for each peer's handle.  One process per GPU
  * (CUDA IPC).  Every rank must make the same sequence of calls; the call
  * counter lives on the device, so calls captured in a CUDA graph may be
- * replayed.  flags: B4_FLAG_PDL (or 0).  INT4, batch 1.  No counterpart in
- * the reference (it has no multi-GPU code). */
+ * replayed.  flags: B4_FLAG_PDL (or 0).  Batch 1; INT4, or NF4 with in_shard
+ * a multiple of 128 (the NF4 kernel's MMA k-step).  No counterpart in the
+ * reference (it has no multi-GPU code). */
 typedef struct b4_p2p b4_p2p;
 int b4_p2p_create(int rank, int world, int max_rows, b4_p2p** out);
 int b4_p2p_ipc_handle(const b4_p2p* p2p, void* handle64);

@@ -231,7 +231,9 @@ class TPDecodeLayer:
         qw, sc = self.w[name]
         if self.tp == 1:
             return self._gemv(name, x, y, stream)
-        if self.p2p is not None and self.fmt == FMT_INT4_G128:
+        # the fused peer-memory kernel takes NF4 shards of whole 128-column
+        # steps (its MMA k-step); narrower NF4 shards keep the NCCL all-reduce
+        if self.p2p is not None and (self.fmt == FMT_INT4_G128 or (qw.shape[1] * 8) % 128 == 0):
             check(f"tp p2p {name}", load().b4_tp_gemv_p2p(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
                                                           qw.shape[0], self.p2p.ptr,
                                                           FLAG_PDL if self.pdl else 0, stream))

@@ -882,6 +882,45 @@ int launch_lean_int4_p2p(const GemvProblem& p, const b4_gemv_config& c, const P2
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st, true);
 }
 
+// A row-parallel NF4 shard at batch 1 with the peer-memory all-reduce fused
+// into the epilogue: the tensor-pipe NF4 kernel's P2P variant.  Geometry:
+// 8 warps per CTA, the fewest power-of-two row groups whose tiles fit two
+// resident CTAs per SM, depth-3 register pipeline.
+int launch_nf4_mma_p2p(const GemvProblem& p, const P2pArgs& a, int flags, cudaStream_t st)
+{
+    if (p.fmt != kNf4 || p.m != 1 || p.in_f % 128) return cudaErrorInvalidValue;
+    if (!aligned(p.qw, 16) || !aligned(p.scale, 8)) return cudaErrorInvalidValue;
+    if (p.out_f > a.max_rows) return cudaErrorInvalidValue;
+    if (nf4_mma_smem(p.in_f, 8, 1) > kTmaSmemLimit) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_nf4_mma_p2p(3);
+    if (!fn) return cudaErrorInvalidValue;
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const long long blocks = (p.out_f + 15) / 16, cap = 2LL * sm_count_cached(dev);
+    int rg = 1;
+    while (rg < 8 && (blocks + rg - 1) / rg > cap) rg *= 2;
+    const int kw = 8 / rg;
+    const long long tiles = (blocks + rg - 1) / rg;
+    LeanNf4Params lp = {};
+    lp.seg[0].qw = p.qw;
+    lp.seg[0].absmax = static_cast<const float*>(p.scale);
+    lp.seg[0].y = p.y;
+    lp.seg[0].out_f = p.out_f;
+    lp.seg[0].tile_end = (int)tiles;
+    lp.nseg = 1;
+    lp.n_tiles = (int)tiles;
+    lp.x = static_cast<const __half*>(p.x);
+    lp.in_f = p.in_f;
+    lp.kw = kw;
+    lp.rg = rg;
+    lp.tr = 16;
+    lp.x_vec = aligned(p.x, 16);
+    lp.p2p = a;
+    // every CTA resident at once: a CTA waits only for the CTA of the same index on the peers
+    return launch_persistent(fn, &lp, tiles, 256, nf4_mma_smem(p.in_f, kw, rg), flags, st, true);
+}
+
 int launch_gemv_nf4_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
     if (p.fmt != kNf4) return cudaErrorInvalidValue;

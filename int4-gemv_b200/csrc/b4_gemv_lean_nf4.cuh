@@ -50,6 +50,7 @@ struct LeanNf4Params {
     int kw, rg;
     int tr;      // engine 7: rows of each warp's 16-row block that carry weights (1..16)
     int x_vec;
+    P2pArgs p2p; // engine 7 P2P kernel: the all-reduce of y over peer memory (b4_p2p.cuh)
 };
 
 template <int BYTES>

@@ -78,7 +78,11 @@ __device__ __forceinline__ void nf4_pair_table_fill(unsigned char* base)
     }
 }
 
-template <int D>   // D >= 2
+// P2P = 1: a row-parallel shard of a tensor-parallel GEMV, y all-reduced over
+// the ranks through peer memory as in the INT4 lean kernel (b4_p2p.cuh): each
+// 16-row block's partial rows are pushed to every rank as soon as they are
+// done, and summed in rank order after the CTA's last block.  One segment.
+template <int D, int P2P = 0>   // D >= 2
 __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Params p)
 {
     extern __shared__ __align__(16) uint4 lsm[];
@@ -165,6 +169,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     asm volatile("griddepcontrol.wait;" ::: "memory");
     stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = v; });
     __syncthreads();
+    const uint32_t epoch = P2P ? p2p_epoch(p.p2p) : 0u;
 
     // B carries x only on lanes (g, q) with g == q >> 1 (columns 0/1 = blocks 0/1)
     const bool x_lane = g == (q >> 1);
@@ -238,7 +243,30 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
         }
 
         // rows r0+g and r0+g+8: lanes q = 0 hold them (columns 0 and 1 of D)
-        if (p.kw == 1) {
+        if constexpr (P2P) {
+            // push this block's partial rows to every rank; summed after the last block
+            const int nrows = max(0, min(p.tr, out_f - r0));
+            if (p.kw == 1) {
+                // lane i < tr: row r0 + i, from lane (i & 7) * 4 (q = 0)
+                const float va_i = __shfl_sync(0xffffffffu, acc_a, (lane & 7) * 4);
+                const float vb_i = __shfl_sync(0xffffffffu, acc_b, (lane & 7) * 4);
+                p2p_push(p.p2p, epoch, r0, nrows, lane < 8 ? va_i : vb_i);
+            } else {
+                float* mine = red + (grp * p.kw + ks) * 16;
+                if (q == 0) {
+                    mine[g] = acc_a;
+                    mine[g + 8] = acc_b;
+                }
+                __syncthreads();
+                if (ks == 0) {
+                    float t = 0.0f;
+                    if (lane < 16)
+                        for (int k2 = 0; k2 < p.kw; ++k2) t += red[(grp * p.kw + k2) * 16 + lane];
+                    p2p_push(p.p2p, epoch, r0, nrows, t);
+                }
+                __syncthreads();
+            }
+        } else if (p.kw == 1) {
             if (q == 0) {
                 if (va) y[r0 + g] = acc_a;
                 if (vb) y[r0 + g + 8] = acc_b;
@@ -258,8 +286,20 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
             __syncthreads();
         }
     }
+    if constexpr (P2P) {
+        // every rank's copy of this warp's blocks, summed in rank order (one segment)
+        if (ks == 0) {
+            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+                const int rr = t * rows_per_tile + grp * p.tr;
+                p2p_reduce(p.p2p, epoch, rr, max(0, min(p.tr, p.seg[0].out_f - rr)), p.seg[0].y);
+            }
+        }
+        __syncthreads();   // every warp of the CTA has read the epoch
+        if (threadIdx.x == 0) p2p_finish(p.p2p, epoch);
+    }
 }
 
 void* gemv_kernel_nf4_mma(int depth);
+void* gemv_kernel_nf4_mma_p2p(int depth);
 
 }  // namespace b4

@@ -33,6 +33,8 @@ int launch_gemv(const GemvProblem& p, const b4_gemv_config& cfg, cudaStream_t st
 // A row-parallel INT4 shard at batch 1 whose epilogue all-reduces y over the
 // ranks' peer memory (b4_p2p.cuh); cfg must be a lean INT4 config.
 int launch_lean_int4_p2p(const GemvProblem& p, const b4_gemv_config& cfg, const P2pArgs& a, cudaStream_t st);
+// ... and an NF4 shard (in_f a multiple of 128) on the tensor-pipe NF4 kernel.
+int launch_nf4_mma_p2p(const GemvProblem& p, const P2pArgs& a, int flags, cudaStream_t st);
 
 // Several weight matrices over one x (b4_gemv_multi): the dispatch rule over
 // their total rows, and the launch (one kernel for the lean engines at m = 1).

@@ -133,7 +133,8 @@ int b4_tp_gemv_p2p(int fmt, const uint32_t* qw_shard, const void* scale_shard, c
     const GemvProblem p{fmt, qw_shard, scale_shard, x_shard, y, in_shard, out_f, 1, in_shard, out_f};
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
-    if (fmt != B4_FMT_INT4_G128 || (flags & ~B4_FLAG_PDL)) return cudaErrorInvalidValue;
+    if (flags & ~B4_FLAG_PDL) return cudaErrorInvalidValue;
+    if (fmt == B4_FMT_NF4_B64) return launch_nf4_mma_p2p(p, args_of(h), flags, reinterpret_cast<cudaStream_t>(stream));
     b4_gemv_config c;
     default_config(p, &c);
     c.flags = flags;

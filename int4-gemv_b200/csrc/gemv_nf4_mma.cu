@@ -11,3 +11,9 @@ void* b4::gemv_kernel_nf4_mma(int depth)
     }
     return nullptr;
 }
+
+// the row-parallel shard with the all-reduce fused in (b4_tp_gemv_p2p)
+void* b4::gemv_kernel_nf4_mma_p2p(int depth)
+{
+    return depth == 3 ? (void*)&b4::b4_gemv_nf4_mma_kernel<3, 1> : nullptr;
+}

@@ -223,7 +223,7 @@ def test_tp1_layer_fused_and_pdl_match_separate_launches(cuda, fmt):
             assert rel_err(lay.buf[n].cpu().numpy(), b.cpu().numpy().astype(np.float64)) < 1e-5, (n, fused, pdl)
 
 
-def _p2p_worker(rank, world, port, mode, results):
+def _p2p_worker(rank, world, port, mode, results, fmt=0):
     import sys
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     here = os.path.dirname(os.path.abspath(__file__))
@@ -248,9 +248,9 @@ def _p2p_worker(rank, world, port, mode, results):
     lib = b4gemv.load()
     out = {}
     try:
-        qw, sc = quantise_full(0, out_f, in_f, 7, dev)
+        qw, sc = quantise_full(fmt, out_f, in_f, 7, dev)
         c0, c1 = col_range(in_f, 128, world, rank)
-        qs, ss = shard_columns(0, qw, sc, c0, c1)
+        qs, ss = shard_columns(fmt, qw, sc, c0, c1)
         g = torch.Generator(device=dev)
         g.manual_seed(3)
         x = torch.randn((1, in_f), generator=g, device=dev).half()
@@ -261,11 +261,11 @@ def _p2p_worker(rank, world, port, mode, results):
         flags = 0
         if mode == "timeout":
             if rank == 0:   # the peer never makes this call: every wait must give up by itself
-                assert lib.b4_tp_gemv_p2p(0, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, st) == 0
+                assert lib.b4_tp_gemv_p2p(fmt, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, st) == 0
                 torch.cuda.synchronize()
                 out["status"] = p2p.status(clear=True)
                 out["rows_nan"] = bool(torch.isnan(y).all().item())   # no partial sums pass as results
-                y2 = b4gemv.gemv(0, qw, sc, x)      # the GPU is still usable
+                y2 = b4gemv.gemv(fmt, qw, sc, x)      # the GPU is still usable
                 torch.cuda.synchronize()
                 out["after"] = bool(torch.isfinite(y2).all().item())
             dist.barrier()
@@ -275,7 +275,7 @@ def _p2p_worker(rank, world, port, mode, results):
         for i in range(4):   # successive calls: the call counter advances on the device
             flags = b4gemv.FLAG_PDL if i >= 2 else 0
             y.fill_(float("nan"))
-            assert lib.b4_tp_gemv_p2p(0, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, st) == 0
+            assert lib.b4_tp_gemv_p2p(fmt, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, st) == 0
             torch.cuda.synchronize()
             ys.append(y.clone())
         # captured once, replayed: still a fresh epoch every replay
@@ -284,7 +284,7 @@ def _p2p_worker(rank, world, port, mode, results):
         cs.wait_stream(torch.cuda.current_stream())
         with torch.cuda.graph(graph, stream=cs, capture_error_mode="relaxed"):
             s2 = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-            lib.b4_tp_gemv_p2p(0, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, s2)
+            lib.b4_tp_gemv_p2p(fmt, P(qs), P(ss), P(xs), P(y), c1 - c0, out_f, p2p.ptr, flags, s2)
         torch.cuda.current_stream().wait_stream(cs)
         for _ in range(3):
             y.fill_(float("nan"))
@@ -294,12 +294,12 @@ def _p2p_worker(rank, world, port, mode, results):
         del graph
         out["status"] = p2p.status()
         out["same_calls"] = all(torch.equal(ys[0], t) for t in ys)
-        ref = Oracle().gemv_f64(False, qw.cpu().numpy().view(np.uint32), sc.cpu().numpy().view(np.uint16),
-                                x.cpu().numpy())
+        ref = Oracle().gemv_f64(fmt == 1, qw.cpu().numpy().view(np.uint32),
+                                sc.cpu().numpy().view(np.uint16) if fmt == 0 else sc.cpu().numpy(), x.cpu().numpy())
         out["err"] = rel_err(ys[0].cpu().numpy(), ref)
         comm = NcclComm(rank, world)
         yn = torch.zeros((1, out_f), device=dev)
-        assert lib.b4_tp_gemv_allreduce(0, P(qs), P(ss), P(xs), P(yn), c1 - c0, out_f, 1, comm.ptr, st) == 0
+        assert lib.b4_tp_gemv_allreduce(fmt, P(qs), P(ss), P(xs), P(yn), c1 - c0, out_f, 1, comm.ptr, st) == 0
         torch.cuda.synchronize()
         comm.destroy()
         out["vs_nccl"] = rel_err(ys[0].cpu().numpy(), yn.cpu().numpy().astype(np.float64))
@@ -309,8 +309,8 @@ def _p2p_worker(rank, world, port, mode, results):
         # the decode layer with both row-parallel projections on the P2P path
         # against the same layer on NCCL (world 2: a + b either way, bit for bit)
         comm = NcclComm(rank, world)
-        lp = TPDecodeLayer(0, rank, world, comm, dev, seed=3, pdl=True, p2p=p2p, **SMALL)
-        ln = TPDecodeLayer(0, rank, world, comm, dev, seed=3, pdl=True, **SMALL)
+        lp = TPDecodeLayer(fmt, rank, world, comm, dev, seed=3, pdl=True, p2p=p2p, **SMALL)
+        ln = TPDecodeLayer(fmt, rank, world, comm, dev, seed=3, pdl=True, **SMALL)
         xl = torch.randn((1, SMALL["hidden"]), generator=g, device=dev).half()
         a0, a1 = lp.ranges["o"]
         attn = torch.randn((1, SMALL["q_out"]), generator=g, device=dev).half()[:, a0:a1].contiguous()
@@ -327,12 +327,12 @@ def _p2p_worker(rank, world, port, mode, results):
         dist.destroy_process_group()
 
 
-def _run_p2p(world, mode):
+def _run_p2p(world, mode, fmt=0):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     res = ctx.Manager().dict()
     port = _port()
-    ps = [ctx.Process(target=_p2p_worker, args=(r, world, port, mode, res)) for r in range(world)]
+    ps = [ctx.Process(target=_p2p_worker, args=(r, world, port, mode, res, fmt)) for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
@@ -345,8 +345,9 @@ def _run_p2p(world, mode):
 
 
 @pytest.mark.skipif(_n_gpus() < 2, reason="needs 2 GPUs")
-def test_p2p_rowparallel_gemv_matches_nccl_and_is_identical_on_every_rank():
-    res = _run_p2p(2, "parity")
+@pytest.mark.parametrize("fmt", [0, 1], ids=["int4", "nf4"])
+def test_p2p_rowparallel_gemv_matches_nccl_and_is_identical_on_every_rank(fmt):
+    res = _run_p2p(2, "parity", fmt)
     for r in (0, 1):
         assert res[r]["status"] == 0, res
         assert res[r]["same_calls"], res       # 4 calls + 3 graph replays, bit for bit
@@ -358,8 +359,9 @@ def test_p2p_rowparallel_gemv_matches_nccl_and_is_identical_on_every_rank():
 
 
 @pytest.mark.skipif(_n_gpus() < 2, reason="needs 2 GPUs")
-def test_p2p_wait_for_a_peer_that_never_arrives_times_out_and_the_gpu_stays_usable():
-    res = _run_p2p(2, "timeout")
+@pytest.mark.parametrize("fmt", [0, 1], ids=["int4", "nf4"])
+def test_p2p_wait_for_a_peer_that_never_arrives_times_out_and_the_gpu_stays_usable(fmt):
+    res = _run_p2p(2, "timeout", fmt)
     assert res[0]["status"] == 10901, res      # B4_STATUS_TIMEOUT
     assert res[0]["rows_nan"], res
     assert res[0]["after"], res
