@@ -20,10 +20,13 @@
 //     to within 2^-22 relative; the MMA multiplies both by fp16 x exactly and
 //     accumulates in fp32, so y carries fp32-level rounding, like an FMA
 //     chain over the fp32 dequantised weights.
-//   * MMA m16n8k16: lane (g, q) holds rows r0+g and r0+g+8; a 128-column step
-//     of a row is 64 bytes, lane q taking bytes 16q .. 16q+15 (columns 32q ..
-//     32q+31, NF4 block q >> 1).  MMA j uses bytes 2j and 2j+1 of each of its
-//     rows.  The two NF4 blocks of the step are kept apart by B's columns:
+//   * MMA m16n8k16, one per weight row set: lane (g, q) streams rows r0+g and
+//     r0+g+8; a 128-column step of a row is 64 bytes, lane q taking bytes
+//     16q .. 16q+15 (columns 32q .. 32q+31, NF4 block q >> 1).  MMA j of row
+//     r0+g uses bytes 2j and 2j+1: A row g holds their high parts and A row
+//     g+8 their low parts, so the two words of one lookup are A registers
+//     (a0, a1) or (a2, a3) as loaded, and D row g + D row g+8 is the sum.
+//     Rows r0+8 .. r0+15 take a second MMA with the same B.  The two NF4 blocks of the step are kept apart by B's columns:
 //     column 0 of B holds x at block 0's positions (zero elsewhere), column 1
 //     x at block 1's, the rest zero, so D[row][0] and D[row][1] are the two
 //     blocks' partial sums and the absmax of each block scales its own sum
@@ -199,7 +202,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
                     xp += 16 * p.kw;
                     const uint32_t wa[4] = {bufa[d].x, bufa[d].y, bufa[d].z, bufa[d].w};
                     const uint32_t wb[4] = {bufb[d].x, bufb[d].y, bufb[d].z, bufb[d].w};
-                    // four chains: (j odd?, lo part?)
+                    // four chains: (j odd?, row g + 8?)
                     float c[4][4];
 #pragma unroll
                     for (int h = 0; h < 4; ++h) c[h][0] = c[h][1] = c[h][2] = c[h][3] = 0.0f;
@@ -221,19 +224,24 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
                         }
                         const uint2 ea0 = nf4_pair_lookup(tb, oa0), eb0 = nf4_pair_lookup(tb, ob0);
                         const uint2 ea1 = nf4_pair_lookup(tb, oa1), eb1 = nf4_pair_lookup(tb, ob1);
-                        const uint32_t a_hi[4] = {ea0.x, eb0.x, ea1.x, eb1.x};
-                        const uint32_t a_lo[4] = {ea0.y, eb0.y, ea1.y, eb1.y};
+                        // one MMA per 8-row set: A rows 0-7 = the rows' high parts,
+                        // rows 8-15 = their low parts, so each lookup's two words
+                        // are A registers (a0, a1) or (a2, a3) as they come
+                        const uint32_t a_ra[4] = {ea0.x, ea0.y, ea1.x, ea1.y};
+                        const uint32_t a_rb[4] = {eb0.x, eb0.y, eb1.x, eb1.y};
                         // x[32q + 4j .. +3]: halves 0..3 or 4..7 of slot j >> 1
                         const uint4 xq = xv[j >> 1];
                         const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
                         const int ch = (j & 1) * 2;
-                        mma_16816_pure(c[ch], a_hi, b0, b1, c[ch]);
-                        mma_16816_pure(c[ch + 1], a_lo, b0, b1, c[ch + 1]);
+                        mma_16816_pure(c[ch], a_ra, b0, b1, c[ch]);
+                        mma_16816_pure(c[ch + 1], a_rb, b0, b1, c[ch + 1]);
                     }
-                    const float d00 = (c[0][0] + c[1][0]) + (c[2][0] + c[3][0]);   // row g, block 0
-                    const float d01 = (c[0][1] + c[1][1]) + (c[2][1] + c[3][1]);   // row g, block 1
-                    const float d10 = (c[0][2] + c[1][2]) + (c[2][2] + c[3][2]);   // row g+8, block 0
-                    const float d11 = (c[0][3] + c[1][3]) + (c[2][3] + c[3][3]);   // row g+8, block 1
+                    // D of a row's MMA (lane q = 0): [0] high block 0, [1] high
+                    // block 1, [2] low block 0, [3] low block 1
+                    const float d00 = (c[0][0] + c[0][2]) + (c[2][0] + c[2][2]);   // row g, block 0
+                    const float d01 = (c[0][1] + c[0][3]) + (c[2][1] + c[2][3]);   // row g, block 1
+                    const float d10 = (c[1][0] + c[1][2]) + (c[3][0] + c[3][2]);   // row g+8, block 0
+                    const float d11 = (c[1][1] + c[1][3]) + (c[3][1] + c[3][3]);   // row g+8, block 1
                     acc_a = fmaf(d00, ama[d].x, acc_a);
                     acc_a = fmaf(d01, ama[d].y, acc_a);
                     acc_b = fmaf(d10, amb[d].x, acc_b);
