@@ -883,25 +883,40 @@ int launch_lean_int4_p2p(const GemvProblem& p, const b4_gemv_config& c, const P2
 }
 
 // A row-parallel NF4 shard at batch 1 with the peer-memory all-reduce fused
-// into the epilogue: the tensor-pipe NF4 kernel's P2P variant.  Geometry:
-// 8 warps per CTA, the fewest power-of-two row groups whose tiles fit two
-// resident CTAs per SM, depth-3 register pipeline.
+// into the epilogue: the tensor-pipe NF4 kernel's P2P variant.  Geometry: the
+// dispatch rule's when it picks this kernel (so each rank's partial sums are
+// the plain GEMV's, bit for bit), else 8 warps per CTA, the fewest
+// power-of-two row groups whose tiles fit two resident CTAs per SM, depth 3.
 int launch_nf4_mma_p2p(const GemvProblem& p, const P2pArgs& a, int flags, cudaStream_t st)
 {
     if (p.fmt != kNf4 || p.m != 1 || p.in_f % 128) return cudaErrorInvalidValue;
     if (!aligned(p.qw, 16) || !aligned(p.scale, 8)) return cudaErrorInvalidValue;
     if (p.out_f > a.max_rows) return cudaErrorInvalidValue;
-    if (nf4_mma_smem(p.in_f, 8, 1) > kTmaSmemLimit) return cudaErrorInvalidValue;
-    void* fn = gemv_kernel_nf4_mma_p2p(3);
-    if (!fn) return cudaErrorInvalidValue;
     int dev = 0;
     const cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const long long blocks = (p.out_f + 15) / 16, cap = 2LL * sm_count_cached(dev);
-    int rg = 1;
-    while (rg < 8 && (blocks + rg - 1) / rg > cap) rg *= 2;
-    const int kw = 8 / rg;
-    const long long tiles = (blocks + rg - 1) / rg;
+    b4_gemv_config c;
+    default_config(p, &c);
+    int kw, rg, tr, depth;
+    if (c.engine == B4_ENGINE_MMA_NF4 && gemv_kernel_nf4_mma_p2p(c.stages)) {
+        kw = c.warps_k;
+        rg = c.row_groups;
+        tr = c.tile_rows ? c.tile_rows : 16;
+        depth = c.stages;
+    } else {
+        const long long blocks = (p.out_f + 15) / 16, cap = 2LL * sm_count_cached(dev);
+        rg = 1;
+        while (rg < 8 && (blocks + rg - 1) / rg > cap) rg *= 2;
+        kw = 8 / rg;
+        tr = 16;
+        depth = 3;
+    }
+    if (kw * rg > 8 || tr < 1 || tr > 16) return cudaErrorInvalidValue;
+    if (nf4_mma_smem(p.in_f, kw, rg) > kTmaSmemLimit) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_nf4_mma_p2p(depth);
+    if (!fn) return cudaErrorInvalidValue;
+    const long long rows_per_cta = (long long)rg * tr;
+    const long long tiles = (p.out_f + rows_per_cta - 1) / rows_per_cta;
     LeanNf4Params lp = {};
     lp.seg[0].qw = p.qw;
     lp.seg[0].absmax = static_cast<const float*>(p.scale);
@@ -914,11 +929,11 @@ int launch_nf4_mma_p2p(const GemvProblem& p, const P2pArgs& a, int flags, cudaSt
     lp.in_f = p.in_f;
     lp.kw = kw;
     lp.rg = rg;
-    lp.tr = 16;
+    lp.tr = tr;
     lp.x_vec = aligned(p.x, 16);
     lp.p2p = a;
     // every CTA resident at once: a CTA waits only for the CTA of the same index on the peers
-    return launch_persistent(fn, &lp, tiles, 256, nf4_mma_smem(p.in_f, kw, rg), flags, st, true);
+    return launch_persistent(fn, &lp, tiles, 32 * kw * rg, nf4_mma_smem(p.in_f, kw, rg), flags, st, true);
 }
 
 int launch_gemv_nf4_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)

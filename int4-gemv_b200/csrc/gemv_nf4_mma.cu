@@ -15,5 +15,10 @@ void* b4::gemv_kernel_nf4_mma(int depth)
 // the row-parallel shard with the all-reduce fused in (b4_tp_gemv_p2p)
 void* b4::gemv_kernel_nf4_mma_p2p(int depth)
 {
-    return depth == 3 ? (void*)&b4::b4_gemv_nf4_mma_kernel<3, 1> : nullptr;
+    switch (depth) {
+        case 2: return (void*)&b4::b4_gemv_nf4_mma_kernel<2, 1>;
+        case 3: return (void*)&b4::b4_gemv_nf4_mma_kernel<3, 1>;
+        case 4: return (void*)&b4::b4_gemv_nf4_mma_kernel<4, 1>;
+    }
+    return nullptr;
 }
