@@ -170,12 +170,16 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     nf4_pair_table_fill(base);
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = v; });
+    // x slot w is stored at w ^ 2 when bit 3 of w is set: the four x lanes read
+    // slots 4q + i (+ 16 per step), and without the swap lanes q and q + 2 hit
+    // the same banks (two wavefronts per load instead of one)
+    stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w ^ ((w >> 2) & 2)] = v; });
     __syncthreads();
     const uint32_t epoch = P2P ? p2p_epoch(p.p2p) : 0u;
 
     // B carries x only on lanes (g, q) with g == q >> 1 (columns 0/1 = blocks 0/1)
     const bool x_lane = g == (q >> 1);
+    const int xsw = (q >> 1) << 1;   // the slot swap of this lane's x slots
     const unsigned char* tb = base;
 
     for (; tile < n_tiles; tile += gridDim.x) {
@@ -197,7 +201,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
                     if (it + D - 1 < n_it) fetch(nxt);
                     if (x_lane) {
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) xv[i] = xp[i];
+                        for (int i = 0; i < 4; ++i) xv[i] = xp[i ^ xsw];
                     }
                     xp += 16 * p.kw;
                     const uint32_t wa[4] = {bufa[d].x, bufa[d].y, bufa[d].z, bufa[d].w};
