@@ -243,7 +243,9 @@ def _p2p_worker(rank, world, port, mode, results, fmt=0):
     dev = torch.device("cuda", rank)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
-    out_f, in_f = 1000, 2048
+    # NF4: at least 2048 rows, where the dispatch rule picks the tensor-pipe
+    # kernel that the fused path runs (ragged last block either way)
+    out_f, in_f = (1000, 2048) if fmt == 0 else (2056, 2048)
     p2p = P2pComm(rank, world, max_rows=4096)
     lib = b4gemv.load()
     out = {}
@@ -319,6 +321,7 @@ def _p2p_worker(rank, world, port, mode, results, fmt=0):
         torch.cuda.synchronize()
         comm.destroy()
         out["layer_equal"] = torch.equal(y_p, y_n)
+        out["layer_err"] = rel_err(y_p.cpu().numpy(), y_n.cpu().numpy().astype(np.float64))
         out["layer_status"] = p2p.status()
         results[rank] = out
     finally:
@@ -353,8 +356,16 @@ def test_p2p_rowparallel_gemv_matches_nccl_and_is_identical_on_every_rank(fmt):
         assert res[r]["same_calls"], res       # 4 calls + 3 graph replays, bit for bit
         assert res[r]["err"] < 1e-3, res       # against the double GEMV of the full matrix
         assert res[r]["vs_nccl"] < 1e-5, res   # against the NCCL all-reduce of the same partials
+        if fmt == 1:   # same kernel and geometry as the plain GEMV: the same partials, the same sum
+            assert res[r]["vs_nccl"] == 0.0, res
         assert res[r]["same_ranks"], res       # every rank sums in rank order
-        assert res[r]["layer_equal"], res      # TPDecodeLayer(p2p=...) against TPDecodeLayer on NCCL
+        # TPDecodeLayer(p2p=...) against TPDecodeLayer on NCCL: bit for bit for
+        # INT4; for NF4 the small layer's o/down (1024 rows) run the CUDA-core
+        # NF4 kernel on the NCCL path and the tensor-pipe one fused: fp32 rounding
+        if fmt == 0:
+            assert res[r]["layer_equal"], res
+        else:
+            assert res[r]["layer_err"] < 1e-6, res
         assert res[r]["layer_status"] == 0, res
 
 
