@@ -8,15 +8,16 @@
 // 4*nb + (c & 3), and NB = ceil(m / 4) blocks cover the batch.  The code-book
 // lookups (PRMT + one 8-byte shared load per byte) are done once per lane and
 // shared by every batch row; only the MMAs and the x fragments grow with m.
-// As in the batch-1 kernel, one MMA covers an 8-row set: A rows 0-7 hold the
-// rows' high parts and rows 8-15 their low parts, the two added after the MMA.
+// From 5 batch rows (NB >= 2) one MMA covers an 8-row set as in the batch-1
+// kernel: A rows 0-7 hold the rows' high parts and rows 8-15 their low parts,
+// the two added after the MMA; at NB = 1 the high and low parts of all 16 rows
+// take an MMA each (measured faster there).
 //
 // B fragments: lane (g, q) supplies column g at the k-slots of lanes q, whose
 // codes lie in NF4 block q >> 1, so it carries x of batch row 4*nb + (g & 3)
 // when (g >> 2) == (q >> 1) and zero otherwise (16 of 32 lanes load x).
 // D: lane (g, q) holds columns 2q, 2q+1 = NF4 block q >> 1 of batch rows
-// 4*nb + 2(q & 1) and +1, for weight rows g and g+8 (high plus low part of
-// each set's MMA); it scales them by that
+// 4*nb + 2(q & 1) and +1, for weight rows g and g+8; it scales them by that
 // block's absmax, and lanes q and q ^ 2 (the two blocks) are added with one
 // shuffle at the end.  x is staged per CTA for all m rows in natural order.
 #pragma once
@@ -153,10 +154,13 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
                     if (it + D - 1 < n_it) fetch(nxt);
                     const uint32_t wa[4] = {bufa[d].x, bufa[d].y, bufa[d].z, bufa[d].w};
                     const uint32_t wb[4] = {bufb[d].x, bufb[d].y, bufb[d].z, bufb[d].w};
-                    // the A operands of the step's 8 MMA pairs, one per 8-row set:
-                    // A rows 0-7 = the rows' high parts, rows 8-15 = their low
-                    // parts, so a lookup's two words are A registers as loaded
-                    uint32_t a_ra[8][4], a_rb[8][4];
+                    // the A operands of the step's 8 MMA pairs.  NB >= 2: one MMA
+                    // per 8-row set, A rows 0-7 = the rows' high parts, rows 8-15
+                    // = their low parts (a lookup's two words are A registers as
+                    // loaded; m = 8: 23.2 -> 22.5 us, m = 16: 34.9 -> 32.5 us on
+                    // gate_proj).  NB = 1: one MMA for the 16 rows' high parts and
+                    // one for their low parts (m = 2: 15.9 us, 23.8 the other way)
+                    uint32_t a0[8][4], a1[8][4];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         const uint32_t ua = wa[j >> 1], ub = wb[j >> 1];
@@ -174,14 +178,25 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
                         }
                         const uint2 ea0 = nf4_pair_lookup(tb, oa0), eb0 = nf4_pair_lookup(tb, ob0);
                         const uint2 ea1 = nf4_pair_lookup(tb, oa1), eb1 = nf4_pair_lookup(tb, ob1);
-                        a_ra[j][0] = ea0.x;
-                        a_ra[j][1] = ea0.y;
-                        a_ra[j][2] = ea1.x;
-                        a_ra[j][3] = ea1.y;
-                        a_rb[j][0] = eb0.x;
-                        a_rb[j][1] = eb0.y;
-                        a_rb[j][2] = eb1.x;
-                        a_rb[j][3] = eb1.y;
+                        if constexpr (NB >= 2) {
+                            a0[j][0] = ea0.x;
+                            a0[j][1] = ea0.y;
+                            a0[j][2] = ea1.x;
+                            a0[j][3] = ea1.y;
+                            a1[j][0] = eb0.x;
+                            a1[j][1] = eb0.y;
+                            a1[j][2] = eb1.x;
+                            a1[j][3] = eb1.y;
+                        } else {
+                            a0[j][0] = ea0.x;
+                            a0[j][1] = eb0.x;
+                            a0[j][2] = ea1.x;
+                            a0[j][3] = eb1.x;
+                            a1[j][0] = ea0.y;
+                            a1[j][1] = eb0.y;
+                            a1[j][2] = ea1.y;
+                            a1[j][3] = eb1.y;
+                        }
                     }
                     const float am_a = hi_blk ? ama[d].y : ama[d].x;
                     const float am_b = hi_blk ? amb[d].y : amb[d].x;
@@ -202,16 +217,21 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
                             const uint4 xq = xv[j >> 1];
                             const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
                             const int ch = (j & 1) * 2;
-                            mma_16816_pure(c[ch], a_ra[j], b0, b1, c[ch]);
-                            mma_16816_pure(c[ch + 1], a_rb[j], b0, b1, c[ch + 1]);
+                            mma_16816_pure(c[ch], a0[j], b0, b1, c[ch]);
+                            mma_16816_pure(c[ch + 1], a1[j], b0, b1, c[ch + 1]);
                         }
-                        // D of a set's MMA: [0], [1] high parts of batch columns
-                        // 2q, 2q+1; [2], [3] their low parts.  e < 2: row g
-                        // (chains 0, 2), else row g+8 (chains 1, 3)
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const int r = e >> 1, col = e & 1;
-                            const float s = (c[r][col] + c[r][col + 2]) + (c[r + 2][col] + c[r + 2][col + 2]);
+                            float s;
+                            if constexpr (NB >= 2) {
+                                // a set's D: [0], [1] high parts of batch columns 2q,
+                                // 2q+1, [2], [3] their low parts; e < 2: row g
+                                // (chains 0, 2), else row g+8 (chains 1, 3)
+                                const int r = e >> 1, col = e & 1;
+                                s = (c[r][col] + c[r][col + 2]) + (c[r + 2][col] + c[r + 2][col + 2]);
+                            } else {
+                                s = (c[0][e] + c[1][e]) + (c[2][e] + c[3][e]);
+                            }
                             acc[nb][e] = fmaf(s, e < 2 ? am_a : am_b, acc[nb][e]);
                         }
                     }
