@@ -263,7 +263,10 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
         cfg->warps_k = 8 / rg;
         cfg->row_groups = rg;
         cfg->tile_rows = 0;   // full 16-row blocks (q_proj 5.3 us with 13-row tiles, 5.2 us without)
-        cfg->stages = 3;
+        // four row groups (two warps per block): a depth-4 pipeline (gate_proj
+        // 14.05 -> 13.75 us); depth 3 otherwise (eight row groups, the fused
+        // gate+up launch: the step 59.3 -> 59.8 us at depth 4)
+        cfg->stages = rg == 4 ? 4 : 3;
         return;
     }
     if (p.m == 1 && p.fmt == kNf4 && aligned(p.qw, 16) && aligned(p.scale, 4) && words % 4 == 0) {
