@@ -78,7 +78,7 @@ def measured_peak():
 
 ENGINE_KERNELS = {0: "b4_gemv_kernel", 1: "b4_gemv_mma_kernel", 2: "b4_gemv_tma_kernel", 3: "b4_gemv_tma_nf4_kernel",
                   4: "b4_gemv_lean_kernel", 5: "b4_gemv_lean_kernel (cp.async ring)", 6: "b4_gemv_lean_nf4_kernel",
-                  7: "b4_gemv_nf4_mma_kernel"}
+                  7: "b4_gemv_nf4_mma_kernel", 8: "b4_gemv_xtab_kernel"}
 
 
 def engine_kernel(b4, fmt, in_f, out_f):
@@ -280,7 +280,7 @@ class Launcher:
                     for i in group])
                 in_f = SHAPES[group[0]][2]
                 c = b4.GemvConfig()
-                st = lib.b4_gemv_multi_default_config(fmt, segs, len(group), in_f, 1, ctypes.byref(c))
+                st = lib.b4_gemv_multi_default_config_ws(fmt, segs, len(group), in_f, 1, ctypes.byref(c))
                 if st:
                     raise RuntimeError(f"multi config failed with status {st}")
                 c.flags |= b4.FLAG_PDL if pdl else 0
@@ -304,7 +304,8 @@ class Launcher:
                     self.call(a, *calls[a], stream)
                 else:
                     segs, n, x, in_f, c = a
-                    st = self.lib.b4_gemv_multi(self.fmt, segs, n, x, in_f, 1, ctypes.byref(c), stream)
+                    st = self.lib.b4_gemv_multi_ws(self.fmt, segs, n, x, in_f, 1, ctypes.byref(c), self.ws_ptr,
+                                                   self.ws_len, stream)
                     if st:
                         raise RuntimeError(f"GEMV launch failed with status {st}")
                 if events is not None:

@@ -32,6 +32,7 @@
 #ifndef B4GEMV_H
 #define B4GEMV_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -44,7 +45,7 @@ extern "C" {
 #define B4_FMT_INT4_G128 0
 #define B4_FMT_NF4_B64 1
 
-#define B4_ABI_VERSION 4
+#define B4_ABI_VERSION 5
 
 /* Same type as cudaStream_t, spelled without the CUDA headers. */
 typedef struct CUstream_st* b4_stream_t;
@@ -110,6 +111,19 @@ typedef struct b4_gemv_config {
  * MMA's N columns; codes and absmax through a register pipeline of depth
  * `stages` (2, 3, 4).  rows_per_warp 16, vec_words 4. */
 #define B4_ENGINE_MMA_NF4 7
+/* CUDA cores, NF4, batch 1, in_f a multiple of 256, x 4-byte aligned: tables
+ * of x-pair products.  A CTA (16 warps, one per SM) builds, for each column
+ * pair (k, k+1) of a 256-column slice of in_f, the 256 fp32 sums
+ * NF4[b & 15]*x[k] + NF4[b >> 4]*x[k+1] (one per byte value b), so one 4-byte
+ * shared load and one add take a byte (two codes) of a packed row; the NF4
+ * blocks' sums are scaled by their absmax, and the slices' shares of y are
+ * added in y with fp32 atomics after every CTA has zeroed its rows (order of
+ * the slice additions varies from run to run).  Needs a workspace
+ * (b4_gemv_ws, b4_gemv_multi_ws) of B4_XTAB_WORKSPACE_BYTES: two counters,
+ * zero between calls.  `stages` = depth of the register load pipeline (2, 3,
+ * 4); the other fields are ignored. */
+#define B4_ENGINE_NF4_XTAB 8
+#define B4_XTAB_WORKSPACE_BYTES 256
 
 /* Launch as a programmatic dependent of the previous kernel in the stream:
  * the weight stream starts before the producer of x has finished.  Only x is
@@ -153,30 +167,35 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
                int in_f, int out_f, int m, const b4_gemv_config* cfg, b4_stream_t stream);
 
 /* ---- GEMV with a caller-owned workspace --------------------------------------
- * A matrix whose 16-row blocks do not divide evenly over the resident CTAs
- * leaves SMs idle in its last wave; the split path (B4_FLAG_SPLIT) instead
- * gives every warp of the grid an equal run of (block, k-step) units and adds
- * a block's pieces through `ws`: per 16-row block, one arrival counter and
- * the pieces' partial sums.  The warp that completes a block sums its pieces
- * in k order, so y is deterministic.  The cross-CTA sum costs ~2 us, so the
- * rule (b4_gemv_default_config_ws) splits only at batch 1 where whole-row
- * tiles run between one and two waves on rows of at most 8192 columns (INT4
- * 8192x8192: 14.9 -> 12.5 us on B200); any split config can be passed
- * explicitly.  Same operands and semantics as b4_gemv_ex; a replacement for
- * b4_gemv_int4_g128 / b4_gemv_nf4_b64 (kernels.cuh:26-30, 87-91) that runs
- * split where the rule says so and identically elsewhere.
+ * Two kernels need device scratch, which the caller owns:
+ *   - at batch 1, NF4 with in_f a multiple of 256 (x 4-byte aligned) runs on
+ *     the x-pair table kernel (B4_ENGINE_NF4_XTAB): its CTAs each cover a
+ *     256-column slice of in_f, add their shares into y with atomics and
+ *     count themselves in on two counters in `ws` first
+ *     (B4_XTAB_WORKSPACE_BYTES);
+ *   - the split path (B4_FLAG_SPLIT) gives every warp of the grid an equal
+ *     run of (16-row block, k-step) units and adds a block's pieces through
+ *     `ws` (per 16-row block, one arrival counter and the pieces' partial
+ *     sums), the warp that completes a block summing its pieces in k order.
+ *     Its cross-CTA sum costs ~2 us, and no batch-1 shape measured faster
+ *     split than on the tile rule, so the rule never splits; split configs
+ *     are taken when passed explicitly.
+ * The rule of b4_gemv_ws (b4_gemv_default_config_ws) is the x-pair table
+ * kernel where it applies and b4_gemv_default_config's choice elsewhere.
+ * Same operands and semantics as b4_gemv_ex; a replacement for
+ * b4_gemv_int4_g128 / b4_gemv_nf4_b64 (kernels.cuh:26-30, 87-91).
  *
  * b4_gemv_workspace_size: bytes of workspace the call with these arguments
- * needs on the current device (0 when the config does not split; cfg NULL =
- * the dispatch rule).  ws: device memory, 16-byte aligned, at least that
+ * needs on the current device (0 when the config needs none; cfg NULL or
+ * B4_ENGINE_AUTO = the rule of b4_gemv_ws).  ws: device memory, 16-byte aligned, at least that
  * size, ZERO-FILLED before its first use (cudaMemset); every call leaves it
  * zeroed again, so it can be reused by later calls and by CUDA-graph
  * replays.  Calls that may run at the same time (different streams) need
  * different workspaces.  A workspace that is too small returns
  * cudaErrorInvalidValue before anything is launched. */
 int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_config* cfg, size_t* bytes);
-/* The dispatch rule of b4_gemv_ws (cfg NULL): b4_gemv_default_config's choice,
- * or a B4_FLAG_SPLIT config where the split pays (see above). */
+/* The dispatch rule of b4_gemv_ws (cfg NULL): the x-pair table kernel for NF4
+ * at batch 1 with in_f % 256 == 0, b4_gemv_default_config's choice otherwise. */
 int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg);
 int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f, int out_f,
                int m, const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream);
@@ -191,14 +210,18 @@ int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
  * loads the library keeps until the process exits.  It calls no cudaMalloc or
  * cudaFree.  cfg NULL = a split config for the format (INT4: stages x groups
  * chosen by divisibility; NF4: depth 3); a cfg without B4_FLAG_SPLIT is
- * rejected.  A shape whose split needs more than the array holds returns
+ * rejected, and so is NF4 with in_f not a multiple of 128 (the NF4 split
+ * kernel's k-step; cudaErrorInvalidValue: use b4_gemv_nf4_b64 there).  A
+ * shape whose split needs more than the array holds returns
  * B4_STATUS_SCRATCH_TOO_SMALL before anything is launched (b4_gemv_ws and a
  * workspace of b4_gemv_workspace_size bytes handle it).  The first call on a
- * device looks up the array's device address and clears it (synchronously):
- * make it before any stream capture.  Every call clears the counters it uses
- * on `stream` before its kernel.  All calls on a device share the one array:
- * calls that may overlap on the GPU (different streams, unordered threads)
- * race, so serialise them. */
+ * device looks up the array's device address (cudaGetSymbolAddress): make it
+ * before any stream capture, and do not use the entry point across
+ * cudaDeviceReset (the address is kept for the device's first context).
+ * Every call clears the counters it uses with cudaMemsetAsync on `stream`
+ * before its kernel.  All calls on a device share the one array: calls that
+ * may overlap on the GPU (different streams, unordered threads) race, so
+ * serialise them. */
 #define B4_STATIC_SCRATCH_BYTES (1u << 20)
 #define B4_STATUS_SCRATCH_TOO_SMALL 10902
 int b4_gemv_split_noalloc(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f,
@@ -228,6 +251,14 @@ int b4_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x,
                   const b4_gemv_config* cfg, b4_stream_t stream);
 int b4_gemv_multi_default_config(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
                                  b4_gemv_config* cfg);
+/* b4_gemv_multi with a caller-owned workspace (conventions of b4_gemv_ws): the
+ * same one-launch fusion, and at batch 1 for NF4 with in_f % 256 == 0 the
+ * x-pair table kernel over all segments (ws of B4_XTAB_WORKSPACE_BYTES).  cfg
+ * NULL or B4_ENGINE_AUTO = that rule (only cfg->flags' B4_FLAG_PDL is read). */
+int b4_gemv_multi_default_config_ws(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
+                                    b4_gemv_config* cfg);
+int b4_gemv_multi_ws(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                     const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream);
 
 /* nf4_gemv_block_per_row (kernels.cuh:211-215) with its launch geometry
  * <<<out_f, warps_per_block*32>>> (int4_gemv.cu:56-58): one CTA per row,
@@ -345,10 +376,11 @@ int b4_swiglu_f16(const float* gate, const float* up, void* out, long long n, b4
 int b4_cast_f16(const float* in, void* out, long long n, b4_stream_t stream);
 const char* b4_nccl_error_string(int status);
 
-/* Reads (and with clear != 0 resets) the current device's error flag: non-zero
- * after a streaming kernel's bounded wait on its copy ring ran out (the
- * kernel then ended early and its y is not valid).  Returns the flag, or -1
- * if it could not be read. */
+/* Reads (and with clear != 0 resets) the current device's error flags: non-zero
+ * after a bounded wait ran out -- 1: a streaming kernel's wait on its copy
+ * ring (the kernel then ended early), 2: the x-pair table kernel's count-in
+ * (it then carried on without it) -- and that launch's y is not valid.
+ * Returns the flags, or -1 if they could not be read. */
 int b4_device_error(int clear);
 
 /* ---- Misc -------------------------------------------------------------------

@@ -14,8 +14,8 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS, NF4_BLOCK, B4Error,
-                   GemvConfig, GemvSegment, check, load)
+from ._lib import (ENGINE_NF4_XTAB, FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS,
+                   NF4_BLOCK, XTAB_WORKSPACE_BYTES, B4Error, GemvConfig, GemvSegment, check, load)
 
 __all__ = [
     "GROUP", "NF4_BLOCK", "FMT_INT4_G128", "FMT_NF4_B64", "FLAG_PDL", "B4Error",
@@ -23,7 +23,8 @@ __all__ = [
     "gemv_nf4_block_per_row", "dequant_int4", "dequant_nf4", "unpack_codes",
     "quantise_device", "quantise_nf4_device", "default_config", "median", "gemv_multi",
     "multi_default_config", "MAX_SEGMENTS", "GemvSegment", "repack_bnb_nf4", "FLAG_SPLIT",
-    "gemv_ws", "workspace_size", "workspace", "default_config_ws",
+    "gemv_ws", "workspace_size", "workspace", "default_config_ws", "multi_default_config_ws",
+    "ENGINE_NF4_XTAB", "XTAB_WORKSPACE_BYTES",
 ]
 
 
@@ -190,8 +191,10 @@ _AUTO_PDL = {"engine": -1, "flags": FLAG_PDL}
 
 
 def gemv_ws(fmt: int, qw, scale, x, y=None, config: dict | None = None, ws=None, stream=None, pdl: bool = False):
-    """b4_gemv_ws: the GEMV with a workspace (the split kernels when a split
-    config is passed; config None = the dispatch rule, which never splits).
+    """b4_gemv_ws: the GEMV with a workspace (config None = the rule of
+    b4_gemv_ws: the x-pair table kernel for NF4 at batch 1 with in_f % 256 ==
+    0, the plain dispatch rule otherwise; the split kernels when a split
+    config is passed).
     ws: a zero-filled CUDA uint8 tensor of at least workspace_size() bytes, or
     None for the package's per-device workspace.  pdl (with config None): the
     dispatch rule's launch as a programmatic dependent of the previous kernel
@@ -265,14 +268,35 @@ def multi_default_config(fmt: int, pairs, x) -> dict:
     return c.as_dict()
 
 
-def gemv_multi(fmt: int, pairs, x, ys=None, config: dict | None = None, stream=None, pdl: bool = False):
-    """b4_gemv_multi: y_s = dequant(qw_s, scale_s) @ x for every (qw_s, scale_s)
-    in `pairs` (up to four matrices with the same in_f), one launch at batch 1
-    on the lean engines.  pdl (with config None): the dispatch rule's config as
-    a programmatic dependent of the previous kernel.  Returns the list of y_s."""
+def multi_default_config_ws(fmt: int, pairs, x) -> dict:
+    """b4_gemv_multi_default_config_ws: the rule of b4_gemv_multi_ws."""
+    segs, _, in_f, m, _ = _segments(pairs, x, None, alloc=False)
+    c = GemvConfig()
+    check("b4_gemv_multi_default_config_ws",
+          load().b4_gemv_multi_default_config_ws(fmt, segs, len(pairs), in_f, m, ctypes.byref(c)))
+    return c.as_dict()
+
+
+def gemv_multi(fmt: int, pairs, x, ys=None, config: dict | None = None, stream=None, pdl: bool = False,
+               ws=None, use_ws: bool = True):
+    """y_s = dequant(qw_s, scale_s) @ x for every (qw_s, scale_s) in `pairs`
+    (up to four matrices with the same in_f), one launch at batch 1.  With
+    use_ws (the default): b4_gemv_multi_ws with `ws` or the package's
+    per-device workspace (NF4 at batch 1 runs on the x-pair table kernel);
+    else b4_gemv_multi.  pdl (with config None): the rule's launch as a
+    programmatic dependent of the previous kernel.  Returns the list of y_s."""
+    segs, x2, in_f, m, out = _segments(pairs, x, ys)
+    if use_ws:
+        if config is None and pdl:
+            config = _AUTO_PDL
+        if ws is None:
+            ws = workspace(pairs[0][0].device, XTAB_WORKSPACE_BYTES)
+        cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
+        check("b4_gemv_multi_ws", load().b4_gemv_multi_ws(fmt, segs, len(pairs), _ptr(x2), in_f, m, cfg, _ptr(ws),
+                                                          ws.numel(), _stream(stream)))
+        return out
     if pdl and config is None:
         config = dict(multi_default_config(fmt, pairs, x), flags=FLAG_PDL)
-    segs, x2, in_f, m, out = _segments(pairs, x, ys)
     cfg = ctypes.byref(GemvConfig.from_dict(config)) if config is not None else None
     check("b4_gemv_multi", load().b4_gemv_multi(fmt, segs, len(pairs), _ptr(x2), in_f, m, cfg, _stream(stream)))
     return out

@@ -27,6 +27,8 @@ ENGINE_MMA_LEAN = 4
 ENGINE_MMA_LEAN_ASYNC = 5
 ENGINE_FMA_LEAN = 6
 ENGINE_MMA_NF4 = 7
+ENGINE_NF4_XTAB = 8
+XTAB_WORKSPACE_BYTES = 256
 
 
 class GemvConfig(ctypes.Structure):
@@ -88,6 +90,10 @@ SIGNATURES = {
     "b4_gemv_multi": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _P, _I, _I, ctypes.POINTER(GemvConfig), _P]),
     "b4_gemv_multi_default_config": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _I, _I,
                                           ctypes.POINTER(GemvConfig)]),
+    "b4_gemv_multi_default_config_ws": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _I, _I,
+                                             ctypes.POINTER(GemvConfig)]),
+    "b4_gemv_multi_ws": (_I, [_I, ctypes.POINTER(GemvSegment), _I, _P, _I, _I, ctypes.POINTER(GemvConfig), _P,
+                              ctypes.c_size_t, _P]),
     "b4_dequant_int4_g128": (_I, [_P, _P, _P, _I, _I, _P]),
     "b4_dequant_nf4_b64": (_I, [_P, _P, _P, _I, _I, _P]),
     "b4_unpack_codes": (_I, [_P, _P, _I, _I, _P]),

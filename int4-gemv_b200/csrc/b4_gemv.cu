@@ -16,6 +16,7 @@
 #include "b4_gemv_nf4_mma.cuh"
 #include "b4_gemv_nf4_mma_mb.cuh"
 #include "b4_gemv_split.cuh"
+#include "b4_gemv_xtab.cuh"
 #include "b4_internal.h"
 
 namespace b4 {
@@ -996,6 +997,87 @@ int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void
     return cudaSuccess;
 }
 
+// ---- x-pair table NF4 launches (b4_gemv_xtab.cuh) --------------------------------
+
+bool xtab_shape(int fmt, int in_f, int m, const void* x)
+{
+    return fmt == kNf4 && m == 1 && in_f % kXtabCols == 0 && aligned(x, 4);
+}
+
+// One launch of the x-pair table NF4 kernel over nseg weight matrices sharing
+// x (batch 1): one CTA per SM, all resident at once (the start-of-kernel
+// count-in waits for every CTA), the workspace's first 8 bytes as its two
+// counters (zero between calls).
+int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, const b4_gemv_config& c,
+                     void* ws, size_t ws_bytes, cudaStream_t st)
+{
+    if (nseg < 1 || nseg > kXtabMaxSeg || !xtab_shape(kNf4, in_f, 1, x)) return cudaErrorInvalidValue;
+    if (!ws || !aligned(ws, 16) || ws_bytes < B4_XTAB_WORKSPACE_BYTES) return cudaErrorInvalidValue;
+    void* fn = gemv_kernel_xtab(c.stages);
+    if (!fn) return cudaErrorInvalidValue;
+    XtabParams xp = {};
+    long long nb = 0;
+    for (int s = 0; s < nseg; ++s) {
+        nb += (segs[s].out_f + kXtabBatch - 1) / kXtabBatch;
+        if (nb > INT32_MAX / kXtabBatch) return cudaErrorInvalidValue;
+        xp.seg[s].qw = segs[s].qw;
+        xp.seg[s].absmax = static_cast<const float*>(segs[s].scale);
+        xp.seg[s].y = segs[s].y;
+        xp.seg[s].out_f = segs[s].out_f;
+        xp.seg[s].batch_end = (int)nb;
+    }
+    xp.nseg = nseg;
+    xp.nbatch = (int)nb;
+    xp.in_f = in_f;
+    xp.nslice = in_f / kXtabCols;
+    xp.x = static_cast<const __half*>(x);
+    xp.bar = static_cast<unsigned*>(ws);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const size_t smem = kXtabTableBytes;
+    e = ensure_smem(fn, dev, smem);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    e = occupancy_cached(fn, dev, kXtabThreads, smem, &occ);
+    if (e != cudaSuccess) return e;
+    if (occ < 1) return cudaErrorInvalidValue;
+    const long long grid = (long long)sm_count_cached(dev) * occ;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)grid);
+    lc.blockDim = dim3(kXtabThreads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (c.flags & B4_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+    }
+    void* args[] = {&xp};
+    return cudaLaunchKernelExC(&lc, fn, args);
+}
+
+int launch_gemv_xtab(const GemvProblem& p, const b4_gemv_config& c, void* ws, size_t ws_bytes, cudaStream_t st)
+{
+    if (!xtab_shape(p.fmt, p.in_f, p.m, p.x)) return cudaErrorInvalidValue;
+    const b4_gemv_segment s{p.qw, p.scale, p.y, p.out_f};
+    return launch_xtab_segs(&s, 1, p.x, p.in_f, c, ws, ws_bytes, st);
+}
+
+void xtab_config(b4_gemv_config* cfg)
+{
+    *cfg = b4_gemv_config{};
+    cfg->engine = B4_ENGINE_NF4_XTAB;
+    cfg->vec_words = 1;
+    cfg->rows_per_warp = kXtabBatch;
+    cfg->warps_k = 1;
+    cfg->row_groups = kXtabWarps;
+    cfg->batch_tile = 1;
+    cfg->stages = 3;
+}
+
 // ---- split launches (b4_gemv_split.cuh) ---------------------------------------
 
 int split_plan(const GemvProblem& p, const b4_gemv_config& c, SplitPlan* plan)
@@ -1124,15 +1206,25 @@ int launch_default(const GemvProblem& p, int flags, cudaStream_t st)
 
 void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
 {
-    // Measured on B200 (`b4gemv.diag sweep --split-only --pdl`): the split's
+    // NF4 at batch 1 with in_f a multiple of 256: the x-pair table kernel,
+    // which needs the workspace for its count-in.  Otherwise the plain rule:
+    // measured on B200 (`b4gemv.diag sweep --split-only --pdl`), the split's
     // cross-CTA sum costs ~2 us at the kernel's end (store, fence, atomic, then
     // the last arriver's L2 reads), and once the tile rule gives every CTA one
     // resident tile no batch-1 shape ran faster split (INT4 8192x8192: 11.3 us
     // split, 8.8 us with two 16-row blocks per CTA; Qwen q/o 6.4 vs 3.4 us,
-    // down 13.2 vs 10.5 us; NF4 gate 16.8 vs 14.2 us).  The rule of b4_gemv_ws
-    // is therefore b4_gemv_default_config's; split configs are taken when
-    // passed explicitly.
+    // down 13.2 vs 10.5 us; NF4 gate 16.8 vs 14.2 us); split configs are taken
+    // when passed explicitly.
+    if (xtab_shape(p.fmt, p.in_f, p.m, p.x)) {
+        xtab_config(cfg);
+        return;
+    }
     default_config(p, cfg);
+}
+
+bool needs_workspace(const b4_gemv_config& c)
+{
+    return (c.flags & B4_FLAG_SPLIT) || c.engine == B4_ENGINE_NF4_XTAB;
 }
 
 }  // namespace b4
@@ -1161,7 +1253,7 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     if (e != cudaSuccess) return e;
     if (!cfg || cfg->engine == B4_ENGINE_AUTO)
         return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, reinterpret_cast<cudaStream_t>(stream));
-    if (cfg->flags & B4_FLAG_SPLIT) return cudaErrorInvalidValue;   // needs a workspace: b4_gemv_ws
+    if (needs_workspace(*cfg)) return cudaErrorInvalidValue;   // b4_gemv_ws
     return launch_gemv(p, *cfg, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -1185,9 +1277,13 @@ int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_co
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
     b4_gemv_config c;
-    if (cfg) c = *cfg;
-    else default_config_ws(p, &c);
+    if (cfg && cfg->engine != B4_ENGINE_AUTO) c = *cfg;
+    else default_config_ws(p, &c);   // the rule, as b4_gemv_ws runs it for cfg NULL or B4_ENGINE_AUTO
     *bytes = 0;
+    if (c.engine == B4_ENGINE_NF4_XTAB) {
+        *bytes = B4_XTAB_WORKSPACE_BYTES;
+        return cudaSuccess;
+    }
     if (!(c.flags & B4_FLAG_SPLIT)) return cudaSuccess;
     SplitPlan s;
     e = split_plan(p, c, &s);
@@ -1203,8 +1299,15 @@ int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (!cfg || cfg->engine == B4_ENGINE_AUTO)   // the rule of b4_gemv_ws never splits
-        return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, st);
+    if (!cfg || cfg->engine == B4_ENGINE_AUTO) {
+        b4_gemv_config c;
+        default_config_ws(p, &c);
+        if (c.engine != B4_ENGINE_NF4_XTAB)   // the rule of b4_gemv_ws never splits
+            return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, st);
+        c.flags = cfg ? cfg->flags & B4_FLAG_PDL : 0;
+        return launch_gemv_xtab(p, c, ws, ws_bytes, st);
+    }
+    if (cfg->engine == B4_ENGINE_NF4_XTAB) return launch_gemv_xtab(p, *cfg, ws, ws_bytes, st);
     if (cfg->flags & B4_FLAG_SPLIT) return launch_split(p, *cfg, ws, ws_bytes, st);
     return launch_gemv(p, *cfg, st);
 }
@@ -1281,10 +1384,46 @@ int b4_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x,
     b4_gemv_config c;
     if (cfg) c = *cfg;
     else default_config_multi(fmt, segs, nseg, in_f, m, &c);
+    if (needs_workspace(c)) return cudaErrorInvalidValue;   // b4_gemv_multi_ws
     return launch_gemv_multi(fmt, segs, nseg, x, in_f, m, c, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int b4_device_error(int clear) { return gemv_tma_device_error(clear); }
+int b4_gemv_multi_default_config_ws(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
+                                    b4_gemv_config* cfg)
+{
+    if (!cfg) return cudaErrorInvalidValue;
+    const int e = check_segments(fmt, segs, nseg, reinterpret_cast<const void*>(256), in_f, m, false);
+    if (e != cudaSuccess) return e;
+    if (xtab_shape(fmt, in_f, m, reinterpret_cast<const void*>(256)) && nseg <= kXtabMaxSeg) xtab_config(cfg);
+    else default_config_multi(fmt, segs, nseg, in_f, m, cfg);
+    return cudaSuccess;
+}
+
+int b4_gemv_multi_ws(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
+                     const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream)
+{
+    const int e = check_segments(fmt, segs, nseg, x, in_f, m, true);
+    if (e != cudaSuccess) return e;
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    b4_gemv_config c;
+    if (!cfg || cfg->engine == B4_ENGINE_AUTO) {
+        if (xtab_shape(fmt, in_f, m, x)) xtab_config(&c);
+        else default_config_multi(fmt, segs, nseg, in_f, m, &c);
+        c.flags = cfg ? cfg->flags & B4_FLAG_PDL : 0;
+    } else {
+        c = *cfg;
+    }
+    if (c.engine == B4_ENGINE_NF4_XTAB) return launch_xtab_segs(segs, nseg, x, in_f, c, ws, ws_bytes, st);
+    if (c.flags & B4_FLAG_SPLIT) return cudaErrorInvalidValue;
+    return launch_gemv_multi(fmt, segs, nseg, x, in_f, m, c, st);
+}
+
+int b4_device_error(int clear)
+{
+    const int a = gemv_tma_device_error(clear), b = xtab_device_error(clear);
+    if (a < 0 || b < 0) return -1;
+    return a | b;
+}
 
 int b4_empty_launch(b4_stream_t stream)
 {

@@ -14,12 +14,15 @@
 // In host code the array's name is a host-side stand-in, not a device
 // address: the entry point looks up the device address with
 // cudaGetSymbolAddress once per device (with that device current) and passes
-// that pointer to the kernel.  That first call per device also clears the
-// array (cudaMemset); it should come before any stream capture.  Every call
-// clears the counters it uses (cudaMemsetAsync on its stream) before its
-// kernel, allocates nothing and shares the one array with every other call
-// on the device, so calls that may overlap on the GPU (different streams, or
-// threads without ordering between them) race.
+// that pointer to the kernel.  That first call per device should come before
+// any stream capture; the cached address belongs to the device's context as
+// it was then, so the entry point must not be used across cudaDeviceReset.
+// Every call clears the counters it uses (cudaMemsetAsync on its own stream,
+// so the clear is ordered before its kernel whatever kind of stream it is)
+// and writes every partial sum before reading it, so nothing else needs
+// clearing.  It allocates nothing and shares the one array with every other
+// call on the device, so calls that may overlap on the GPU (different
+// streams, or threads without ordering between them) race.
 #include <mutex>
 
 #include "b4_internal.h"
@@ -30,8 +33,10 @@ static __device__ __align__(256) unsigned char g_split_scratch[B4_STATIC_SCRATCH
 
 constexpr int kMaxDevices = 64;
 
-// The array's device address on `dev` (the current device), looked up and
-// cleared on the first call per device.
+// The array's device address on `dev` (the current device), looked up on the
+// first call per device.  No whole-array clear: a synchronous cudaMemset runs
+// on the legacy default stream, which a caller's non-blocking stream is not
+// ordered after, so it could overlap the first kernel.
 cudaError_t scratch_address(int dev, void** out)
 {
     static std::mutex mu;
@@ -40,9 +45,7 @@ cudaError_t scratch_address(int dev, void** out)
     std::lock_guard<std::mutex> lock(mu);
     if (!addr[dev]) {
         void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_split_scratch);
-        if (e != cudaSuccess) return e;
-        e = cudaMemset(p, 0, B4_STATIC_SCRATCH_BYTES);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_split_scratch);
         if (e != cudaSuccess) return e;
         addr[dev] = p;
     }

@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
         assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
-    assert lib.b4_abi_version() == 4
+    assert lib.b4_abi_version() == 5
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
@@ -176,12 +176,27 @@ def test_median_is_the_reference_upper_median():
 @pytest.mark.parametrize("fmt", [0, 1])
 @pytest.mark.parametrize("out_f,in_f", QWEN + LLAMA_TP)
 @pytest.mark.parametrize("m", [1, 2, 16])
-def test_workspace_rule_is_the_plain_rule(fmt, out_f, in_f, m):
-    """b4_gemv_default_config_ws: no measured shape ran faster split, so the
-    rule of b4_gemv_ws is b4_gemv_default_config's (split only when asked)."""
+def test_workspace_rule(fmt, out_f, in_f, m):
+    """b4_gemv_default_config_ws: the x-pair table kernel for NF4 at batch 1
+    with in_f % 256 == 0 (it needs the workspace), else b4_gemv_default_config's
+    choice (no measured shape ran faster split: split only when asked)."""
     c = b4gemv.default_config_ws(fmt, in_f, out_f, m)
     assert not c["flags"] & b4gemv.FLAG_SPLIT
-    assert c == b4gemv.default_config(fmt, in_f, out_f, m)
+    if fmt == 1 and m == 1 and in_f % 256 == 0:
+        assert c["engine"] == b4gemv.ENGINE_NF4_XTAB
+        assert b4gemv.workspace_size(fmt, in_f, out_f, m, device=0) == b4gemv.XTAB_WORKSPACE_BYTES
+    else:
+        assert c == b4gemv.default_config(fmt, in_f, out_f, m)
+
+
+def test_xtab_config_needs_the_workspace_entry_points():
+    """b4_gemv_ex and b4_gemv_multi have no workspace: an x-pair table config is
+    rejected before any device call; other in_f fall back to the plain rule."""
+    lib = b4gemv.load()
+    c = _lib.GemvConfig.from_dict({"engine": b4gemv.ENGINE_NF4_XTAB, "stages": 3})
+    p = ctypes.c_void_p(4096)
+    assert lib.b4_gemv_ex(1, p, p, p, p, 3584, 3584, 1, ctypes.byref(c), None) == 1
+    assert b4gemv.default_config_ws(1, 1088, 512, 1) == b4gemv.default_config(1, 1088, 512, 1)
 
 
 @pytest.mark.parametrize("out_f,in_f", QWEN + LLAMA_TP)

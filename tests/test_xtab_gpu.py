@@ -1,0 +1,163 @@
+"""GPU parity of the x-pair table NF4 kernel (B4_ENGINE_NF4_XTAB), through the C ABI.
+
+The kernel covers in_f in 256-column slices, one CTA per SM; the slices' shares
+of y meet through fp32 atomic adds after every CTA has zeroed its rows and
+counted itself in on the workspace.  These tests check y against the oracle's
+double GEMV (max relative error below TOL, the metric of int4_gemv.cu:74-81)
+on the shapes that exercise each part of that scheme: one slice, slices shared
+by 10-11 CTAs, more slices than CTAs (each CTA loops over slices), rows not a
+multiple of the 8-row batch, several segments in one launch, y pre-filled with
+NaN (every row must be zeroed), back-to-back calls (the workspace counters
+must come back to zero), and the NaN rows of the reference's edge fixture.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import b4gemv
+from b4gemv._lib import GemvConfig, GemvSegment, load
+from oracle_py import rel_err
+from test_gemv_gpu import QWEN, f64_ref, quantised, rand_problem, to_dev
+
+TOL = 1e-3
+pytestmark = pytest.mark.gpu
+XTAB = b4gemv.ENGINE_NF4_XTAB
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def xtab_cfg(stages=3, flags=0):
+    return dict(engine=XTAB, stages=stages, flags=flags)
+
+
+def run_xtab(qw, am, x, out_f, in_f, cfg, ws, prefill=float("nan")):
+    import torch
+    y = torch.full((1, out_f), prefill, dtype=torch.float32, device=qw.device)
+    c = GemvConfig.from_dict(cfg)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = load().b4_gemv_ws(1, _p(qw), _p(am), _p(x), _p(y), in_f, out_f, 1, ctypes.byref(c), _p(ws), ws.numel(), st)
+    assert rc == 0, rc
+    return y
+
+
+@pytest.mark.parametrize("out_f,in_f", [(9, 512), (70, 3584), (300, 256), (5, 18944), (1000, 2048), (3, 40960),
+                                        (2053, 1024), (1, 256)])
+def test_xtab_every_depth_and_launch_kind(cuda, oracle, out_f, in_f):
+    import torch
+    rng = np.random.default_rng(out_f * 7 + in_f)
+    W, X = rand_problem(rng, out_f, in_f)
+    qw, am = quantised(1, W, cuda)
+    ref = f64_ref(oracle, 1, qw, am, X)
+    x = to_dev(X, cuda)
+    ws = torch.zeros(b4gemv.XTAB_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
+    for stages in (2, 3, 4):
+        for flags in (0, b4gemv.FLAG_PDL):
+            y = run_xtab(qw, am, x, out_f, in_f, xtab_cfg(stages, flags), ws).cpu().numpy()
+            assert np.isfinite(y).all(), (out_f, in_f, stages, flags)
+            assert rel_err(y, ref) < TOL, (out_f, in_f, stages, flags)
+    torch.cuda.synchronize()
+    assert not ws.any().item(), "the counters must be zero between calls"
+    assert load().b4_device_error(1) == 0
+
+
+@pytest.mark.parametrize("name", list(QWEN))
+def test_xtab_is_the_ws_rule_on_qwen_shapes(cuda, oracle, name):
+    out_f, in_f = QWEN[name]
+    cfg = b4gemv.default_config_ws(1, in_f, out_f, 1)
+    assert cfg["engine"] == XTAB
+    assert b4gemv.workspace_size(1, in_f, out_f, 1) == b4gemv.XTAB_WORKSPACE_BYTES
+    rng = np.random.default_rng(len(name) * 31 + out_f)
+    W, X = rand_problem(rng, out_f, in_f)
+    qw, am = quantised(1, W, cuda)
+    ref = f64_ref(oracle, 1, qw, am, X)
+    for pdl in (False, True):
+        y = b4gemv.gemv_nf4(qw, am, to_dev(X, cuda), pdl=pdl).cpu().numpy()
+        assert rel_err(y, ref) < TOL
+
+
+def test_xtab_back_to_back_calls_new_inputs(cuda, oracle):
+    """Two calls in a row with different x and the same y and workspace: the
+    second must not see the first's sums or counters."""
+    import torch
+    rng = np.random.default_rng(5)
+    out_f, in_f = 4096, 3584
+    W, X1 = rand_problem(rng, out_f, in_f)
+    X2 = rng.standard_normal((1, in_f)).astype(np.float16)
+    qw, am = quantised(1, W, cuda)
+    ws = torch.zeros(b4gemv.XTAB_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
+    y = torch.empty((1, out_f), dtype=torch.float32, device=cuda)
+    outs = []
+    for X in (X1, X2, X1):
+        b4gemv.gemv_ws(1, qw, am, to_dev(X, cuda), y, ws=ws, pdl=True)
+        outs.append(y.cpu().numpy().copy())
+    assert rel_err(outs[0], f64_ref(oracle, 1, qw, am, X1)) < TOL
+    assert rel_err(outs[1], f64_ref(oracle, 1, qw, am, X2)) < TOL
+    assert rel_err(outs[2], outs[0]) < 1e-6
+
+
+def test_xtab_multi_segment_one_launch(cuda, oracle):
+    """q/k/v-like and ragged segments in one launch through b4_gemv_multi_ws."""
+    import torch
+    rng = np.random.default_rng(17)
+    for shapes, in_f in [([3584, 512, 512], 3584), ([37, 9, 100, 1], 1024), ([18944, 18944], 3584)]:
+        X = rng.standard_normal((1, in_f)).astype(np.float16)
+        pairs, refs = [], []
+        for out_f in shapes:
+            W = (rng.standard_normal((out_f, in_f)) * 0.02).astype(np.float32)
+            qw, am = quantised(1, W, cuda)
+            pairs.append((qw, am))
+            refs.append(f64_ref(oracle, 1, qw, am, X))
+        assert b4gemv.multi_default_config_ws(1, pairs, to_dev(X, cuda))["engine"] == XTAB
+        ys = [torch.full((1, o), float("nan"), dtype=torch.float32, device=cuda) for o in shapes]
+        for pdl in (False, True):
+            out = b4gemv.gemv_multi(1, pairs, to_dev(X, cuda), ys=ys, pdl=pdl)
+            for y, ref in zip(out, refs):
+                assert rel_err(y.cpu().numpy(), ref) < TOL, (shapes, pdl)
+    assert load().b4_device_error(1) == 0
+
+
+def test_xtab_edge_fixture_nan_rows(cuda, golden, oracle):
+    """The reference's edge case (NaN/inf weights, fp16 scale overflow): rows
+    whose dequantised weights hold NaN or inf give NaN as the oracle does; the
+    other rows stay within tolerance."""
+    import torch
+    g = golden["edge"]
+    qw, am = to_dev(g["nf4_packed"], cuda), to_dev(g["nf4_absmax"], cuda)
+    in_f = g["W"].shape[1]
+    ws = torch.zeros(b4gemv.XTAB_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
+    y = run_xtab(qw, am, to_dev(g["x"], cuda), qw.shape[0], in_f, xtab_cfg(), ws).cpu().numpy()[0]
+    ref = f64_ref(oracle, 1, qw, am, g["x"])[0]
+    assert np.array_equal(np.isfinite(y), np.isfinite(ref))
+    ok = np.isfinite(ref)
+    assert rel_err(y[ok], ref[ok]) < TOL
+
+
+def test_xtab_refusals(cuda):
+    """The kernel needs a workspace and in_f % 256 == 0: the entry points
+    without one, a short workspace and other shapes are refused before any
+    launch."""
+    import torch
+    out_f, in_f = 64, 1024
+    qw = torch.zeros((out_f, in_f // 8), dtype=torch.int32, device=cuda)
+    am = torch.ones((out_f, in_f // 64), dtype=torch.float32, device=cuda)
+    x = torch.zeros((1, in_f), dtype=torch.float16, device=cuda)
+    y = torch.zeros((1, out_f), dtype=torch.float32, device=cuda)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    c = GemvConfig.from_dict(xtab_cfg())
+    lib = load()
+    assert lib.b4_gemv_ex(1, _p(qw), _p(am), _p(x), _p(y), in_f, out_f, 1, ctypes.byref(c), st) == 1
+    ws = torch.zeros(64, dtype=torch.uint8, device=cuda)
+    assert lib.b4_gemv_ws(1, _p(qw), _p(am), _p(x), _p(y), in_f, out_f, 1, ctypes.byref(c), _p(ws), 64, st) == 1
+    ws = torch.zeros(256, dtype=torch.uint8, device=cuda)
+    qw2 = torch.zeros((out_f, 1088 // 8), dtype=torch.int32, device=cuda)
+    am2 = torch.ones((out_f, 1088 // 64), dtype=torch.float32, device=cuda)
+    x2 = torch.zeros((1, 1088), dtype=torch.float16, device=cuda)
+    assert lib.b4_gemv_ws(1, _p(qw2), _p(am2), _p(x2), _p(y), 1088, out_f, 1, ctypes.byref(c), _p(ws), 256, st) == 1
+    seg = (GemvSegment * 1)(GemvSegment(qw.data_ptr(), am.data_ptr(), y.data_ptr(), out_f))
+    assert lib.b4_gemv_multi(1, seg, 1, _p(x), in_f, 1, ctypes.byref(c), st) == 1
+    torch.cuda.synchronize()
