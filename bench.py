@@ -2,21 +2,33 @@
 """Benchmark of the B200 fused 4-bit dequantisation GEMV (one JSON line).
 
 Metric: us/GEMV and achieved HBM GB/s, batch-1 INT4/NF4 GEMV.
-Workload: NF4 b64 GEMV at batch 1 over the seven
-Qwen2.5-7B projections q/k/v/o (3584x3584, 512x3584 x2, 3584x3584), gate/up
-(18944x3584) and down (3584x18944).  A step is one GEMV of each projection,
-issued through the C ABI as decode issues them: q/k/v read one x and gate/up
-another (as in the model), and each of those groups is one b4_gemv_multi
-launch; o and down are b4_gemv_ws launches (4 launches per step, programmatic
-dependents).  value = algorithmic bytes of the step (packed codes + absmax +
-x) x steps / device time, summed over ranks; `separate_launches` reports the
-same step as seven launches.
+
+One GPU (--gpus 1): the workload is BASELINE.json configs[1], the NF4 b64
+GEMV at batch 1 over the seven Qwen2.5-7B projections q/k/v/o (3584x3584,
+512x3584 x2, 3584x3584), gate/up (18944x3584) and down (3584x18944).  A step is
+one GEMV of each, issued through the C ABI as decode issues them: q/k/v read
+one x and gate/up another (as in the model), and each of those groups is one
+b4_gemv_multi_ws launch; o and down are b4_gemv_ws launches (4 launches per
+step, programmatic dependents).  value = algorithmic bytes of the step
+(packed codes + absmax + x) x steps / device time.  Beside it: every
+projection in both formats (configs[0] is INT4 q_proj) with the reference's
+own kernels rebuilt for sm_100a timed on the same buffers, the configs[4]
+small-batch sweep, the configs[2] 28-layer chain, the configs[3] layer on
+one GPU, and the CPU baseline.
+
+N GPUs (torchrun, --gpus N): the workload is configs[3], the Llama-3-70B
+decode layer tensor-parallel over the N ranks (NF4; o/down all-reduced inside
+the GEMV over peer memory); value = the layer's algorithmic bytes x steps /
+max-over-ranks time (strong scaling), and the layer's y is checked against
+the same layer on one GPU (tp_rel_err).  The configs[1] step run as N
+independent replicas is reported as `replicas`.
 
 Timing: W warm-up steps, then exactly K steps bracketed by a barrier and
 torch.cuda.synchronize on both sides, timed with CUDA events on the launching
 stream and maxed over ranks.  The steps are replays of a CUDA graph holding
-100 steps; consecutive steps rotate over 4 independent weight copies (524 MB,
-more than 4x the 126 MB L2), so every GEMV streams its weights from HBM.
+100 steps; consecutive configs[1] steps rotate over 4 independent weight
+copies (524 MB, more than 4x the 126 MB L2), so every GEMV streams its
+weights from HBM.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -357,23 +369,6 @@ def correctness_gate(b4, torch, sets, xs, ys, fmt):
     return worst
 
 
-def per_shape_chained(b4, torch, fmt, reps=200):
-    """Per projection: `reps` back-to-back launches of that one GEMV in a
-    CUDA graph, rotating over N_SETS copies, with plain launches and as
-    programmatic dependents; us per GEMV."""
-    sets, xs, ys = build_weights(b4, torch, torch.device("cuda", torch.cuda.current_device()), fmt)
-    out = {}
-    for pdl in (False, True):
-        lau = Launcher(b4, torch, sets, xs, ys, fmt, pdl=pdl)
-        for i, (name, out_f, in_f) in enumerate(SHAPES):
-            us = chained_us(torch, lau, i, reps)
-            nb = nf4_bytes(out_f, in_f) if fmt == 1 else int4_bytes(out_f, in_f)
-            out.setdefault(name, {})["pdl" if pdl else "plain"] = {"us": round(us, 3), "gbs": round(nb / us / 1e3, 1)}
-    del sets
-    torch.cuda.synchronize()
-    return out
-
-
 def step_graph_ms(torch, launcher, n_steps):
     """ms for n_steps steps of `launcher` captured in one CUDA graph (best of 3
     replays after 2 untimed ones), events on the launching stream."""
@@ -392,54 +387,6 @@ def step_graph_ms(torch, launcher, n_steps):
         best = a.elapsed_time(b) if best is None else min(best, a.elapsed_time(b))
     del g
     return best
-
-
-def chained_us(torch, launcher, i, reps=100):
-    """us per launch of projection i over `reps` back-to-back launches in one
-    CUDA graph, rotating over the N_SETS weight copies."""
-    def body(stream):
-        for k in range(reps):
-            q, sc, x, y, a_in, a_out = launcher.calls[k % N_SETS][i]
-            launcher.call(i, q, sc, x, y, a_in, a_out, stream)
-    g = torch.cuda.CUDAGraph()
-    cs = torch.cuda.Stream()
-    cs.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.graph(g, stream=cs, capture_error_mode="relaxed"):
-        body(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    torch.cuda.current_stream().wait_stream(cs)
-    for _ in range(2):
-        g.replay()
-    torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(3):
-        g.replay()
-    b.record()
-    torch.cuda.synchronize()
-    del g
-    return a.elapsed_time(b) * 1e3 / (3 * reps)
-
-
-def isolated_launches(torch, launcher, reps=100):
-    """The reference's protocol (int4_gemv.cu:88-108): event-bracketed single
-    launches, each followed by a synchronize; median per projection, us."""
-    stream_obj = torch.cuda.current_stream()
-    stream = ctypes.c_void_p(stream_obj.cuda_stream)
-    res = {}
-    for i, (name, out_f, in_f) in enumerate(SHAPES):
-        t = []
-        for k in range(reps):
-            q, sc, x, y, a_in, a_out = launcher.calls[k % N_SETS][i]
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-            launcher.call(i, q, sc, x, y, a_in, a_out, stream)
-            b.record()
-            b.synchronize()
-            t.append(a.elapsed_time(b) * 1e3)
-        res[name] = round(sorted(t)[len(t) // 2], 3)
-    return res
 
 
 def empty_launch_floor(b4, torch, reps=200):
@@ -558,6 +505,115 @@ def cpu_fused_baseline(sets, xs, budget_s=10.0):
                       f"{el:.1f} s, {threads} threads on {os.cpu_count()} host cores"}
 
 
+def load_ref_kernels():
+    """The reference's CUDA kernels (kernels.cuh:26-266) with their benchmark's
+    launch rule (int4_gemv.cu:52-68), compiled in place for sm_100a into
+    oracle/_ref/libref.so by oracle/ref/Makefile: the second baseline, timed
+    beside ours on the same device buffers.  None when it was not built."""
+    path = os.path.join(ROOT, "oracle", "_ref", "libref.so")
+    if not os.path.exists(path):
+        return None
+    lib = ctypes.CDLL(path)
+    fn = lib.ref_launch_dispatch
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                   ctypes.c_int, ctypes.c_void_p]
+    return lib
+
+
+def graph_us(torch, launch, reps):
+    """us per launch over `reps` calls of launch(k, stream) captured in one CUDA
+    graph (best of 3 replays after one untimed), events on the launching
+    stream; None if the first eager call fails."""
+    if launch(0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) != 0:
+        return None
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(g, stream=cs, capture_error_mode="relaxed"):
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for k in range(reps):
+            launch(k, st)
+    torch.cuda.current_stream().wait_stream(cs)
+    g.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(3):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        best = us if best is None else min(best, us)
+    del g
+    return best
+
+
+def isolated_us(torch, launch, reps=100):
+    """The reference's protocol (int4_gemv.cu:88-108): event-bracketed single
+    launches, each followed by a synchronize; median us."""
+    st_obj = torch.cuda.current_stream()
+    st = ctypes.c_void_p(st_obj.cuda_stream)
+    t = []
+    for k in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch(k, st)
+        b.record()
+        b.synchronize()
+        t.append(a.elapsed_time(b) * 1e3)
+    return sorted(t)[len(t) // 2]
+
+
+def shape_table(b4, torch, ref):
+    """Both formats x the seven Qwen2.5-7B projections at batch 1 (configs[0]
+    is INT4 q_proj, configs[1] the NF4 rows): us per GEMV of ours (the rule of
+    b4_gemv_ws, as programmatic dependents and as plain launches) and of the
+    reference's kernels rebuilt for sm_100a (its own launch rule), each as
+    back-to-back launches in one CUDA graph and as isolated event-bracketed
+    launches; every timing rotates over weight copies that together exceed
+    4x L2, so each launch streams its weights from HBM."""
+    from b4gemv.diag import Problem, alg_bytes
+    peak, _ = measured_peak()
+    out = []
+    auto_pdl = b4.GemvConfig.from_dict({"engine": -1, "flags": b4.FLAG_PDL})
+    for fmt in (0, 1):
+        for name, out_f, in_f in SHAPES:
+            prob = Problem(torch, fmt, out_f, in_f, seed=11)
+            reps = max(100, len(prob.copies))
+            nb = alg_bytes(fmt, out_f, in_f)
+            ours = lambda k, st, cfg=auto_pdl: prob.launch(k, cfg, st)
+            ours_plain = lambda k, st: prob.launch(k, None, st)
+            row = {"format": "int4_g128" if fmt == 0 else "nf4_b64", "shape": name, "out_f": out_f, "in_f": in_f,
+                   "bytes": nb, "copies": len(prob.copies),
+                   "kernel": engine_kernel(b4, fmt, in_f, out_f)}
+            us = graph_us(torch, ours, reps)
+            row["us"] = round(us, 3)
+            row["gbs"] = round(nb / us / 1e3, 1)
+            row["frac"] = round(nb / us / 1e3 / peak, 4)
+            row["us_plain_launch"] = round(graph_us(torch, ours_plain, reps), 3)
+            row["us_isolated"] = round(isolated_us(torch, ours_plain), 3)
+            if ref is not None:
+                def ref_launch(k, st):
+                    q, sc = prob.ptrs[k % len(prob.ptrs)]
+                    return ref.ref_launch_dispatch(fmt, q, sc, ctypes.c_void_p(prob.x.data_ptr()),
+                                                   ctypes.c_void_p(prob.y.data_ptr()), in_f, out_f, st)
+                rus = graph_us(torch, ref_launch, reps)
+                row["ref_kernel_us"] = round(rus, 3) if rus is not None else None
+                row["ref_kernel_us_isolated"] = round(isolated_us(torch, ref_launch), 3)
+                if rus:
+                    row["ref_kernel_gbs"] = round(nb / rus / 1e3, 1)
+                    row["speedup_vs_ref_kernel"] = round(rus / us, 2)
+            out.append(row)
+            del prob
+            torch.cuda.empty_cache()
+    return out
+
+
 def small_batch_bench(b4, torch):
     """batch M in {1, 2, 4, 8, 16} on gate_proj and
     down_proj, INT4 and NF4, the dispatch rule's engine per (shape, M); us per
@@ -609,154 +665,188 @@ def chain_bench(b4, torch, dev):
     return out
 
 
-def tp_layer_bench(b4, torch, dev, d, fmt, steps=200):
+L70 = [("q", 8192, 8192), ("k", 1024, 8192), ("v", 1024, 8192), ("o", 8192, 8192), ("gate", 28672, 8192),
+       ("up", 28672, 8192), ("down", 8192, 28672)]
+L70_WORKLOAD = ("Llama-3-70B decode layer (configs[3]): q/o 8192x8192, k/v 1024x8192, gate/up 28672x8192, "
+                "down 8192x28672, batch 1, tensor-parallel over the run's ranks")
+
+
+def l70_bytes(fmt):
+    """Algorithmic bytes of one Llama-3-70B layer's seven projections (codes +
+    scales + the fp16 input each reads); the shards of a tensor-parallel layer
+    partition the weights, so this is also the sum over ranks."""
+    f = nf4_bytes if fmt == 1 else int4_bytes
+    return sum(f(o, i) for _, o, i in L70)
+
+
+class TPBench:
     """the Llama-3-70B decode layer's projections sharded
     over the N ranks of this run (column-parallel q/k/v/gate/up, row-parallel
-    o/down + NCCL all-reduce of fp32 y), replayed from a CUDA graph; us per
-    layer is the max over ranks."""
-    from b4gemv.tp import NcclComm, P2pComm, TPDecodeLayer
-    comm = NcclComm(d.rank, d.world) if d.world > 1 else None
-    layer = TPDecodeLayer(fmt, d.rank, d.world, comm, dev, seed=5, fused=True, pdl=True)
-    g = torch.Generator(device=dev)
-    g.manual_seed(9)
-    x = torch.randn((1, 8192), generator=g, device=dev).half()
-    c0, c1 = layer.ranges["o"]
-    attn = torch.randn((1, c1 - c0), generator=g, device=dev).half()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
+    o/down whose fp32 y is all-reduced, either by NCCL after the GEMV or inside
+    the GEMV over peer memory).  x is replicated and the attention output is a
+    seeded full vector of which each rank feeds its own heads to o, so the
+    sharded layer computes exactly what one GPU computes for the same layer."""
 
-    def time_layer():
-        layer.forward(x, attn)
+    def __init__(self, b4, torch, dev, d, fmt, comm):
+        from b4gemv.tp import TPDecodeLayer
+        self.torch, self.dev, self.d, self.fmt = torch, dev, d, fmt
+        self.layer = TPDecodeLayer(fmt, d.rank, d.world, comm, dev, seed=5, fused=True, pdl=True)
+        g = torch.Generator(device=dev)
+        g.manual_seed(9)
+        self.x = torch.randn((1, 8192), generator=g, device=dev).half()
+        self.attn_full = torch.randn((1, 8192), generator=g, device=dev).half()
+        c0, c1 = self.layer.ranges["o"]
+        self.attn = self.attn_full[:, c0:c1].contiguous()
+        self.bytes = l70_bytes(fmt)
+
+    def graph(self, p2p, reps):
+        torch = self.torch
+        self.layer.p2p = p2p
+        self.layer.forward(self.x, self.attn)
         torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
+        g = torch.cuda.CUDAGraph()
         cs = torch.cuda.Stream()
         cs.wait_stream(torch.cuda.current_stream())
-        reps = 20
-        with torch.cuda.graph(graph, stream=cs, capture_error_mode="relaxed"):
+        with torch.cuda.graph(g, stream=cs, capture_error_mode="relaxed"):
             for _ in range(reps):
-                layer.forward(x, attn)
+                self.layer.forward(self.x, self.attn)
         torch.cuda.current_stream().wait_stream(cs)
+        return g
+
+    def us_per_layer(self, p2p, steps=200, reps=20):
+        """us per layer, max over ranks: a graph of `reps` layers replayed."""
+        torch, d = self.torch, self.d
+        g = self.graph(p2p, reps)
         for _ in range(3):
-            graph.replay()
+            g.replay()
         torch.cuda.synchronize()
         d.barrier()
         n = max(1, steps // reps)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(n):
-            graph.replay()
+            g.replay()
         b.record()
         torch.cuda.synchronize()
         d.barrier()
-        del graph
+        del g
         torch.cuda.synchronize()
-        return d.max(a.elapsed_time(b) * 1e3 / (n * reps), dev)
+        self.layer.p2p = None
+        return d.max(a.elapsed_time(b) * 1e3 / (n * reps), self.dev)
 
-    us_max = time_layer()
-    # N > 1: o/down with the all-reduce fused into the GEMV over peer memory
-    # (b4_tp_gemv_p2p) instead of the NCCL all-reduce
-    us_p2p = None
-    p2p_status = None
-    if d.world > 1:
-        p2p = P2pComm(d.rank, d.world, max_rows=8192)
-        layer.p2p = p2p
-        us_p2p = time_layer()
-        p2p_status = p2p.status()
-        layer.p2p = None
+    def rel_err(self, p2p, y_ref):
+        """max |y - y_ref| / max |y_ref| over every rank's y (gathered to rank
+        0), y_ref the same layer on one GPU; None on the other ranks."""
+        torch, d = self.torch, self.d
+        self.layer.p2p = p2p
+        y = self.layer.forward(self.x, self.attn).clone()
         torch.cuda.synchronize()
-        d.barrier()
-        p2p.destroy()
-    wb = layer.weight_bytes()
-    # the layer's two fp32 all-reduces alone (32 KB each), eager NCCL through
-    # torch.distributed on the same ranks: the collective share of the layer
-    ar_us = None
-    if d.world > 1:
-        import torch.distributed as dist
-        buf = torch.zeros(8192, dtype=torch.float32, device=dev)
-        for _ in range(20):
-            dist.all_reduce(buf)
-        torch.cuda.synchronize()
-        d.barrier()
-        a.record()
-        for _ in range(200):
-            dist.all_reduce(buf)
-            dist.all_reduce(buf)
-        b.record()
-        torch.cuda.synchronize()
-        ar_us = d.max(a.elapsed_time(b) * 1e3 / 200, dev)
-    if comm is not None:
-        comm.destroy()
-    del layer
-    torch.cuda.empty_cache()
+        self.layer.p2p = None
+        ys = [torch.empty_like(y) for _ in range(d.world)]
+        if d.pg:
+            d.pg.all_gather(ys, y)
+        else:
+            ys = [y]
+        if d.rank != 0:
+            return None
+        ref = y_ref.double()
+        return max(float((t.double() - ref).abs().max() / ref.abs().max()) for t in ys)
+
+    def reference_y(self):
+        """Rank 0: the same seeded layer at tp = 1 on this GPU, y for the full
+        attention vector (the parity reference of the sharded layers)."""
+        from b4gemv.tp import TPDecodeLayer
+        one = TPDecodeLayer(self.fmt, 0, 1, None, self.dev, seed=5, fused=True, pdl=True)
+        y = one.forward(self.x, self.attn_full).clone()
+        self.torch.cuda.synchronize()
+        del one
+        self.torch.cuda.empty_cache()
+        return y
+
+    def close(self):
+        del self.layer
+        self.torch.cuda.empty_cache()
+
+
+def tp_layer_detail(b4, torch, dev, d, fmt, comm, p2p, skip_p2p_time=False):
+    """One format's TP layer: us per layer with NCCL and with the fused
+    peer-memory all-reduce (max over ranks), and both paths' y against the
+    same layer on one GPU (tp_rel_err)."""
+    tb = TPBench(b4, torch, dev, d, fmt, comm)
     peak, _ = measured_peak()
-    return {"format": "int4_g128" if fmt == 0 else "nf4_b64", "tp": d.world, "us_per_layer": round(us_max, 2),
-            "weight_bytes_per_rank": wb, "gbs_per_rank": round(wb / us_max / 1e3, 1),
-            "frac_per_rank": round(wb / us_max / 1e3 / peak, 4),
-            "allreduces_per_layer": 2 if d.world > 1 else 0,
-            "two_allreduces_us": round(ar_us, 2) if ar_us is not None else None,
-            "us_per_layer_p2p": round(us_p2p, 2) if us_p2p is not None else None,
-            "p2p_status": p2p_status,
-            "launches": "q/k/v and gate/up fused (b4_gemv_multi), GEMVs as programmatic dependents; "
-                        "us_per_layer: o/down + NCCL all-reduce; us_per_layer_p2p: o/down with the "
-                        "all-reduce fused into the GEMV over peer memory"}
+    res = {"format": "int4_g128" if fmt == 0 else "nf4_b64", "tp": d.world, "layer_bytes": tb.bytes,
+           "weight_bytes_per_rank": tb.layer.weight_bytes()}
+    us_nccl = tb.us_per_layer(None)
+    res["us_per_layer_nccl" if d.world > 1 else "us_per_layer"] = round(us_nccl, 2)
+    if d.world > 1:
+        us_p2p = tb.us_per_layer(p2p)
+        res["us_per_layer_p2p"] = round(us_p2p, 2)
+        res["p2p_status"] = p2p.status()
+        best = min(us_p2p, us_nccl)
+    else:
+        best = us_nccl
+    res["gbs"] = round(tb.bytes / best / 1e3, 1)
+    res["gbs_per_rank"] = round(tb.bytes / d.world / best / 1e3, 1)
+    res["frac_per_rank"] = round(tb.bytes / d.world / best / 1e3 / peak, 4)
+    if d.world > 1:
+        y_ref = tb.reference_y() if d.rank == 0 else None
+        e_nccl = tb.rel_err(None, y_ref)
+        e_p2p = tb.rel_err(p2p, y_ref)
+        if d.rank == 0:
+            res["tp_rel_err"] = {"nccl": e_nccl, "p2p": e_p2p,
+                                 "vs": "the same seeded layer at tp = 1 on rank 0's GPU, every rank's y"}
+    tb.close()
+    res["launches"] = ("q/k/v and gate/up fused (b4_gemv_multi_ws), GEMVs as programmatic dependents; "
+                       "o/down + NCCL all-reduce (us_per_layer_nccl) or with the all-reduce fused into the "
+                       "GEMV over peer memory (us_per_layer_p2p)")
+    return res
 
 
-def run_ours(args, d):
-    import torch
-    import b4gemv as b4
-    torch.cuda.set_device(d.local)
-    dev = torch.device("cuda", d.local)
-    d.init("nccl")
-    b4.load()
+def clock_sampler(d):
+    return ClockSampler(d.local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                        os.environ["CUDA_VISIBLE_DEVICES"].split(",")[d.local])
 
+
+def qwen_step_main(args, b4, torch, dev, d):
+    """The configs[1] step (NF4, the seven Qwen2.5-7B projections, 4 launches)
+    timed by the contract's rules: W warm-up steps, then K steps bracketed by
+    a barrier and a synchronize on both sides, CUDA events on the launching
+    stream, max over ranks.  Returns the timing and the objects the other legs
+    reuse."""
     sets, xs, ys = build_weights(b4, torch, dev, 1)
     gate_err = correctness_gate(b4, torch, sets, xs, ys, 1)
     # the timed step as decode runs it: q/k/v and gate/up (one x each) as one
-    # b4_gemv_multi launch each; `separate`: the seven GEMVs as seven launches
+    # launch each; `separate`: the seven GEMVs as seven launches
     launcher = Launcher(b4, torch, sets, xs, ys, 1, pdl=not args.no_pdl, fused=True)
     separate = Launcher(b4, torch, sets, xs, ys, 1, pdl=not args.no_pdl)
-    plain = Launcher(b4, torch, sets, xs, ys, 1, pdl=False)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     for s in range(N_SETS):
         launcher.step(s, stream)  # eager first launches (attribute set-up) before capture
         separate.step(s, stream)
     torch.cuda.synchronize()
-
     K, W = args.steps, args.warmup
     gsteps = min(GRAPH_STEPS, K)
     g_main, _ = capture(torch, launcher, gsteps, 0, with_events=False)
     rem = K % gsteps
     g_rem = capture(torch, launcher, rem, 0, with_events=False)[0] if rem else None
-
-    def run_steps(n):
-        full, r = divmod(n, gsteps)
-        for j in range(full):
-            g_main.replay()
-        for _ in range(r):
-            launcher.step(0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-
-    # warm-up, plus an untimed soak of the same work so the clock sampler sees
-    # the GPU under this load (the timed region itself may be shorter than a
-    # sampling period)
-    sampler = ClockSampler(d.local if "CUDA_VISIBLE_DEVICES" not in os.environ else
-                           os.environ["CUDA_VISIBLE_DEVICES"].split(",")[d.local])
+    sampler = clock_sampler(d)
     sampler.start()
     time.sleep(0.5)
     t_soak = time.time()
-    run_steps(max(W, 3))
+    for _ in range(max(1, -(-W // gsteps))):
+        g_main.replay()
     torch.cuda.synchronize()
     soak_until = time.time() + args.soak_seconds
     while time.time() < soak_until:
         g_main.replay()
         torch.cuda.synchronize()
-
     d.barrier()
     torch.cuda.synchronize()
-    t_clock0 = time.time()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()
-    full, r = divmod(K, gsteps)
-    for j in range(full):
+    for _ in range(K // gsteps):
         g_main.replay()
     if g_rem is not None:
         g_rem.replay()
@@ -766,44 +856,41 @@ def run_ours(args, d):
     t_clock1 = time.time()
     time.sleep(0.3)
     sampler.stop()
-    ms = start.elapsed_time(end)
-    ms_max = d.max(ms, dev)
-
-    # per-GEMV durations: each projection launched 100 times back to back in
-    # a CUDA graph (rotating over the weight copies), events around the replay
-    # on the launching stream.  (Timing events inside the step graph would add
-    # their own gaps between kernels.)
-    per_us = {name: round(chained_us(torch, launcher, i), 3) for i, (name, _, _) in enumerate(SHAPES)}
+    ms_max = d.max(start.elapsed_time(end), dev)
     sep_ms = d.max(step_graph_ms(torch, separate, min(K, 500)), dev)
-    per_us_plain = {name: round(chained_us(torch, plain, i), 3) for i, (name, _, _) in enumerate(SHAPES)}
-
-    peak, peak_kind = measured_peak()
-    dom = "gate_proj"
-    dom_bytes = nf4_bytes(18944, 3584)
-    dom_us = per_us.get(dom)
-    achieved = dom_bytes / dom_us / 1e3 if dom_us else None  # GB/s
-    traffic = profiled_traffic("nf4_gate_proj")
-
     clocks = sampler.summary(t_soak, t_clock1)
     clocks["window"] = "warm-up soak and timed region"
+    del g_main, g_rem, separate
+    torch.cuda.synchronize()
+    return {"ms_max": ms_max, "sep_ms": sep_ms, "gsteps": gsteps, "clocks": clocks, "gate_err": gate_err,
+            "launches_per_step": launcher.launches_per_step(), "sets": sets, "xs": xs, "ys": ys}
+
+
+def run_single(args, b4, torch, dev, d):
+    K, W = args.steps, args.warmup
+    q = qwen_step_main(args, b4, torch, dev, d)
+    sets, xs, ys = q["sets"], q["xs"], q["ys"]
+    ms_max = q["ms_max"]
+    peak, peak_kind = measured_peak()
+
+    # per projection and format, ours and the reference kernel, HBM-fed
+    ref = load_ref_kernels()
+    table = shape_table(b4, torch, ref)
+    nf4_rows = {r["shape"]: r for r in table if r["format"] == "nf4_b64"}
+    dom = nf4_rows["gate_proj"]
+    traffic = profiled_traffic("nf4_gate_proj")
 
     # end to end through the public API with host buffers
     e2e_n = max(3, min(K, 200))
     e2e_ms, h2d, d2h = e2e_steps(b4, torch, sets, xs, ys, e2e_n)
-    e2e_ms_max = d.max(e2e_ms, dev)
     e2e_eager_ms, _, _ = e2e_steps(b4, torch, sets, xs, ys, e2e_n, graph=False)
-    e2e_eager_ms_max = d.max(e2e_eager_ms, dev)
-
-    # detail: the reference's isolated-launch protocol and the launch floor
-    iso = isolated_launches(torch, plain)
     floor = empty_launch_floor(b4, torch)
 
-    n = d.world
     result = {
         "metric": METRIC,
-        "value": round(n * K * STEP_BYTES / (ms_max / 1e3) / 1e9, 2),
+        "value": round(K * STEP_BYTES / (ms_max / 1e3) / 1e9, 2),
         "unit": "GB/s",
-        "n_gpus": n,
+        "n_gpus": 1,
         "steps": K,
         "warmup": W,
         "ms_per_step": round(ms_max / K, 5),
@@ -816,52 +903,209 @@ def run_ours(args, d):
                    "shapes": {nm: [o, i] for nm, o, i in SHAPES},
                    "bytes_per_step": STEP_BYTES,
                    "l2": f"{N_SETS} rotating weight copies, {N_SETS * STEP_BYTES / 1e6:.0f} MB (> 4x the 126 MB L2)",
-                   "timing": f"CUDA graphs of {gsteps} steps, events on the launching stream",
+                   "timing": f"CUDA graphs of {q['gsteps']} steps, events on the launching stream",
                    "launches": "q/k/v read one x and gate/up another (as in the model) and run as one "
-                               "b4_gemv_multi launch each: 4 launches per step, programmatic dependents",
-                   "parallelism": f"{n} independent replicas (no data-path collective)" if n > 1 else "1 GPU"},
-        "us_per_gemv": per_us,
-        "us_per_gemv_how": ("100 launches of one projection back to back in a CUDA graph, each a programmatic "
-                            "dependent of the previous (B4_FLAG_PDL)" if not args.no_pdl else
-                            "100 launches of one projection back to back in a CUDA graph"),
-        "us_per_gemv_plain_launch": per_us_plain,
-        "gbs_per_gemv": {nm: round(nf4_bytes(o, i) / per_us[nm] / 1e3, 1) for nm, o, i in SHAPES if nm in per_us},
-        "roofline": {"bound": "hbm", "kernel": f"{engine_kernel(b4, 1, 3584, 18944)} (NF4, gate_proj 18944x3584)",
-                     "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
-                     "bytes_per_launch": dom_bytes, "us_per_launch": dom_us,
+                               "b4_gemv_multi_ws launch each: 4 launches per step, programmatic dependents",
+                   "parallelism": "1 GPU"},
+        "us_per_gemv": {nm: r["us"] for nm, r in nf4_rows.items()},
+        "gbs_per_gemv": {nm: r["gbs"] for nm, r in nf4_rows.items()},
+        "us_per_gemv_how": "per projection: back-to-back launches in one CUDA graph as programmatic dependents, "
+                           "rotating over weight copies > 4x L2 (shape_table)",
+        "roofline": {"bound": "hbm", "kernel": f"{dom['kernel']} (NF4, gate_proj 18944x3584)",
+                     "achieved": dom["gbs"], "peak": peak, "unit": "GB/s", "frac": dom["frac"],
+                     "peak_source": peak_kind, "bytes_per_launch": dom["bytes"], "us_per_launch": dom["us"],
                      "traffic": traffic},
-        "e2e": {"value": round(n * e2e_n * STEP_BYTES / (e2e_ms_max / 1e3) / 1e9, 2), "unit": "GB/s",
+        "step_roofline_frac": round(STEP_BYTES / (ms_max / K * 1e-3) / 1e9 / peak, 4),
+        "e2e": {"value": round(e2e_n * STEP_BYTES / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "how": "public API b4gemv.gemv_nf4(pdl=True) -> C ABI per GEMV, the seven calls of a step "
-                       "captured once in a CUDA graph and replayed; pinned x copied in and y copied out and read "
-                       "on the host every step", "steps": e2e_n,
-                "eager_value": round(n * e2e_n * STEP_BYTES / (e2e_eager_ms_max / 1e3) / 1e9, 2),
-                "eager_how": "the same with the seven b4gemv.gemv_nf4 Python calls made every step"},
-        "isolated_launch_us": iso,
+                "how": "public API b4gemv.gemv_nf4 / gemv_multi (pdl=True) -> C ABI, the step's calls captured "
+                       "once in a CUDA graph and replayed; pinned x copied in and y copied out and read on the "
+                       "host every step", "steps": e2e_n,
+                "eager_value": round(e2e_n * STEP_BYTES / (e2e_eager_ms / 1e3) / 1e9, 2),
+                "eager_how": "the same with the step's Python API calls made every step"},
+        "shape_table": table,
         "empty_launch_floor_us": floor,
-        "gpu_launches": K * launcher.launches_per_step(),
-        "separate_launches": {"value": round(n * min(K, 500) * STEP_BYTES / (sep_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                              "ms_per_step": round(sep_ms / min(K, 500), 5), "launches_per_step": len(SHAPES),
+        "gpu_launches": K * q["launches_per_step"],
+        "separate_launches": {"value": round(min(K, 500) * STEP_BYTES / (q["sep_ms"] / 1e3) / 1e9, 2),
+                              "unit": "GB/s", "ms_per_step": round(q["sep_ms"] / min(K, 500), 5),
+                              "launches_per_step": len(SHAPES),
                               "how": "the same step as seven launches, one per projection (programmatic "
                                      "dependents)"},
-        "correctness_rel_err": gate_err,
-        "clocks": clocks,
+        "correctness_rel_err": q["gate_err"],
+        "clocks": q["clocks"],
     }
-    del launcher, g_main, g_rem
-    torch.cuda.synchronize()
-    if args.detail:
-        result["int4_chained"] = per_shape_chained(b4, torch, 0)
-        result["nf4_chained"] = per_shape_chained(b4, torch, 1)
+    if ref is None:
+        result["ref_kernel_note"] = "oracle/_ref/libref.so not built: no reference-kernel timings"
+    if not args.no_small_batch:
         result["small_batch"] = small_batch_bench(b4, torch)
     if not args.no_chain:
         result["qwen28_int4_chain"] = chain_bench(b4, torch, dev)
     if not args.no_tp:
-        result["l70_tp_layer"] = [tp_layer_bench(b4, torch, dev, d, fmt) for fmt in (0, 1)]
-    if n == 1 and d.rank == 0 and not args.no_cpu:
+        result["l70_tp_layer"] = [tp_layer_detail(b4, torch, dev, d, fmt, None, None) for fmt in (0, 1)]
+    if not args.no_cpu:
         result["cpu_baseline"] = cpu_fused_baseline(sets, xs, budget_s=args.cpu_seconds)
+    print(json.dumps(result), flush=True)
+
+
+def tp_e2e(torch, tb, p2p, n_steps):
+    """configs[3] end to end: every step copies x and this rank's attention
+    shard from pinned host memory, replays the layer graph and copies y back
+    and reads it; ms, h2d and d2h bytes per step."""
+    hx = tb.x.cpu().pin_memory()
+    ha = tb.attn.cpu().pin_memory()
+    hy = torch.empty((1, 8192), dtype=torch.float32).pin_memory()
+    g = tb.graph(p2p, 1)
+    y = tb.layer.buf["y"]
+
+    def one():
+        tb.x.copy_(hx, non_blocking=True)
+        tb.attn.copy_(ha, non_blocking=True)
+        g.replay()
+        hy.copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return float(hy[0, 0])
+
+    for _ in range(3):
+        one()
+    tb.d.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n_steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    tb.d.barrier()
+    del g
+    tb.layer.p2p = None
+    return a.elapsed_time(b), hx.numel() * 2 + ha.numel() * 2, hy.numel() * 4
+
+
+def run_multi(args, b4, torch, dev, d):
+    """N > 1: the contract value is configs[3], the Llama-3-70B layer
+    tensor-parallel over the N ranks (NF4, o/down with the all-reduce fused
+    into the GEMV over peer memory): total layer bytes per step / max-over-
+    ranks time, strong scaling (the layer is fixed as N grows).  The layer's
+    y is checked against the same layer on one GPU (tp_rel_err); the
+    independent-replica figure of the configs[1] step is kept as
+    `replicas`."""
+    from b4gemv.tp import NcclComm, P2pComm
+    K, W = args.steps, args.warmup
+    comm = NcclComm(d.rank, d.world)
+    p2p = P2pComm(d.rank, d.world, max_rows=8192)
+    peak, peak_kind = measured_peak()
+    tb = TPBench(b4, torch, dev, d, 1, comm)
+    gsteps = min(GRAPH_STEPS, K)
+    g = tb.graph(p2p, gsteps)
+    sampler = clock_sampler(d)
+    sampler.start()
+    time.sleep(0.5)
+    t_soak = time.time()
+    for _ in range(max(1, -(-W // gsteps))):
+        g.replay()
+    torch.cuda.synchronize()
+    soak_until = time.time() + args.soak_seconds
+    while time.time() < soak_until:
+        g.replay()
+        torch.cuda.synchronize()
+    d.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    n_rep = max(1, K // gsteps)
+    steps = n_rep * gsteps
+    start.record()
+    for _ in range(n_rep):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    d.barrier()
+    t_clock1 = time.time()
+    time.sleep(0.3)
+    sampler.stop()
+    del g
+    tb.layer.p2p = None
+    torch.cuda.synchronize()
+    ms_max = d.max(start.elapsed_time(end), dev)
+    clocks = sampler.summary(t_soak, t_clock1)
+    clocks["window"] = "warm-up soak and timed region"
+    status = p2p.status()
+    e2e_n = max(3, min(K, 200))
+    e2e_ms, h2d, d2h = tp_e2e(torch, tb, p2p, e2e_n)
+    e2e_ms = d.max(e2e_ms, dev)
+    y_ref = tb.reference_y() if d.rank == 0 else None
+    err = {"p2p": tb.rel_err(p2p, y_ref), "nccl": tb.rel_err(None, y_ref)}
+    us_nccl = tb.us_per_layer(None)
+    tb.close()
+    del y_ref
+    value = steps * tb.bytes / (ms_max / 1e3) / 1e9
+    result = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": d.world,
+        "steps": steps,
+        "warmup": W,
+        "ms_per_step": round(ms_max / steps, 5),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "u4 codes, fp32 accumulate (fp16 x, fp32 y)",
+        "data": "synthetic: W ~ N(0, 0.02) seeded per projection, quantised on the device; x and the attention "
+                "output ~ N(0, 1) fp16",
+        "config": {"workload": L70_WORKLOAD, "format": "nf4_b64", "batch": 1, "tp": d.world,
+                   "layer_bytes": tb.bytes,
+                   "l2": f"one layer streams {tb.bytes / d.world / 1e6:.0f} MB per rank per step (inputs larger "
+                         f"than L2 where that is > 126 MB; the layer is replayed as decode replays it)",
+                   "timing": f"CUDA graphs of {gsteps} layer steps, events on the launching stream, max over ranks",
+                   "launches": "per rank: q/k/v (one b4_gemv_multi_ws launch), o with the all-reduce fused in "
+                               "over peer memory (b4_tp_gemv_p2p), fp16 cast, gate/up (one launch), SwiGLU, "
+                               "down with the fused all-reduce: 6 launches, programmatic dependents",
+                   "parallelism": f"tp{d.world}"},
+        "us_per_layer": round(ms_max * 1e3 / steps, 2),
+        "us_per_layer_nccl": round(us_nccl, 2),
+        "p2p_status": status,
+        "gbs_per_rank": round(value / d.world, 1),
+        "roofline": {"bound": "hbm", "kernel": "the layer's GEMVs (per rank)", "achieved": round(value / d.world, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(value / d.world / peak, 4),
+                     "peak_source": peak_kind, "traffic": None},
+        "tp_rel_err": err if d.rank == 0 else None,
+        "e2e": {"value": round(e2e_n * tb.bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_n,
+                "how": "per step and rank: x and the rank's attention shard copied in from pinned host memory, "
+                       "the layer (TPDecodeLayer, C ABI calls captured in a CUDA graph) replayed, y copied out "
+                       "and read on the host; max over ranks"},
+        "gpu_launches": steps * 6,
+        "clocks": clocks,
+    }
+    if not args.no_tp:
+        result["l70_tp_layer_int4"] = tp_layer_detail(b4, torch, dev, d, 0, comm, p2p)
+    # the configs[1] step on every rank at once, no data-path collective
+    q = qwen_step_main(args, b4, torch, dev, d)
+    result["replicas"] = {"value": round(d.world * K * STEP_BYTES / (q["ms_max"] / 1e3) / 1e9, 2), "unit": "GB/s",
+                          "ms_per_step": round(q["ms_max"] / K, 5), "workload": WORKLOAD,
+                          "how": f"{d.world} independent replicas of the configs[1] step (no collective), value = "
+                                 "all ranks' bytes / max-over-ranks time"}
+    del q
+    torch.cuda.synchronize()
+    d.barrier()
+    p2p.destroy()
+    comm.destroy()
     if d.rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def run_ours(args, d):
+    import torch
+    import b4gemv as b4
+    torch.cuda.set_device(d.local)
+    dev = torch.device("cuda", d.local)
+    d.init("nccl")
+    b4.load()
+    if d.world == 1:
+        run_single(args, b4, torch, dev, d)
+    else:
+        run_multi(args, b4, torch, dev, d)
     d.close()
 
 
@@ -937,7 +1181,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--detail", action="store_true", help="also per-shape chained us for INT4 and NF4")
+    ap.add_argument("--no-small-batch", action="store_true", help="skip the configs[4] small-batch sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-chain", action="store_true", help="skip the 28-layer INT4 graph chain")
     ap.add_argument("--no-tp", action="store_true", help="skip the Llama-3-70B tensor-parallel layer")

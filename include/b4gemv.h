@@ -120,8 +120,9 @@ typedef struct b4_gemv_config {
  * added in y with fp32 atomics after every CTA has zeroed its rows (order of
  * the slice additions varies from run to run).  Needs a workspace
  * (b4_gemv_ws, b4_gemv_multi_ws) of B4_XTAB_WORKSPACE_BYTES: two counters,
- * zero between calls.  `stages` = depth of the register load pipeline (2, 3,
- * 4); the other fields are ignored. */
+ * zero between calls.  Codes and absmax 16-byte aligned.  row_groups = warps
+ * per CTA and stages = cp.async ring stages per warp: (16, 3), (20, 3),
+ * (24, 2) or (28, 2); the other fields are ignored. */
 #define B4_ENGINE_NF4_XTAB 8
 #define B4_XTAB_WORKSPACE_BYTES 256
 

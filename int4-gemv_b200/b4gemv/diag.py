@@ -40,7 +40,9 @@ def alg_bytes(fmt, out_f, in_f, m=1):
 
 
 class Problem:
-    """Device buffers for one shape: enough weight copies to exceed 4x L2."""
+    """Device buffers for one shape: enough weight copies that together exceed
+    4x L2 (so a launch that rotates over them reads its weights from HBM, not
+    from the 126 MB L2, even when the copies are reused)."""
 
     def __init__(self, torch, fmt, out_f, in_f, m=1, seed=0, copies=None):
         from . import quantise_device, quantise_nf4_device
@@ -51,7 +53,7 @@ class Problem:
         qw, sc, _ = (quantise_nf4_device if fmt == FMT_NF4_B64 else quantise_device)(W)
         del W
         nb = alg_bytes(fmt, out_f, in_f)
-        n = copies or max(2, min(64, -(-4 * L2_BYTES // nb)))
+        n = copies or max(2, min(4096, -(-4 * L2_BYTES // nb)))
         self.copies = [(qw, sc)] + [(qw.clone(), sc.clone()) for _ in range(n - 1)]
         self.x = torch.randn((m, in_f), generator=g, device=dev).half()
         self.y = torch.empty((m, out_f), device=dev)
@@ -69,9 +71,13 @@ class Problem:
                                  ctypes.c_void_p(self.ws.data_ptr()), self.ws.numel(), stream)
 
 
-def time_chained(torch, prob, cfg, reps=100):
-    """us per GEMV over `reps` launches captured in one CUDA graph; None if
+def time_chained(torch, prob, cfg, reps=None):
+    """us per GEMV over `reps` launches captured in one CUDA graph (default:
+    at least 100 and at least one per weight copy, so every copy is read once
+    per replay and the copies between two reads of one exceed 4x L2); None if
     the config is rejected."""
+    if reps is None:
+        reps = max(100, len(prob.copies))
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     if prob.launch(0, cfg, stream) != 0:
         return None

@@ -23,7 +23,8 @@ from __future__ import annotations
 
 import ctypes
 
-from ._lib import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, GemvConfig, GemvSegment, check, load
+from ._lib import (FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, XTAB_WORKSPACE_BYTES,
+                   GemvConfig, GemvSegment, check, load)
 
 
 def row_range(n: int, tp: int, rank: int):
@@ -193,13 +194,16 @@ class TPDecodeLayer:
                                                 for n in names])
             c = GemvConfig()
             in_f = self.w[names[0]][0].shape[1] * 8
-            check("multi config", lib.b4_gemv_multi_default_config(fmt, segs, len(names), in_f, 1, ctypes.byref(c)))
+            check("multi config", lib.b4_gemv_multi_default_config_ws(fmt, segs, len(names), in_f, 1,
+                                                                      ctypes.byref(c)))
             c.flags = FLAG_PDL if pdl else 0
             self.segs[group] = (segs, len(names), in_f)
             self.cfg[group] = c
-        # single GEMVs through b4_gemv_ws: the few-row ones run split with this
-        # layer's workspace (its GEMVs run one after another on one stream)
-        need = 0
+        # every GEMV through the workspace entry points (b4_gemv_ws,
+        # b4_gemv_multi_ws) with this layer's workspace: NF4 runs on the x-pair
+        # table kernel, whose count-in needs it (the layer's GEMVs run one after
+        # another on one stream, so they share it)
+        need = XTAB_WORKSPACE_BYTES
         for name in self.NAMES:
             qw = self.w[name][0]
             c = GemvConfig()
@@ -224,8 +228,9 @@ class TPDecodeLayer:
 
     def _multi(self, group, x, stream):
         segs, n, in_f = self.segs[group]
-        check(f"gemv {group}", load().b4_gemv_multi(self.fmt, segs, n, _p(x), in_f, 1, ctypes.byref(self.cfg[group]),
-                                                    stream))
+        check(f"gemv {group}", load().b4_gemv_multi_ws(self.fmt, segs, n, _p(x), in_f, 1,
+                                                       ctypes.byref(self.cfg[group]), _p(self.ws), self.ws.numel(),
+                                                       stream))
 
     def _rowpar(self, name, x, y, stream):
         qw, sc = self.w[name]

@@ -1004,6 +1004,14 @@ bool xtab_shape(int fmt, int in_f, int m, const void* x)
     return fmt == kNf4 && m == 1 && in_f % kXtabCols == 0 && aligned(x, 4);
 }
 
+// codes and absmax are copied in 16-byte pieces
+bool xtab_buffers(const b4_gemv_segment* segs, int nseg)
+{
+    for (int s = 0; s < nseg; ++s)
+        if (!aligned(segs[s].qw, 16) || !aligned(segs[s].scale, 16)) return false;
+    return true;
+}
+
 // One launch of the x-pair table NF4 kernel over nseg weight matrices sharing
 // x (batch 1): one CTA per SM, all resident at once (the start-of-kernel
 // count-in waits for every CTA), the workspace's first 8 bytes as its two
@@ -1011,9 +1019,11 @@ bool xtab_shape(int fmt, int in_f, int m, const void* x)
 int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, const b4_gemv_config& c,
                      void* ws, size_t ws_bytes, cudaStream_t st)
 {
-    if (nseg < 1 || nseg > kXtabMaxSeg || !xtab_shape(kNf4, in_f, 1, x)) return cudaErrorInvalidValue;
+    if (nseg < 1 || nseg > kXtabMaxSeg || !xtab_shape(kNf4, in_f, 1, x) || !xtab_buffers(segs, nseg))
+        return cudaErrorInvalidValue;
     if (!ws || !aligned(ws, 16) || ws_bytes < B4_XTAB_WORKSPACE_BYTES) return cudaErrorInvalidValue;
-    void* fn = gemv_kernel_xtab(c.stages);
+    const int nw = c.row_groups;   // warps per CTA
+    void* fn = gemv_kernel_xtab(nw, c.stages);
     if (!fn) return cudaErrorInvalidValue;
     XtabParams xp = {};
     long long nb = 0;
@@ -1035,17 +1045,25 @@ int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int i
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const size_t smem = kXtabTableBytes;
+    int reserved = 0;   // dynamic shared memory starts after the reserved part of the window
+    e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    if (e != cudaSuccess) return e;
+    const size_t smem = xtab_smem_bytes(nw, c.stages, (uint32_t)reserved);
+    int smem_max = 0;
+    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (smem > (size_t)smem_max) return cudaErrorInvalidValue;
+    xp.smem = (uint32_t)smem;
     e = ensure_smem(fn, dev, smem);
     if (e != cudaSuccess) return e;
     int occ = 0;
-    e = occupancy_cached(fn, dev, kXtabThreads, smem, &occ);
+    e = occupancy_cached(fn, dev, 32 * nw, smem, &occ);
     if (e != cudaSuccess) return e;
     if (occ < 1) return cudaErrorInvalidValue;
     const long long grid = (long long)sm_count_cached(dev) * occ;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3((unsigned)grid);
-    lc.blockDim = dim3(kXtabThreads);
+    lc.blockDim = dim3(32 * nw);
     lc.dynamicSmemBytes = smem;
     lc.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1073,9 +1091,9 @@ void xtab_config(b4_gemv_config* cfg)
     cfg->vec_words = 1;
     cfg->rows_per_warp = kXtabBatch;
     cfg->warps_k = 1;
-    cfg->row_groups = kXtabWarps;
+    cfg->row_groups = 24;   // warps per CTA
     cfg->batch_tile = 1;
-    cfg->stages = 3;
+    cfg->stages = 2;        // ring stages per warp
 }
 
 // ---- split launches (b4_gemv_split.cuh) ---------------------------------------
@@ -1215,7 +1233,8 @@ void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
     // split, 8.8 us with two 16-row blocks per CTA; Qwen q/o 6.4 vs 3.4 us,
     // down 13.2 vs 10.5 us; NF4 gate 16.8 vs 14.2 us); split configs are taken
     // when passed explicitly.
-    if (xtab_shape(p.fmt, p.in_f, p.m, p.x)) {
+    const b4_gemv_segment seg{p.qw, p.scale, p.y, p.out_f};
+    if (xtab_shape(p.fmt, p.in_f, p.m, p.x) && xtab_buffers(&seg, 1)) {
         xtab_config(cfg);
         return;
     }
@@ -1394,7 +1413,7 @@ int b4_gemv_multi_default_config_ws(int fmt, const b4_gemv_segment* segs, int ns
     if (!cfg) return cudaErrorInvalidValue;
     const int e = check_segments(fmt, segs, nseg, reinterpret_cast<const void*>(256), in_f, m, false);
     if (e != cudaSuccess) return e;
-    if (xtab_shape(fmt, in_f, m, reinterpret_cast<const void*>(256)) && nseg <= kXtabMaxSeg) xtab_config(cfg);
+    if (xtab_shape(fmt, in_f, m, reinterpret_cast<const void*>(256)) && xtab_buffers(segs, nseg)) xtab_config(cfg);
     else default_config_multi(fmt, segs, nseg, in_f, m, cfg);
     return cudaSuccess;
 }
@@ -1407,7 +1426,7 @@ int b4_gemv_multi_ws(int fmt, const b4_gemv_segment* segs, int nseg, const void*
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     b4_gemv_config c;
     if (!cfg || cfg->engine == B4_ENGINE_AUTO) {
-        if (xtab_shape(fmt, in_f, m, x)) xtab_config(&c);
+        if (xtab_shape(fmt, in_f, m, x) && xtab_buffers(segs, nseg)) xtab_config(&c);
         else default_config_multi(fmt, segs, nseg, in_f, m, &c);
         c.flags = cfg ? cfg->flags & B4_FLAG_PDL : 0;
     } else {

@@ -57,14 +57,13 @@
 
 #include <cstdint>
 #include <cuda_fp16.h>
+#include <type_traits>
 
 #include "b4_common.cuh"
 
 namespace b4 {
 
 constexpr int kXtabCols = 256;                          // columns per slice: 32 words
-constexpr int kXtabWarps = 16;
-constexpr int kXtabThreads = 32 * kXtabWarps;
 constexpr int kXtabBatch = 8;                           // rows per warp batch
 constexpr int kXtabTableBytes = 4 * 256 * 32 * 4;       // 4 byte positions x 256 values x 32 lanes x fp32
 constexpr int kXtabMaxSeg = 4;
@@ -89,6 +88,7 @@ struct XtabParams {
     int nslice;          // in_f / 256
     const __half* x;
     unsigned* bar;       // workspace: [0] arrivals, [1] departures; zero between calls
+    uint32_t smem;       // dynamic shared memory of the launch (bytes)
 };
 
 // The device error flag of this translation unit (read by xtab_device_error).
@@ -101,11 +101,46 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
     return v;
 }
 
+// fire-and-forget fp32 add in L2 (a generic-address atomicAdd compiles to a
+// returning generic atomic)
+__device__ __forceinline__ void red_add_f32(float* p, float v)
+{
+    asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ float lds_f32(uint32_t addr)
 {
     float v;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
     return v;
+}
+
+// PRMT with the selector's sign-replicate bits honoured (a nibble with bit 3
+// set gives the selected byte's sign bit in all 8 bits), written as PTX
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "n"(SEL));
+    return r;
+}
+
+template <int OFF>
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(OFF));
+    return v;
+}
+
+// f(integral_constant<int, D>) for D = D0 .. N - 1, each with a compile-time D
+template <int D0, int N, typename F>
+__device__ __forceinline__ void xtab_unroll(F&& f)
+{
+    if constexpr (D0 < N) {
+        f(std::integral_constant<int, D0>{});
+        xtab_unroll<D0 + 1, N>(f);
+    }
 }
 
 __device__ __forceinline__ void sts_f32(uint32_t addr, float v)
@@ -156,42 +191,159 @@ __device__ __forceinline__ int xtab_seg_of(const XtabParams& p, int b, int& r0)
     return sg;
 }
 
-template <int D>
-__global__ void __launch_bounds__(kXtabThreads, 1) b4_gemv_xtab_kernel(const XtabParams p)
+// The shared-memory ring of one warp: R stages of a batch's codes (8 rows x
+// 128 bytes).  absmax goes straight into registers.
+constexpr int kXtabStageBytes = kXtabBatch * 128;
+constexpr int kErrXtabLayout = 4;
+
+// Shared-memory layout.  The two 64 KB halves of the tables (byte positions
+// j = 0, 1 and j = 2, 3) start on 64 KB boundaries of the CTA's shared window,
+// so that for a lane register holding  half base + 128 * (j & 1) + 4 * lane
+// (bits 8..15 zero) one PRMT that drops a code byte into bits 8..15 yields the
+// entry's complete shared address.  The rings go below the first boundary
+// when they fit there, else after the tables.  `base` is the window address
+// where dynamic shared memory starts (the reserved shared memory before it).
+__host__ __device__ constexpr uint32_t xtab_align64k(uint32_t base) { return (base + 65535u) & ~65535u; }
+
+__host__ __device__ constexpr uint32_t xtab_ring_bytes(int nw, int r) { return (uint32_t)(nw * r * kXtabStageBytes); }
+
+__host__ __device__ constexpr uint32_t xtab_smem_bytes(int nw, int r, uint32_t base)
 {
+    return (xtab_align64k(base) - base) + (uint32_t)kXtabTableBytes +
+           (xtab_ring_bytes(nw, r) <= xtab_align64k(base) - base ? 0u : xtab_ring_bytes(nw, r));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+template <int NW, int R>
+__global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabParams p)
+{
+    static_assert(R >= 2, "ring stages: at least 2");
     extern __shared__ __align__(16) float xtab[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int G = gridDim.x, c = blockIdx.x;
-    const int words = p.in_f >> 3;
     const int nblk = p.in_f >> 6;
-    const uint32_t tab0 = static_cast<uint32_t>(__cvta_generic_to_shared(xtab));
-    const uint32_t lane4 = (uint32_t)lane * 4, lane4b = lane4 + 128;
+    const long long rowb = p.in_f >> 1;          // bytes of codes per row
+    const int lr = lane & 7, lq = lane >> 3;     // this lane's row of a batch and NF4 block of the slice
 
-    // ---- per-batch loads: this lane's word of 8 rows and one absmax ----------
-    uint32_t wbuf[D][kXtabBatch];
-    float abuf[D];
-    int s = 0, b0 = 0, b1 = 0;
-    auto fetch = [&](int b, int slot) {
-        int r0;
-        const XtabSeg& sg = p.seg[xtab_seg_of(p, b, r0)];
-        const int last = sg.out_f - 1 - r0;   // rows past out_f load the last row
-        const uint32_t* q = sg.qw + (long long)r0 * words + s * 32 + lane;
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(xtab));
+    const uint32_t tab = xtab_align64k(base);
+    const uint32_t ring0 = xtab_ring_bytes(NW, R) <= tab - base ? base : tab + kXtabTableBytes;
+    if (xtab_smem_bytes(NW, R, base) > p.smem) {   // the launch did not size this layout: leave untouched
+        if (threadIdx.x == 0) atomicOr(&g_xtab_error, kErrXtabLayout);
+        return;
+    }
+    // table build: lane L writes its own column (word L) of the four pairs' tables
+    const uint32_t lk0 = tab + (uint32_t)lane * 4, lk1 = lk0 + 128, lk2 = lk0 + 65536, lk3 = lk1 + 65536;
+
+    // this warp's ring of codes; lane L copies 16-byte pieces L and L + 32 of a
+    // stage (rows L / 8 and L / 8 + 4, piece L % 8)
+    const uint32_t ring_s = ring0 + (uint32_t)(warp * R * kXtabStageBytes);
+    const uint32_t wr_q = ring_s + lane * 16;
+    // Step k (0..7) of a batch: lane L takes word w = 8 * (L >> 3) + ((k + L) & 7)
+    // of its row L & 7 -- its NF4 block's 8 words in an order rotated by the
+    // lane, so the 32 lanes of a step hold 32 different words and their
+    // lookups hit 32 different table columns.  cr[k]: the word's address in a
+    // stage; lw[k]: bytes (4w, 4w + 128, T, T + 1) with T = the tables' base
+    // >> 16, from which one PRMT per byte position j forms the entry's address
+    //     T*65536 + (j >> 1)*65536 + b*256 + (j & 1)*128 + 4w
+    // (byte 3 of the address is a sign-replicated copy of T: zero).
+    const uint32_t T = tab >> 16;
+    uint32_t cr[kXtabBatch], lw[kXtabBatch];
 #pragma unroll
-        for (int i = 0; i < kXtabBatch; ++i)
-            wbuf[slot][i] = ld_stream<1>(q + (long long)min(i, last) * words).w[0];
-        abuf[slot] = __ldg(sg.absmax + (long long)(r0 + min(lane & 7, last)) * nblk + 4 * s + (lane >> 3));
+    for (int k = 0; k < kXtabBatch; ++k) {
+        const uint32_t w = 8u * lq + ((k + lane) & 7);
+        cr[k] = ring_s + lr * 128 + 4 * w;
+        lw[k] = ((T + 1) << 24) | (T << 16) | ((4 * w + 128) << 8) | (4 * w);
+    }
+
+    int s = 0, b0 = 0, b1 = 0;
+    // segment cursor (a warp's batches only increase) and the next batch's copy
+    // sources: this lane's first code piece and its absmax (row L & 7, block L >> 3)
+    int sg = -1, sg_first = 0, sg_end = 0, out_f = 0;
+    float* yseg = nullptr;
+    const unsigned char* qsrc = nullptr;
+    const float* asrc = nullptr;
+    int bnext = 0;
+    auto seek = [&](int b) {   // point the copy sources at batch b
+        while (b >= sg_end) {
+            sg_first = sg_end;
+            ++sg;
+            sg_end = p.seg[sg].batch_end;
+        }
+        const XtabSeg& g = p.seg[sg];
+        out_f = g.out_f;
+        yseg = g.y;
+        const int r0 = (b - sg_first) * kXtabBatch;
+        qsrc = reinterpret_cast<const unsigned char*>(g.qw) + s * 128 + (r0 + (lane >> 3)) * rowb + (lane & 7) * 16;
+        asrc = g.absmax + (long long)(r0 + lr) * nblk + 4 * s + lq;
+        bnext = b;
+    };
+    float* yb[R];
+    int nvb[R];
+    float ab[R];
+    // the next batch of this warp (bnext) into ring slot `slot`; rows past
+    // out_f copy the segment's last row
+    auto issue = [&](int slot) {
+        if (bnext >= sg_end) seek(bnext);
+        const int r0 = (bnext - sg_first) * kXtabBatch;
+        const int nv = min(kXtabBatch, out_f - r0);
+        const uint32_t st = (uint32_t)(slot * kXtabStageBytes);
+        if (nv == kXtabBatch) {
+            cp_async16(wr_q + st, qsrc);
+            cp_async16(wr_q + st + 512, qsrc + 4 * rowb);
+            ab[slot] = __ldg(asrc);
+        } else {
+            const unsigned char* q = qsrc - (lane >> 3) * rowb;
+            cp_async16(wr_q + st, q + min(lane >> 3, nv - 1) * rowb);
+            cp_async16(wr_q + st + 512, q + min((lane >> 3) + 4, nv - 1) * rowb);
+            ab[slot] = __ldg(asrc + (long long)(min(lr, nv - 1) - lr) * nblk);
+        }
+        yb[slot] = yseg + r0;
+        nvb[slot] = nv;
+        bnext += NW;
+        qsrc += NW * kXtabBatch * rowb;
+        asrc += (long long)NW * kXtabBatch * nblk;
+    };
+    auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+    // batch `it` of this warp from ring slot D (it + R - 1 issued first if `more`)
+    auto step = [&](auto dc, bool more) {
+        constexpr int D = decltype(dc)::value;
+        __syncwarp();   // every lane is done with the slot refilled next
+        if (more) issue((D + R - 1) % R);
+        commit();
+        asm volatile("cp.async.wait_group %0;" ::"n"(R - 1) : "memory");
+        __syncwarp();   // every lane's copies of this batch have landed
+        float a0 = 0.0f, a1 = 0.0f;   // this lane's block of its row
+#pragma unroll
+        for (int k = 0; k < kXtabBatch; ++k) {
+            const uint32_t w = lds_u32<D * kXtabStageBytes>(cr[k]);
+            const float e0 = lds_f32(prmt<0xE604u>(w, lw[k]));
+            const float e1 = lds_f32(prmt<0xE615u>(w, lw[k]));
+            const float e2 = lds_f32(prmt<0xE724u>(w, lw[k]));
+            const float e3 = lds_f32(prmt<0xE735u>(w, lw[k]));
+            if (k & 1) a1 += (e0 + e1) + (e2 + e3);
+            else a0 += (e0 + e1) + (e2 + e3);
+        }
+        float r = (a0 + a1) * ab[D];                  // row L & 7, block L >> 3
+        r += __shfl_xor_sync(0xffffffffu, r, 8);      // + the slice's other blocks
+        r += __shfl_xor_sync(0xffffffffu, r, 16);
+        if (lane < nvb[D]) red_add_f32(yb[D] + lane, r);
     };
 
     int k_item = 0;
     bool have = xtab_item(p, c, 0, s, b0, b1);
+    int nb = have && b1 > b0 + warp ? (b1 - b0 - warp + NW - 1) / NW : 0;
     // weights first: they do not depend on the preceding grid
-    if (have) {
+    if (nb > 0) seek(b0 + warp);
 #pragma unroll
-        for (int d = 0; d < D - 1; ++d) {
-            const int b = b0 + warp + d * kXtabWarps;
-            if (b < b1) fetch(b, d);
-        }
+    for (int d = 0; d < R - 1; ++d) {
+        if (d < nb) issue(d);
+        commit();
     }
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -199,11 +351,11 @@ __global__ void __launch_bounds__(kXtabThreads, 1) b4_gemv_xtab_kernel(const Xta
     // ---- zero this CTA's share of y, then count in ----------------------------
     {
         const int z0 = (int)((long long)c * p.nbatch / G), z1 = (int)((long long)(c + 1) * p.nbatch / G);
-        for (int i = z0 * kXtabBatch + (int)threadIdx.x; i < z1 * kXtabBatch; i += kXtabThreads) {
+        for (int i = z0 * kXtabBatch + (int)threadIdx.x; i < z1 * kXtabBatch; i += 32 * NW) {
             int r0;
-            const XtabSeg& sg = p.seg[xtab_seg_of(p, i / kXtabBatch, r0)];
+            const XtabSeg& zs = p.seg[xtab_seg_of(p, i / kXtabBatch, r0)];
             const int r = r0 + (i % kXtabBatch);
-            if (r < sg.out_f) sg.y[r] = 0.0f;
+            if (r < zs.out_f) zs.y[r] = 0.0f;
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -214,100 +366,69 @@ __global__ void __launch_bounds__(kXtabThreads, 1) b4_gemv_xtab_kernel(const Xta
     bool counted_in = false;   // this warp has seen every CTA's zeroes
 
     while (have) {
-        // ---- the slice's tables: warp w fills byte position j = w & 3, values
-        // 64 * (w >> 2) .. +63, lane L its own column (conflict-free stores)
+        // ---- the slice's tables: warp w fills byte values w, w + NW, ...; lane L
+        // its own column of each of its four pairs' tables (conflict-free stores);
+        // the previous item's lookups are done (__syncthreads below the batches)
         {
-            const int j = warp & 3, h = warp >> 2;
-            const int k0 = s * kXtabCols + 8 * lane + 2 * j;
-            const __half2 xp = *reinterpret_cast<const __half2*>(p.x + k0);
-            const float x0 = __low2float(xp), x1 = __high2float(xp);
-            float a[16];
+            const __half2* xp = reinterpret_cast<const __half2*>(p.x + s * kXtabCols + 8 * lane);
+            float x0[4], x1[4];
 #pragma unroll
-            for (int c0 = 0; c0 < 16; ++c0) a[c0] = c_nf4_table[c0] * x0;
-            const uint32_t wbase = tab0 + (uint32_t)((j >> 1) * 65536 + (j & 1) * 128) + lane4;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int c1 = 4 * h + q;
-                const float t1 = c_nf4_table[c1];
-#pragma unroll
-                for (int c0 = 0; c0 < 16; ++c0) sts_f32(wbase + (uint32_t)(16 * c1 + c0) * 256, fmaf(t1, x1, a[c0]));
+            for (int j = 0; j < 4; ++j) {
+                const __half2 h = xp[j];
+                x0[j] = __low2float(h);
+                x1[j] = __high2float(h);
+            }
+            for (int b = warp; b < 256; b += NW) {
+                const float t0 = c_nf4_table[b & 15], t1 = c_nf4_table[b >> 4];
+                const uint32_t o = (uint32_t)b << 8;
+                sts_f32(lk0 + o, fmaf(t1, x1[0], t0 * x0[0]));
+                sts_f32(lk1 + o, fmaf(t1, x1[1], t0 * x0[1]));
+                sts_f32(lk2 + o, fmaf(t1, x1[2], t0 * x0[2]));
+                sts_f32(lk3 + o, fmaf(t1, x1[3], t0 * x0[3]));
             }
         }
         __syncthreads();
-
-        // ---- the batches ----------------------------------------------------------
-        const int nb = b1 > b0 + warp ? (b1 - b0 - warp + kXtabWarps - 1) / kXtabWarps : 0;
-        for (int it0 = 0; it0 < nb; it0 += D) {
-#pragma unroll
-            for (int d = 0; d < D; ++d) {
-                const int it = it0 + d;
-                if (it < nb) {
-                    if (it + D - 1 < nb) fetch(b0 + warp + (it + D - 1) * kXtabWarps, (d + D - 1) % D);
-                    float v[kXtabBatch];
-#pragma unroll
-                    for (int i = 0; i < kXtabBatch; ++i) {
-                        const uint32_t w = wbuf[d][i];
-                        const float e0 = lds_f32(tab0 + __byte_perm(w, lane4, 0x5504u));
-                        const float e1 = lds_f32(tab0 + __byte_perm(w, lane4b, 0x5514u));
-                        const float e2 = lds_f32(tab0 + 65536u + __byte_perm(w, lane4, 0x5524u));
-                        const float e3 = lds_f32(tab0 + 65536u + __byte_perm(w, lane4b, 0x5534u));
-                        v[i] = (e0 + e1) + (e2 + e3);
+        if (!counted_in && nb > 0) {
+            // every CTA has zeroed its rows of y before any add (bounded wait)
+            if (lane == 0) {
+                unsigned n = 0;
+                while (ld_acquire_u32(&p.bar[0]) < (unsigned)G) {
+                    if (++n >= kXtabMaxPolls) {
+                        atomicOr(&g_xtab_error, kErrXtabBarrier);
+                        break;
                     }
-                    // transposed butterfly over the 8 lanes of this lane's NF4 block:
-                    // lane L keeps row L & 7
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const bool hi = lane & 1;
-                        const float send = hi ? v[2 * k] : v[2 * k + 1];
-                        const float keep = hi ? v[2 * k + 1] : v[2 * k];
-                        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-                    }
-#pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        const bool hi = lane & 2;
-                        const float send = hi ? v[2 * k] : v[2 * k + 1];
-                        const float keep = hi ? v[2 * k + 1] : v[2 * k];
-                        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-                    }
-                    {
-                        const bool hi = lane & 4;
-                        const float send = hi ? v[0] : v[1];
-                        const float keep = hi ? v[1] : v[0];
-                        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-                    }
-                    float r = v[0] * abuf[d];
-                    r += __shfl_xor_sync(0xffffffffu, r, 8);
-                    r += __shfl_xor_sync(0xffffffffu, r, 16);
-                    if (!counted_in) {
-                        // every CTA has zeroed its rows of y before any add (bounded wait)
-                        if (lane == 0) {
-                            unsigned n = 0;
-                            while (ld_acquire_u32(&p.bar[0]) < (unsigned)G) {
-                                if (++n >= kXtabMaxPolls) {
-                                    atomicOr(&g_xtab_error, kErrXtabBarrier);
-                                    break;
-                                }
-                                __nanosleep(64);
-                            }
-                        }
-                        __syncwarp();
-                        counted_in = true;
-                    }
-                    int r0;
-                    const XtabSeg& sg = p.seg[xtab_seg_of(p, b0 + warp + it * kXtabWarps, r0)];
-                    if (lane < kXtabBatch && r0 + lane < sg.out_f) atomicAdd(sg.y + r0 + lane, r);
+                    __nanosleep(64);
                 }
             }
+            __syncwarp();
+            counted_in = true;
         }
+
+        // ---- the batches, R per round so that ring slots are compile-time; the
+        // steady rounds issue a batch per step, the last R - 1 steps do not
+        int it = 0;
+        for (; it + 2 * R - 1 <= nb; it += R)
+            xtab_unroll<0, R>([&](auto dc) { step(dc, true); });
+        for (; it < nb; it += R)
+            xtab_unroll<0, R>([&](auto dc) {
+                constexpr int D = decltype(dc)::value;
+                if (it + D < nb) step(dc, it + D + R - 1 < nb);
+            });
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
         ++k_item;
         have = xtab_item(p, c, k_item, s, b0, b1);
-        __syncthreads();   // every warp is done with the tables before they are refilled
-        if (have) {
+        __syncthreads();   // every warp is done with the tables and its ring
+        nb = have && b1 > b0 + warp ? (b1 - b0 - warp + NW - 1) / NW : 0;
+        if (nb > 0) {
+            sg = -1;
+            sg_first = 0;
+            sg_end = 0;
+            seek(b0 + warp);
+        }
 #pragma unroll
-            for (int d = 0; d < D - 1; ++d) {
-                const int b = b0 + warp + d * kXtabWarps;
-                if (b < b1) fetch(b, d);
-            }
+        for (int d = 0; d < R - 1; ++d) {
+            if (d < nb) issue(d);
+            commit();
         }
     }
 
@@ -323,7 +444,7 @@ __global__ void __launch_bounds__(kXtabThreads, 1) b4_gemv_xtab_kernel(const Xta
     }
 }
 
-void* gemv_kernel_xtab(int depth);
+void* gemv_kernel_xtab(int warps, int stages);
 int xtab_device_error(int clear);
 
 }  // namespace b4

@@ -1,15 +1,17 @@
-// Instantiations of the batch-1 NF4 GEMV from x-pair product tables (register
-// load pipeline of depth 2, 3 or 4), and the reader of this translation
-// unit's device error flag.
+// Instantiations of the batch-1 NF4 GEMV from x-pair product tables (warps per
+// CTA x cp.async ring stages per warp, within the shared memory of one CTA per
+// SM), and the reader of this translation unit's device error flag.
 #include "b4_gemv_xtab.cuh"
 
-void* b4::gemv_kernel_xtab(int depth)
+void* b4::gemv_kernel_xtab(int warps, int stages)
 {
-    switch (depth) {
-        case 2: return (void*)&b4::b4_gemv_xtab_kernel<2>;
-        case 3: return (void*)&b4::b4_gemv_xtab_kernel<3>;
-        case 4: return (void*)&b4::b4_gemv_xtab_kernel<4>;
-    }
+#define B4_XTAB_PICK(NW, R) \
+    if (warps == NW && stages == R) return (void*)&b4::b4_gemv_xtab_kernel<NW, R>;
+    B4_XTAB_PICK(16, 3)
+    B4_XTAB_PICK(20, 3)
+    B4_XTAB_PICK(24, 2)
+    B4_XTAB_PICK(28, 2)
+#undef B4_XTAB_PICK
     return nullptr;
 }
 

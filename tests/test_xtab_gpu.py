@@ -31,8 +31,11 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-def xtab_cfg(stages=3, flags=0):
-    return dict(engine=XTAB, stages=stages, flags=flags)
+VARIANTS = [(16, 3), (20, 3), (24, 2), (28, 2)]   # (warps per CTA, ring stages per warp)
+
+
+def xtab_cfg(warps=24, stages=2, flags=0):
+    return dict(engine=XTAB, row_groups=warps, stages=stages, flags=flags)
 
 
 def run_xtab(qw, am, x, out_f, in_f, cfg, ws, prefill=float("nan")):
@@ -47,7 +50,7 @@ def run_xtab(qw, am, x, out_f, in_f, cfg, ws, prefill=float("nan")):
 
 @pytest.mark.parametrize("out_f,in_f", [(9, 512), (70, 3584), (300, 256), (5, 18944), (1000, 2048), (3, 40960),
                                         (2053, 1024), (1, 256)])
-def test_xtab_every_depth_and_launch_kind(cuda, oracle, out_f, in_f):
+def test_xtab_every_variant_and_launch_kind(cuda, oracle, out_f, in_f):
     import torch
     rng = np.random.default_rng(out_f * 7 + in_f)
     W, X = rand_problem(rng, out_f, in_f)
@@ -55,11 +58,11 @@ def test_xtab_every_depth_and_launch_kind(cuda, oracle, out_f, in_f):
     ref = f64_ref(oracle, 1, qw, am, X)
     x = to_dev(X, cuda)
     ws = torch.zeros(b4gemv.XTAB_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
-    for stages in (2, 3, 4):
+    for warps, stages in VARIANTS:
         for flags in (0, b4gemv.FLAG_PDL):
-            y = run_xtab(qw, am, x, out_f, in_f, xtab_cfg(stages, flags), ws).cpu().numpy()
-            assert np.isfinite(y).all(), (out_f, in_f, stages, flags)
-            assert rel_err(y, ref) < TOL, (out_f, in_f, stages, flags)
+            y = run_xtab(qw, am, x, out_f, in_f, xtab_cfg(warps, stages, flags), ws).cpu().numpy()
+            assert np.isfinite(y).all(), (out_f, in_f, warps, stages, flags)
+            assert rel_err(y, ref) < TOL, (out_f, in_f, warps, stages, flags)
     torch.cuda.synchronize()
     assert not ws.any().item(), "the counters must be zero between calls"
     assert load().b4_device_error(1) == 0
@@ -160,4 +163,6 @@ def test_xtab_refusals(cuda):
     assert lib.b4_gemv_ws(1, _p(qw2), _p(am2), _p(x2), _p(y), 1088, out_f, 1, ctypes.byref(c), _p(ws), 256, st) == 1
     seg = (GemvSegment * 1)(GemvSegment(qw.data_ptr(), am.data_ptr(), y.data_ptr(), out_f))
     assert lib.b4_gemv_multi(1, seg, 1, _p(x), in_f, 1, ctypes.byref(c), st) == 1
+    bad = GemvConfig.from_dict(xtab_cfg(32, 3))   # no such (warps, stages) kernel
+    assert lib.b4_gemv_ws(1, _p(qw), _p(am), _p(x), _p(y), in_f, out_f, 1, ctypes.byref(bad), _p(ws), 256, st) == 1
     torch.cuda.synchronize()
