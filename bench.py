@@ -88,8 +88,8 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-ENGINE_KERNELS = {0: "b4_gemv_kernel", 1: "b4_gemv_mma_kernel", 2: "b4_gemv_tma_kernel", 3: "b4_gemv_tma_nf4_kernel",
-                  4: "b4_gemv_lean_kernel", 5: "b4_gemv_lean_kernel (cp.async ring)", 6: "b4_gemv_lean_nf4_kernel",
+ENGINE_KERNELS = {0: "b4_gemv_kernel", 1: "b4_gemv_mma_kernel", 2: "b4_gemv_tma_kernel",
+                  5: "b4_gemv_lean_kernel (cp.async ring)", 6: "b4_gemv_lean_nf4_kernel",
                   7: "b4_gemv_nf4_mma_kernel", 8: "b4_gemv_xtab_kernel"}
 
 

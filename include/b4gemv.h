@@ -45,7 +45,7 @@ extern "C" {
 #define B4_FMT_INT4_G128 0
 #define B4_FMT_NF4_B64 1
 
-#define B4_ABI_VERSION 5
+#define B4_ABI_VERSION 6
 
 /* Same type as cudaStream_t, spelled without the CUDA headers. */
 typedef struct CUstream_st* b4_stream_t;
@@ -88,15 +88,14 @@ typedef struct b4_gemv_config {
  * rows_per_warp 16, batch_tile 8 (m <= 8) or 16 (m <= 16), vec_words 4; the
  * whole of x must fit in shared memory next to the rings.  Persistent grid. */
 #define B4_ENGINE_MMA_TMA 2
-/* CUDA cores (NF4, m = 1) fed by a per-warp bulk-copy ring of codes and absmax:
- * rows_per_warp 4, 8 or 16, vec_words 2 or 4, in_f a multiple of 256*vec_words,
- * codes and absmax 16-byte aligned.  Persistent grid. */
+/* Engine numbers 3 (a CUDA-core NF4 kernel fed by bulk copies) and 4 (the lean
+ * INT4 kernel with its codes in registers) are retired: no shape's rule picked
+ * them; configs naming them return cudaErrorInvalidValue. */
 #define B4_ENGINE_FMA_TMA 3
-/* Tensor pipe, batch 1 only, lean inner loop (INT4): rows_per_warp 16,
- * vec_words 4, `stages` = depth of the register load pipeline (2, 3, 4, 6). */
 #define B4_ENGINE_MMA_LEAN 4
-/* As B4_ENGINE_MMA_LEAN, with the in-flight codes in a per-lane cp.async ring
- * in shared memory instead of registers; a stage holds `stage_groups`
+/* Tensor pipe, INT4, lean inner loop (batch 1; m = 2..16 with batch rows in
+ * the MMA's N): rows_per_warp 16, vec_words 4; the in-flight codes in a
+ * per-lane cp.async ring in shared memory; a stage holds `stage_groups`
  * consecutive 128-column groups ((stages, stage_groups) = (4,1), (6,1), (8,1),
  * (3,2), (4,2), (6,2), (2,4) or (3,4); stage_groups must divide in_f/128). */
 #define B4_ENGINE_MMA_LEAN_ASYNC 5

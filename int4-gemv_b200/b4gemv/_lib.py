@@ -22,8 +22,8 @@ ENGINE_AUTO = -1
 ENGINE_FMA = 0
 ENGINE_MMA = 1
 ENGINE_MMA_TMA = 2
-ENGINE_FMA_TMA = 3
-ENGINE_MMA_LEAN = 4
+ENGINE_FMA_TMA = 3      # retired: rejected
+ENGINE_MMA_LEAN = 4     # retired: rejected
 ENGINE_MMA_LEAN_ASYNC = 5
 ENGINE_FMA_LEAN = 6
 ENGINE_MMA_NF4 = 7

@@ -107,9 +107,9 @@ def time_chained(torch, prob, cfg, reps=None):
 
 TMA_VARIANTS = [(4, 4), (3, 4), (6, 4), (4, 2), (4, 8), (8, 2)]   # (stages, stage_groups) instantiated
 LEAN_VARIANTS = [(4, 1), (6, 1), (8, 1), (3, 2), (4, 2), (6, 2), (2, 4), (3, 4)]   # engine 5 (stages, stage_groups)
+XTAB_VARIANTS = [(16, 3), (20, 3), (24, 2), (28, 2)]   # engine 8 (warps per CTA, ring stages)
 NF4_LEAN_VARIANTS = [(4, 4, 2, 0), (4, 8, 2, 0), (6, 4, 2, 0), (4, 4, 4, 0), (4, 4, 2, 2), (4, 8, 2, 2),
                      (6, 4, 2, 2), (8, 4, 2, 2), (4, 4, 4, 2)]   # (stages, rw, vw, lut) instantiated
-NF4_TMA_VARIANTS = [(4, 2, 4), (4, 2, 8), (8, 2, 4), (8, 2, 6), (16, 2, 4), (4, 4, 4), (8, 4, 4)]  # (rw, vw, st)
 
 
 SPLIT_INT4_VARIANTS = [(4, 1), (6, 1), (3, 2), (4, 2), (2, 4), (3, 4)]   # split INT4 (stages, stage_groups)
@@ -131,10 +131,6 @@ def config_grid(fmt, m=1):
     if m == 1:
         yield from split_grid(fmt)
     if fmt == FMT_INT4_G128 and m == 1:
-        for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (2, 3, 4, 6)):
-            if kw * rg <= 8:
-                yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
-                           x_tile=0, flags=0, engine=4, stages=st, stage_groups=1)
         for kw, rg, (st, sg) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), LEAN_VARIANTS):
             if kw * rg <= 8:
                 yield dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
@@ -155,6 +151,10 @@ def config_grid(fmt, m=1):
             if kw * rg <= 8 and (nt == 8 or m > 8):
                 yield dict(vec_words=4, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=nt, nf4_lut=0,
                            x_tile=0, flags=0, engine=1)
+    if fmt == FMT_NF4_B64 and m == 1:   # x-pair table kernel: (warps per CTA, ring stages)
+        for nw, st in XTAB_VARIANTS:
+            yield dict(vec_words=1, rows_per_warp=8, warps_k=1, row_groups=nw, batch_tile=1, nf4_lut=0,
+                       x_tile=0, flags=0, engine=8, stages=st, stage_groups=0)
     if fmt == FMT_NF4_B64 and m <= 16:
         for kw, rg, st in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), (2, 3, 4) if m == 1 else (2, 3)):
             if kw * rg <= 8:
@@ -164,10 +164,6 @@ def config_grid(fmt, m=1):
             if kw * rg <= 8:
                 yield dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=lut,
                            x_tile=0, flags=0, engine=6, stages=st, stage_groups=0)
-        for kw, rg, (rw, vw, st) in itertools.product((1, 2, 4, 8), (1, 2, 4, 8), NF4_TMA_VARIANTS):
-            if kw * rg <= 8:
-                yield dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=0,
-                           x_tile=0, flags=0, engine=3, stages=st, stage_groups=0)
     luts = (0,) if fmt == FMT_INT4_G128 else (0, 1)
     mbs = (1,) if m == 1 else ((2,) if m == 2 else (4,))
     for vw, rw, kw, rg, mb, lut in itertools.product((2, 4), (1, 2, 4, 8), (1, 2, 4, 8), (1, 2, 4, 8), mbs, luts):

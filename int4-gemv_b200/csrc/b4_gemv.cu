@@ -9,7 +9,6 @@
 #include "b4_gemv_kernel.cuh"
 #include "b4_gemv_mma.cuh"
 #include "b4_gemv_tma.cuh"
-#include "b4_gemv_tma_nf4.cuh"
 #include "b4_gemv_lean.cuh"
 #include "b4_gemv_lean_mb.cuh"
 #include "b4_gemv_lean_nf4.cuh"
@@ -104,11 +103,11 @@ size_t lean_nf4_smem(int in_f, int kw, int rg, int rw, int vw, int depth, int lu
 }
 
 // Shared memory of the lean INT4 kernel: [x][reduction][rings].
-size_t lean_int4_smem(int in_f, int kw, int rg, int stages, int groups, int async_ring)
+size_t lean_int4_smem(int in_f, int kw, int rg, int stages, int groups)
 {
     size_t smem = (size_t)in_f * 2 + (size_t)(rg * kw * 16 + 3) / 4 * 16;
     // per warp: stages x groups x 2 rows x 32 lanes x 16 B
-    if (async_ring) smem += (size_t)kw * rg * stages * groups * 64 * 16;
+    smem += (size_t)kw * rg * stages * groups * 64 * 16;
     return smem;
 }
 
@@ -156,10 +155,27 @@ int check_problem(const GemvProblem& p)
     return cudaSuccess;
 }
 
+namespace {
+int sm_count_cached(int dev);
+}
+
+// SMs of the current device (148 on a B200; a partitioned or MPS-limited
+// device reports fewer), 148 when no device can be queried (the rule asked for
+// on a machine without a GPU).
+int current_sms()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    return sm_count_cached(dev);
+}
+
 void default_config(const GemvProblem& p, b4_gemv_config* cfg)
 {
     const int words = p.in_f / 8;
-    const int sms = 148;  // the rule is fitted to B200; it stays valid elsewhere
+    const int sms = current_sms();   // the rule's tile counts were fitted on B200 (148 SMs)
     cfg->nf4_lut = 0;
     cfg->x_tile = 0;
     cfg->flags = 0;
@@ -194,7 +210,7 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
         for (int pass = 0; pass < 2; ++pass) {
             for (const auto& v : variants) {
                 if (ng % v[1] || (v[1] > 1 && !aligned(p.scale, 2u * v[1]))) continue;
-                const size_t smem = lean_int4_smem(p.in_f, cfg->warps_k, rg, v[0], v[1], 1);
+                const size_t smem = lean_int4_smem(p.in_f, cfg->warps_k, rg, v[0], v[1]);
                 if (smem > (pass == 0 ? kTmaSmemLimit / 2 - 1024 : kTmaSmemLimit)) continue;
                 cfg->engine = B4_ENGINE_MMA_LEAN_ASYNC;
                 cfg->stages = v[0];
@@ -356,7 +372,6 @@ void default_config(const GemvProblem& p, b4_gemv_config* cfg)
 
 int launch_gemv_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_tma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
-int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_lean(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_lean_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
 int launch_gemv_nf4_mma(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st);
@@ -365,8 +380,7 @@ int launch_gemv(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
 {
     if (c.engine == B4_ENGINE_MMA) return launch_gemv_mma(p, c, st);
     if (c.engine == B4_ENGINE_MMA_TMA) return launch_gemv_tma(p, c, st);
-    if (c.engine == B4_ENGINE_FMA_TMA) return launch_gemv_tma_nf4(p, c, st);
-    if (c.engine == B4_ENGINE_MMA_LEAN || c.engine == B4_ENGINE_MMA_LEAN_ASYNC) return launch_gemv_lean(p, c, st);
+    if (c.engine == B4_ENGINE_MMA_LEAN_ASYNC) return launch_gemv_lean(p, c, st);
     if (c.engine == B4_ENGINE_FMA_LEAN) return launch_gemv_lean_nf4(p, c, st);
     if (c.engine == B4_ENGINE_MMA_NF4) return launch_gemv_nf4_mma(p, c, st);
     if (c.engine != B4_ENGINE_FMA) return cudaErrorInvalidValue;
@@ -552,7 +566,10 @@ int sm_count_cached(int dev)
     if (dev < 0 || dev >= 64) return 148;
     int n = cache[dev].load(std::memory_order_relaxed);
     if (n == 0) {
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            cudaGetLastError();   // no device: the rule keeps B200's count
+            n = 148;
+        }
         cache[dev].store(n, std::memory_order_relaxed);
     }
     return n;
@@ -669,40 +686,6 @@ cudaError_t launch_persistent(void* fn, void* params, long long tiles, int threa
 
 }  // namespace
 
-int launch_gemv_tma_nf4(const GemvProblem& p, const b4_gemv_config& c, cudaStream_t st)
-{
-    if (p.fmt != kNf4 || p.m != 1) return cudaErrorInvalidValue;
-    const int rw = c.rows_per_warp, vw = c.vec_words, kw = c.warps_k, rg = c.row_groups;
-    if (kw < 1 || rg < 1 || kw * rg > 8) return cudaErrorInvalidValue;
-    if (vw != 2 && vw != 4) return cudaErrorInvalidValue;
-    if (p.in_f % (256 * vw)) return cudaErrorInvalidValue;
-    if (!aligned(p.qw, 16) || !aligned(p.scale, 16)) return cudaErrorInvalidValue;
-    void* fn = gemv_kernel_nf4_tma(rw, vw, c.stages);
-    if (!fn) return cudaErrorInvalidValue;
-    const size_t stage_bytes = (size_t)rw * (128 * vw + 16 * vw);
-    const size_t x_red = (size_t)p.in_f * 4 + (size_t)rg * kw * rw * 4;
-    TmaNf4Params tp;
-    tp.ring_offset = (int)((x_red + 127) / 128 * 128);
-    tp.bar_offset = tp.ring_offset + (int)((size_t)kw * rg * c.stages * stage_bytes);
-    const size_t total = (size_t)tp.bar_offset + (size_t)kw * rg * c.stages * 8;
-    KParams& kp = tp.k;
-    kp.qw = p.qw;
-    kp.scale = p.scale;
-    kp.x = static_cast<const __half*>(p.x);
-    kp.y = p.y;
-    kp.in_f = p.in_f;
-    kp.out_f = p.out_f;
-    kp.m = p.m;
-    kp.x_ld = p.x_ld;
-    kp.y_ld = p.y_ld;
-    kp.kw = kw;
-    kp.rg = rg;
-    kp.tile_chunks = 0;
-    kp.x_vec = aligned(p.x, 8);
-    const long long rows_per_cta = (long long)rg * rw;
-    return launch_persistent(fn, &tp, (p.out_f + rows_per_cta - 1) / rows_per_cta, 32 * kw * rg, total, c.flags, st);
-}
-
 namespace {
 
 bool lean_geometry_ok(const b4_gemv_config& c) { return c.warps_k >= 1 && c.row_groups >= 1 && c.warps_k * c.row_groups <= 8; }
@@ -720,12 +703,12 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
     if (m > 1 && c.engine != B4_ENGINE_MMA_LEAN_ASYNC) return cudaErrorInvalidValue;
     if (nseg < 1 || nseg > kLeanMaxSeg) return cudaErrorInvalidValue;
     const int kw = c.warps_k, rg = c.row_groups;
-    const int async_ring = c.engine == B4_ENGINE_MMA_LEAN_ASYNC;
-    const int groups = async_ring ? c.stage_groups : 1;
+    if (c.engine != B4_ENGINE_MMA_LEAN_ASYNC) return cudaErrorInvalidValue;
+    const int groups = c.stage_groups;
     if (groups != 1 && groups != 2 && groups != 4) return cudaErrorInvalidValue;
     if ((in_f / kGroup) % groups) return cudaErrorInvalidValue;   // a stage of `groups` groups tiles the row
     const int nb = m > 8 ? 2 : 1;
-    void* fn = m == 1 ? gemv_kernel_int4_lean(c.stages, groups, async_ring)
+    void* fn = m == 1 ? gemv_kernel_int4_lean(c.stages, groups)
                       : gemv_kernel_int4_lean_mb(c.stages, groups, nb, wide);
     if (!fn) return cudaErrorInvalidValue;
     const int tr = c.tile_rows ? c.tile_rows : 16;
@@ -759,7 +742,7 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
         const size_t smem = lean_int4_mb_smem(in_f, m, kw, rg, c.stages, groups);
         return launch_persistent(fn, &mp, tiles, 32 * kw * rg, smem, c.flags, st);
     }
-    const size_t smem = lean_int4_smem(in_f, kw, rg, c.stages, groups, async_ring);
+    const size_t smem = lean_int4_smem(in_f, kw, rg, c.stages, groups);
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
 }
 
@@ -851,14 +834,13 @@ int launch_lean_int4_p2p(const GemvProblem& p, const b4_gemv_config& c, const P2
 {
     if (p.fmt != kInt4 || p.m != 1 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c))
         return cudaErrorInvalidValue;
-    if (c.engine != B4_ENGINE_MMA_LEAN && c.engine != B4_ENGINE_MMA_LEAN_ASYNC) return cudaErrorInvalidValue;
+    if (c.engine != B4_ENGINE_MMA_LEAN_ASYNC) return cudaErrorInvalidValue;
     const int kw = c.warps_k, rg = c.row_groups;
-    const int async_ring = c.engine == B4_ENGINE_MMA_LEAN_ASYNC;
-    const int groups = async_ring ? c.stage_groups : 1;
+    const int groups = c.stage_groups;
     if (groups != 1 && groups != 2 && groups != 4) return cudaErrorInvalidValue;
     if ((p.in_f / kGroup) % groups) return cudaErrorInvalidValue;
     if (!aligned(p.qw, 16) || !aligned(p.scale, 2u * groups)) return cudaErrorInvalidValue;
-    void* fn = gemv_kernel_int4_lean_p2p(c.stages, groups, async_ring);
+    void* fn = gemv_kernel_int4_lean_p2p(c.stages, groups);
     if (!fn) return cudaErrorInvalidValue;
     const int tr = c.tile_rows ? c.tile_rows : 16;
     if (tr < 1 || tr > 16) return cudaErrorInvalidValue;
@@ -880,7 +862,7 @@ int launch_lean_int4_p2p(const GemvProblem& p, const b4_gemv_config& c, const P2
     lp.tr = tr;
     lp.x_vec = aligned(p.x, 16);
     lp.p2p = a;
-    const size_t smem = lean_int4_smem(p.in_f, kw, rg, c.stages, groups, async_ring);
+    const size_t smem = lean_int4_smem(p.in_f, kw, rg, c.stages, groups);
     // a CTA waits only for the CTA of the same index on every peer, so with
     // every CTA resident no wait can depend on a CTA that is not running
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st, true);
@@ -981,7 +963,7 @@ void default_config_multi(int fmt, const b4_gemv_segment* segs, int nseg, int in
 int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
                       const b4_gemv_config& c, cudaStream_t st)
 {
-    if (fmt == kInt4 && ((m == 1 && c.engine == B4_ENGINE_MMA_LEAN) || (m <= 16 && c.engine == B4_ENGINE_MMA_LEAN_ASYNC)))
+    if (fmt == kInt4 && m <= 16 && c.engine == B4_ENGINE_MMA_LEAN_ASYNC)
         return launch_lean_int4_segs(segs, nseg, x, in_f, m, c, st);
     if (m == 1 && fmt == kNf4 && c.engine == B4_ENGINE_FMA_LEAN)
         return launch_lean_nf4_segs(segs, nseg, x, in_f, m, c, st);

@@ -31,14 +31,13 @@
 // tiles of up to four weight matrices that share x (q/k/v, gate/up) form one
 // tile space, so a fused projection is one launch.
 //
-// ASYNC = 1 moves the in-flight codes out of registers: each lane copies its
-// own 16-byte pieces of every future stage with cp.async into private ring
-// slots in shared memory (((stage*G + group)*2 + row)*32 + lane: a warp's
-// copies and reads of one slot are 512 contiguous bytes, conflict-free) and
-// reads them back when the stage's turn comes.  Lanes only ever read what they
-// copied themselves, so the per-thread cp.async.wait_group is the only
-// ordering needed, and D stages in flight cost shared memory instead of
-// registers.  ASYNC = 0 keeps them in registers (G = 1 only).
+// The in-flight codes live in shared memory, not registers: each lane copies
+// its own 16-byte pieces of every future stage with cp.async into private ring
+// slots (((stage*G + group)*2 + row)*32 + lane: a warp's copies and reads of
+// one slot are 512 contiguous bytes, conflict-free) and reads them back when
+// the stage's turn comes.  Lanes only ever read what they copied themselves,
+// so the per-thread cp.async.wait_group is the only ordering needed, and D
+// stages in flight cost shared memory instead of registers.
 //
 // The first tile's first D-1 stages are requested before the kernel waits on
 // the grid it depends on (griddepcontrol.wait): codes and scales are inputs
@@ -143,10 +142,9 @@ __device__ __forceinline__ void lean_group(const uint4 wav, const uint4 wbv, con
 // over the ranks through peer memory in the epilogue (b4_p2p.cuh), one warp
 // block at a time, so the transfer of early blocks overlaps the math of later
 // ones.  One segment only.
-template <int D, int G, int ASYNC, int P2P = 0>   // D >= 2; G in {1, 2, 4}; ASYNC = 0 needs G = 1
+template <int D, int G, int P2P = 0>   // D >= 2; G in {1, 2, 4}
 __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p)
 {
-    static_assert(ASYNC || G == 1, "register pipeline holds one group per stage");
     using ST = typename LeanScale<G>::T;
     extern __shared__ __align__(16) uint4 lsm[];
     const int lane = threadIdx.x & 31;
@@ -161,20 +159,19 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     const int n_tiles = p.n_tiles;
     uint4* xs = lsm;                                         // one slot per word
     float* red = reinterpret_cast<float*>(xs + words);      // rg*kw*16
-    // ASYNC: this warp's ring, D stages x G groups x 2 rows x 32 lanes x 16 bytes
+    // this warp's ring, D stages x G groups x 2 rows x 32 lanes x 16 bytes
     uint4* ring = xs + words + (p.rg * p.kw * 16 + 3) / 4 + warp * (D * G * 64);
 
     // stages of this warp: ks, ks + kw, ...; n_it is warp-uniform
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
     const int wstep = 4 * G * p.kw;                          // uint4 per stage step
 
-    // ASYNC: scales run SD - 1 stages ahead of their use (codes D - 1): a
-    // scale is one small global load whose latency the codes' cp.async ring
-    // does not hide, and a stage of 4 groups is only ~0.3 us of work
-    constexpr int SD = ASYNC ? 2 * D : D;
+    // scales run SD - 1 stages ahead of their use (codes D - 1): a scale is
+    // one small global load whose latency the codes' cp.async ring does not
+    // hide, and a stage of 4 groups is only ~0.3 us of work
+    constexpr int SD = 2 * D;
     const uint4 *pa = nullptr, *pb = nullptr;
     const ST *sa_p = nullptr, *sb_p = nullptr;
-    uint4 bufa[ASYNC ? 1 : D] = {}, bufb[ASYNC ? 1 : D] = {};
     ST bsa[SD] = {}, bsb[SD] = {};
     int r0 = 0, out_f = 0;
     bool va = false, vb = false;   // this lane's rows r0+g, r0+g+8 carry weights
@@ -208,21 +205,10 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     };
     auto fetch = [&](int slot) {
         // rows that carry no weights load nothing (their MMA rows are never stored)
-        if constexpr (ASYNC) {
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                if (va) cp_async16(ring + ((slot * G + h) * 2) * 32 + lane, pa + 4 * h);
-                if (vb) cp_async16(ring + ((slot * G + h) * 2 + 1) * 32 + lane, pb + 4 * h);
-            }
-        } else {
-            if (va) {
-                const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pa));
-                bufa[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
-            }
-            if (vb) {
-                const WordVec<4> v = ld_stream<4>(reinterpret_cast<const uint32_t*>(pb));
-                bufb[slot] = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
-            }
+        for (int h = 0; h < G; ++h) {
+            if (va) cp_async16(ring + ((slot * G + h) * 2) * 32 + lane, pa + 4 * h);
+            if (vb) cp_async16(ring + ((slot * G + h) * 2 + 1) * 32 + lane, pb + 4 * h);
         }
         pa += wstep;
         pb += wstep;
@@ -240,7 +226,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
 #pragma unroll
         for (int d = 0; d < D - 1; ++d) {
             if (d < n_it) fetch(d);
-            if constexpr (ASYNC) cp_async_commit();   // one group per stage, even if empty
+            cp_async_commit();   // one group per stage, even if empty
         }
     };
 
@@ -275,23 +261,15 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                     const int cs = d % D, nxt = (d + D - 1) % D;
                     if (it + D - 1 < n_it) fetch(nxt);
                     if (it + SD - 1 < n_it) fetch_scales((d + SD - 1) % SD);
-                    if constexpr (ASYNC) {
-                        cp_async_commit();
-                        cp_async_wait<D - 1>();            // this lane's copies of stage it landed
-                    }
+                    cp_async_commit();
+                    cp_async_wait<D - 1>();                // this lane's copies of stage it landed
                     float sa[G], sb[G];
                     lean_scales_to_f32<G>(bsa[d], sa);
                     lean_scales_to_f32<G>(bsb[d], sb);
 #pragma unroll
                     for (int h = 0; h < G; ++h) {
-                        uint4 wav, wbv;
-                        if constexpr (ASYNC) {
-                            wav = ring[((cs * G + h) * 2) * 32 + lane];
-                            wbv = ring[((cs * G + h) * 2 + 1) * 32 + lane];
-                        } else {
-                            wav = bufa[cs];
-                            wbv = bufb[cs];
-                        }
+                        const uint4 wav = ring[((cs * G + h) * 2) * 32 + lane];
+                        const uint4 wbv = ring[((cs * G + h) * 2 + 1) * 32 + lane];
                         if (g == 0) {   // B column 0 = x; the other lanes keep their zeros
 #pragma unroll
                             for (int i = 0; i < 4; ++i) xv[i] = xp[16 * h + i];
@@ -305,7 +283,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
                 }
             }
         }
-        if constexpr (ASYNC) cp_async_wait<0>();   // nothing of this tile left in flight
+        cp_async_wait<0>();   // nothing of this tile left in flight
 
         // rows r0+g and r0+g+8; lanes q = 0..3 hold the same values
         if constexpr (P2P) {
@@ -364,7 +342,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     }
 }
 
-void* gemv_kernel_int4_lean(int depth, int groups, int async_ring);
-void* gemv_kernel_int4_lean_p2p(int depth, int groups, int async_ring);
+void* gemv_kernel_int4_lean(int depth, int groups);
+void* gemv_kernel_int4_lean_p2p(int depth, int groups);
 
 }  // namespace b4

@@ -131,8 +131,7 @@ def kernel_configs():
     """Every instantiated kernel (vec_words, rows_per_warp, batch_tile, nf4_lut)."""
     out = [(0, 4, rw, mb, 0, 1) for rw in (16, 32) for mb in (8, 16)]  # tensor-pipe INT4
     out += [(0, 4, 16, mb, 0, 2) for mb in (8, 16)]                     # tensor pipe + bulk-copy ring
-    out += [(1, vw, rw, 1, 0, 3) for rw, vw in [(4, 2), (8, 2), (16, 2), (4, 4), (8, 4)]]  # NF4 + ring
-    out += [(0, 4, 16, 1, 0, 4), (0, 4, 16, 1, 0, 5)]                                    # lean INT4, m = 1
+    out += [(0, 4, 16, 1, 0, 5)]                                                         # lean INT4, m = 1
     out += [(1, vw, rw, 1, lut, 6) for vw, rw, lut in [(2, 4, 0), (2, 8, 0), (4, 4, 0), (2, 4, 2), (2, 8, 2),
                                                        (4, 4, 2)]]                       # lean NF4, m = 1
     out += [(1, 4, 16, 1, 0, 7)]                                                         # NF4 tensor pipe, m = 1
@@ -156,13 +155,10 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
         cases += [(100, 1024, 11 if mb == 16 else 7), (33, 2048, mb), (48, 640, 8), (16, 128, 1)]
     if engine == 6:   # m = 1, ragged last step included
         cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 64, 1), (5, 18944, 1), (3, 1088, 1)]
-    if engine in (4, 5):   # m = 1
+    if engine == 5:        # m = 1
         cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 128, 1), (5, 18944, 1)]
     if engine == 7:        # m = 1, in_f a multiple of 128
         cases = [(37, 1152, 1), (9, 512, 1), (70, 3584, 1), (300, 128, 1), (5, 18944, 1), (33, 896, 1)]
-    if engine == 3:   # m = 1, in_f a multiple of 256 * vec_words
-        cases = [(37, 1024, 1), (9, 2048, 1), (70, 3584, 1) if vw == 2 else (70, 4096, 1), (300, 1024, 1),
-                 (5, 18944, 1) if vw == 2 else (5, 8192, 1)]
     for out_f, in_f, m in cases:
         W, X = rand_problem(rng, out_f, in_f, m)
         qw, sc = quantised(fmt, W, cuda)
@@ -201,8 +197,8 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                     assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 cfg.update(tile_rows=0)
                 continue
-            if engine in (4, 5):
-                variants = [(st, 1) for st in (2, 3, 4, 6)] if engine == 4 else LEAN_VARIANTS
+            if engine == 5:
+                variants = LEAN_VARIANTS
                 for st, sg in variants:
                     cfg.update(stages=st, stage_groups=sg)
                     if (in_f // 128) % sg:   # a stage of sg groups must tile the row
@@ -218,13 +214,6 @@ def test_gemv_every_kernel(cuda, oracle, fmt, vw, rw, mb, lut, engine):
                     y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
                     assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
                 cfg.update(tile_rows=0)
-                continue
-            if engine == 3:
-                for st in {(4, 2): (4, 8), (8, 2): (4, 6), (16, 2): (4,), (4, 4): (4,), (8, 4): (4,)}[(rw, vw)]:
-                    cfg.update(stages=st)
-                    y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
-                    assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
-                assert b4gemv.load().b4_device_error(1) == 0
                 continue
             y = b4gemv.gemv(fmt, qw, sc, Xd, config=cfg).cpu().numpy()
             assert rel_err(y, ref) < TOL, (out_f, in_f, m, cfg)
@@ -339,11 +328,10 @@ def test_gemv_multi_segments_one_launch(cuda, oracle, fmt):
             cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=5,
                           stages=st, stage_groups=sg) for kw, rg in [(8, 1), (2, 4), (1, 2)]
                      for st, sg in LEAN_VARIANTS]
-            cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=4, row_groups=2, batch_tile=1, engine=4, stages=3)]
             cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=2, row_groups=2, batch_tile=8, engine=1)]
             cfgs += [dict(vec_words=4, rows_per_warp=16, warps_k=kw, row_groups=rg, batch_tile=1, engine=e, stages=st,
                           stage_groups=sg, tile_rows=tr) for kw, rg in [(8, 1), (2, 2)] for tr in (3, 13)
-                     for e, st, sg in [(4, 4, 1), (5, 2, 4)]]
+                     for e, st, sg in [(5, 4, 1), (5, 2, 4)]]
         else:
             cfgs += [dict(vec_words=vw, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=1, nf4_lut=lut,
                           engine=6, stages=4) for vw, rw, lut in [(2, 4, 0), (4, 4, 0), (2, 8, 2)]
