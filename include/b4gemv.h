@@ -120,8 +120,8 @@ typedef struct b4_gemv_config {
  * the slice additions varies from run to run).  Needs a workspace
  * (b4_gemv_ws, b4_gemv_multi_ws) of B4_XTAB_WORKSPACE_BYTES: two counters,
  * zero between calls.  Codes and absmax 16-byte aligned.  row_groups = warps
- * per CTA and stages = cp.async ring stages per warp: (16, 3), (20, 3),
- * (24, 2) or (28, 2); the other fields are ignored. */
+ * per CTA and stages = cp.async ring stages per warp: (12, 3), (16, 3),
+ * (20, 2) or (24, 2); the other fields are ignored. */
 #define B4_ENGINE_NF4_XTAB 8
 #define B4_XTAB_WORKSPACE_BYTES 256
 
@@ -168,11 +168,13 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
 
 /* ---- GEMV with a caller-owned workspace --------------------------------------
  * Two kernels need device scratch, which the caller owns:
- *   - at batch 1, NF4 with in_f a multiple of 256 (x 4-byte aligned) runs on
- *     the x-pair table kernel (B4_ENGINE_NF4_XTAB): its CTAs each cover a
+ *   - at batch 1, NF4 with in_f a multiple of 256 (x 4-byte aligned, codes
+ *     and absmax 16-byte aligned) and at least 24 MB of weights runs on the
+ *     x-pair table kernel (B4_ENGINE_NF4_XTAB): its CTAs each cover a
  *     256-column slice of in_f, add their shares into y with atomics and
  *     count themselves in on two counters in `ws` first
- *     (B4_XTAB_WORKSPACE_BYTES);
+ *     (B4_XTAB_WORKSPACE_BYTES); smaller NF4 matrices keep the plain rule
+ *     (the kernel's ~4 us start-up costs more than it saves there);
  *   - the split path (B4_FLAG_SPLIT) gives every warp of the grid an equal
  *     run of (16-row block, k-step) units and adds a block's pieces through
  *     `ws` (per 16-row block, one arrival counter and the pieces' partial
@@ -195,7 +197,8 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
  * cudaErrorInvalidValue before anything is launched. */
 int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_config* cfg, size_t* bytes);
 /* The dispatch rule of b4_gemv_ws (cfg NULL): the x-pair table kernel for NF4
- * at batch 1 with in_f % 256 == 0, b4_gemv_default_config's choice otherwise. */
+ * at batch 1 with in_f % 256 == 0 and at least 24 MB of weights,
+ * b4_gemv_default_config's choice otherwise. */
 int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg);
 int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f, int out_f,
                int m, const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream);
@@ -252,8 +255,9 @@ int b4_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void* x,
 int b4_gemv_multi_default_config(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
                                  b4_gemv_config* cfg);
 /* b4_gemv_multi with a caller-owned workspace (conventions of b4_gemv_ws): the
- * same one-launch fusion, and at batch 1 for NF4 with in_f % 256 == 0 the
- * x-pair table kernel over all segments (ws of B4_XTAB_WORKSPACE_BYTES).  cfg
+ * same one-launch fusion, and at batch 1 for NF4 with in_f % 256 == 0 and at
+ * least 24 MB of weights over all segments the x-pair table kernel (ws of
+ * B4_XTAB_WORKSPACE_BYTES).  cfg
  * NULL or B4_ENGINE_AUTO = that rule (only cfg->flags' B4_FLAG_PDL is read). */
 int b4_gemv_multi_default_config_ws(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
                                     b4_gemv_config* cfg);
@@ -343,6 +347,12 @@ int b4_shard_columns(int fmt, const uint32_t* qw, const void* scale, int in_f, i
  * ncclAllReduce(y, y, m*out_f, fp32, sum) on the same stream. */
 int b4_tp_gemv_allreduce(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard,
                          float* y, int in_shard, int out_f, int m, void* nccl_comm, b4_stream_t stream);
+/* The same with the GEMV through b4_gemv_ws (the rule of b4_gemv_ws, a
+ * caller-owned workspace as b4_gemv_ws takes it): NF4 shards with in_shard a
+ * multiple of 256 run on the x-pair table kernel. */
+int b4_tp_gemv_allreduce_ws(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard,
+                            float* y, int in_shard, int out_f, int m, void* ws, size_t ws_bytes, void* nccl_comm,
+                            b4_stream_t stream);
 
 /* Row-parallel GEMV with the all-reduce fused into its epilogue over NVLink
  * peer memory, no collective library: each warp stores its finished rows into

@@ -109,6 +109,7 @@ SIGNATURES = {
     "b4_nccl_wait": (_I, [_P, _P, _I]),
     "b4_shard_columns": (_I, [_I, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "b4_tp_gemv_allreduce": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "b4_tp_gemv_allreduce_ws": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P, ctypes.c_size_t, _P, _P]),
     "b4_p2p_create": (_I, [_I, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
     "b4_p2p_ipc_handle": (_I, [_P, _P]),
     "b4_p2p_open_peer": (_I, [_P, _I, _P]),

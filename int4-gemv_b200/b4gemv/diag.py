@@ -107,7 +107,7 @@ def time_chained(torch, prob, cfg, reps=None):
 
 TMA_VARIANTS = [(4, 4), (3, 4), (6, 4), (4, 2), (4, 8), (8, 2)]   # (stages, stage_groups) instantiated
 LEAN_VARIANTS = [(4, 1), (6, 1), (8, 1), (3, 2), (4, 2), (6, 2), (2, 4), (3, 4)]   # engine 5 (stages, stage_groups)
-XTAB_VARIANTS = [(16, 3), (20, 3), (24, 2), (28, 2)]   # engine 8 (warps per CTA, ring stages)
+XTAB_VARIANTS = [(12, 3), (16, 3), (20, 2), (24, 2)]   # engine 8 (warps per CTA, ring stages)
 NF4_LEAN_VARIANTS = [(4, 4, 2, 0), (4, 8, 2, 0), (6, 4, 2, 0), (4, 4, 4, 0), (4, 4, 2, 2), (4, 8, 2, 2),
                      (6, 4, 2, 2), (8, 4, 2, 2), (4, 4, 4, 2)]   # (stages, rw, vw, lut) instantiated
 

@@ -243,8 +243,9 @@ class TPDecodeLayer:
                                                           qw.shape[0], self.p2p.ptr,
                                                           FLAG_PDL if self.pdl else 0, stream))
             return
-        check(f"tp {name}", load().b4_tp_gemv_allreduce(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
-                                                         qw.shape[0], 1, self.comm.ptr, stream))
+        check(f"tp {name}", load().b4_tp_gemv_allreduce_ws(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
+                                                            qw.shape[0], 1, _p(self.ws), self.ws.numel(),
+                                                            self.comm.ptr, stream))
 
     def forward(self, x, attn, stream=None):
         """x: fp16 [1, hidden] (replicated); attn: fp16 [1, q shard] (this

@@ -1066,16 +1066,34 @@ int launch_gemv_xtab(const GemvProblem& p, const b4_gemv_config& c, void* ws, si
     return launch_xtab_segs(&s, 1, p.x, p.in_f, c, ws, ws_bytes, st);
 }
 
-void xtab_config(b4_gemv_config* cfg)
+// The x-pair table kernel pays ~4.4 us per launch before it streams (the
+// tables, the zeroing of y, the previous launch's drain: it holds one CTA per
+// SM) and then streams at ~4.2 TB/s; the tensor-pipe and CUDA-core NF4
+// kernels start in ~3 us and stream at ~3.5 TB/s or less (B200, PDL chains,
+// every Qwen2.5-7B, Llama-3-70B and tensor-parallel shard shape and the fused
+// q/k/v and gate/up launches).  It is taken from 24 MB of weights up
+// (Qwen gate/up 13.9 us against 13.8, fused gate+up 23.1 against 25.1, down
+// 14.4 against 22.3, Llama-3-70B gate/up 37.2 against 53.7, down 43.8 against
+// 60.5); 24 warps with 2 ring stages from 48 MB or for rows longer than 8192
+// columns, else 16 warps with 3.
+bool xtab_pays(long long weight_bytes) { return weight_bytes >= 24LL * 1000 * 1000; }
+
+void xtab_config(b4_gemv_config* cfg, long long weight_bytes, int in_f)
 {
     *cfg = b4_gemv_config{};
     cfg->engine = B4_ENGINE_NF4_XTAB;
     cfg->vec_words = 1;
     cfg->rows_per_warp = kXtabBatch;
     cfg->warps_k = 1;
-    cfg->row_groups = 24;   // warps per CTA
+    const bool big = weight_bytes >= 48LL * 1000 * 1000 || in_f > 8192;
+    cfg->row_groups = big ? 24 : 16;   // warps per CTA
     cfg->batch_tile = 1;
-    cfg->stages = 2;        // ring stages per warp
+    cfg->stages = big ? 2 : 3;         // ring stages per warp
+}
+
+long long nf4_weight_bytes(long long rows, int in_f)
+{
+    return rows * in_f / 2 + rows * (in_f / kNf4Block) * 4;
 }
 
 // ---- split launches (b4_gemv_split.cuh) ---------------------------------------
@@ -1216,8 +1234,9 @@ void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
     // down 13.2 vs 10.5 us; NF4 gate 16.8 vs 14.2 us); split configs are taken
     // when passed explicitly.
     const b4_gemv_segment seg{p.qw, p.scale, p.y, p.out_f};
-    if (xtab_shape(p.fmt, p.in_f, p.m, p.x) && xtab_buffers(&seg, 1)) {
-        xtab_config(cfg);
+    const long long wb = nf4_weight_bytes(p.out_f, p.in_f);
+    if (xtab_shape(p.fmt, p.in_f, p.m, p.x) && xtab_buffers(&seg, 1) && xtab_pays(wb)) {
+        xtab_config(cfg, wb, p.in_f);
         return;
     }
     default_config(p, cfg);
@@ -1395,7 +1414,11 @@ int b4_gemv_multi_default_config_ws(int fmt, const b4_gemv_segment* segs, int ns
     if (!cfg) return cudaErrorInvalidValue;
     const int e = check_segments(fmt, segs, nseg, reinterpret_cast<const void*>(256), in_f, m, false);
     if (e != cudaSuccess) return e;
-    if (xtab_shape(fmt, in_f, m, reinterpret_cast<const void*>(256)) && xtab_buffers(segs, nseg)) xtab_config(cfg);
+    long long rows = 0;
+    for (int s = 0; s < nseg; ++s) rows += segs[s].out_f;
+    const long long wb = nf4_weight_bytes(rows, in_f);
+    if (xtab_shape(fmt, in_f, m, reinterpret_cast<const void*>(256)) && xtab_buffers(segs, nseg) && xtab_pays(wb))
+        xtab_config(cfg, wb, in_f);
     else default_config_multi(fmt, segs, nseg, in_f, m, cfg);
     return cudaSuccess;
 }
@@ -1408,7 +1431,10 @@ int b4_gemv_multi_ws(int fmt, const b4_gemv_segment* segs, int nseg, const void*
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     b4_gemv_config c;
     if (!cfg || cfg->engine == B4_ENGINE_AUTO) {
-        if (xtab_shape(fmt, in_f, m, x) && xtab_buffers(segs, nseg)) xtab_config(&c);
+        long long rows = 0;
+        for (int s = 0; s < nseg; ++s) rows += segs[s].out_f;
+        const long long wb = nf4_weight_bytes(rows, in_f);
+        if (xtab_shape(fmt, in_f, m, x) && xtab_buffers(segs, nseg) && xtab_pays(wb)) xtab_config(&c, wb, in_f);
         else default_config_multi(fmt, segs, nseg, in_f, m, &c);
         c.flags = cfg ? cfg->flags & B4_FLAG_PDL : 0;
     } else {

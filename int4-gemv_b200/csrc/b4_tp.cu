@@ -166,6 +166,19 @@ int b4_tp_gemv_allreduce(int fmt, const uint32_t* qw_shard, const void* scale_sh
                                    reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int b4_tp_gemv_allreduce_ws(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard,
+                            float* y, int in_shard, int out_f, int m, void* ws, size_t ws_bytes, void* comm,
+                            b4_stream_t stream)
+{
+    const NcclApi& n = nccl();
+    if (!n.ok) return B4_STATUS_NCCL_MISSING;
+    if (!comm) return cudaErrorInvalidValue;
+    const int e = b4_gemv_ws(fmt, qw_shard, scale_shard, x_shard, y, in_shard, out_f, m, nullptr, ws, ws_bytes, stream);
+    if (e != 0) return e;
+    return nccl_status(n.AllReduce(y, y, (size_t)m * out_f, ncclFloat32, ncclSum, static_cast<ncclComm_t>(comm),
+                                   reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int b4_swiglu_f16(const float* gate, const float* up, void* out, long long n, b4_stream_t stream)
 {
     if (!gate || !up || !out || n <= 0) return cudaErrorInvalidValue;

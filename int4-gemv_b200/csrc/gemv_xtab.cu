@@ -7,10 +7,10 @@ void* b4::gemv_kernel_xtab(int warps, int stages)
 {
 #define B4_XTAB_PICK(NW, R) \
     if (warps == NW && stages == R) return (void*)&b4::b4_gemv_xtab_kernel<NW, R>;
+    B4_XTAB_PICK(12, 3)
     B4_XTAB_PICK(16, 3)
-    B4_XTAB_PICK(20, 3)
+    B4_XTAB_PICK(20, 2)
     B4_XTAB_PICK(24, 2)
-    B4_XTAB_PICK(28, 2)
 #undef B4_XTAB_PICK
     return nullptr;
 }

@@ -520,6 +520,7 @@ def test_int4_sixteen_warp_ctas_need_nine_rows(cuda):
 # ---- full-size properties (Llama-3-70B shapes, too large for a full CPU reference) ----
 
 L70 = {"qo": (8192, 8192), "gate_up": (28672, 8192), "down": (8192, 28672)}
+ORDER_TOL = 1e-6   # fp32 rounding of a different order of at most ~112 slice partials
 
 
 def device_quantised(fmt, out_f, in_f, seed, cuda):
@@ -539,7 +540,10 @@ def test_full_size_doubling_row_permutation_and_sampled_rows(cuda, oracle, name,
     2 is exact in fp16 and doubles every product and partial sum exactly);
     permuting the weight rows permutes y bit for bit (rows are independent);
     64 sampled rows within TOL of the double GEMV over their dequantised
-    weights."""
+    weights.  Where the rule picks the x-pair table kernel (NF4 here), whose
+    256-column slices meet in y through atomic adds in run-dependent order,
+    both properties hold to fp32 summation-order rounding instead: within
+    ORDER_TOL of max |y|."""
     import torch
     out_f, in_f = L70[name]
     qw, sc = device_quantised(fmt, out_f, in_f, 40 + fmt, cuda)
@@ -551,10 +555,17 @@ def test_full_size_doubling_row_permutation_and_sampled_rows(cuda, oracle, name,
     y2 = fn(qw, sc, x * 2)
     torch.cuda.synchronize()
     assert torch.isfinite(y1).all()
-    assert torch.equal(y2, y1 * 2)
+    order_free = b4gemv.default_config_ws(fmt, in_f, out_f, 1)["engine"] == b4gemv.ENGINE_NF4_XTAB
+
+    def same(a, b):
+        if not order_free:
+            return torch.equal(a, b)
+        return float((a.double() - b.double()).abs().max()) <= ORDER_TOL * float(b.double().abs().max())
+
+    assert same(y2, y1 * 2)
     perm = torch.randperm(out_f, generator=torch.Generator().manual_seed(7)).to(cuda)
     yp = fn(qw[perm].contiguous(), sc[perm].contiguous(), x)
-    assert torch.equal(yp, y1[:, perm])
+    assert same(yp, y1[:, perm])
     rows = np.sort(rng.choice(out_f, 64, replace=False))
     ref = f64_ref(oracle, fmt, qw[rows].contiguous(), sc[rows].contiguous(), X)
     assert rel_err(y1.cpu().numpy()[:, rows], ref) < TOL
