@@ -1,9 +1,12 @@
-"""Tensor-parallel decode layer on 2 GPUs (one process per GPU, NCCL created
-through the C ABI; gloo only hands over the NCCL unique id).
+"""Tensor-parallel decode layer on 2, 4 and 8 GPUs (one process per GPU, NCCL
+created through the C ABI; gloo only hands over the NCCL unique id); each
+world size runs where that many GPUs are visible.
 
-* parity: the layer's y at tp=2 against the same layer at tp=1 on one GPU,
-  and each row-parallel projection's all-reduced y against a double GEMV of
-  the full matrix (1e-3, the rel metric of int4_gemv.cu:74-81);
+* parity: the layer's y at tp = 2/4/8 against the same layer at tp=1 on one
+  GPU (a small layer, and the Llama-3-70B-shaped layer with both all-reduce
+  paths: NCCL and the fused peer-memory one), and each row-parallel
+  projection's all-reduced y against a double GEMV of the full matrix (1e-3,
+  the rel metric of int4_gemv.cu:74-81);
 * failure detection without a GPU fault: b4_nccl_wait's host deadline on a
   stream that is merely busy (a finite sleep kernel), and a rank that leaves
   between steps, which the other learns of through the store before its next
@@ -102,14 +105,93 @@ def _run(world, fmt):
     return dict(res)
 
 
-@pytest.mark.skipif(_n_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("fmt", [0, 1])
-def test_tp2_layer_matches_single_gpu(fmt):
-    res = _run(2, fmt)
-    for r in (0, 1):
+def test_tp_layer_matches_single_gpu(fmt, world):
+    if _n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, fmt)
+    for r in range(world):
         assert res[r]["layer"] < 1e-3, res
         assert res[r]["o_proj"] < 1e-3, res
         assert res[r]["q_rows"] == 0.0, res
+
+
+def _l70_worker(rank, world, port, fmt, results):
+    """The Llama-3-70B-shaped layer at tp = world, row-parallel projections on
+    NCCL and on the fused peer-memory all-reduce, every rank's y gathered to
+    rank 0 and compared with the same seeded layer at tp = 1."""
+    import sys
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.join(os.path.dirname(here), "int4-gemv_b200"))
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from b4gemv.tp import NcclComm, P2pComm, TPDecodeLayer
+    from oracle_py import rel_err
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    comm = NcclComm(rank, world)
+    p2p = P2pComm(rank, world, max_rows=8192)
+    out = {}
+    try:
+        layer = TPDecodeLayer(fmt, rank, world, comm, dev, seed=5, pdl=True)
+        g = torch.Generator(device=dev)
+        g.manual_seed(9)
+        x = torch.randn((1, 8192), generator=g, device=dev).half()
+        attn = torch.randn((1, 8192), generator=g, device=dev).half()
+        c0, c1 = layer.ranges["o"]
+        shard = attn[:, c0:c1].contiguous()
+        y_nccl = layer.forward(x, shard).clone()
+        layer.p2p = p2p
+        y_p2p = layer.forward(x, shard).clone()
+        torch.cuda.synchronize()
+        out["p2p_status"] = p2p.status()
+        mine = np.stack([y_nccl.cpu().numpy()[0], y_p2p.cpu().numpy()[0]])
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine)
+        if rank == 0:
+            del layer
+            torch.cuda.empty_cache()
+            one = TPDecodeLayer(fmt, 0, 1, None, dev, seed=5, pdl=True)
+            ref = one.forward(x, attn).cpu().numpy().astype(np.float64)
+            out["err"] = max(rel_err(a[None, :], ref) for ys in gathered for a in ys)
+        results[rank] = out
+    finally:
+        dist.barrier()
+        p2p.destroy()
+        comm.destroy()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("fmt", [0, 1], ids=["int4", "nf4"])
+def test_tp_llama70b_layer_both_allreduce_paths_match_single_gpu(fmt, world):
+    if _n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    res = ctx.Manager().dict()
+    port = _port()
+    ps = [ctx.Process(target=_l70_worker, args=(r, world, port, fmt, res)) for r in range(world)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=600)
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+    res = dict(res)
+    assert res[0]["err"] < 1e-3, res
+    assert all(res[r]["p2p_status"] == 0 for r in range(world)), res
 
 
 def _leaver(rank, world, port, results):
