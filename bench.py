@@ -625,7 +625,7 @@ def small_batch_bench(b4, torch):
         for name, out_f, in_f in (("gate_proj", 18944, 3584), ("down_proj", 3584, 18944)):
             for m in (1, 2, 4, 8, 16):
                 prob = Problem(torch, fmt, out_f, in_f, m=m)
-                rule = b4.default_config(fmt, in_f, out_f, m)
+                rule = b4.default_config_ws(fmt, in_f, out_f, m)   # the rule the timed launches (b4_gemv_ws) use
                 # the rule as the entry points run it (B4_ENGINE_AUTO: batch chunks where x
                 # does not fit the tensor-pipe engines), each launch a programmatic dependent
                 cfg = b4.GemvConfig.from_dict(dict(rule, engine=-1, flags=b4.FLAG_PDL))
@@ -878,7 +878,7 @@ def run_single(args, b4, torch, dev, d):
     table = shape_table(b4, torch, ref)
     nf4_rows = {r["shape"]: r for r in table if r["format"] == "nf4_b64"}
     dom = nf4_rows["gate_proj"]
-    traffic = profiled_traffic("nf4_gate_proj")
+    traffic = profiled_traffic("nf4_xtab_gate_proj_18944x3584")
 
     # end to end through the public API with host buffers
     e2e_n = max(3, min(K, 200))

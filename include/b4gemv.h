@@ -381,7 +381,9 @@ int b4_tp_gemv_p2p(int fmt, const uint32_t* qw_shard, const void* scale_shard, c
                    int in_shard, int out_f, b4_p2p* p2p, int flags, b4_stream_t stream);
 
 /* Elementwise glue of the decode layer: out = fp16(silu(gate) * up) (the MLP
- * activation between gate/up and down) and out = fp16(in). */
+ * activation between gate/up and down) and out = fp16(in).  Launched as
+ * programmatic dependents: each waits for the preceding kernel's completion
+ * before it reads, and lets the next kernel launch at once. */
 int b4_swiglu_f16(const float* gate, const float* up, void* out, long long n, b4_stream_t stream);
 int b4_cast_f16(const float* in, void* out, long long n, b4_stream_t stream);
 const char* b4_nccl_error_string(int status);

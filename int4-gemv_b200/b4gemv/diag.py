@@ -8,8 +8,12 @@ src/diag_aspect.cu on B200): the measurements the dispatch rule is fitted to.
       the three sweeps of diag_aspect.cu:346-358 (aspect ratio at constant
       weight count, rows at fixed x, x size at fixed rows) with the dispatch
       rule's config.
-  python -m b4gemv.diag run     --fmt nf4 --shape gate_proj [--launches 4] [--config k=v,...]
+  python -m b4gemv.diag run     --fmt nf4 --shape gate_proj [--m 1] [--launches 4] [--config k=v,...]
       a few launches of one GEMV (the command profiled by ncu).
+  python -m b4gemv.diag step    [--steps 10]
+      the benchmark's NF4 decode step, eagerly (the launch list's command).
+  python -m b4gemv.diag glue    [--n 28672] [--launches 3]
+      the decode layer's elementwise kernels.
 Run from int4-gemv_b200/ (or with it on sys.path).
 """
 from __future__ import annotations
@@ -20,7 +24,7 @@ import itertools
 import json
 import sys
 
-from . import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load
+from . import FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GemvConfig, check, load, quantise_nf4_device
 
 SHAPES = {"q_proj": (3584, 3584), "k_proj": (512, 3584), "v_proj": (512, 3584), "o_proj": (3584, 3584),
           "gate_proj": (18944, 3584), "up_proj": (18944, 3584), "down_proj": (3584, 18944),
@@ -264,6 +268,51 @@ def cmd_run(args, torch):
     print(f"ran {args.launches} launches of {args.fmt} {args.shape} {out_f}x{in_f} m={args.m}")
 
 
+def cmd_step(args, torch):
+    """The benchmark's NF4 decode step (q/k/v and gate/up as one launch each, o
+    and down alone, programmatic dependents, the package's workspace) run
+    `steps` times eagerly: the command whose launch list is profiled."""
+    from . import gemv_multi, gemv_ws
+    dev = torch.device("cuda", torch.cuda.current_device())
+    shapes = [SHAPES[n] for n in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")]
+    mats = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    for out_f, in_f in shapes:
+        W = torch.randn((out_f, in_f), generator=g, device=dev) * 0.02
+        qw, sc, _ = quantise_nf4_device(W)
+        mats.append((qw, sc))
+        del W
+    xa = torch.randn((1, 3584), generator=g, device=dev).half()
+    xo = torch.randn((1, 3584), generator=g, device=dev).half()
+    xm = torch.randn((1, 3584), generator=g, device=dev).half()
+    xd = torch.randn((1, 18944), generator=g, device=dev).half()
+    for _ in range(args.steps):
+        gemv_multi(FMT_NF4_B64, mats[0:3], xa, pdl=True)
+        gemv_ws(FMT_NF4_B64, *mats[3], xo, pdl=True)
+        gemv_multi(FMT_NF4_B64, mats[4:6], xm, pdl=True)
+        gemv_ws(FMT_NF4_B64, *mats[6], xd, pdl=True)
+    torch.cuda.synchronize()
+    print(f"ran {args.steps} NF4 decode steps (4 launches each)")
+
+
+def cmd_glue(args, torch):
+    """The decode layer's elementwise kernels (b4_swiglu_f16, b4_cast_f16) on
+    `n` elements, `launches` times each."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = load()
+    g = torch.randn((args.n,), device=dev)
+    u = torch.randn((args.n,), device=dev)
+    out = torch.empty((args.n,), dtype=torch.float16, device=dev)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    for _ in range(args.launches):
+        check("b4_swiglu_f16", lib.b4_swiglu_f16(P(g), P(u), P(out), args.n, st))
+        check("b4_cast_f16", lib.b4_cast_f16(P(g), P(out), args.n, st))
+    torch.cuda.synchronize()
+    print(f"ran {args.launches} x (swiglu, cast) on {args.n} elements")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m b4gemv.diag")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -284,10 +333,15 @@ def main(argv=None):
     r.add_argument("--launches", type=int, default=4)
     r.add_argument("--copies", type=int, default=4)
     r.add_argument("--config", default="")
+    t = sub.add_parser("step")
+    t.add_argument("--steps", type=int, default=10)
+    gl = sub.add_parser("glue")
+    gl.add_argument("--n", type=int, default=28672)
+    gl.add_argument("--launches", type=int, default=3)
     args = ap.parse_args(argv)
     import torch
     torch.cuda.init()
-    {"sweep": cmd_sweep, "aspect": cmd_aspect, "run": cmd_run}[args.cmd](args, torch)
+    {"sweep": cmd_sweep, "aspect": cmd_aspect, "run": cmd_run, "step": cmd_step, "glue": cmd_glue}[args.cmd](args, torch)
 
 
 if __name__ == "__main__":

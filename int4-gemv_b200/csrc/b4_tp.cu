@@ -58,9 +58,14 @@ int nccl_status(ncclResult_t r) { return r == ncclSuccess ? 0 : B4_STATUS_NCCL_B
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// The glue kernels run as programmatic dependents (launch_glue): they let the
+// next kernel (a GEMV, whose weight stream does not depend on them) launch
+// at once, then wait for the grid that produced their input.
 __global__ void swiglu_kernel(const float* __restrict__ gate, const float* __restrict__ up,
                               __half* __restrict__ out, long long n)
 {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x)
         out[i] = __float2half_rn(silu(gate[i]) * up[i]);
@@ -68,12 +73,32 @@ __global__ void swiglu_kernel(const float* __restrict__ gate, const float* __res
 
 __global__ void cast_f16_kernel(const float* __restrict__ in, __half* __restrict__ out, long long n)
 {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x)
         out[i] = __float2half_rn(in[i]);
 }
 
 int grid_for(long long n) { long long g = (n + 255) / 256; return (int)(g > 148 * 8 ? 148 * 8 : (g < 1 ? 1 : g)); }
+
+// Launches a glue kernel as a programmatic dependent of the previous kernel
+// in the stream.  Safe after any kernel: the glue waits (griddepcontrol.wait)
+// for the preceding grid's completion and memory before it reads.
+template <typename... Args>
+cudaError_t launch_glue(void (*fn)(Args...), long long n, cudaStream_t st, Args... args)
+{
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)grid_for(n));
+    lc.blockDim = dim3(256);
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, fn, args...);
+}
 
 }  // namespace
 }  // namespace b4
@@ -182,16 +207,14 @@ int b4_tp_gemv_allreduce_ws(int fmt, const uint32_t* qw_shard, const void* scale
 int b4_swiglu_f16(const float* gate, const float* up, void* out, long long n, b4_stream_t stream)
 {
     if (!gate || !up || !out || n <= 0) return cudaErrorInvalidValue;
-    swiglu_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(gate, up,
-                                                                                    static_cast<__half*>(out), n);
-    return cudaGetLastError();
+    return launch_glue(swiglu_kernel, n, reinterpret_cast<cudaStream_t>(stream), gate, up, static_cast<__half*>(out),
+                       n);
 }
 
 int b4_cast_f16(const float* in, void* out, long long n, b4_stream_t stream)
 {
     if (!in || !out || n <= 0) return cudaErrorInvalidValue;
-    cast_f16_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(in, static_cast<__half*>(out), n);
-    return cudaGetLastError();
+    return launch_glue(cast_f16_kernel, n, reinterpret_cast<cudaStream_t>(stream), in, static_cast<__half*>(out), n);
 }
 
 const char* b4_nccl_error_string(int status)
