@@ -118,8 +118,9 @@ def default_config(fmt: int, in_f: int, out_f: int, m: int = 1) -> dict:
 
 
 def default_config_ws(fmt: int, in_f: int, out_f: int, m: int = 1) -> dict:
-    """b4_gemv_default_config_ws: the config b4_gemv_ws uses (split for few-row
-    shapes at batch 1, b4_gemv_default_config's choice otherwise)."""
+    """b4_gemv_default_config_ws: the config b4_gemv_ws uses (the x-pair table
+    kernel for NF4 at batch 1 on matrices of >= 24 MB of weights,
+    b4_gemv_default_config's choice otherwise)."""
     c = GemvConfig()
     check("b4_gemv_default_config_ws", load().b4_gemv_default_config_ws(fmt, in_f, out_f, m, ctypes.byref(c)))
     return c.as_dict()
@@ -154,8 +155,9 @@ _WS = {}
 
 def workspace_size(fmt: int, in_f: int, out_f: int, m: int = 1, config: dict | None = None, device=None) -> int:
     """b4_gemv_workspace_size on the current device (or `device`, an index):
-    bytes of workspace b4_gemv_ws needs for this shape (0 when the config does
-    not split).  Rule answers are cached per (shape, device)."""
+    bytes of workspace b4_gemv_ws needs for this shape (0 when the config needs
+    none: neither the x-pair table kernel nor a split).  Rule answers are
+    cached per (shape, device)."""
     import torch
     if config is None:
         key = (fmt, in_f, out_f, m, torch.cuda.current_device() if device is None else device)
@@ -212,11 +214,11 @@ def gemv_ws(fmt: int, qw, scale, x, y=None, config: dict | None = None, ws=None,
     return y
 
 
-def gemv_int4(qw, scales, x, y=None, stream=None, split: bool = True, pdl: bool = False):
+def gemv_int4(qw, scales, x, y=None, stream=None, use_ws: bool = True, pdl: bool = False):
     """The INT4 g128 GEMV with the dispatch rule's config: b4_gemv_ws with the
-    package's workspace (split: True; pdl: as a programmatic dependent of the
-    previous kernel), or b4_gemv_int4_g128 (split: False)."""
-    if split:
+    package's workspace (use_ws: True; pdl: as a programmatic dependent of the
+    previous kernel), or b4_gemv_int4_g128 (use_ws: False)."""
+    if use_ws:
         return gemv_ws(FMT_INT4_G128, qw, scales, x, y, stream=stream, pdl=pdl)
     out_f, in_f, m, x2, y = _gemv_args(qw, scales, x, y)
     check("b4_gemv_int4_g128", load().b4_gemv_int4_g128(_ptr(qw), _ptr(scales), _ptr(x2), _ptr(y), in_f,
@@ -224,11 +226,12 @@ def gemv_int4(qw, scales, x, y=None, stream=None, split: bool = True, pdl: bool 
     return y
 
 
-def gemv_nf4(qw, absmax, x, y=None, stream=None, split: bool = True, pdl: bool = False):
+def gemv_nf4(qw, absmax, x, y=None, stream=None, use_ws: bool = True, pdl: bool = False):
     """The NF4 b64 GEMV with the dispatch rule's config: b4_gemv_ws with the
-    package's workspace (split: True; pdl: as a programmatic dependent of the
-    previous kernel), or b4_gemv_nf4_b64 (split: False)."""
-    if split:
+    package's workspace (use_ws: True, the x-pair table kernel where the rule
+    picks it; pdl: as a programmatic dependent of the previous kernel), or
+    b4_gemv_nf4_b64 (use_ws: False)."""
+    if use_ws:
         return gemv_ws(FMT_NF4_B64, qw, absmax, x, y, stream=stream, pdl=pdl)
     out_f, in_f, m, x2, y = _gemv_args(qw, absmax, x, y)
     check("b4_gemv_nf4_b64", load().b4_gemv_nf4_b64(_ptr(qw), _ptr(absmax), _ptr(x2), _ptr(y), in_f,

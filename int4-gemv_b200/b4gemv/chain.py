@@ -6,9 +6,10 @@ overhead the isolated-launch numbers hide; with programmatic dependent launch
 each GEMV streams its first weights while the previous one finishes, and with
 `fused` the q/k/v and gate/up projections of a layer run as one launch each
 (b4_gemv_multi), 112 launches per token instead of 196.  The other GEMVs go
-through b4_gemv_ws with the chain's workspace, so the few-row o/down
-projections run split (B4_FLAG_SPLIT); the GEMVs run one after another on one
-stream, so they share it.
+through b4_gemv_ws with the chain's workspace and the config of its rule
+(b4_gemv_default_config_ws: for INT4 the plain tile rule, which never splits;
+a split config passed in is kept); the GEMVs run one after another on one
+stream, so they share the workspace.
 """
 from __future__ import annotations
 

@@ -51,7 +51,7 @@ def test_explicit_split_matches_the_rule_and_oracle(cuda, oracle, fmt, out_f, in
     y = b4gemv.gemv_ws(fmt, qw, sc, to_dev(X, cuda), config=cfg, ws=ws).cpu().numpy()
     ref = f64_ref(oracle, fmt, qw, sc, X)
     assert rel_err(y, ref) < TOL
-    y0 = (b4gemv.gemv_int4 if fmt == 0 else b4gemv.gemv_nf4)(qw, sc, to_dev(X, cuda), split=False).cpu().numpy()
+    y0 = (b4gemv.gemv_int4 if fmt == 0 else b4gemv.gemv_nf4)(qw, sc, to_dev(X, cuda), use_ws=False).cpu().numpy()
     assert rel_err(y, y0) < TOL
     # the counters (the workspace's first bytes) are zero again after the call
     assert int(ws[: ((out_f + 15) // 16) * 4].count_nonzero()) == 0
