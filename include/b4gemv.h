@@ -111,17 +111,18 @@ typedef struct b4_gemv_config {
  * `stages` (2, 3, 4).  rows_per_warp 16, vec_words 4. */
 #define B4_ENGINE_MMA_NF4 7
 /* CUDA cores, NF4, batch 1, in_f a multiple of 256, x 4-byte aligned: tables
- * of x-pair products.  A CTA (16 warps, one per SM) builds, for each column
- * pair (k, k+1) of a 256-column slice of in_f, the 256 fp32 sums
+ * of x-pair products.  A CTA (one per SM) builds, for each column pair
+ * (k, k+1) of a 256-column slice of in_f, the 256 fp32 sums
  * NF4[b & 15]*x[k] + NF4[b >> 4]*x[k+1] (one per byte value b), so one 4-byte
- * shared load and one add take a byte (two codes) of a packed row; the NF4
- * blocks' sums are scaled by their absmax, and the slices' shares of y are
- * added in y with fp32 atomics after every CTA has zeroed its rows (order of
- * the slice additions varies from run to run).  Needs a workspace
- * (b4_gemv_ws, b4_gemv_multi_ws) of B4_XTAB_WORKSPACE_BYTES: two counters,
- * zero between calls.  Codes and absmax 16-byte aligned.  row_groups = warps
- * per CTA and stages = cp.async ring stages per warp: (12, 3), (16, 3),
- * (20, 2) or (24, 2); the other fields are ignored. */
+ * shared load and one add take a byte (two codes) of a packed row; codes come
+ * straight into registers in whole 128-byte lines; the NF4 blocks' sums are
+ * scaled by their absmax, and the slices' shares of y are added in y with
+ * fp32 atomics after every CTA has zeroed its rows (order of the slice
+ * additions varies from run to run).  Needs a workspace (b4_gemv_ws,
+ * b4_gemv_multi_ws) of B4_XTAB_WORKSPACE_BYTES: two counters, zero between
+ * calls.  Codes and absmax 16-byte aligned.  row_groups = warps per CTA and
+ * stages = batches of 16 rows each warp keeps in flight: (8, 4), (12, 2),
+ * (12, 3), (16, 2), (20, 1) or (24, 1); the other fields are ignored. */
 #define B4_ENGINE_NF4_XTAB 8
 #define B4_XTAB_WORKSPACE_BYTES 256
 
@@ -169,7 +170,8 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
 /* ---- GEMV with a caller-owned workspace --------------------------------------
  * Two kernels need device scratch, which the caller owns:
  *   - at batch 1, NF4 with in_f a multiple of 256 (x 4-byte aligned, codes
- *     and absmax 16-byte aligned) and at least 24 MB of weights runs on the
+ *     and absmax 16-byte aligned) and at least 17.5 MB of weights (5 MB for
+ *     rows of 8192 columns or more) runs on the
  *     x-pair table kernel (B4_ENGINE_NF4_XTAB): its CTAs each cover a
  *     256-column slice of in_f, add their shares into y with atomics and
  *     count themselves in on two counters in `ws` first
@@ -197,8 +199,8 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
  * cudaErrorInvalidValue before anything is launched. */
 int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_config* cfg, size_t* bytes);
 /* The dispatch rule of b4_gemv_ws (cfg NULL): the x-pair table kernel for NF4
- * at batch 1 with in_f % 256 == 0 and at least 24 MB of weights,
- * b4_gemv_default_config's choice otherwise. */
+ * at batch 1 with in_f % 256 == 0 and at least 17.5 MB of weights (5 MB for
+ * in_f >= 8192), b4_gemv_default_config's choice otherwise. */
 int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_config* cfg);
 int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, float* y, int in_f, int out_f,
                int m, const b4_gemv_config* cfg, void* ws, size_t ws_bytes, b4_stream_t stream);
@@ -256,8 +258,8 @@ int b4_gemv_multi_default_config(int fmt, const b4_gemv_segment* segs, int nseg,
                                  b4_gemv_config* cfg);
 /* b4_gemv_multi with a caller-owned workspace (conventions of b4_gemv_ws): the
  * same one-launch fusion, and at batch 1 for NF4 with in_f % 256 == 0 and at
- * least 24 MB of weights over all segments the x-pair table kernel (ws of
- * B4_XTAB_WORKSPACE_BYTES).  cfg
+ * least 17.5 MB of weights over all segments (5 MB for in_f >= 8192) the
+ * x-pair table kernel (ws of B4_XTAB_WORKSPACE_BYTES).  cfg
  * NULL or B4_ENGINE_AUTO = that rule (only cfg->flags' B4_FLAG_PDL is read). */
 int b4_gemv_multi_default_config_ws(int fmt, const b4_gemv_segment* segs, int nseg, int in_f, int m,
                                     b4_gemv_config* cfg);

@@ -118,9 +118,9 @@ def default_config(fmt: int, in_f: int, out_f: int, m: int = 1) -> dict:
 
 
 def default_config_ws(fmt: int, in_f: int, out_f: int, m: int = 1) -> dict:
-    """b4_gemv_default_config_ws: the config b4_gemv_ws uses (the x-pair table
-    kernel for NF4 at batch 1 on matrices of >= 24 MB of weights,
-    b4_gemv_default_config's choice otherwise)."""
+    """b4_gemv_default_config_ws: the config b4_gemv_ws uses: the x-pair table
+    kernel for NF4 at batch 1 on matrices of >= 17.5 MB of weights (5 MB for
+    in_f >= 8192), b4_gemv_default_config's choice otherwise."""
     c = GemvConfig()
     check("b4_gemv_default_config_ws", load().b4_gemv_default_config_ws(fmt, in_f, out_f, m, ctypes.byref(c)))
     return c.as_dict()

@@ -111,7 +111,7 @@ def time_chained(torch, prob, cfg, reps=None):
 
 TMA_VARIANTS = [(4, 4), (3, 4), (6, 4), (4, 2), (4, 8), (8, 2)]   # (stages, stage_groups) instantiated
 LEAN_VARIANTS = [(4, 1), (6, 1), (8, 1), (3, 2), (4, 2), (6, 2), (2, 4), (3, 4)]   # engine 5 (stages, stage_groups)
-XTAB_VARIANTS = [(12, 3), (16, 3), (20, 2), (24, 2)]   # engine 8 (warps per CTA, ring stages)
+XTAB_VARIANTS = [(8, 4), (12, 2), (12, 3), (16, 2), (20, 1), (24, 1)]   # engine 8 (warps per CTA, batches in flight)
 NF4_LEAN_VARIANTS = [(4, 4, 2, 0), (4, 8, 2, 0), (6, 4, 2, 0), (4, 4, 4, 0), (4, 4, 2, 2), (4, 8, 2, 2),
                      (6, 4, 2, 2), (8, 4, 2, 2), (4, 4, 4, 2)]   # (stages, rw, vw, lut) instantiated
 
@@ -155,7 +155,7 @@ def config_grid(fmt, m=1):
             if kw * rg <= 8 and (nt == 8 or m > 8):
                 yield dict(vec_words=4, rows_per_warp=rw, warps_k=kw, row_groups=rg, batch_tile=nt, nf4_lut=0,
                            x_tile=0, flags=0, engine=1)
-    if fmt == FMT_NF4_B64 and m == 1:   # x-pair table kernel: (warps per CTA, ring stages)
+    if fmt == FMT_NF4_B64 and m == 1:   # x-pair table kernel: (warps per CTA, batches in flight per warp)
         for nw, st in XTAB_VARIANTS:
             yield dict(vec_words=1, rows_per_warp=8, warps_k=1, row_groups=nw, batch_tile=1, nf4_lut=0,
                        x_tile=0, flags=0, engine=8, stages=st, stage_groups=0)

@@ -198,6 +198,44 @@ __device__ __forceinline__ void stage_x_words(const __half* x, int n, bool vec, 
 
 constexpr int kXUnroll = 8;   // x words in flight per thread while staging
 
+// x of a small batch in shared memory, for B fragments that lane q reads as
+// logical words 4q .. 4q + 3 of a 16-word group (one 16-byte load per word):
+// each row's 16-word groups are stored transposed (word s at 4 (s & 3) + (s >> 2))
+// so that the four q lanes of a load read four consecutive 16-byte slots, and
+// rows are kXmbPad words longer than in_f / 8 (a row stride of 4 slots mod 8),
+// so the two rows of a quarter warp take the two halves of the 32 banks.
+constexpr int kXmbPad = 4;
+
+__host__ __device__ constexpr int xmb_stride(int words) { return words + kXmbPad; }
+
+__device__ __forceinline__ int xmb_slot(int w) { return (w & ~15) | ((w & 3) << 2) | ((w >> 2) & 3); }
+
+// stage_x_words over [m][words] with store(row, word, value)
+template <int XU, typename Store>
+__device__ __forceinline__ void stage_x_rows(const __half* x, int m, int words, bool vec, Store store)
+{
+    const int n = m * words;
+    const float inv = 1.0f / (float)words;
+    for (int i0 = threadIdx.x; i0 < n; i0 += XU * blockDim.x) {
+        uint4 r[XU];
+#pragma unroll
+        for (int u = 0; u < XU; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            r[u] = i < n ? ld_x_word(x + (long long)i * 8, vec) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < XU; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            if (i < n) {
+                int row = __float2int_rz(__int2float_rn(i) * inv);   // i / words, corrected below
+                if (row * words > i) --row;
+                else if ((row + 1) * words <= i) ++row;
+                store(row, i - row * words, r[u]);
+            }
+        }
+    }
+}
+
 // ---- NF4 decode ---------------------------------------------------------------
 // Warp-register code book: lane L holds NF4[L & 15]; a shuffle with the packed
 // word shifted right by 4k as the source lane reads NF4[nibble k], since the

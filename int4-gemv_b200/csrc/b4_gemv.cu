@@ -115,7 +115,8 @@ size_t lean_int4_smem(int in_f, int kw, int rg, int stages, int groups)
 size_t lean_int4_mb_smem(int in_f, int m, int kw, int rg, int stages, int groups)
 {
     const int nc = m > 8 ? 16 : 8;
-    return (size_t)m * in_f * 2 + (size_t)rg * kw * 16 * nc * 4 + (size_t)kw * rg * stages * groups * 64 * 16;
+    return (size_t)m * xmb_stride(in_f / 8) * 16 + (size_t)rg * kw * 16 * nc * 4 +
+           (size_t)kw * rg * stages * groups * 64 * 16;
 }
 
 // Shared memory of the NF4 tensor-pipe kernel: [pair table][x][reduction].
@@ -128,7 +129,7 @@ size_t nf4_mma_smem(int in_f, int kw, int rg)
 size_t nf4_mma_mb_smem(int in_f, int m, int kw, int rg)
 {
     const int nr = (m + 3) / 4 > 2 ? 16 : ((m + 3) / 4) * 4;
-    return (size_t)kNf4PairTableBytes + (size_t)m * in_f * 2 + (size_t)rg * kw * 16 * nr * 4;
+    return (size_t)kNf4PairTableBytes + (size_t)m * xmb_stride(in_f / 8) * 16 + (size_t)rg * kw * 16 * nr * 4;
 }
 
 // Rows per 16-row MMA block for the tensor-pipe batch-1 engines: when a
@@ -1004,7 +1005,7 @@ int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int i
     if (nseg < 1 || nseg > kXtabMaxSeg || !xtab_shape(kNf4, in_f, 1, x) || !xtab_buffers(segs, nseg))
         return cudaErrorInvalidValue;
     if (!ws || !aligned(ws, 16) || ws_bytes < B4_XTAB_WORKSPACE_BYTES) return cudaErrorInvalidValue;
-    const int nw = c.row_groups;   // warps per CTA
+    const int nw = c.row_groups;   // warps per CTA; c.stages = batches each warp keeps in flight
     void* fn = gemv_kernel_xtab(nw, c.stages);
     if (!fn) return cudaErrorInvalidValue;
     XtabParams xp = {};
@@ -1030,7 +1031,7 @@ int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int i
     int reserved = 0;   // dynamic shared memory starts after the reserved part of the window
     e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
     if (e != cudaSuccess) return e;
-    const size_t smem = xtab_smem_bytes(nw, c.stages, (uint32_t)reserved);
+    const size_t smem = xtab_smem_bytes((uint32_t)reserved);
     int smem_max = 0;
     e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
@@ -1066,29 +1067,35 @@ int launch_gemv_xtab(const GemvProblem& p, const b4_gemv_config& c, void* ws, si
     return launch_xtab_segs(&s, 1, p.x, p.in_f, c, ws, ws_bytes, st);
 }
 
-// The x-pair table kernel pays ~4.4 us per launch before it streams (the
-// tables, the zeroing of y, the previous launch's drain: it holds one CTA per
-// SM) and then streams at ~4.2 TB/s; the tensor-pipe and CUDA-core NF4
-// kernels start in ~3 us and stream at ~3.5 TB/s or less (B200, PDL chains,
-// every Qwen2.5-7B, Llama-3-70B and tensor-parallel shard shape and the fused
-// q/k/v and gate/up launches).  It is taken from 24 MB of weights up
-// (Qwen gate/up 13.9 us against 13.8, fused gate+up 23.1 against 25.1, down
-// 14.4 against 22.3, Llama-3-70B gate/up 37.2 against 53.7, down 43.8 against
-// 60.5); 24 warps with 2 ring stages from 48 MB or for rows longer than 8192
-// columns, else 16 warps with 3.
-bool xtab_pays(long long weight_bytes) { return weight_bytes >= 24LL * 1000 * 1000; }
+// The x-pair table kernel pays ~4 us per launch before it streams (the tables,
+// the zeroing of y, the previous launch's drain: it holds one CTA per SM) and
+// then streams faster than the tensor-pipe and CUDA-core NF4 kernels, which
+// start in ~3 us (B200, PDL chains over every Qwen2.5-7B, Llama-3-70B and
+// tensor-parallel shard shape and the fused q/k/v and gate/up launches).  It
+// is taken from 17.5 MB of weights up, and from 5 MB where rows are 8192
+// columns or longer (the other kernels are slowest there): Qwen gate/up 12.4
+// us against 13.8, fused gate+up 19.1 against 25.0, down 11.6 against 22.3,
+// Llama-3-70B q/o 12.9 against 17.0, tp4 q 6.6 against 8.8, tp8 gate/up 8.6
+// against 9.3, tp8 q/k/v (5.9 MB) 6.0 against 6.9; below, e.g. Qwen q/o (7.2
+// MB) 5.9 against 5.0.  16 warps with two batches in flight each from 9 MB,
+// 12 warps with three below.
+bool xtab_pays(long long weight_bytes, int in_f)
+{
+    return weight_bytes >= 17500LL * 1000 || (in_f >= 8192 && weight_bytes >= 5000LL * 1000);
+}
 
 void xtab_config(b4_gemv_config* cfg, long long weight_bytes, int in_f)
 {
+    (void)in_f;
     *cfg = b4_gemv_config{};
     cfg->engine = B4_ENGINE_NF4_XTAB;
-    cfg->vec_words = 1;
+    cfg->vec_words = 4;
     cfg->rows_per_warp = kXtabBatch;
     cfg->warps_k = 1;
-    const bool big = weight_bytes >= 48LL * 1000 * 1000 || in_f > 8192;
-    cfg->row_groups = big ? 24 : 16;   // warps per CTA
+    const bool big = weight_bytes >= 9LL * 1000 * 1000;
+    cfg->row_groups = big ? 16 : 12;   // warps per CTA
     cfg->batch_tile = 1;
-    cfg->stages = big ? 2 : 3;         // ring stages per warp
+    cfg->stages = big ? 2 : 3;         // batches in flight per warp
 }
 
 long long nf4_weight_bytes(long long rows, int in_f)
@@ -1235,7 +1242,7 @@ void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
     // when passed explicitly.
     const b4_gemv_segment seg{p.qw, p.scale, p.y, p.out_f};
     const long long wb = nf4_weight_bytes(p.out_f, p.in_f);
-    if (xtab_shape(p.fmt, p.in_f, p.m, p.x) && xtab_buffers(&seg, 1) && xtab_pays(wb)) {
+    if (xtab_shape(p.fmt, p.in_f, p.m, p.x) && xtab_buffers(&seg, 1) && xtab_pays(wb, p.in_f)) {
         xtab_config(cfg, wb, p.in_f);
         return;
     }
@@ -1417,7 +1424,7 @@ int b4_gemv_multi_default_config_ws(int fmt, const b4_gemv_segment* segs, int ns
     long long rows = 0;
     for (int s = 0; s < nseg; ++s) rows += segs[s].out_f;
     const long long wb = nf4_weight_bytes(rows, in_f);
-    if (xtab_shape(fmt, in_f, m, reinterpret_cast<const void*>(256)) && xtab_buffers(segs, nseg) && xtab_pays(wb))
+    if (xtab_shape(fmt, in_f, m, reinterpret_cast<const void*>(256)) && xtab_buffers(segs, nseg) && xtab_pays(wb, in_f))
         xtab_config(cfg, wb, in_f);
     else default_config_multi(fmt, segs, nseg, in_f, m, cfg);
     return cudaSuccess;
@@ -1434,7 +1441,7 @@ int b4_gemv_multi_ws(int fmt, const b4_gemv_segment* segs, int nseg, const void*
         long long rows = 0;
         for (int s = 0; s < nseg; ++s) rows += segs[s].out_f;
         const long long wb = nf4_weight_bytes(rows, in_f);
-        if (xtab_shape(fmt, in_f, m, x) && xtab_buffers(segs, nseg) && xtab_pays(wb)) xtab_config(&c, wb, in_f);
+        if (xtab_shape(fmt, in_f, m, x) && xtab_buffers(segs, nseg) && xtab_pays(wb, in_f)) xtab_config(&c, wb, in_f);
         else default_config_multi(fmt, segs, nseg, in_f, m, &c);
         c.flags = cfg ? cfg->flags & B4_FLAG_PDL : 0;
     } else {

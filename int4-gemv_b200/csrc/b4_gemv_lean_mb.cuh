@@ -12,7 +12,8 @@
 // that carry weights, warps_k warps splitting in_f by stages of G groups, a
 // per-lane cp.async ring of D stages, weights requested before
 // griddepcontrol.wait, up to four matrices sharing x in one launch.  x is
-// staged per CTA for all m rows in pair order ([row][word] 16-byte slots);
+// staged per CTA for all m rows in pair order ([row][word] 16-byte slots, the
+// bank-spread layout of xmb_slot);
 // lane (g, q) reads the B fragments of batch row nb*8 + g (clamped to m - 1:
 // columns past m are computed and dropped).  D's columns 2q, 2q+1 of rows
 // g, g+8 are batch rows 2q, 2q+1 of those weight rows, so each lane keeps four
@@ -51,8 +52,9 @@ __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_m
     const int rows_per_tile = p.rg * p.tr;
     const int n_tiles = p.n_tiles;
     constexpr int NC = 8 * NB;                               // batch columns of D
-    uint4* xs = lsm;                                         // [m][words] slots
-    float* red = reinterpret_cast<float*>(xs + (size_t)m * words);   // rg*kw*16*NC
+    const int xst = xmb_stride(words);
+    uint4* xs = lsm;                                         // [m][xst] slots, groups transposed
+    float* red = reinterpret_cast<float*>(xs + (size_t)m * xst);   // rg*kw*16*NC
     uint4* ring = reinterpret_cast<uint4*>(red + p.rg * p.kw * 16 * NC) + warp * (D * G * 64);
 
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
@@ -119,13 +121,14 @@ __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_m
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // x is [m][in_f], contiguous: word i of the whole batch is at x + 8i
-    stage_x_words<kXUnroll>(p.x, m * words, p.x_vec, [&](int i, uint4 v) { xs[i] = int4_pair_order(v); });
+    stage_x_rows<kXUnroll>(p.x, m, words, p.x_vec,
+                           [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = int4_pair_order(v); });
     __syncthreads();
 
     // the batch rows this lane feeds into B (columns g of each block)
     const uint4* xrow[NB];
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb) xrow[nb] = xs + (size_t)min(nb * 8 + g, m - 1) * words + ks * 16 * G + q * 4;
+    for (int nb = 0; nb < NB; ++nb) xrow[nb] = xs + (size_t)min(nb * 8 + g, m - 1) * xst + ks * 16 * G + q;
 
     for (; tile < n_tiles; tile += gridDim.x) {
         if (tile != (int)blockIdx.x) {
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_m
 #pragma unroll
                         for (int nb = 0; nb < NB; ++nb) {
                             const uint4* xp = xrow[nb] + xoff + 16 * h;
-                            const uint4 xv[4] = {xp[0], xp[1], xp[2], xp[3]};
+                            const uint4 xv[4] = {xp[0], xp[4], xp[8], xp[12]};   // logical words 4q .. 4q + 3
                             float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {

@@ -19,7 +19,8 @@
 // D: lane (g, q) holds columns 2q, 2q+1 = NF4 block q >> 1 of batch rows
 // 4*nb + 2(q & 1) and +1, for weight rows g and g+8; it scales them by that
 // block's absmax, and lanes q and q ^ 2 (the two blocks) are added with one
-// shuffle at the end.  x is staged per CTA for all m rows in natural order.
+// shuffle at the end.  x is staged per CTA for all m rows in natural order
+// within the bank-spread layout of xmb_slot.
 #pragma once
 
 #include "b4_gemv_nf4_mma.cuh"
@@ -38,7 +39,7 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     const int m = pm.m;
     extern __shared__ __align__(16) uint4 lsm[];
     unsigned char* base = reinterpret_cast<unsigned char*>(lsm);
-    uint4* xs = reinterpret_cast<uint4*>(base + kNf4PairTableBytes);        // [m][in_f / 8] slots
+    uint4* xs = reinterpret_cast<uint4*>(base + kNf4PairTableBytes);        // [m][xmb_stride] slots
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
     const int warp = threadIdx.x >> 5;
@@ -48,7 +49,8 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     const int nblk = p.in_f >> 6;
     const int nst = p.in_f >> 7;
     constexpr int NR = 4 * NB;                                             // batch rows per pass
-    float* red = reinterpret_cast<float*>(xs + (size_t)m * words);        // rg*kw*16*NR
+    const int xst = xmb_stride(words);
+    float* red = reinterpret_cast<float*>(xs + (size_t)m * xst);          // rg*kw*16*NR
     const int rows_per_tile = p.rg * p.tr;
     const int n_tiles = p.n_tiles;
     const int n_it = nst > ks ? (nst - ks + p.kw - 1) / p.kw : 0;
@@ -119,7 +121,7 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // x is [m][in_f], contiguous: word i of the whole batch is at x + 8i
-    stage_x_words<kXUnroll>(p.x, m * words, p.x_vec, [&](int i, uint4 v) { xs[i] = v; });
+    stage_x_rows<kXUnroll>(p.x, m, words, p.x_vec, [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = v; });
     __syncthreads();
 
     // B: this lane carries batch row 4*nb + (g & 3) when (g >> 2) == (q >> 1)
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     for (int nb = 0; nb < NB; ++nb) {
         const int b = 4 * nb + (g & 3);
         x_on[nb] = x_lane && b < m;
-        xrow[nb] = xs + (size_t)min(b, m - 1) * words + ks * 16 + q * 4;
+        xrow[nb] = xs + (size_t)min(b, m - 1) * xst + ks * 16 + q;
     }
     const unsigned char* tb = base;
     const bool hi_blk = q >= 2;   // the NF4 block of this lane's D columns
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
                         if (x_on[nb]) {
                             const uint4* xp = xrow[nb] + xoff;
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) xv[i] = xp[i];
+                            for (int i = 0; i < 4; ++i) xv[i] = xp[4 * i];   // logical words 4q + i
                         }
                         float c[4][4];
 #pragma unroll

@@ -2,8 +2,8 @@
 //
 // The code book is what bounds the other NF4 kernels: every code costs a
 // shared-memory read of its value (4 bytes per code on the tensor-pipe kernel,
-// fp16 high + low part), and the shared-memory data path (128 B/clk/SM) runs
-// out before HBM does.  This kernel moves x into the table instead:
+// fp16 high + low part), and the shared-memory path runs out before HBM does.
+// This kernel moves x into the table instead:
 //
 //   for a column pair (k, k+1) and a byte b of a packed word (codes c0 = b & 15
 //   of column k, c1 = b >> 4 of column k+1):
@@ -19,37 +19,48 @@
 //
 // Geometry.  A table costs 1 KB per column pair, so a CTA (one per SM, its
 // 128 KB of tables filling most of the SM's shared memory) covers a
-// 256-column SLICE of in_f: 32 packed words, each word four column pairs
-// (byte positions j = 0..3).  The table of pair (word w, byte j) is column w
-// of the layout
-//       float [j >> 1][b][j & 1][w]        (b = the byte value)
-// so lookups of 32 different words hit the 32 banks once, whatever the bytes.
+// 256-column SLICE of in_f: 32 packed words of 4 byte positions each.  The
+// matrix is cut into (slice, 16-row batch) units.  With S = in_f/256 slices
+// and G CTAs, slice s gets G/S or G/S + 1 CTAs that split its batches evenly
+// (S > G: each CTA takes slices c, c + G, ... with every batch).  A warp takes
+// the batches b0 + warp, b0 + warp + NW, ... of its CTA's range.
 //
-// Work.  The matrix is cut into (slice, 16-row batch) units.  With S =
-// in_f/256 slices and G CTAs, slice s gets G/S or G/S + 1 CTAs that split its
-// batches evenly (S > G: each CTA takes slices c, c + G, ... with every
-// batch).  A warp takes the batches b0 + warp, b0 + warp + NW, ... of its CTA's
-// range; each batch's codes (16 rows x 128 bytes) come through the warp's
-// cp.async ring in shared memory, R stages deep.  Lane L works on rows L & 7
-// and (L & 7) + 8 of a batch, in NF4 block L >> 3 of the slice (words
-// 8 (L >> 3) .. + 7): at step k (0..7) it takes word 8 (L >> 3) + (k ^ (L & 7))
-// of both rows -- its block's 8 words in an order permuted by the lane, so the
-// 32 lanes of a step hold 32 different words and their lookups hit 32
-// different table columns -- and adds the 4 + 4 looked-up pair sums to the
-// two rows' block sums.  Each block sum is scaled by its absmax; two shuffles
-// add the slice's four blocks; lanes 0..15 then add the slice's share of the
-// batch's 16 rows into y.
+// Codes go straight from global memory into registers, P batches ahead, in
+// whole 128-byte lines (the lookups are then the only shared-memory traffic
+// of the steady state; staging the codes through shared memory cost 16 writes
+// and 16 reads per batch next to the 64 lookups, and ran 10-15 % slower):
+// lane L loads the 16-byte piece pc = L & 7 (words 4 pc .. 4 pc + 3 of the
+// slice) of rows rq + 4t of a batch (rq = L >> 3, t = 0..3) and does that
+// piece's lookups.  Registers cannot be indexed by a lane-dependent order, so
+// at step (t, k) a lane uses word 4 pc + k of row rq + 4t, and the bank spread
+// over the 32 lanes of a lookup comes from the table layout and a per-lane
+// rotation: each code word is rotated right by 8 rq bits once, so byte
+// position j of a lane is the word's byte jj = (j + rq) & 3.  The table of
+// column pair (word w, byte jj) sits at
+//     T*65536 + (w>>1 & 1)*65536 + b*256 + (w & 1)*128 + (w >> 2)*16 + jj*4
+// (T = the tables' 64 KB-aligned base >> 16), so the bank (address bits 2..6)
+// is (w >> 2 = pc, jj): different for the 32 lanes of every lookup, whatever
+// the bytes.  The other bits depend only on k: a lane keeps per byte position
+// j a register with the two possible low address bytes (k even, odd) and T,
+// T + 1, and one PRMT with a constant selector forms a lookup's complete
+// shared address from the code byte: one PRMT + one LDS + one FADD per two
+// codes.
+//
+// A lane's four row sums (its piece of rows rq + 4t) are scaled by the
+// absmax of its NF4 block (pc >> 1) and reduced over the 8 pieces of a row
+// with four shuffles (a reduce-scatter), after which lanes with pc even hold
+// row rq + 4 ((pc >> 1) & 3) and add it into y.
 //
 // The slices' shares meet in y through fp32 atomic adds (reductions in L2,
 // fire and forget: no cross-CTA wait at the end of the kernel).  y must be zero
 // first: each CTA zeroes its share of y's rows right after the grid-dependency
-// wait and counts itself in on a workspace counter (a release reduction); a
-// warp keeps the results of its first kXtabHold batches in registers and
-// waits (bounded) for all G arrivals before its first add, which by then has
-// normally happened, so the count-in is off the critical path.  The last CTA to leave resets the two counters,
-// so the workspace is zero between calls.  Summation order across slices
-// therefore varies from run to run (within fp32 rounding); everything else is
-// fixed.
+// wait and, once its first tables are built, counts itself in on a workspace
+// counter (a release reduction); a warp keeps the results of its first
+// kXtabHold batches in registers and waits (bounded) for all G arrivals before
+// its first add, which by then has normally happened, so the count-in is off
+// the critical path.  The last CTA to leave resets the two counters, so the
+// workspace is zero between calls.  Summation order across slices therefore
+// varies from run to run (within fp32 rounding); everything else is fixed.
 //
 // Waits: the arrival wait is the only one.  It is bounded (kXtabMaxPolls polls
 // with a short sleep); when it runs out the kernel raises its device error
@@ -147,12 +158,16 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b)
     return r;
 }
 
-template <int OFF>
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr)
+// The four lookups of a (rotated) code word at step k of its row: the sum of
+// the word's four column-pair entries.  Selector bytes: the low address byte
+// (lw byte 0 or 1 by k bit 0), code byte j, T or T + 1 (k bit 1), zero (the
+// sign of T).
+template <int K>
+__device__ __forceinline__ float xtab_word(uint32_t w, const uint32_t (&lw)[4])
 {
-    uint32_t v;
-    asm("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(OFF));
-    return v;
+    constexpr uint32_t S = 0xE000u | ((6u + ((K >> 1) & 1)) << 8) | (4u + (K & 1));
+    return (lds_f32(prmt<S>(w, lw[0])) + lds_f32(prmt<S | 0x10u>(w, lw[1]))) +
+           (lds_f32(prmt<S | 0x20u>(w, lw[2])) + lds_f32(prmt<S | 0x30u>(w, lw[3])));
 }
 
 // f(integral_constant<int, D>) for D = D0 .. N - 1, each with a compile-time D
@@ -213,91 +228,65 @@ __device__ __forceinline__ int xtab_seg_of(const XtabParams& p, int b, int& r0)
     return sg;
 }
 
-// The shared-memory ring of one warp: R stages of a batch's codes (16 rows x
-// 128 bytes).  absmax goes straight into registers.
-constexpr int kXtabStageBytes = kXtabBatch * 128;
-constexpr int kErrXtabLayout = 4;
-
-// Shared-memory layout.  The two 64 KB halves of the tables (byte positions
-// j = 0, 1 and j = 2, 3) start on 64 KB boundaries of the CTA's shared window,
-// so one PRMT that drops a code byte into bits 8..15 of a lane register
-// holding  half base + 128 * (j & 1) + 4 * w  yields the entry's complete
-// shared address.  `base` is the window address where dynamic shared memory
-// starts (after the reserved part); the warps' rings fill the space below
-// the first boundary as far as whole rings fit, the rest go after the tables.
+// The tables' two 64 KB halves start on a 64 KB boundary of the CTA's shared
+// window (`base` = where dynamic shared memory starts, after the reserved part),
+// so a PRMT can place T and T + 1 in the address's third byte.
 __host__ __device__ constexpr uint32_t xtab_align64k(uint32_t base) { return (base + 65535u) & ~65535u; }
 
-__host__ __device__ constexpr uint32_t xtab_ring_bytes(int r) { return (uint32_t)(r * kXtabStageBytes); }
+constexpr int kErrXtabLayout = 4;
 
-// warps whose rings fit below the tables
-__host__ __device__ constexpr int xtab_low_warps(int nw, int r, uint32_t base)
+__host__ __device__ constexpr uint32_t xtab_smem_bytes(uint32_t base)
 {
-    return (int)((xtab_align64k(base) - base) / xtab_ring_bytes(r)) < nw
-               ? (int)((xtab_align64k(base) - base) / xtab_ring_bytes(r))
-               : nw;
+    return (xtab_align64k(base) - base) + (uint32_t)kXtabTableBytes;
 }
 
-__host__ __device__ constexpr uint32_t xtab_smem_bytes(int nw, int r, uint32_t base)
+__device__ __forceinline__ void ldg_v4_na(uint32_t& d0, uint32_t& d1, uint32_t& d2, uint32_t& d3, const void* p)
 {
-    return (xtab_align64k(base) - base) + (uint32_t)kXtabTableBytes +
-           (uint32_t)(nw - xtab_low_warps(nw, r, base)) * xtab_ring_bytes(r);
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+                 : "l"(p));
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src)
-{
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-
-template <int NW, int R>
+template <int NW, int P>
 __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabParams p)
 {
-    static_assert(R >= 2, "ring stages: at least 2");
+    static_assert(P >= 1, "register stages: at least 1");
     extern __shared__ __align__(16) float xtab[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int G = gridDim.x, c = blockIdx.x;
     const int nblk = p.in_f >> 6;
-    const long long rowb = p.in_f >> 1;          // bytes of codes per row
-    const int lr = lane & 7, lq = lane >> 3;     // this lane's rows (lr, lr + 8) and NF4 block of the slice
+    const long long rowb = p.in_f >> 1;
+    const int rq = lane >> 3, pc = lane & 7;
+    const int myrow = rq + 4 * ((pc >> 1) & 3);   // the row this lane adds into y (pc even)
+    const bool adder = (pc & 1) == 0;
 
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(xtab));
     const uint32_t tab = xtab_align64k(base);
-    if (xtab_smem_bytes(NW, R, base) > p.smem) {   // the launch did not size this layout: leave untouched
+    if (xtab_smem_bytes(base) > p.smem) {
         if (threadIdx.x == 0) atomicOr(&g_xtab_error, kErrXtabLayout);
         return;
     }
-    // table build: lane L writes its own column (word L) of the four pairs' tables
-    const uint32_t lk0 = tab + (uint32_t)lane * 4, lk1 = lk0 + 128, lk2 = lk0 + 65536, lk3 = lk1 + 65536;
-
-    // this warp's ring of codes; lane L copies 16-byte pieces L + 32 t (t = 0..3)
-    // of a stage: rows L / 8 + 4 t, piece L % 8
-    const int low = xtab_low_warps(NW, R, base);
-    const uint32_t ring_s = warp < low ? base + (uint32_t)warp * xtab_ring_bytes(R)
-                                       : tab + kXtabTableBytes + (uint32_t)(warp - low) * xtab_ring_bytes(R);
-    const uint32_t wr_q = ring_s + lane * 16;
-    // Step k (0..7): word w = 8 * (L >> 3) + (k ^ (L & 7)) of rows L & 7 and
-    // (L & 7) + 8.  With w0 its step-0 word, 4w = 4 w0 ^ 4k (bits 2..4), so
-    //   row address  = cr0 ^ 4k   (cr0 = the ring slot of row L & 7, word w0)
-    //   lookup base  = lw0 ^ 0x404 k
-    // where lw0 holds the bytes (4 w0, 4 w0 + 128, T, T + 1), T = the tables'
-    // base >> 16, from which one PRMT per byte position j forms the address
-    //     T*65536 + (j >> 1)*65536 + b*256 + (j & 1)*128 + 4w
-    // (byte 3 is a sign-replicated copy of T: zero).
     const uint32_t T = tab >> 16;
-    const uint32_t w0 = 8u * lq + (uint32_t)lr;
-    const uint32_t cr0 = ring_s + lr * 128 + 4 * w0;
-    const uint32_t lw0 = ((T + 1) << 24) | (T << 16) | ((4 * w0 + 128) << 8) | (4 * w0);
+    uint32_t lwr[4];   // per byte position j: (low byte for k even, for k odd, T, T + 1)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t jj = ((uint32_t)(j + rq)) & 3u;
+        const uint32_t lo0 = ((uint32_t)pc << 4) | (jj << 2);
+        lwr[j] = ((T + 1) << 24) | (T << 16) | ((lo0 | 128u) << 8) | lo0;
+    }
+    // table build: lane L writes word bits 2..4 = L >> 2, byte position L & 3,
+    // the four words t = 0..3 of that group (w bit 0 -> +128, w bit 1 -> +64 KB)
+    const uint32_t bl = tab + 4u * (uint32_t)lane;
+    const int xcol = 32 * (lane >> 2) + 2 * (lane & 3);   // column of word t = 0's pair in the slice
 
     int s = 0, b0 = 0, b1 = 0;
-    // segment cursor (a warp's batches only increase) and the next batch's copy
-    // sources: this lane's first code piece and its absmax (row L & 7, block L >> 3)
     int sg = -1, sg_first = 0, sg_end = 0, out_f = 0;
     float* yseg = nullptr;
-    const unsigned char* qsrc = nullptr;
-    const float* asrc = nullptr;
+    const unsigned char* qsrc = nullptr;   // row rq of the next batch, this lane's piece
+    const float* asrc = nullptr;           // absmax of row rq, this lane's block
     int bnext = 0;
-    const long long astep8 = 8LL * nblk;   // absmax floats between rows r and r + 8
-    auto seek = [&](int b) {   // point the copy sources at batch b
+    auto seek = [&](int b) {
         while (b >= sg_end) {
             sg_first = sg_end;
             ++sg;
@@ -307,49 +296,80 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
         out_f = g.out_f;
         yseg = g.y;
         const int r0 = (b - sg_first) * kXtabBatch;
-        qsrc = reinterpret_cast<const unsigned char*>(g.qw) + s * 128 + (r0 + (lane >> 3)) * rowb + (lane & 7) * 16;
-        asrc = g.absmax + (long long)(r0 + lr) * nblk + 4 * s + lq;
+        qsrc = reinterpret_cast<const unsigned char*>(g.qw) + s * 128 + (long long)(r0 + rq) * rowb + pc * 16;
+        asrc = g.absmax + (long long)(r0 + rq) * nblk + 4 * s + (pc >> 1);
         bnext = b;
     };
-    float* yb[R];
-    int nvb[R];
-    float aba[R], abb[R];
-    // the next batch of this warp (bnext) into ring slot `slot`; rows past
-    // out_f copy the segment's last row
-    auto issue = [&](int slot) {
+    uint32_t cw[P][16];   // words 4 pc .. 4 pc + 3 of rows rq, rq + 4, rq + 8, rq + 12
+    float ab[P][4];
+    float* yb[P];
+    int nvb[P];
+    const uint32_t q4 = (uint32_t)(4 * rowb);   // bytes between a lane's rows rq + 4t and rq + 4t + 4
+    const uint32_t q8 = 2 * q4, q12 = 3 * q4;
+    const int a4 = 4 * nblk;                    // absmax floats between them
+    auto issue = [&](auto dc) {
+        constexpr int D = decltype(dc)::value;
         if (bnext >= sg_end) seek(bnext);
         const int r0 = (bnext - sg_first) * kXtabBatch;
         const int nv = min(kXtabBatch, out_f - r0);
-        const uint32_t st = (uint32_t)(slot * kXtabStageBytes);
         if (nv == kXtabBatch) {
+            ldg_v4_na(cw[D][0], cw[D][1], cw[D][2], cw[D][3], qsrc);
+            ldg_v4_na(cw[D][4], cw[D][5], cw[D][6], cw[D][7], qsrc + q4);
+            ldg_v4_na(cw[D][8], cw[D][9], cw[D][10], cw[D][11], qsrc + q8);
+            ldg_v4_na(cw[D][12], cw[D][13], cw[D][14], cw[D][15], qsrc + q12);
+            ab[D][0] = __ldg(asrc);
+            ab[D][1] = __ldg(asrc + a4);
+            ab[D][2] = __ldg(asrc + 2 * a4);
+            ab[D][3] = __ldg(asrc + 3 * a4);
+        } else {   // rows past out_f read the segment's last row
 #pragma unroll
-            for (int t = 0; t < 4; ++t) cp_async16(wr_q + st + 512 * t, qsrc + 4 * t * rowb);
-            aba[slot] = __ldg(asrc);
-            abb[slot] = __ldg(asrc + astep8);
-        } else {
-            const unsigned char* q = qsrc - (lane >> 3) * rowb;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) cp_async16(wr_q + st + 512 * t, q + min((lane >> 3) + 4 * t, nv - 1) * rowb);
-            aba[slot] = __ldg(asrc + (long long)(min(lr, nv - 1) - lr) * nblk);
-            abb[slot] = __ldg(asrc + (long long)(min(lr + 8, nv - 1) - lr) * nblk);
+            for (int t = 0; t < 4; ++t) {
+                const int dr = min(rq + 4 * t, nv - 1) - rq;
+                ldg_v4_na(cw[D][4 * t], cw[D][4 * t + 1], cw[D][4 * t + 2], cw[D][4 * t + 3], qsrc + dr * rowb);
+                ab[D][t] = __ldg(asrc + (long long)dr * nblk);
+            }
         }
-        yb[slot] = yseg + r0;
-        nvb[slot] = nv;
+        yb[D] = yseg + r0;
+        nvb[D] = nv;
         bnext += NW;
         qsrc += NW * kXtabBatch * rowb;
         asrc += (long long)NW * kXtabBatch * nblk;
     };
-    auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
-    // This warp's adds into y wait until every CTA has counted in.  The count
-    // is not awaited before the batches: the results of a warp's first
-    // kHold batches are held in registers, and the wait comes before the
-    // first add, by when the count is normally complete.
+    const bool h4 = (pc & 4) != 0, h2 = (pc & 2) != 0;
+    // the lookups of register stage D and the lane's row sum; stage D takes the
+    // warp's next batch (if `more`) once its codes are used
+    auto compute = [&](auto dc, bool more) -> float {
+        constexpr int D = decltype(dc)::value;
+        const uint32_t sh = 8u * (uint32_t)rq;
+        float v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t* wt = cw[D] + 4 * t;
+            const float e0 = xtab_word<0>(__funnelshift_r(wt[0], wt[0], sh), lwr) +
+                             xtab_word<2>(__funnelshift_r(wt[2], wt[2], sh), lwr);
+            const float e1 = xtab_word<1>(__funnelshift_r(wt[1], wt[1], sh), lwr) +
+                             xtab_word<3>(__funnelshift_r(wt[3], wt[3], sh), lwr);
+            v[t] = (e0 + e1) * ab[D][t];
+        }
+        if (more) issue(dc);
+        // reduce-scatter over the 8 pieces of each row: xor 4 keeps rows t = 2 h4 + {0, 1},
+        // xor 2 keeps t = 2 h4 + h2, xor 1 completes it
+        const float s0 = h4 ? v[0] : v[2], s1 = h4 ? v[1] : v[3];
+        const float k0 = (h4 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, s0, 4);
+        const float k1 = (h4 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, s1, 4);
+        float r = (h2 ? k1 : k0) + __shfl_xor_sync(0xffffffffu, h2 ? k0 : k1, 2);
+        r += __shfl_xor_sync(0xffffffffu, r, 1);
+        return r;
+    };
+    auto add = [&](float* yd, int nd, float r) {
+        if (adder && myrow < nd) red_add_f32(yd + myrow, r);
+    };
+    // This warp's adds into y wait until every CTA has counted in: the results
+    // of an item's first kXtabHold batches are held in registers, and the
+    // (first item's) wait comes after them, by when the count is normally
+    // complete.
     bool counted_in = false;
-    float hold_r[kXtabHold];
-    float* hold_y[kXtabHold];
-    int hold_n[kXtabHold];
-    int held = 0;
-    auto count_in = [&]() {
+    auto wait_count = [&]() {
         if (lane == 0) {
             unsigned n = 0;
             while (ld_acquire_u32(&p.bar[0]) < (unsigned)G) {
@@ -362,87 +382,29 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
         }
         __syncwarp();
         counted_in = true;
-#pragma unroll
-        for (int i = 0; i < kXtabHold; ++i)
-            if (i < held && lane < hold_n[i]) red_add_f32(hold_y[i] + lane, hold_r[i]);
-        held = 0;
     };
-    // batch `it` of this warp from ring slot D (it + R - 1 issued first if `more`)
-    auto step = [&](auto dc, bool more) {
-        constexpr int D = decltype(dc)::value;
-        __syncwarp();   // every lane is done with the slot refilled next
-        if (more) issue((D + R - 1) % R);
-        commit();
-        asm volatile("cp.async.wait_group %0;" ::"n"(R - 1) : "memory");
-        __syncwarp();   // every lane's copies of this batch have landed
-        // this batch's ring addresses: after the wait, and distinct per batch
-        const uint32_t crb = opaque(cr0);
-        float a0 = 0.0f, a1 = 0.0f, c0 = 0.0f, c1 = 0.0f;   // block sums of rows L & 7 and (L & 7) + 8
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t ca = crb ^ (4u * k);
-            const uint32_t lw = lw0 ^ (0x404u * k);
-            const uint32_t wa = lds_u32<D * kXtabStageBytes>(ca);
-            const uint32_t wb = lds_u32<D * kXtabStageBytes + 8 * 128>(ca);
-            const float ea = (lds_f32(prmt<0xE604u>(wa, lw)) + lds_f32(prmt<0xE615u>(wa, lw))) +
-                             (lds_f32(prmt<0xE724u>(wa, lw)) + lds_f32(prmt<0xE735u>(wa, lw)));
-            const float eb = (lds_f32(prmt<0xE604u>(wb, lw)) + lds_f32(prmt<0xE615u>(wb, lw))) +
-                             (lds_f32(prmt<0xE724u>(wb, lw)) + lds_f32(prmt<0xE735u>(wb, lw)));
-            if (k & 1) {
-                a1 += ea;
-                c1 += eb;
-            } else {
-                a0 += ea;
-                c0 += eb;
-            }
-        }
-        float ra = (a0 + a1) * aba[D];                // row L & 7, block L >> 3
-        float rb = (c0 + c1) * abb[D];                // row (L & 7) + 8
-        ra += __shfl_xor_sync(0xffffffffu, ra, 8);    // + the slice's other blocks
-        rb += __shfl_xor_sync(0xffffffffu, rb, 8);
-        ra += __shfl_xor_sync(0xffffffffu, ra, 16);
-        rb += __shfl_xor_sync(0xffffffffu, rb, 16);
-        // lanes 0..7 hold rows 0..7 in ra, lanes 8..15 rows 8..15 in rb
-        const float r = lane < 8 ? ra : rb;
-        if (!counted_in) {
-            if (held < kXtabHold) {   // keep it until the count-in (a compile-time slot per case)
-#pragma unroll
-                for (int i = 0; i < kXtabHold; ++i)
-                    if (i == held) {
-                        hold_r[i] = r;
-                        hold_y[i] = yb[D];
-                        hold_n[i] = nvb[D];
-                    }
-                ++held;
-                return;
-            }
-            count_in();
-        }
-        if (lane < nvb[D]) red_add_f32(yb[D] + lane, r);
-    };
+    constexpr int H = kXtabHold;
 
     int k_item = 0;
     bool have = xtab_item(p, c, 0, s, b0, b1);
     int nb = have && b1 > b0 + warp ? (b1 - b0 - warp + NW - 1) / NW : 0;
     // weights first: they do not depend on the preceding grid
     if (nb > 0) seek(b0 + warp);
-#pragma unroll
-    for (int d = 0; d < R - 1; ++d) {
-        if (d < nb) issue(d);
-        commit();
-    }
+    xtab_unroll<0, P>([&](auto dc) {
+        constexpr int D = decltype(dc)::value;
+        if (D < nb) issue(dc);
+    });
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // the first item's x pieces (the table build below), requested before the zeroing
+    // x pairs of the first item's tables, requested before the zeroing
     __half2 xh[4];
     if (have) {
-        const __half2* xp = reinterpret_cast<const __half2*>(p.x + s * kXtabCols + 8 * lane);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xh[j] = xp[j];
+        for (int t = 0; t < 4; ++t) xh[t] = *reinterpret_cast<const __half2*>(p.x + s * kXtabCols + xcol + 8 * t);
     }
 
-    // ---- zero this CTA's share of y, then count in ----------------------------
+    // ---- zero this CTA's share of y (the count-in follows the table build) ---
     {
         const int z0 = (int)((long long)c * p.nbatch / G), z1 = (int)((long long)(c + 1) * p.nbatch / G);
         for (int i = z0 * kXtabBatch + (int)threadIdx.x; i < z1 * kXtabBatch; i += 32 * NW) {
@@ -451,54 +413,81 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
             const int r = r0 + (i % kXtabBatch);
             if (r < zs.out_f) zs.y[r] = 0.0f;
         }
-        __syncthreads();
-        // release: the CTA's zeroes (ordered before it by the barrier) are
-        // visible to whoever sees the count; nothing here waits for it
-        if (threadIdx.x == 0) red_release_add_u32(&p.bar[0], 1u);
+        if (!have) {
+            __syncthreads();
+            if (threadIdx.x == 0) red_release_add_u32(&p.bar[0], 1u);
+        }
     }
 
     while (have) {
-        // ---- the slice's tables: warp w fills byte values w, w + NW, ...; lane L
-        // its own column of each of its four pairs' tables (conflict-free stores);
-        // the previous item's lookups are done (__syncthreads below the batches)
+        // ---- the slice's tables: warp w fills byte values w, w + NW, ...
         {
             if (k_item > 0) {
-                const __half2* xp = reinterpret_cast<const __half2*>(p.x + s * kXtabCols + 8 * lane);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) xh[j] = xp[j];
+                for (int t = 0; t < 4; ++t)
+                    xh[t] = *reinterpret_cast<const __half2*>(p.x + s * kXtabCols + xcol + 8 * t);
             }
             float x0[4], x1[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                x0[j] = __low2float(xh[j]);
-                x1[j] = __high2float(xh[j]);
+            for (int t = 0; t < 4; ++t) {
+                x0[t] = __low2float(xh[t]);
+                x1[t] = __high2float(xh[t]);
             }
             for (int b = warp; b < 256; b += NW) {
                 const float t0 = c_nf4_table[b & 15], t1 = c_nf4_table[b >> 4];
-                const uint32_t o = (uint32_t)b << 8;
-                sts_f32(lk0 + o, fmaf(t1, x1[0], t0 * x0[0]));
-                sts_f32(lk1 + o, fmaf(t1, x1[1], t0 * x0[1]));
-                sts_f32(lk2 + o, fmaf(t1, x1[2], t0 * x0[2]));
-                sts_f32(lk3 + o, fmaf(t1, x1[3], t0 * x0[3]));
+                const uint32_t o = bl + ((uint32_t)b << 8);
+                sts_f32(o, fmaf(t1, x1[0], t0 * x0[0]));
+                sts_f32(o + 128, fmaf(t1, x1[1], t0 * x0[1]));
+                sts_f32(o + 65536, fmaf(t1, x1[2], t0 * x0[2]));
+                sts_f32(o + 65536 + 128, fmaf(t1, x1[3], t0 * x0[3]));
             }
         }
         __syncthreads();
+        if (k_item == 0 && threadIdx.x == 32 * (NW - 1)) red_release_add_u32(&p.bar[0], 1u);   // count in
+        // the lookups' addresses, as values defined after the barrier (the shared
+        // loads are not volatile and must not move above it)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) lwr[j] = opaque(lwr[j]);
 
-        // ---- the batches, R per round so that ring slots are compile-time; the
-        // steady rounds issue a batch per step, the last R - 1 steps do not
-        int it = 0;
-        for (; it + 2 * R - 1 <= nb; it += R)
-            xtab_unroll<0, R>([&](auto dc) { step(dc, true); });
-        for (; it < nb; it += R)
-            xtab_unroll<0, R>([&](auto dc) {
-                constexpr int D = decltype(dc)::value;
-                if (it + D < nb) step(dc, it + D + R - 1 < nb);
+        // ---- the batches: batch i sits in register stage i % P (compile-time
+        // below); the first H hold their results until the count-in
+        float hr[H];
+        float* hy[H];
+        int hn[H];
+        xtab_unroll<0, H>([&](auto hc) {
+            constexpr int h = decltype(hc)::value;
+            if (h < nb) {
+                hy[h] = yb[h % P];
+                hn[h] = nvb[h % P];
+                hr[h] = compute(std::integral_constant<int, h % P>{}, h + P < nb);
+            }
+        });
+        if (!counted_in) wait_count();
+        xtab_unroll<0, H>([&](auto hc) {
+            constexpr int h = decltype(hc)::value;
+            if (h < nb) add(hy[h], hn[h], hr[h]);
+        });
+        int it = H;
+        for (; it + 2 * P <= nb; it += P)   // every batch of the round refills its stage
+            xtab_unroll<0, P>([&](auto ec) {
+                constexpr int D = (H + decltype(ec)::value) % P;
+                float* const yd = yb[D];
+                const int nd = nvb[D];
+                add(yd, nd, compute(std::integral_constant<int, D>{}, true));
             });
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        if (held > 0) count_in();   // a warp with fewer batches than kHold
+        for (; it < nb; it += P)
+            xtab_unroll<0, P>([&](auto ec) {
+                constexpr int E = decltype(ec)::value;
+                constexpr int D = (H + E) % P;
+                if (it + E < nb) {
+                    float* const yd = yb[D];
+                    const int nd = nvb[D];
+                    add(yd, nd, compute(std::integral_constant<int, D>{}, it + E + P < nb));
+                }
+            });
         ++k_item;
         have = xtab_item(p, c, k_item, s, b0, b1);
-        __syncthreads();   // every warp is done with the tables and its ring
+        __syncthreads();   // every warp is done with the tables
         nb = have && b1 > b0 + warp ? (b1 - b0 - warp + NW - 1) / NW : 0;
         if (nb > 0) {
             sg = -1;
@@ -506,11 +495,10 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
             sg_end = 0;
             seek(b0 + warp);
         }
-#pragma unroll
-        for (int d = 0; d < R - 1; ++d) {
-            if (d < nb) issue(d);
-            commit();
-        }
+        xtab_unroll<0, P>([&](auto dc) {
+            constexpr int D = decltype(dc)::value;
+            if (D < nb) issue(dc);
+        });
     }
 
     // ---- leave: the last CTA out resets the counters for the next call ------------

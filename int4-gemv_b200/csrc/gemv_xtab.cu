@@ -1,16 +1,19 @@
 // Instantiations of the batch-1 NF4 GEMV from x-pair product tables (warps per
-// CTA x cp.async ring stages per warp, within the shared memory of one CTA per
-// SM), and the reader of this translation unit's device error flag.
+// CTA x batches each warp keeps in flight in registers; one CTA per SM, within
+// the registers of one CTA per SM without spills), and the reader of this
+// translation unit's device error flag.
 #include "b4_gemv_xtab.cuh"
 
 void* b4::gemv_kernel_xtab(int warps, int stages)
 {
-#define B4_XTAB_PICK(NW, R) \
-    if (warps == NW && stages == R) return (void*)&b4::b4_gemv_xtab_kernel<NW, R>;
+#define B4_XTAB_PICK(NW, P) \
+    if (warps == NW && stages == P) return (void*)&b4::b4_gemv_xtab_kernel<NW, P>;
+    B4_XTAB_PICK(8, 4)
+    B4_XTAB_PICK(12, 2)
     B4_XTAB_PICK(12, 3)
-    B4_XTAB_PICK(16, 3)
-    B4_XTAB_PICK(20, 2)
-    B4_XTAB_PICK(24, 2)
+    B4_XTAB_PICK(16, 2)
+    B4_XTAB_PICK(20, 1)
+    B4_XTAB_PICK(24, 1)
 #undef B4_XTAB_PICK
     return nullptr;
 }

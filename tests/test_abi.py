@@ -178,16 +178,17 @@ def test_median_is_the_reference_upper_median():
 @pytest.mark.parametrize("m", [1, 2, 16])
 def test_workspace_rule(fmt, out_f, in_f, m):
     """b4_gemv_default_config_ws: the x-pair table kernel for NF4 at batch 1
-    with in_f % 256 == 0 and at least 24 MB of weights (it needs the
-    workspace), else b4_gemv_default_config's choice (no measured shape ran
-    faster split: split only when asked)."""
+    with in_f % 256 == 0 and at least 17.5 MB of weights (5 MB for rows of 8192
+    columns or more; it needs the workspace), else b4_gemv_default_config's
+    choice (no measured shape ran faster split: split only when asked)."""
     c = b4gemv.default_config_ws(fmt, in_f, out_f, m)
     assert not c["flags"] & b4gemv.FLAG_SPLIT
     weight_bytes = out_f * in_f // 2 + out_f * (in_f // 64) * 4
-    if fmt == 1 and m == 1 and in_f % 256 == 0 and weight_bytes >= 24_000_000:
+    pays = weight_bytes >= 17_500_000 or (in_f >= 8192 and weight_bytes >= 5_000_000)
+    if fmt == 1 and m == 1 and in_f % 256 == 0 and pays:
         assert c["engine"] == b4gemv.ENGINE_NF4_XTAB
-        big = weight_bytes >= 48_000_000 or in_f > 8192
-        assert (c["row_groups"], c["stages"]) == ((24, 2) if big else (16, 3))
+        big = weight_bytes >= 9_000_000
+        assert (c["row_groups"], c["stages"]) == ((16, 2) if big else (12, 3))
         assert b4gemv.workspace_size(fmt, in_f, out_f, m, device=0) == b4gemv.XTAB_WORKSPACE_BYTES
     else:
         assert c == b4gemv.default_config(fmt, in_f, out_f, m)

@@ -59,12 +59,18 @@ def test_explicit_split_matches_the_rule_and_oracle(cuda, oracle, fmt, out_f, in
 
 @pytest.mark.parametrize("name", list(QWEN))
 def test_rule_does_not_split_where_it_does_not_pay(cuda, name):
-    """No batch-1 shape measured faster split once every CTA has one resident tile."""
+    """No batch-1 shape measured faster split once every CTA has one resident tile:
+    the workspace rule never sets B4_FLAG_SPLIT, and the only workspace it asks
+    for is the x-pair table kernel's two counters (NF4, >= 24 MB of weights)."""
     out_f, in_f = QWEN[name]
     for fmt in (0, 1):
-        assert b4gemv.workspace_size(fmt, in_f, out_f) == 0
-        assert b4gemv.workspace_size(fmt, 8192, 8192) == 0
-        assert b4gemv.workspace_size(fmt, 28672, 8192) == 0
+        for o, i in ((out_f, in_f), (8192, 8192), (28672, 8192)):
+            cfg = b4gemv.default_config_ws(fmt, i, o, 1)
+            assert not cfg["flags"] & b4gemv.FLAG_SPLIT
+            xtab = cfg["engine"] == b4gemv.ENGINE_NF4_XTAB
+            wb = o * i // 2 + o * (i // 64) * 4
+            assert xtab == (fmt == 1 and (wb >= 17_500_000 or (i >= 8192 and wb >= 5_000_000)))
+            assert b4gemv.workspace_size(fmt, i, o) == (b4gemv.XTAB_WORKSPACE_BYTES if xtab else 0)
 
 
 @pytest.mark.parametrize("stages,groups", INT4_VARIANTS)

@@ -6,7 +6,7 @@ counted itself in on the workspace.  These tests check y against the oracle's
 double GEMV (max relative error below TOL, the metric of int4_gemv.cu:74-81)
 on the shapes that exercise each part of that scheme: one slice, slices shared
 by 10-11 CTAs, more slices than CTAs (each CTA loops over slices), rows not a
-multiple of the 8-row batch, several segments in one launch, y pre-filled with
+multiple of the 16-row batch, several segments in one launch, y pre-filled with
 NaN (every row must be zeroed), back-to-back calls (the workspace counters
 must come back to zero), and the NaN rows of the reference's edge fixture.
 """
@@ -31,10 +31,10 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-VARIANTS = [(12, 3), (16, 3), (20, 2), (24, 2)]   # (warps per CTA, ring stages per warp)
+VARIANTS = [(8, 4), (12, 2), (12, 3), (16, 2), (20, 1), (24, 1)]   # (warps per CTA, batches in flight per warp)
 
 
-def xtab_cfg(warps=16, stages=3, flags=0):
+def xtab_cfg(warps=12, stages=3, flags=0):
     return dict(engine=XTAB, row_groups=warps, stages=stages, flags=flags)
 
 
@@ -122,7 +122,7 @@ def test_xtab_multi_segment_one_launch(cuda, oracle):
         rule = b4gemv.multi_default_config_ws(1, pairs, to_dev(X, cuda))
         assert (rule["engine"] == XTAB) == (sum(shapes) == 2 * 18944)   # only gate+up is large enough
         ys = [torch.full((1, o), float("nan"), dtype=torch.float32, device=cuda) for o in shapes]
-        for cfg in (None, xtab_cfg(), xtab_cfg(24, 2, b4gemv.FLAG_PDL)):
+        for cfg in (None, xtab_cfg(), xtab_cfg(24, 1, b4gemv.FLAG_PDL), xtab_cfg(16, 2, b4gemv.FLAG_PDL)):
             for y in ys:
                 y.fill_(float("nan"))
             out = b4gemv.gemv_multi(1, pairs, to_dev(X, cuda), ys=ys, config=cfg, pdl=cfg is None)
@@ -140,11 +140,12 @@ def test_xtab_edge_fixture_nan_rows(cuda, golden, oracle):
     qw, am = to_dev(g["nf4_packed"], cuda), to_dev(g["nf4_absmax"], cuda)
     in_f = g["W"].shape[1]
     ws = torch.zeros(b4gemv.XTAB_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
-    y = run_xtab(qw, am, to_dev(g["x"], cuda), qw.shape[0], in_f, xtab_cfg(), ws).cpu().numpy()[0]
     ref = f64_ref(oracle, 1, qw, am, g["x"])[0]
-    assert np.array_equal(np.isfinite(y), np.isfinite(ref))
     ok = np.isfinite(ref)
-    assert rel_err(y[ok], ref[ok]) < TOL
+    for warps, stages in ((12, 3), (24, 1)):
+        y = run_xtab(qw, am, to_dev(g["x"], cuda), qw.shape[0], in_f, xtab_cfg(warps, stages), ws).cpu().numpy()[0]
+        assert np.array_equal(np.isfinite(y), np.isfinite(ref)), warps
+        assert rel_err(y[ok], ref[ok]) < TOL, warps
 
 
 def test_xtab_refusals(cuda):
@@ -170,6 +171,7 @@ def test_xtab_refusals(cuda):
     assert lib.b4_gemv_ws(1, _p(qw2), _p(am2), _p(x2), _p(y), 1088, out_f, 1, ctypes.byref(c), _p(ws), 256, st) == 1
     seg = (GemvSegment * 1)(GemvSegment(qw.data_ptr(), am.data_ptr(), y.data_ptr(), out_f))
     assert lib.b4_gemv_multi(1, seg, 1, _p(x), in_f, 1, ctypes.byref(c), st) == 1
-    bad = GemvConfig.from_dict(xtab_cfg(32, 3))   # no such (warps, stages) kernel
-    assert lib.b4_gemv_ws(1, _p(qw), _p(am), _p(x), _p(y), in_f, out_f, 1, ctypes.byref(bad), _p(ws), 256, st) == 1
+    for bad_cfg in (xtab_cfg(32, 3), xtab_cfg(16, 5), xtab_cfg(24, 2)):   # no such (warps, stages) kernel
+        bad = GemvConfig.from_dict(bad_cfg)
+        assert lib.b4_gemv_ws(1, _p(qw), _p(am), _p(x), _p(y), in_f, out_f, 1, ctypes.byref(bad), _p(ws), 256, st) == 1
     torch.cuda.synchronize()
