@@ -698,10 +698,13 @@ class TPBench:
         c0, c1 = self.layer.ranges["o"]
         self.attn = self.attn_full[:, c0:c1].contiguous()
         self.bytes = l70_bytes(fmt)
+        self.glue_fused = False
 
     def graph(self, p2p, reps):
         torch = self.torch
         self.layer.p2p = p2p
+        if p2p is not None:
+            self.glue_fused = self.layer.glue_fused()   # 4 launches per layer, else 6
         self.layer.forward(self.x, self.attn)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -796,10 +799,12 @@ def tp_layer_detail(b4, torch, dev, d, fmt, comm, p2p, skip_p2p_time=False):
         if d.rank == 0:
             res["tp_rel_err"] = {"nccl": e_nccl, "p2p": e_p2p,
                                  "vs": "the same seeded layer at tp = 1 on rank 0's GPU, every rank's y"}
+    glue = tb.glue_fused
     tb.close()
     res["launches"] = ("q/k/v and gate/up fused (b4_gemv_multi_ws), GEMVs as programmatic dependents; "
-                       "o/down + NCCL all-reduce (us_per_layer_nccl) or with the all-reduce fused into the "
-                       "GEMV over peer memory (us_per_layer_p2p)")
+                       "o/down + NCCL all-reduce with the cast and SwiGLU glue launches (us_per_layer_nccl), or "
+                       "with the all-reduce fused into the GEMV over peer memory (us_per_layer_p2p" +
+                       (": the cast and SwiGLU folded into o and down, 4 launches)" if glue else ")"))
     return res
 
 
@@ -1058,9 +1063,12 @@ def run_multi(args, b4, torch, dev, d):
                    "l2": f"one layer streams {tb.bytes / d.world / 1e6:.0f} MB per rank per step (inputs larger "
                          f"than L2 where that is > 126 MB; the layer is replayed as decode replays it)",
                    "timing": f"CUDA graphs of {gsteps} layer steps, events on the launching stream, max over ranks",
-                   "launches": "per rank: q/k/v (one b4_gemv_multi_ws launch), o with the all-reduce fused in "
-                               "over peer memory (b4_tp_gemv_p2p), fp16 cast, gate/up (one launch), SwiGLU, "
-                               "down with the fused all-reduce: 6 launches, programmatic dependents",
+                   "launches": ("per rank: q/k/v (one b4_gemv_multi_ws launch), o with the all-reduce over peer "
+                                "memory and the fp16 cast folded in (b4_tp_gemv_p2p_ex), gate/up (one launch), "
+                                "down with the SwiGLU of gate/up computed as it stages x and the all-reduce "
+                                "folded in: 4 launches, programmatic dependents") if tb.glue_fused else
+                               ("per rank: q/k/v (one b4_gemv_multi_ws launch), o with the fused all-reduce, fp16 "
+                                "cast, gate/up (one launch), SwiGLU, down with the fused all-reduce: 6 launches"),
                    "parallelism": f"tp{d.world}"},
         "us_per_layer": round(ms_max * 1e3 / steps, 2),
         "us_per_layer_nccl": round(us_nccl, 2),
@@ -1075,7 +1083,7 @@ def run_multi(args, b4, torch, dev, d):
                 "how": "per step and rank: x and the rank's attention shard copied in from pinned host memory, "
                        "the layer (TPDecodeLayer, C ABI calls captured in a CUDA graph) replayed, y copied out "
                        "and read on the host; max over ranks"},
-        "gpu_launches": steps * 6,
+        "gpu_launches": steps * (4 if tb.glue_fused else 6),
         "clocks": clocks,
     }
     if not args.no_tp:

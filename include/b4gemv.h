@@ -45,7 +45,7 @@ extern "C" {
 #define B4_FMT_INT4_G128 0
 #define B4_FMT_NF4_B64 1
 
-#define B4_ABI_VERSION 6
+#define B4_ABI_VERSION 7
 
 /* Same type as cudaStream_t, spelled without the CUDA headers. */
 typedef struct CUstream_st* b4_stream_t;
@@ -381,6 +381,18 @@ int b4_p2p_status(b4_p2p* p2p, int clear);   /* B4_STATUS_TIMEOUT if a wait gave
 int b4_p2p_destroy(b4_p2p* p2p);
 int b4_tp_gemv_p2p(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard, float* y,
                    int in_shard, int out_f, b4_p2p* p2p, int flags, b4_stream_t stream);
+/* b4_tp_gemv_p2p with the decode layer's elementwise glue folded in, so that a
+ * layer needs no glue launches on this path:
+ *   y16 (optional, NULL = none): y is also written rounded to fp16, as
+ *     b4_cast_f16 would write it (the o projection's output, the next GEMV's x);
+ *   flags B4_FLAG_X_SWIGLU: x_shard is fp32 [2][in_shard], this rank's gate
+ *     rows then its up rows (16-byte aligned), and the GEMV's x is
+ *     fp16(silu(gate) * up), computed while x is staged, rounded as
+ *     b4_swiglu_f16 rounds it (the down projection after gate/up).
+ * y is then bit-identical to the glue launches followed by b4_tp_gemv_p2p. */
+#define B4_FLAG_X_SWIGLU 4
+int b4_tp_gemv_p2p_ex(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard, float* y,
+                      void* y16, int in_shard, int out_f, b4_p2p* p2p, int flags, b4_stream_t stream);
 
 /* Elementwise glue of the decode layer: out = fp16(silu(gate) * up) (the MLP
  * activation between gate/up and down) and out = fp16(in).  Launched as

@@ -18,6 +18,7 @@ GROUP = 128
 NF4_BLOCK = 64
 FLAG_PDL = 1
 FLAG_SPLIT = 2
+FLAG_X_SWIGLU = 4   # b4_tp_gemv_p2p_ex: x = fp16(silu(gate) * up) of fp32 [gate | up]
 ENGINE_AUTO = -1
 ENGINE_FMA = 0
 ENGINE_MMA = 1
@@ -116,6 +117,7 @@ SIGNATURES = {
     "b4_p2p_status": (_I, [_P, _I]),
     "b4_p2p_destroy": (_I, [_P]),
     "b4_tp_gemv_p2p": (_I, [_I, _P, _P, _P, _P, _I, _I, _P, _I, _P]),
+    "b4_tp_gemv_p2p_ex": (_I, [_I, _P, _P, _P, _P, _P, _I, _I, _P, _I, _P]),
     "b4_swiglu_f16": (_I, [_P, _P, _P, ctypes.c_longlong, _P]),
     "b4_cast_f16": (_I, [_P, _P, ctypes.c_longlong, _P]),
     "b4_nccl_error_string": (ctypes.c_char_p, [_I]),

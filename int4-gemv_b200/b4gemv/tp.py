@@ -15,6 +15,11 @@ its output shard is an input):
   h                    -> gate, up shards -> silu(gate) * up (fp16) -> down partial
                        -> all-reduce -> y (fp32, replicated)
 
+On the peer-memory path the two elementwise steps are folded into the GEMVs
+(b4_tp_gemv_p2p_ex): o's all-reduce also writes h in fp16, and down computes
+silu(gate) * up while it stages its x, so a layer is four launches (q/k/v,
+o, gate/up, down); with NCCL the glue kernels run between them.
+
 The GEMVs, the sharding copies, the activation and the all-reduce are C ABI
 calls (include/b4gemv.h); torch.distributed is only used to hand the NCCL
 unique id from rank 0 to the others.  The reference has no multi-GPU code.
@@ -23,8 +28,8 @@ from __future__ import annotations
 
 import ctypes
 
-from ._lib import (FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK, XTAB_WORKSPACE_BYTES,
-                   GemvConfig, GemvSegment, check, load)
+from ._lib import (FLAG_PDL, FLAG_SPLIT, FLAG_X_SWIGLU, FMT_INT4_G128, FMT_NF4_B64, GROUP, NF4_BLOCK,
+                   XTAB_WORKSPACE_BYTES, GemvConfig, GemvSegment, check, load)
 
 
 def row_range(n: int, tp: int, rank: int):
@@ -177,11 +182,14 @@ class TPDecodeLayer:
         f32 = dict(dtype=torch.float32, device=device)
         f16 = dict(dtype=torch.float16, device=device)
         rq, rk, rg = (self.ranges[n][1] - self.ranges[n][0] for n in ("q", "k", "gate"))
+        # gate and up rows side by side in one buffer: [gate | up] is the x of the
+        # down projection's SwiGLU mode (b4_tp_gemv_p2p_ex, B4_FLAG_X_SWIGLU)
+        assert tp == 1 or self.ranges["down"] == self.ranges["gate"], "gate rows and down columns must shard alike"
+        gu = torch.empty((1, 2 * rg), **f32)
         self.buf = {"q": torch.empty((1, rq), **f32), "k": torch.empty((1, rk), **f32),
                     "v": torch.empty((1, rk), **f32), "h": torch.empty((1, hidden), **f32),
-                    "h16": torch.empty((1, hidden), **f16), "gate": torch.empty((1, rg), **f32),
-                    "up": torch.empty((1, rg), **f32), "act": torch.empty((1, rg), **f16),
-                    "y": torch.empty((1, hidden), **f32)}
+                    "h16": torch.empty((1, hidden), **f16), "gu": gu, "gate": gu[:, :rg], "up": gu[:, rg:],
+                    "act": torch.empty((1, rg), **f16), "y": torch.empty((1, hidden), **f32)}
         torch.cuda.synchronize(device)
         # launch configs: q/k/v and gate/up as one launch each (b4_gemv_multi)
         # when fused, else one per projection; PDL on the GEMV launches if asked
@@ -232,16 +240,31 @@ class TPDecodeLayer:
                                                        ctypes.byref(self.cfg[group]), _p(self.ws), self.ws.numel(),
                                                        stream))
 
+    def _p2p_ok(self, name):
+        # the fused peer-memory kernel takes NF4 shards of whole 128-column
+        # steps (its MMA k-step); narrower NF4 shards keep the NCCL all-reduce
+        qw = self.w[name][0]
+        return self.tp > 1 and self.p2p is not None and (self.fmt == FMT_INT4_G128 or (qw.shape[1] * 8) % 128 == 0)
+
+    def glue_fused(self) -> bool:
+        """True when the layer runs without glue launches: o writes h in fp16 as
+        well, and down computes silu(gate) * up while it stages x (both on the
+        peer-memory path)."""
+        return self._p2p_ok("o") and self._p2p_ok("down")
+
+    def _p2p_ex(self, name, x, y, y16, flags, stream):
+        qw, sc = self.w[name]
+        check(f"tp p2p {name}", load().b4_tp_gemv_p2p_ex(self.fmt, _p(qw), _p(sc), _p(x), _p(y),
+                                                         _p(y16) if y16 is not None else None, qw.shape[1] * 8,
+                                                         qw.shape[0], self.p2p.ptr,
+                                                         flags | (FLAG_PDL if self.pdl else 0), stream))
+
     def _rowpar(self, name, x, y, stream):
         qw, sc = self.w[name]
         if self.tp == 1:
             return self._gemv(name, x, y, stream)
-        # the fused peer-memory kernel takes NF4 shards of whole 128-column
-        # steps (its MMA k-step); narrower NF4 shards keep the NCCL all-reduce
-        if self.p2p is not None and (self.fmt == FMT_INT4_G128 or (qw.shape[1] * 8) % 128 == 0):
-            check(f"tp p2p {name}", load().b4_tp_gemv_p2p(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
-                                                          qw.shape[0], self.p2p.ptr,
-                                                          FLAG_PDL if self.pdl else 0, stream))
+        if self._p2p_ok(name):
+            self._p2p_ex(name, x, y, None, 0, stream)
             return
         check(f"tp {name}", load().b4_tp_gemv_allreduce_ws(self.fmt, _p(qw), _p(sc), _p(x), _p(y), qw.shape[1] * 8,
                                                             qw.shape[0], 1, _p(self.ws), self.ws.numel(),
@@ -260,13 +283,20 @@ class TPDecodeLayer:
             self._gemv("q", x, b["q"], s)
             self._gemv("k", x, b["k"], s)
             self._gemv("v", x, b["v"], s)
-        self._rowpar("o", attn, b["h"], s)
-        check("cast", lib.b4_cast_f16(_p(b["h"]), _p(b["h16"]), b["h"].numel(), s))
+        glue = not self.glue_fused()
+        if glue:
+            self._rowpar("o", attn, b["h"], s)
+            check("cast", lib.b4_cast_f16(_p(b["h"]), _p(b["h16"]), b["h"].numel(), s))
+        else:   # o writes h and its fp16 copy (the cast folded into the all-reduce)
+            self._p2p_ex("o", attn, b["h"], b["h16"], 0, s)
         if self.fused:
             self._multi("gateup", b["h16"], s)
         else:
             self._gemv("gate", b["h16"], b["gate"], s)
             self._gemv("up", b["h16"], b["up"], s)
-        check("swiglu", lib.b4_swiglu_f16(_p(b["gate"]), _p(b["up"]), _p(b["act"]), b["act"].numel(), s))
-        self._rowpar("down", b["act"], b["y"], s)
+        if glue:
+            check("swiglu", lib.b4_swiglu_f16(_p(b["gate"]), _p(b["up"]), _p(b["act"]), b["act"].numel(), s))
+            self._rowpar("down", b["act"], b["y"], s)
+        else:   # down stages x = fp16(silu(gate) * up) from [gate | up] itself
+            self._p2p_ex("down", b["gu"], b["y"], None, FLAG_X_SWIGLU, s)
         return b["y"]

@@ -198,6 +198,49 @@ __device__ __forceinline__ void stage_x_words(const __half* x, int n, bool vec, 
 
 constexpr int kXUnroll = 8;   // x words in flight per thread while staging
 
+// The gated activation of the decode layer's MLP: silu(g) = g / (1 + e^-g).
+// The SwiGLU glue kernel and the GEMVs that compute their x from gate/up
+// rows use this one definition, so both round the same way.
+__device__ __forceinline__ float swiglu_silu(float g) { return g / (1.0f + expf(-g)); }
+
+// stage_x_words for an x computed as fp16(silu(gate[k]) * up[k]) from fp32
+// gate = gu[0 .. n_words * 8), up = gu[n_words * 8 ..): gu 16-byte aligned.
+template <int XU, typename Store>
+__device__ __forceinline__ void stage_x_swiglu(const float* gu, int n_words, Store store)
+{
+    const float4* g4 = reinterpret_cast<const float4*>(gu);
+    const float4* u4 = g4 + 2 * (size_t)n_words;
+    for (int i0 = threadIdx.x; i0 < n_words; i0 += XU * blockDim.x) {
+        float4 g[XU][2], u[XU][2];
+#pragma unroll
+        for (int k = 0; k < XU; ++k) {
+            const int i = i0 + k * (int)blockDim.x;
+            if (i < n_words) {
+                g[k][0] = g4[2 * i];
+                g[k][1] = g4[2 * i + 1];
+                u[k][0] = u4[2 * i];
+                u[k][1] = u4[2 * i + 1];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < XU; ++k) {
+            const int i = i0 + k * (int)blockDim.x;
+            if (i < n_words) {
+                const float gv[8] = {g[k][0].x, g[k][0].y, g[k][0].z, g[k][0].w, g[k][1].x, g[k][1].y, g[k][1].z, g[k][1].w};
+                const float uv[8] = {u[k][0].x, u[k][0].y, u[k][0].z, u[k][0].w, u[k][1].x, u[k][1].y, u[k][1].z, u[k][1].w};
+                uint32_t h[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const __half lo = __float2half_rn(swiglu_silu(gv[2 * j]) * uv[2 * j]);
+                    const __half hi = __float2half_rn(swiglu_silu(gv[2 * j + 1]) * uv[2 * j + 1]);
+                    h[j] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+                }
+                store(i, make_uint4(h[0], h[1], h[2], h[3]));
+            }
+        }
+    }
+}
+
 // x of a small batch in shared memory, for B fragments that lane q reads as
 // logical words 4q .. 4q + 3 of a 16-word group (one 16-byte load per word):
 // each row's 16-word groups are stored transposed (word s at 4 (s & 3) + (s >> 2))

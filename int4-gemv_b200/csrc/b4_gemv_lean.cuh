@@ -237,7 +237,10 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     }
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = int4_pair_order(v); });
+    if (P2P && p.p2p.xgu)   // x = the SwiGLU of this rank's gate/up rows
+        stage_x_swiglu<2>(p.p2p.xgu, words, [&](int w, uint4 v) { xs[w] = int4_pair_order(v); });
+    else
+        stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = int4_pair_order(v); });
     __syncthreads();
     const uint32_t epoch = P2P ? p2p_epoch(p.p2p) : 0u;
 

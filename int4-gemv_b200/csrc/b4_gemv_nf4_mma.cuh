@@ -173,7 +173,10 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     // x slot w is stored at w ^ 2 when bit 3 of w is set: the four x lanes read
     // slots 4q + i (+ 16 per step), and without the swap lanes q and q + 2 hit
     // the same banks (two wavefronts per load instead of one)
-    stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w ^ ((w >> 2) & 2)] = v; });
+    if (P2P && p.p2p.xgu)   // x = the SwiGLU of this rank's gate/up rows
+        stage_x_swiglu<2>(p.p2p.xgu, words, [&](int w, uint4 v) { xs[w ^ ((w >> 2) & 2)] = v; });
+    else
+        stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w ^ ((w >> 2) & 2)] = v; });
     __syncthreads();
     const uint32_t epoch = P2P ? p2p_epoch(p.p2p) : 0u;
 

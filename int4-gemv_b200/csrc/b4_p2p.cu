@@ -124,21 +124,36 @@ int b4_p2p_destroy(b4_p2p* h)
     return first;
 }
 
-int b4_tp_gemv_p2p(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard, float* y,
-                   int in_shard, int out_f, b4_p2p* h, int flags, b4_stream_t stream)
+int b4_tp_gemv_p2p_ex(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard, float* y,
+                      void* y16, int in_shard, int out_f, b4_p2p* h, int flags, b4_stream_t stream)
 {
     if (!h) return cudaErrorInvalidValue;
     for (int r = 0; r < h->world; ++r)
         if (!h->peers[r]) return cudaErrorInvalidValue;   // every peer must be mapped first
+    if (flags & ~(B4_FLAG_PDL | B4_FLAG_X_SWIGLU)) return cudaErrorInvalidValue;
+    const bool swiglu = flags & B4_FLAG_X_SWIGLU;
+    // the checks see an fp16 x of in_shard columns; an fp32 gate/up pair needs 16-byte alignment
+    if (swiglu && (!x_shard || reinterpret_cast<uintptr_t>(x_shard) % 16)) return cudaErrorInvalidValue;
+    if (y16 && reinterpret_cast<uintptr_t>(y16) % 2) return cudaErrorInvalidValue;
     const GemvProblem p{fmt, qw_shard, scale_shard, x_shard, y, in_shard, out_f, 1, in_shard, out_f};
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
-    if (flags & ~B4_FLAG_PDL) return cudaErrorInvalidValue;
-    if (fmt == B4_FMT_NF4_B64) return launch_nf4_mma_p2p(p, args_of(h), flags, reinterpret_cast<cudaStream_t>(stream));
+    P2pArgs a = args_of(h);
+    a.y16 = static_cast<__half*>(y16);
+    a.xgu = swiglu ? static_cast<const float*>(x_shard) : nullptr;
+    const int lf = flags & B4_FLAG_PDL;
+    if (fmt == B4_FMT_NF4_B64) return launch_nf4_mma_p2p(p, a, lf, reinterpret_cast<cudaStream_t>(stream));
     b4_gemv_config c;
     default_config(p, &c);
-    c.flags = flags;
-    return launch_lean_int4_p2p(p, c, args_of(h), reinterpret_cast<cudaStream_t>(stream));
+    c.flags = lf;
+    return launch_lean_int4_p2p(p, c, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int b4_tp_gemv_p2p(int fmt, const uint32_t* qw_shard, const void* scale_shard, const void* x_shard, float* y,
+                   int in_shard, int out_f, b4_p2p* h, int flags, b4_stream_t stream)
+{
+    if (flags & ~B4_FLAG_PDL) return cudaErrorInvalidValue;
+    return b4_tp_gemv_p2p_ex(fmt, qw_shard, scale_shard, x_shard, y, nullptr, in_shard, out_f, h, flags, stream);
 }
 
 }  // extern "C"

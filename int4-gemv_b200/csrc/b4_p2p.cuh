@@ -30,6 +30,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 
 namespace b4 {
 
@@ -44,6 +45,9 @@ struct P2pArgs {
     uint32_t* error;                          // this rank's error word
     int rank, world;
     int max_rows;
+    __half* y16;         // optional: y rounded to fp16 as well (the next GEMV's x)
+    const float* xgu;    // optional: x = fp16(silu(gate) * up) of fp32 gate = xgu[0 .. in_f),
+                         // up = xgu[in_f .. 2 in_f), computed while x is staged
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
@@ -122,6 +126,7 @@ __device__ __forceinline__ void p2p_reduce(const P2pArgs& a, uint32_t epoch, int
             s += __uint_as_float((uint32_t)w);
         }
         y[r0 + lane] = s;
+        if (a.y16) a.y16[r0 + lane] = __float2half_rn(s);
     }
 }
 

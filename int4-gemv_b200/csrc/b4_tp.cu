@@ -56,7 +56,6 @@ const NcclApi& nccl()
 
 int nccl_status(ncclResult_t r) { return r == ncclSuccess ? 0 : B4_STATUS_NCCL_BASE + (int)r; }
 
-__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
 // The glue kernels run as programmatic dependents (launch_glue): they let the
 // next kernel (a GEMV, whose weight stream does not depend on them) launch
@@ -68,7 +67,7 @@ __global__ void swiglu_kernel(const float* __restrict__ gate, const float* __res
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x)
-        out[i] = __float2half_rn(silu(gate[i]) * up[i]);
+        out[i] = __float2half_rn(swiglu_silu(gate[i]) * up[i]);
 }
 
 __global__ void cast_f16_kernel(const float* __restrict__ in, __half* __restrict__ out, long long n)

@@ -458,3 +458,52 @@ def test_p2p_wait_for_a_peer_that_never_arrives_times_out_and_the_gpu_stays_usab
     assert res[0]["status"] == 10901, res      # B4_STATUS_TIMEOUT
     assert res[0]["rows_nan"], res
     assert res[0]["after"], res
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_p2p_ex_folds_the_glue_bit_identically(cuda, fmt):
+    """b4_tp_gemv_p2p_ex on one GPU (a world of one rank, its own slots): with
+    B4_FLAG_X_SWIGLU the GEMV of [gate | up] equals b4_swiglu_f16 followed by
+    b4_tp_gemv_p2p bit for bit, and y16 equals y rounded to fp16 (what
+    b4_cast_f16 writes); bad flags and a misaligned gate/up buffer are refused
+    before any launch."""
+    import ctypes
+
+    import torch
+
+    import b4gemv
+    from b4gemv._lib import FLAG_PDL, FLAG_X_SWIGLU, load
+    lib = load()
+    h = ctypes.c_void_p()
+    assert lib.b4_p2p_create(0, 1, 4096, ctypes.byref(h)) == 0
+    try:
+        out_f, in_f = 2048, 3584
+        g = torch.Generator(device=cuda)
+        g.manual_seed(11 + fmt)
+        W = torch.randn((out_f, in_f), generator=g, device=cuda) * 0.02
+        qw, sc, _ = (b4gemv.quantise_nf4_device if fmt else b4gemv.quantise_device)(W)
+        gu = torch.randn((2 * in_f,), generator=g, device=cuda) * 3.0
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        act = torch.empty((in_f,), dtype=torch.float16, device=cuda)
+        assert lib.b4_swiglu_f16(P(gu), ctypes.c_void_p(gu.data_ptr() + 4 * in_f), P(act), in_f, st) == 0
+        y_ref = torch.empty((out_f,), device=cuda)
+        assert lib.b4_tp_gemv_p2p(fmt, P(qw), P(sc), P(act), P(y_ref), in_f, out_f, h, 0, st) == 0
+        for flags in (0, FLAG_PDL):
+            y = torch.full((out_f,), float("nan"), device=cuda)
+            assert lib.b4_tp_gemv_p2p_ex(fmt, P(qw), P(sc), P(gu), P(y), None, in_f, out_f, h,
+                                         FLAG_X_SWIGLU | flags, st) == 0
+            assert torch.equal(y, y_ref)
+            y2 = torch.full((out_f,), float("nan"), device=cuda)
+            y16 = torch.empty((out_f,), dtype=torch.float16, device=cuda)
+            assert lib.b4_tp_gemv_p2p_ex(fmt, P(qw), P(sc), P(act), P(y2), P(y16), in_f, out_f, h, flags, st) == 0
+            assert torch.equal(y2, y_ref)
+            assert torch.equal(y16, y_ref.half())
+        assert lib.b4_tp_gemv_p2p_ex(fmt, P(qw), P(sc), P(gu), P(y), None, in_f, out_f, h, 64, st) == 1
+        assert lib.b4_tp_gemv_p2p_ex(fmt, P(qw), P(sc), ctypes.c_void_p(gu.data_ptr() + 8), P(y), None, in_f, out_f,
+                                     h, FLAG_X_SWIGLU, st) == 1
+        assert lib.b4_tp_gemv_p2p(fmt, P(qw), P(sc), P(gu), P(y), in_f, out_f, h, FLAG_X_SWIGLU, st) == 1
+        torch.cuda.synchronize()
+        assert lib.b4_p2p_status(h, 1) == 0
+    finally:
+        lib.b4_p2p_destroy(h)
