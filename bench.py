@@ -738,6 +738,46 @@ class TPBench:
         self.layer.p2p = None
         return d.max(a.elapsed_time(b) * 1e3 / (n * reps), self.dev)
 
+    def breakdown(self, p2p, reps=20, rounds=5):
+        """us per launch of each of the layer's four launch groups on the
+        glue-free peer-memory path, each timed alone (a graph of `reps`
+        back-to-back launches of that group, programmatic dependents), max
+        over ranks; the layer's own time is less than their sum by the overlap
+        of consecutive launches."""
+        torch, d = self.torch, self.d
+        self.layer.p2p = p2p
+        out = {}
+        if not self.layer.glue_fused():
+            self.layer.p2p = None
+            return out
+        for name in self.layer.STAGES:
+            self.layer.stage(name, self.x, self.attn)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            cs = torch.cuda.Stream()
+            cs.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(g, stream=cs, capture_error_mode="relaxed"):
+                for _ in range(reps):
+                    self.layer.stage(name, self.x, self.attn)
+            torch.cuda.current_stream().wait_stream(cs)
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            d.barrier()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(rounds):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            d.barrier()
+            del g
+            out[name] = round(d.max(a.elapsed_time(b) * 1e3 / (rounds * reps), self.dev), 2)
+        torch.cuda.synchronize()
+        self.layer.p2p = None
+        return out
+
     def rel_err(self, p2p, y_ref):
         """max |y - y_ref| / max |y_ref| over every rank's y (gathered to rank
         0), y_ref the same layer on one GPU; None on the other ranks."""
@@ -785,6 +825,7 @@ def tp_layer_detail(b4, torch, dev, d, fmt, comm, p2p, skip_p2p_time=False):
     if d.world > 1:
         us_p2p = tb.us_per_layer(p2p)
         res["us_per_layer_p2p"] = round(us_p2p, 2)
+        res["p2p_us_per_launch_alone"] = tb.breakdown(p2p)
         res["p2p_status"] = p2p.status()
         best = min(us_p2p, us_nccl)
     else:
@@ -1041,6 +1082,7 @@ def run_multi(args, b4, torch, dev, d):
     y_ref = tb.reference_y() if d.rank == 0 else None
     err = {"p2p": tb.rel_err(p2p, y_ref), "nccl": tb.rel_err(None, y_ref)}
     us_nccl = tb.us_per_layer(None)
+    per_launch = tb.breakdown(p2p)
     tb.close()
     del y_ref
     value = steps * tb.bytes / (ms_max / 1e3) / 1e9
@@ -1072,6 +1114,7 @@ def run_multi(args, b4, torch, dev, d):
                    "parallelism": f"tp{d.world}"},
         "us_per_layer": round(ms_max * 1e3 / steps, 2),
         "us_per_layer_nccl": round(us_nccl, 2),
+        "us_per_launch_alone": per_launch,
         "p2p_status": status,
         "gbs_per_rank": round(value / d.world, 1),
         "roofline": {"bound": "hbm", "kernel": "the layer's GEMVs (per rank)", "achieved": round(value / d.world, 1),

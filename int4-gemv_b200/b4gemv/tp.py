@@ -270,6 +270,29 @@ class TPDecodeLayer:
                                                             qw.shape[0], 1, _p(self.ws), self.ws.numel(),
                                                             self.comm.ptr, stream))
 
+    STAGES = ("qkv", "o", "gateup", "down")
+
+    def stage(self, name, x, attn, stream=None):
+        """One launch group of forward() alone ("qkv", "o", "gateup", "down"), on
+        this layer's buffers, as forward() issues it on the glue-free
+        peer-memory path (for timing each launch of a layer; every rank must
+        call the same stages, the row-parallel ones exchange rows)."""
+        import torch
+        assert self.fused and self.glue_fused(), "stage() times the fused, glue-free layer"
+        st = stream if stream is not None else torch.cuda.current_stream()
+        s = ctypes.c_void_p(st.cuda_stream)
+        b = self.buf
+        if name == "qkv":
+            self._multi("qkv", x, s)
+        elif name == "o":
+            self._p2p_ex("o", attn, b["h"], b["h16"], 0, s)
+        elif name == "gateup":
+            self._multi("gateup", b["h16"], s)
+        elif name == "down":
+            self._p2p_ex("down", b["gu"], b["y"], None, FLAG_X_SWIGLU, s)
+        else:
+            raise ValueError(name)
+
     def forward(self, x, attn, stream=None):
         """x: fp16 [1, hidden] (replicated); attn: fp16 [1, q shard] (this
         rank's heads of the attention output).  Returns y fp32 [1, hidden]."""
