@@ -631,15 +631,20 @@ def small_batch_bench(b4, torch):
                 cfg = b4.GemvConfig.from_dict(dict(rule, engine=-1, flags=b4.FLAG_PDL))
                 us = time_chained(torch, prob, cfg)
                 engine, launches = rule["engine"], 1
-                if m > 1 and engine not in (5, 7):   # the entry points' batch chunks
+                if rule["flags"] & b4.FLAG_KSLICE:   # column slices in one launch + their sum
+                    launches = 2
+                elif m > 1 and engine not in (5, 7):   # the entry points' batch chunks
                     for mc in (8, 4, 2):
                         e = b4.default_config(fmt, in_f, out_f, mc)["engine"] if mc < m else -1
                         if e in (5, 7):
                             engine, launches = e, -(-m // mc)
                             break
                 nb = alg_bytes(fmt, out_f, in_f, m)
-                out.append({"format": "int4_g128" if fmt == 0 else "nf4_b64", "shape": name, "m": m,
-                            "engine": engine, "launches": launches, "us": round(us, 3),
+                row = {"format": "int4_g128" if fmt == 0 else "nf4_b64", "shape": name, "m": m,
+                       "engine": engine, "launches": launches}
+                if rule["flags"] & b4.FLAG_KSLICE:
+                    row["column_slices"] = in_f // rule["x_tile"]
+                out.append({**row, "us": round(us, 3),
                             "gbs": round(nb / us / 1e3, 1), "tflops": round(2.0 * m * out_f * in_f / us / 1e6, 2)})
                 del prob
                 torch.cuda.empty_cache()

@@ -138,6 +138,15 @@ typedef struct b4_gemv_config {
  * B4_ENGINE_MMA_NF4 (NF4: register pipeline of `stages`), batch 1.  Only
  * b4_gemv_ws takes it (the other entry points reject it). */
 #define B4_FLAG_SPLIT 2
+/* Batches of 2..16 rows: split the columns into in_f / x_tile slices of
+ * x_tile columns (2..4 slices, each a whole number of the engine's k-steps:
+ * 128 * stage_groups columns for INT4 on B4_ENGINE_MMA_LEAN_ASYNC, 128 for NF4
+ * on B4_ENGINE_MMA_NF4), run them as the segments of one small-batch launch
+ * (x staged per slice, so long rows of a whole batch fit in shared memory and
+ * row blocks x slices spread over every SM), and sum the slices' partial y in
+ * a fixed order in a second launch.  Needs a workspace of
+ * slices * m * out_f * 4 bytes; only b4_gemv_ws takes it. */
+#define B4_FLAG_KSLICE 8
 
 /* ---- GEMV: y[b][r] = sum_k dequant(W)[r][k] * x[b][k], b < m ----------------
  * qw     : uint32 [out_f][in_f/8] packed codes

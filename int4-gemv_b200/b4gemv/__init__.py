@@ -14,7 +14,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (ENGINE_NF4_XTAB, FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS,
+from ._lib import (ENGINE_NF4_XTAB, FLAG_KSLICE, FLAG_PDL, FLAG_SPLIT, FMT_INT4_G128, FMT_NF4_B64, GROUP, MAX_SEGMENTS,
                    NF4_BLOCK, XTAB_WORKSPACE_BYTES, B4Error, GemvConfig, GemvSegment, check, load)
 
 __all__ = [
@@ -22,7 +22,7 @@ __all__ = [
     "GemvConfig", "load", "quantise", "quantise_nf4", "gemv_int4", "gemv_nf4", "gemv",
     "gemv_nf4_block_per_row", "dequant_int4", "dequant_nf4", "unpack_codes",
     "quantise_device", "quantise_nf4_device", "default_config", "median", "gemv_multi",
-    "multi_default_config", "MAX_SEGMENTS", "GemvSegment", "repack_bnb_nf4", "FLAG_SPLIT",
+    "multi_default_config", "MAX_SEGMENTS", "GemvSegment", "repack_bnb_nf4", "FLAG_SPLIT", "FLAG_KSLICE",
     "gemv_ws", "workspace_size", "workspace", "default_config_ws", "multi_default_config_ws",
     "ENGINE_NF4_XTAB", "XTAB_WORKSPACE_BYTES",
 ]

@@ -19,6 +19,7 @@ NF4_BLOCK = 64
 FLAG_PDL = 1
 FLAG_SPLIT = 2
 FLAG_X_SWIGLU = 4   # b4_tp_gemv_p2p_ex: x = fp16(silu(gate) * up) of fp32 [gate | up]
+FLAG_KSLICE = 8     # b4_gemv_ws, batch 2..16: column slices of x_tile columns, summed by a second launch
 ENGINE_AUTO = -1
 ENGINE_FMA = 0
 ENGINE_MMA = 1

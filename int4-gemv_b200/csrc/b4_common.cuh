@@ -279,6 +279,32 @@ __device__ __forceinline__ void stage_x_rows(const __half* x, int m, int words, 
     }
 }
 
+// the same with source rows src_ld words (of 8 halves) apart
+template <int XU, typename Store>
+__device__ __forceinline__ void stage_x_rows(const __half* x, int m, int words, int src_ld, bool vec, Store store)
+{
+    const int n = m * words;
+    const float inv = 1.0f / (float)words;
+    for (int i0 = threadIdx.x; i0 < n; i0 += XU * blockDim.x) {
+        uint4 r[XU];
+        int row[XU];
+#pragma unroll
+        for (int u = 0; u < XU; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            int rr = __float2int_rz(__int2float_rn(i) * inv);   // i / words, corrected below
+            if (rr * words > i) --rr;
+            else if ((rr + 1) * words <= i) ++rr;
+            row[u] = rr;
+            r[u] = i < n ? ld_x_word(x + ((long long)rr * src_ld + (i - rr * words)) * 8, vec) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < XU; ++u) {
+            const int i = i0 + u * (int)blockDim.x;
+            if (i < n) store(row[u], i - row[u] * words, r[u]);
+        }
+    }
+}
+
 // ---- NF4 decode ---------------------------------------------------------------
 // Warp-register code book: lane L holds NF4[L & 15]; a shuffle with the packed
 // word shifted right by 4k as the source lane reads NF4[nibble k], since the

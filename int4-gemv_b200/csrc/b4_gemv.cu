@@ -691,10 +691,27 @@ namespace {
 
 bool lean_geometry_ok(const b4_gemv_config& c) { return c.warps_k >= 1 && c.row_groups >= 1 && c.warps_k * c.row_groups <= 8; }
 
+// Row strides and column slices of a small-batch launch whose segments are
+// k slices of one matrix (launch_ksliced); nullptr: segments are whole
+// matrices sharing x.
+struct MbSlices {
+    int ld_words, ld_scales, x_ld;
+    int xoff[kLeanMaxSeg];
+};
+
+template <typename MP>
+void set_mb_slices(MP& mp, const MbSlices* sl, int in_f, int scales_per_row)
+{
+    mp.ld_words = sl ? sl->ld_words : in_f / 8;
+    mp.ld_scales = sl ? sl->ld_scales : scales_per_row;
+    mp.x_ld = sl ? sl->x_ld : in_f;
+    for (int s = 0; s < kLeanMaxSeg; ++s) mp.xoff[s] = sl ? sl->xoff[s] : 0;
+}
+
 // One launch of the lean INT4 kernel over nseg weight matrices sharing x
 // (m = 1; m = 2..16 with the cp.async ring: the small-batch kernel).
 int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
-                          const b4_gemv_config& c, cudaStream_t st)
+                          const b4_gemv_config& c, cudaStream_t st, const MbSlices* sl = nullptr)
 {
     // CTAs of 16 warps: batches of 9..16 rows on the 4-stage single-group ring
     const bool wide = c.warps_k >= 1 && c.row_groups >= 1 && c.warps_k * c.row_groups == 16;
@@ -710,7 +727,7 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
     if ((in_f / kGroup) % groups) return cudaErrorInvalidValue;   // a stage of `groups` groups tiles the row
     const int nb = m > 8 ? 2 : 1;
     void* fn = m == 1 ? gemv_kernel_int4_lean(c.stages, groups)
-                      : gemv_kernel_int4_lean_mb(c.stages, groups, nb, wide);
+                      : gemv_kernel_int4_lean_mb(c.stages, groups, nb, wide, sl ? 1 : 0);
     if (!fn) return cudaErrorInvalidValue;
     const int tr = c.tile_rows ? c.tile_rows : 16;
     if (tr < 1 || tr > 16) return cudaErrorInvalidValue;
@@ -740,9 +757,11 @@ int launch_lean_int4_segs(const b4_gemv_segment* segs, int nseg, const void* x, 
         LeanMbParams mp;
         mp.base = lp;
         mp.m = m;
+        set_mb_slices(mp, sl, in_f, in_f / kGroup);
         const size_t smem = lean_int4_mb_smem(in_f, m, kw, rg, c.stages, groups);
         return launch_persistent(fn, &mp, tiles, 32 * kw * rg, smem, c.flags, st);
     }
+    if (sl) return cudaErrorInvalidValue;
     const size_t smem = lean_int4_smem(in_f, kw, rg, c.stages, groups);
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
 }
@@ -783,13 +802,13 @@ int launch_lean_nf4_segs(const b4_gemv_segment* segs, int nseg, const void* x, i
 
 // One launch of the NF4 tensor-pipe kernel over nseg weight matrices sharing x.
 int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, int m,
-                        const b4_gemv_config& c, cudaStream_t st)
+                        const b4_gemv_config& c, cudaStream_t st, const MbSlices* sl = nullptr)
 {
     if (m < 1 || m > 16 || c.vec_words != 4 || c.rows_per_warp != 16 || !lean_geometry_ok(c))
         return cudaErrorInvalidValue;
     if (nseg < 1 || nseg > kLeanMaxSeg || in_f % 128) return cudaErrorInvalidValue;
     const int nb = (m + 3) / 4 > 2 ? 4 : (m + 3) / 4;   // 8-column MMA blocks of 4 batch rows
-    void* fn = m == 1 ? gemv_kernel_nf4_mma(c.stages) : gemv_kernel_nf4_mma_mb(c.stages, nb);
+    void* fn = m == 1 ? gemv_kernel_nf4_mma(c.stages) : gemv_kernel_nf4_mma_mb(c.stages, nb, sl ? 1 : 0);
     if (!fn) return cudaErrorInvalidValue;
     const int kw = c.warps_k, rg = c.row_groups;
     const int tr = c.tile_rows ? c.tile_rows : 16;
@@ -820,9 +839,11 @@ int launch_nf4_mma_segs(const b4_gemv_segment* segs, int nseg, const void* x, in
         Nf4MmaMbParams mp;
         mp.base = lp;
         mp.m = m;
+        set_mb_slices(mp, sl, in_f, in_f / kNf4Block);
         const size_t smem = nf4_mma_mb_smem(in_f, m, kw, rg);
         return launch_persistent(fn, &mp, tiles, 32 * kw * rg, smem, c.flags, st);
     }
+    if (sl) return cudaErrorInvalidValue;
     const size_t smem = nf4_mma_smem(in_f, kw, rg);
     return launch_persistent(fn, &lp, tiles, 32 * kw * rg, smem, c.flags, st);
 }
@@ -978,6 +999,88 @@ int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+// ---- k-sliced small batches ----------------------------------------------------
+
+// y[i] = part[0][i] + ... + part[S - 1][i] (fixed order), as a programmatic
+// dependent of the sliced GEMV.
+__global__ void slice_sum_kernel(const float* __restrict__ part, float* __restrict__ y, long long n, int S)
+{
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        float t = part[i];
+        for (int s = 1; s < S; ++s) t += part[(long long)s * n + i];
+        y[i] = t;
+    }
+}
+
+bool ksliced_shape(const GemvProblem& p, const b4_gemv_config& c, int* slices)
+{
+    const int sw = c.x_tile;
+    if (p.m < 2 || p.m > 16 || sw <= 0 || p.in_f % sw) return false;
+    const int S = p.in_f / sw;
+    if (S < 2 || S > kLeanMaxSeg) return false;
+    if (p.fmt == kInt4) {
+        if (c.engine != B4_ENGINE_MMA_LEAN_ASYNC || c.stage_groups < 1 || sw % (kGroup * c.stage_groups)) return false;
+    } else if (c.engine != B4_ENGINE_MMA_NF4 || sw % 128) {
+        return false;
+    }
+    *slices = S;
+    return true;
+}
+
+size_t ksliced_ws_bytes(const GemvProblem& p, int slices) { return (size_t)slices * p.m * p.out_f * sizeof(float); }
+
+// The batch's GEMV as `slices` column slices of x_tile columns, one segment
+// each in one launch of the small-batch kernel (x staged per slice, so a
+// batch of long rows fits in shared memory and the row blocks times slices
+// spread over every SM), each slice's partial y in the workspace; a second
+// launch sums the slices in order into y.
+int launch_ksliced(const GemvProblem& p, const b4_gemv_config& c, void* ws, size_t ws_bytes, cudaStream_t st)
+{
+    int S = 0;
+    if (!ksliced_shape(p, c, &S)) return cudaErrorInvalidValue;
+    if (!ws || !aligned(ws, 16) || ws_bytes < ksliced_ws_bytes(p, S)) return cudaErrorInvalidValue;
+    const int sw = c.x_tile;
+    float* part = static_cast<float*>(ws);
+    const long long n = (long long)p.m * p.out_f;
+    b4_gemv_segment segs[kLeanMaxSeg];
+    MbSlices sl = {};
+    sl.ld_words = p.in_f / 8;
+    if (p.x_ld % 8) return cudaErrorInvalidValue;
+    sl.x_ld = (int)p.x_ld;
+    for (int s = 0; s < S; ++s) {
+        segs[s].qw = p.qw + (size_t)s * sw / 8;
+        segs[s].scale = p.fmt == kInt4
+                            ? static_cast<const void*>(static_cast<const __half*>(p.scale) + (size_t)s * sw / kGroup)
+                            : static_cast<const void*>(static_cast<const float*>(p.scale) + (size_t)s * sw / kNf4Block);
+        segs[s].y = part + (size_t)s * n;
+        segs[s].out_f = p.out_f;
+        sl.xoff[s] = s * sw;
+    }
+    b4_gemv_config k = c;
+    k.flags &= B4_FLAG_PDL;
+    int e;
+    if (p.fmt == kInt4) {
+        sl.ld_scales = p.in_f / kGroup;
+        e = launch_lean_int4_segs(segs, S, p.x, sw, p.m, k, st, &sl);
+    } else {
+        sl.ld_scales = p.in_f / kNf4Block;
+        e = launch_nf4_mma_segs(segs, S, p.x, sw, p.m, k, st, &sl);
+    }
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)std::min<long long>((n + 255) / 256, 1184));
+    lc.blockDim = dim3(256);
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, slice_sum_kernel, static_cast<const float*>(part), p.y, n, S);
 }
 
 // ---- x-pair table NF4 launches (b4_gemv_xtab.cuh) --------------------------------
@@ -1229,6 +1332,39 @@ int launch_default(const GemvProblem& p, int flags, cudaStream_t st)
     return launch_gemv(p, c, st);
 }
 
+// Batches of 2..16 rows whose x does not fit beside the small-batch kernels'
+// buffers (long rows: down_proj from 8 rows): the fewest column slices whose
+// x does (B4_FLAG_KSLICE), instead of the batch chunks of the plain entry
+// points, which stream the weights once per chunk.  Measured on B200 (PDL
+// chains, us): INT4 down 3584x18944 m = 8 19.3 against 32.8, m = 16 31.7
+// against 66.4; NF4 down m = 8 36.6 against 67.2, m = 16 53.2 against 134.1.
+// Where the whole batch fits, slicing measured slower (the second launch and
+// the per-slice x): gate_proj and down_proj at m = 2, 4.
+bool ksliced_rule(const GemvProblem& p, b4_gemv_config* cfg)
+{
+    if (p.m < 2 || p.m > 16 || p.in_f % 128) return false;
+    const int want = p.fmt == kInt4 ? B4_ENGINE_MMA_LEAN_ASYNC : B4_ENGINE_MMA_NF4;
+    b4_gemv_config plain;
+    default_config(p, &plain);
+    if (plain.engine == want) return false;
+    const int ng = p.in_f / 128;
+    for (int S = 2; S <= kLeanMaxSeg; ++S) {
+        if (ng % S) continue;
+        GemvProblem q = p;
+        q.in_f = p.in_f / S;
+        b4_gemv_config c;
+        default_config(q, &c);
+        if (c.engine != want) continue;
+        if (p.fmt == kInt4)
+            while (c.stage_groups > 1 && (q.in_f / kGroup) % c.stage_groups) c.stage_groups /= 2;
+        c.flags = B4_FLAG_KSLICE;
+        c.x_tile = q.in_f;
+        *cfg = c;
+        return true;
+    }
+    return false;
+}
+
 void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
 {
     // NF4 at batch 1 with in_f a multiple of 256: the x-pair table kernel,
@@ -1246,12 +1382,13 @@ void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg)
         xtab_config(cfg, wb, p.in_f);
         return;
     }
+    if (aligned(p.qw, 16) && aligned(p.scale, 16) && aligned(p.x, 16) && ksliced_rule(p, cfg)) return;
     default_config(p, cfg);
 }
 
 bool needs_workspace(const b4_gemv_config& c)
 {
-    return (c.flags & B4_FLAG_SPLIT) || c.engine == B4_ENGINE_NF4_XTAB;
+    return (c.flags & (B4_FLAG_SPLIT | B4_FLAG_KSLICE)) || c.engine == B4_ENGINE_NF4_XTAB;
 }
 
 }  // namespace b4
@@ -1311,6 +1448,12 @@ int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_co
         *bytes = B4_XTAB_WORKSPACE_BYTES;
         return cudaSuccess;
     }
+    if (c.flags & B4_FLAG_KSLICE) {
+        int S = 0;
+        if (!ksliced_shape(p, c, &S)) return cudaErrorInvalidValue;
+        *bytes = ksliced_ws_bytes(p, S);
+        return cudaSuccess;
+    }
     if (!(c.flags & B4_FLAG_SPLIT)) return cudaSuccess;
     SplitPlan s;
     e = split_plan(p, c, &s);
@@ -1329,13 +1472,19 @@ int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     if (!cfg || cfg->engine == B4_ENGINE_AUTO) {
         b4_gemv_config c;
         default_config_ws(p, &c);
+        const int pdl = cfg ? cfg->flags & B4_FLAG_PDL : 0;
+        if (c.flags & B4_FLAG_KSLICE) {
+            c.flags |= pdl;
+            return launch_ksliced(p, c, ws, ws_bytes, st);
+        }
         if (c.engine != B4_ENGINE_NF4_XTAB)   // the rule of b4_gemv_ws never splits
-            return launch_default(p, cfg ? cfg->flags & B4_FLAG_PDL : 0, st);
-        c.flags = cfg ? cfg->flags & B4_FLAG_PDL : 0;
+            return launch_default(p, pdl, st);
+        c.flags = pdl;
         return launch_gemv_xtab(p, c, ws, ws_bytes, st);
     }
     if (cfg->engine == B4_ENGINE_NF4_XTAB) return launch_gemv_xtab(p, *cfg, ws, ws_bytes, st);
     if (cfg->flags & B4_FLAG_SPLIT) return launch_split(p, *cfg, ws, ws_bytes, st);
+    if (cfg->flags & B4_FLAG_KSLICE) return launch_ksliced(p, *cfg, ws, ws_bytes, st);
     return launch_gemv(p, *cfg, st);
 }
 

@@ -27,6 +27,13 @@ namespace b4 {
 struct LeanMbParams {
     LeanParams base;   // seg[].y is [m][out_f_s] (leading dimension out_f_s)
     int m;             // batch rows, 2..8*NB
+    // Rows of the weights hold ld_words code words and ld_scales scales, rows
+    // of x hold x_ld halves; segment s reads x from column xoff[s] (base.in_f
+    // columns).  In a k-sliced launch (the kernel's SL = 1) the segments are
+    // column slices of one matrix; each CTA then takes a contiguous run of
+    // tiles and restages x when the segment changes.
+    int ld_words, ld_scales, x_ld;
+    int xoff[kLeanMaxSeg];
 };
 
 // MAXT = 512: CTAs of 16 warps, one per SM, for batches of 9..16 rows, whose x
@@ -34,7 +41,7 @@ struct LeanMbParams {
 // CTAs of 8 warps would not fit.  An explicit config only: on B200 it ran
 // gate_proj at m = 16 in 23.5 us against 22.2 us for one 8-warp CTA per SM
 // with 3 stages of 2 groups, which the dispatch rule keeps.
-template <int D, int G, int NB, int MAXT = 256>
+template <int D, int G, int NB, int MAXT = 256, int SL = 0>
 __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_mb_kernel(const LeanMbParams pm)
 {
     using ST = typename LeanScale<G>::T;
@@ -87,10 +94,11 @@ __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_m
         vb = g + 8 < p.tr && r0 + g + 8 < out_f;
         const int ra = min(r0 + g, out_f - 1);
         const int rb = min(r0 + g + 8, out_f - 1);
-        pa = reinterpret_cast<const uint4*>(qw + (long long)ra * words) + ks * 4 * G + q;
-        pb = reinterpret_cast<const uint4*>(qw + (long long)rb * words) + ks * 4 * G + q;
-        sa_p = reinterpret_cast<const ST*>(sc + (long long)ra * ng) + ks;
-        sb_p = reinterpret_cast<const ST*>(sc + (long long)rb * ng) + ks;
+        const int lw = SL ? pm.ld_words : words, ls = SL ? pm.ld_scales : ng;   // row strides
+        pa = reinterpret_cast<const uint4*>(qw + (long long)ra * lw) + ks * 4 * G + q;
+        pb = reinterpret_cast<const uint4*>(qw + (long long)rb * lw) + ks * 4 * G + q;
+        sa_p = reinterpret_cast<const ST*>(sc + (long long)ra * ls) + ks;
+        sb_p = reinterpret_cast<const ST*>(sc + (long long)rb * ls) + ks;
     };
     auto fetch = [&](int slot) {
 #pragma unroll
@@ -113,16 +121,43 @@ __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_m
         }
     };
 
-    int tile = blockIdx.x;
-    if (tile < n_tiles) {
+    // tiles of this CTA: every gridDim.x-th, or (k-sliced) a contiguous run;
+    // computed where used, so that they hold no registers in the tile loop
+    auto first_tile = [&]() {
+        return SL ? (int)((long long)blockIdx.x * n_tiles / gridDim.x) : (int)blockIdx.x;
+    };
+    auto end_tile = [&]() {
+        return SL ? (int)((long long)(blockIdx.x + 1) * n_tiles / gridDim.x) : n_tiles;
+    };
+    // the segment of a tile (its x columns start at pm.xoff[segment])
+    auto seg_of = [&](int t) {
+        int sg = 0;
+#pragma unroll
+        for (int s = 1; s < kLeanMaxSeg; ++s)
+            if (s < p.nseg && t >= p.seg[s - 1].tile_end) sg = s;
+        return sg;
+    };
+    int tile = first_tile();
+    if (tile < end_tile()) {
         setup(tile);
         prologue();
     }
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // x is [m][in_f], contiguous: word i of the whole batch is at x + 8i
-    stage_x_rows<kXUnroll>(p.x, m, words, p.x_vec,
-                           [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = int4_pair_order(v); });
+    // x rows are x_ld halves apart; a segment's columns start at pm.xoff[segment]
+    auto stage_x = [&](int sg) {
+        if constexpr (SL) {
+            int xo = pm.xoff[0];   // pm.xoff[sg], by constant indices
+#pragma unroll
+            for (int s = 1; s < kLeanMaxSeg; ++s)
+                if (sg == s) xo = pm.xoff[s];
+            stage_x_rows<kXUnroll>(p.x + xo, m, words, pm.x_ld >> 3, p.x_vec,
+                                   [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = int4_pair_order(v); });
+        } else {   // x is [m][in_f], contiguous
+            stage_x_rows<kXUnroll>(p.x, m, words, p.x_vec, [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = int4_pair_order(v); });
+        }
+    };
+    stage_x(seg_of(tile));
     __syncthreads();
 
     // the batch rows this lane feeds into B (columns g of each block)
@@ -130,10 +165,18 @@ __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_m
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) xrow[nb] = xs + (size_t)min(nb * 8 + g, m - 1) * xst + ks * 16 * G + q;
 
-    for (; tile < n_tiles; tile += gridDim.x) {
-        if (tile != (int)blockIdx.x) {
+    for (; tile < end_tile(); tile += SL ? 1 : (int)gridDim.x) {
+        if (tile != first_tile()) {
             setup(tile);
             prologue();
+            if constexpr (SL) {
+                const int sg = seg_of(tile);
+                if (sg != seg_of(tile - 1)) {   // the next column slice (uniform per CTA)
+                    __syncthreads();
+                    stage_x(sg);
+                    __syncthreads();
+                }
+            }
         }
         float acc[NB][4];
 #pragma unroll
@@ -228,6 +271,6 @@ __global__ void __launch_bounds__(MAXT, MAXT == 512 ? 1 : 3 - NB) b4_gemv_lean_m
     }
 }
 
-void* gemv_kernel_int4_lean_mb(int depth, int groups, int nb, int wide = 0);
+void* gemv_kernel_int4_lean_mb(int depth, int groups, int nb, int wide = 0, int sliced = 0);
 
 }  // namespace b4

@@ -30,9 +30,12 @@ namespace b4 {
 struct Nf4MmaMbParams {
     LeanNf4Params base;   // seg[].y is [m][out_f_s]
     int m;                // batch rows, 2..4*NB
+    // Row strides and k slices as in LeanMbParams (ld_scales: absmax per row).
+    int ld_words, ld_scales, x_ld;
+    int xoff[kLeanMaxSeg];
 };
 
-template <int D, int NB>
+template <int D, int NB, int SL = 0>
 __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4MmaMbParams pm)
 {
     const LeanNf4Params& p = pm.base;
@@ -85,10 +88,11 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
         vb = g + 8 < p.tr && r0 + g + 8 < out_f;
         const int ra = min(r0 + g, out_f - 1);
         const int rb = min(r0 + g + 8, out_f - 1);
-        pa = reinterpret_cast<const uint4*>(qw + (long long)ra * words) + ks * 4 + q;
-        pb = reinterpret_cast<const uint4*>(qw + (long long)rb * words) + ks * 4 + q;
-        sa_p = reinterpret_cast<const float2*>(am + (long long)ra * nblk) + ks;
-        sb_p = reinterpret_cast<const float2*>(am + (long long)rb * nblk) + ks;
+        const int lw = SL ? pm.ld_words : words, ls = SL ? pm.ld_scales : nblk;   // row strides
+        pa = reinterpret_cast<const uint4*>(qw + (long long)ra * lw) + ks * 4 + q;
+        pb = reinterpret_cast<const uint4*>(qw + (long long)rb * lw) + ks * 4 + q;
+        sa_p = reinterpret_cast<const float2*>(am + (long long)ra * ls) + ks;
+        sb_p = reinterpret_cast<const float2*>(am + (long long)rb * ls) + ks;
     };
     auto fetch = [&](int slot) {
         if (va) {
@@ -112,16 +116,44 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
             if (d < n_it) fetch(d);
     };
 
-    int tile = blockIdx.x;
-    if (tile < n_tiles) {
+    // tiles of this CTA: every gridDim.x-th, or (k-sliced) a contiguous run;
+    // computed where used, so that they hold no registers in the tile loop
+    auto first_tile = [&]() {
+        return SL ? (int)((long long)blockIdx.x * n_tiles / gridDim.x) : (int)blockIdx.x;
+    };
+    auto end_tile = [&]() {
+        return SL ? (int)((long long)(blockIdx.x + 1) * n_tiles / gridDim.x) : n_tiles;
+    };
+    // the segment of a tile (its x columns start at pm.xoff[segment])
+    auto seg_of = [&](int t) {
+        int sg = 0;
+#pragma unroll
+        for (int s = 1; s < kLeanMaxSeg; ++s)
+            if (s < p.nseg && t >= p.seg[s - 1].tile_end) sg = s;
+        return sg;
+    };
+    int tile = first_tile();
+    if (tile < end_tile()) {
         setup(tile);
         prologue();
     }
     nf4_pair_table_fill(base);
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // x is [m][in_f], contiguous: word i of the whole batch is at x + 8i
-    stage_x_rows<kXUnroll>(p.x, m, words, p.x_vec, [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = v; });
+    // x rows are x_ld halves apart; a segment's columns start at pm.xoff[segment]
+    auto stage_x = [&](int sg) {
+        if constexpr (SL) {
+            int xo = pm.xoff[0];   // pm.xoff[sg], by constant indices
+#pragma unroll
+            for (int s = 1; s < kLeanMaxSeg; ++s)
+                if (sg == s) xo = pm.xoff[s];
+            stage_x_rows<kXUnroll>(p.x + xo, m, words, pm.x_ld >> 3, p.x_vec,
+                                   [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = v; });
+        } else {   // x is [m][in_f], contiguous
+            stage_x_rows<kXUnroll>(p.x, m, words, p.x_vec, [&](int r, int w, uint4 v) { xs[r * xst + xmb_slot(w)] = v; });
+        }
+    };
+    stage_x(seg_of(tile));
     __syncthreads();
 
     // B: this lane carries batch row 4*nb + (g & 3) when (g >> 2) == (q >> 1)
@@ -137,10 +169,18 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     const unsigned char* tb = base;
     const bool hi_blk = q >= 2;   // the NF4 block of this lane's D columns
 
-    for (; tile < n_tiles; tile += gridDim.x) {
-        if (tile != (int)blockIdx.x) {
+    for (; tile < end_tile(); tile += SL ? 1 : (int)gridDim.x) {
+        if (tile != first_tile()) {
             setup(tile);
             prologue();
+            if constexpr (SL) {
+                const int sg = seg_of(tile);
+                if (sg != seg_of(tile - 1)) {   // the next column slice (uniform per CTA)
+                    __syncthreads();
+                    stage_x(sg);
+                    __syncthreads();
+                }
+            }
         }
         float acc[NB][4];
 #pragma unroll
@@ -287,6 +327,6 @@ __global__ void __launch_bounds__(256, 1) b4_gemv_nf4_mma_mb_kernel(const Nf4Mma
     }
 }
 
-void* gemv_kernel_nf4_mma_mb(int depth, int nb);
+void* gemv_kernel_nf4_mma_mb(int depth, int nb, int sliced = 0);
 
 }  // namespace b4

@@ -190,6 +190,20 @@ def test_workspace_rule(fmt, out_f, in_f, m):
         big = weight_bytes >= 9_000_000
         assert (c["row_groups"], c["stages"]) == ((16, 2) if big else (12, 3))
         assert b4gemv.workspace_size(fmt, in_f, out_f, m, device=0) == b4gemv.XTAB_WORKSPACE_BYTES
+    elif c["flags"] & b4gemv.FLAG_KSLICE:
+        # a batch whose x does not fit beside the small-batch kernel: the fewest
+        # column slices whose x does, each run by that kernel
+        plain = b4gemv.default_config(fmt, in_f, out_f, m)
+        assert m >= 2 and plain["engine"] not in (5, 7)
+        sw = c["x_tile"]
+        slices = in_f // sw
+        assert in_f % sw == 0 and 2 <= slices <= 4 and sw % 128 == 0
+        for fewer in range(2, slices):
+            if (in_f // 128) % fewer == 0:
+                assert b4gemv.default_config(fmt, in_f // fewer, out_f, m)["engine"] not in (5, 7)
+        one = b4gemv.default_config(fmt, sw, out_f, m)
+        assert c["engine"] == one["engine"] in (5, 7) and c["row_groups"] == one["row_groups"]
+        assert b4gemv.workspace_size(fmt, in_f, out_f, m, device=0) == slices * m * out_f * 4
     else:
         assert c == b4gemv.default_config(fmt, in_f, out_f, m)
 

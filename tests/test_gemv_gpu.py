@@ -448,7 +448,8 @@ def test_nf4_small_batch_tensor_pipe_kernel(cuda, oracle, m):
 def test_long_rows_large_batch_run_as_tensor_pipe_chunks(cuda, oracle, fmt, m):
     """x for 8+ rows of 18944 columns does not fit next to the tensor-pipe
     engines' buffers: with the dispatch rule (cfg NULL, or B4_ENGINE_AUTO with
-    the PDL flag) the entry points run batch chunks through them."""
+    the PDL flag) the plain entry points run batch chunks through them, and
+    b4_gemv_ws (the Python default) runs column slices (B4_FLAG_KSLICE)."""
     import ctypes
     import torch
     out_f, in_f = 640, 18944
@@ -468,6 +469,56 @@ def test_long_rows_large_batch_run_as_tensor_pipe_chunks(cuda, oracle, fmt, m):
                                     in_f, out_f, m, ctypes.byref(cfg), st) == 0
     torch.cuda.synchronize()
     assert rel_err(y2.cpu().numpy(), ref) < TOL
+
+
+def ksliced_config(fmt, in_f, out_f, m, slices, pdl=False):
+    """The k-sliced small-batch config: the rule's small-batch geometry for
+    one slice, B4_FLAG_KSLICE, x_tile = the slice width."""
+    sw = in_f // slices
+    c = b4gemv.default_config(fmt, sw, out_f, m)
+    assert c["engine"] in (5, 7), c
+    if fmt == 0:
+        while (sw // 128) % c["stage_groups"]:
+            c["stage_groups"] //= 2
+    c["flags"] = b4gemv.FLAG_KSLICE | (b4gemv.FLAG_PDL if pdl else 0)
+    c["x_tile"] = sw
+    return c
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("m", [2, 3, 8, 9, 16])
+@pytest.mark.parametrize("out_f,in_f,slices", [(640, 18944, 4), (300, 4096, 2), (37, 2048, 4), (1200, 9472, 2)])
+def test_ksliced_small_batch(cuda, oracle, fmt, m, out_f, in_f, slices):
+    """B4_FLAG_KSLICE: the batch's GEMV as column slices (segments of one
+    small-batch launch, x staged per slice, CTAs on contiguous tile runs) and
+    an ordered sum of the slices' partial y; within tolerance of the oracle,
+    the workspace size as b4_gemv_workspace_size reports it, and refused
+    without one or with slices that do not tile the rows."""
+    import ctypes
+    import torch
+    rng = np.random.default_rng(400 + m + fmt + in_f + out_f)
+    W, X = rand_problem(rng, out_f, in_f, m)
+    qw, sc = quantised(fmt, W, cuda)
+    ref = f64_ref(oracle, fmt, qw, sc, X)
+    Xd = to_dev(X, cuda)
+    for pdl in (False, True):
+        cfg = ksliced_config(fmt, in_f, out_f, m, slices, pdl)
+        n = b4gemv.workspace_size(fmt, in_f, out_f, m, cfg)
+        assert n == slices * m * out_f * 4
+        ws = torch.zeros(n, dtype=torch.uint8, device=cuda)
+        y = b4gemv.gemv_ws(fmt, qw, sc, Xd, torch.full((m, out_f), float("nan"), device=cuda), config=cfg,
+                           ws=ws).cpu().numpy()
+        assert rel_err(y, ref) < TOL, (pdl, cfg)
+    lib, p = b4gemv.load(), ctypes.c_void_p
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    y = torch.empty((m, out_f), device=cuda)
+    c = b4gemv.GemvConfig.from_dict(cfg)
+    args = (fmt, p(qw.data_ptr()), p(sc.data_ptr()), p(Xd.data_ptr()), p(y.data_ptr()), in_f, out_f, m, ctypes.byref(c))
+    assert lib.b4_gemv_ws(*args, p(ws.data_ptr()), n - 4, st) == 1
+    assert lib.b4_gemv_ex(*args, st) == 1
+    bad = b4gemv.GemvConfig.from_dict(dict(cfg, x_tile=in_f // slices + 64))
+    assert lib.b4_gemv_ws(*args[:-1], ctypes.byref(bad), p(ws.data_ptr()), n, st) == 1
+    torch.cuda.synchronize()
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
