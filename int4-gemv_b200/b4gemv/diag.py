@@ -313,6 +313,43 @@ def cmd_glue(args, torch):
     print(f"ran {args.launches} x (swiglu, cast) on {args.n} elements")
 
 
+def cmd_p2p(args, torch):
+    """The row-parallel GEMV with the peer-memory all-reduce in its epilogue
+    (b4_tp_gemv_p2p_ex) in a world of one rank (its own slots, no peer, no
+    collective: one process, so the kernel can be profiled alone), on a
+    row-parallel shard's shape; --swiglu: x computed from fp32 [gate | up]
+    while it is staged, and y also written in fp16."""
+    from . import quantise_device
+    from ._lib import FLAG_PDL, FLAG_X_SWIGLU
+    fmt = FMT_NF4_B64 if args.fmt == "nf4" else FMT_INT4_G128
+    out_f, in_f = SHAPES[args.shape]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = load()
+    h = ctypes.c_void_p()
+    check("b4_p2p_create", lib.b4_p2p_create(0, 1, out_f, ctypes.byref(h)))
+    try:
+        g = torch.Generator(device=dev)
+        g.manual_seed(2)
+        W = torch.randn((out_f, in_f), generator=g, device=dev) * 0.02
+        qw, sc, _ = (quantise_nf4_device if fmt == FMT_NF4_B64 else quantise_device)(W)
+        del W
+        x = (torch.randn((2 * in_f,), generator=g, device=dev) if args.swiglu else
+             torch.randn((in_f,), generator=g, device=dev).half())
+        y = torch.empty((out_f,), device=dev)
+        y16 = torch.empty((out_f,), dtype=torch.float16, device=dev)
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        flags = FLAG_PDL | (FLAG_X_SWIGLU if args.swiglu else 0)
+        for _ in range(args.launches):
+            check("b4_tp_gemv_p2p_ex", lib.b4_tp_gemv_p2p_ex(fmt, P(qw), P(sc), P(x), P(y), P(y16) if args.swiglu else None,
+                                                             in_f, out_f, h, flags, st))
+        torch.cuda.synchronize()
+        check("b4_p2p_status", lib.b4_p2p_status(h, 1))
+    finally:
+        lib.b4_p2p_destroy(h)
+    print(f"ran {args.launches} peer-memory row-parallel GEMVs of {args.fmt} {args.shape} {out_f}x{in_f} (world 1)")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m b4gemv.diag")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -338,10 +375,16 @@ def main(argv=None):
     gl = sub.add_parser("glue")
     gl.add_argument("--n", type=int, default=28672)
     gl.add_argument("--launches", type=int, default=3)
+    pp = sub.add_parser("p2p")
+    pp.add_argument("--fmt", default="nf4", choices=["nf4", "int4"])
+    pp.add_argument("--shape", default="tp2_down", choices=list(SHAPES))
+    pp.add_argument("--launches", type=int, default=3)
+    pp.add_argument("--swiglu", action="store_true")
     args = ap.parse_args(argv)
     import torch
     torch.cuda.init()
-    {"sweep": cmd_sweep, "aspect": cmd_aspect, "run": cmd_run, "step": cmd_step, "glue": cmd_glue}[args.cmd](args, torch)
+    {"sweep": cmd_sweep, "aspect": cmd_aspect, "run": cmd_run, "step": cmd_step, "glue": cmd_glue,
+     "p2p": cmd_p2p}[args.cmd](args, torch)
 
 
 if __name__ == "__main__":
