@@ -374,14 +374,17 @@ int b4_tp_gemv_allreduce_ws(int fmt, const uint32_t* qw_shard, const void* scale
  * their rows of y are NaN, b4_p2p_status reports B4_STATUS_TIMEOUT, and the
  * GPU stays usable (then destroy and re-create the b4_p2p on every rank: the
  * call counters disagree).  Set-up, once per rank and device: b4_p2p_create
- * (one device allocation of 16 * world * max_rows + 256 bytes, max_rows >=
+ * (one device allocation of 16 * world * max_rows + 4 * max_rows + 512 bytes, max_rows >=
  * the out_f of every call), b4_p2p_ipc_handle -> send the 64-byte handle to
  * every peer -> b4_p2p_open_peer for each peer's handle.  One process per GPU
  * (CUDA IPC).  Every rank must make the same sequence of calls; the call
  * counter lives on the device, so calls captured in a CUDA graph may be
  * replayed.  flags: B4_FLAG_PDL (or 0).  Batch 1; INT4, or NF4 with in_shard
- * a multiple of 128 (the NF4 kernel's MMA k-step).  No counterpart in the
- * reference (it has no multi-GPU code). */
+ * a multiple of 128 (the NF4 kernel's MMA k-step).  NF4 shards that the
+ * x-pair table kernel takes (b4_gemv_default_config_ws) run it into a partial
+ * y in the b4_p2p allocation and the same all-reduce as a second launch (y
+ * then varies from call to call within fp32 rounding, identically on every
+ * rank).  No counterpart in the reference (it has no multi-GPU code). */
 typedef struct b4_p2p b4_p2p;
 int b4_p2p_create(int rank, int world, int max_rows, b4_p2p** out);
 int b4_p2p_ipc_handle(const b4_p2p* p2p, void* handle64);

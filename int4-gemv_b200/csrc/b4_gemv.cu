@@ -1103,7 +1103,7 @@ bool xtab_buffers(const b4_gemv_segment* segs, int nseg)
 // count-in waits for every CTA), the workspace's first 8 bytes as its two
 // counters (zero between calls).
 int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, const b4_gemv_config& c,
-                     void* ws, size_t ws_bytes, cudaStream_t st)
+                     void* ws, size_t ws_bytes, cudaStream_t st, const float* xgu)
 {
     if (nseg < 1 || nseg > kXtabMaxSeg || !xtab_shape(kNf4, in_f, 1, x) || !xtab_buffers(segs, nseg))
         return cudaErrorInvalidValue;
@@ -1128,6 +1128,8 @@ int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int i
     xp.nslice = in_f / kXtabCols;
     xp.x = static_cast<const __half*>(x);
     xp.bar = static_cast<unsigned*>(ws);
+    xp.xgu = xgu;
+    if (xgu && !aligned(xgu, 16)) return cudaErrorInvalidValue;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -1167,7 +1169,7 @@ int launch_gemv_xtab(const GemvProblem& p, const b4_gemv_config& c, void* ws, si
 {
     if (!xtab_shape(p.fmt, p.in_f, p.m, p.x)) return cudaErrorInvalidValue;
     const b4_gemv_segment s{p.qw, p.scale, p.y, p.out_f};
-    return launch_xtab_segs(&s, 1, p.x, p.in_f, c, ws, ws_bytes, st);
+    return launch_xtab_segs(&s, 1, p.x, p.in_f, c, ws, ws_bytes, st, nullptr);
 }
 
 // The x-pair table kernel pays ~4 us per launch before it streams (the tables,
@@ -1204,6 +1206,19 @@ void xtab_config(b4_gemv_config* cfg, long long weight_bytes, int in_f)
 long long nf4_weight_bytes(long long rows, int in_f)
 {
     return rows * in_f / 2 + rows * (in_f / kNf4Block) * 4;
+}
+
+int launch_xtab_shard(const GemvProblem& p, const float* xgu, int flags, void* ws, cudaStream_t st)
+{
+    const b4_gemv_segment s{p.qw, p.scale, p.y, p.out_f};
+    const long long wb = nf4_weight_bytes(p.out_f, p.in_f);
+    if (!xtab_shape(p.fmt, p.in_f, p.m, xgu ? static_cast<const void*>(xgu) : p.x) || !xtab_buffers(&s, 1) ||
+        !xtab_pays(wb, p.in_f))
+        return cudaErrorNotSupported;
+    b4_gemv_config c;
+    xtab_config(&c, wb, p.in_f);
+    c.flags = flags & B4_FLAG_PDL;
+    return launch_xtab_segs(&s, 1, p.x, p.in_f, c, ws, B4_XTAB_WORKSPACE_BYTES, st, xgu);
 }
 
 // ---- split launches (b4_gemv_split.cuh) ---------------------------------------
@@ -1596,7 +1611,7 @@ int b4_gemv_multi_ws(int fmt, const b4_gemv_segment* segs, int nseg, const void*
     } else {
         c = *cfg;
     }
-    if (c.engine == B4_ENGINE_NF4_XTAB) return launch_xtab_segs(segs, nseg, x, in_f, c, ws, ws_bytes, st);
+    if (c.engine == B4_ENGINE_NF4_XTAB) return launch_xtab_segs(segs, nseg, x, in_f, c, ws, ws_bytes, st, nullptr);
     if (c.flags & B4_FLAG_SPLIT) return cudaErrorInvalidValue;
     return launch_gemv_multi(fmt, segs, nseg, x, in_f, m, c, st);
 }

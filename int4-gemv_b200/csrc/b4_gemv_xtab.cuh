@@ -105,6 +105,7 @@ struct XtabParams {
     const __half* x;
     unsigned* bar;       // workspace: [0] arrivals, [1] departures; zero between calls
     uint32_t smem;       // dynamic shared memory of the launch (bytes)
+    const float* xgu;    // non-null: x = fp16(silu(gate) * up) of fp32 gate = xgu[0 .. in_f), up = xgu[in_f ..)
 };
 
 // The device error flag of this translation unit (read by xtab_device_error).
@@ -397,12 +398,25 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // x pairs of the first item's tables, requested before the zeroing
+    // x of the tables' column pairs (columns xcol + 8t and the next, t = 0..3,
+    // of slice sl): fp16 x, or fp16(silu(gate) * up) from fp32 gate/up rows
     __half2 xh[4];
-    if (have) {
+    float2 xg[4], xu[4];
+    auto load_x = [&](int sl) {
+        if (p.xgu) {
+            const float* g = p.xgu + sl * kXtabCols + xcol;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) xh[t] = *reinterpret_cast<const __half2*>(p.x + s * kXtabCols + xcol + 8 * t);
-    }
+            for (int t = 0; t < 4; ++t) {
+                xg[t] = *reinterpret_cast<const float2*>(g + 8 * t);
+                xu[t] = *reinterpret_cast<const float2*>(g + p.in_f + 8 * t);
+            }
+        } else {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) xh[t] = *reinterpret_cast<const __half2*>(p.x + sl * kXtabCols + xcol + 8 * t);
+        }
+    };
+    // the first item's x, requested before the zeroing
+    if (have) load_x(s);
 
     // ---- zero this CTA's share of y (the count-in follows the table build) ---
     {
@@ -422,16 +436,20 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
     while (have) {
         // ---- the slice's tables: warp w fills byte values w, w + NW, ...
         {
-            if (k_item > 0) {
-#pragma unroll
-                for (int t = 0; t < 4; ++t)
-                    xh[t] = *reinterpret_cast<const __half2*>(p.x + s * kXtabCols + xcol + 8 * t);
-            }
+            if (k_item > 0) load_x(s);
             float x0[4], x1[4];
+            if (p.xgu) {   // rounded as the SwiGLU glue kernel rounds it
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                x0[t] = __low2float(xh[t]);
-                x1[t] = __high2float(xh[t]);
+                for (int t = 0; t < 4; ++t) {
+                    x0[t] = __half2float(__float2half_rn(swiglu_silu(xg[t].x) * xu[t].x));
+                    x1[t] = __half2float(__float2half_rn(swiglu_silu(xg[t].y) * xu[t].y));
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    x0[t] = __low2float(xh[t]);
+                    x1[t] = __high2float(xh[t]);
+                }
             }
             for (int b = warp; b < 256; b += NW) {
                 const float t0 = c_nf4_table[b & 15], t1 = c_nf4_table[b >> 4];

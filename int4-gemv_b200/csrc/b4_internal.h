@@ -57,8 +57,15 @@ int split_plan(const GemvProblem& p, const b4_gemv_config& cfg, SplitPlan* plan)
 // (16-byte aligned, at least the plan's ws_bytes, counters zero).
 int launch_split(const GemvProblem& p, const b4_gemv_config& cfg, void* ws, size_t ws_bytes, cudaStream_t st);
 
-// The workspace rule: default_config, switched to a split config (B4_FLAG_SPLIT)
-// for batch-1 matrices with too few rows to balance whole-row tiles.
+// The workspace rule: default_config, switched to the x-pair table kernel for
+// large NF4 matrices at batch 1 and to column slices (B4_FLAG_KSLICE) for
+// small batches of long rows.
 void default_config_ws(const GemvProblem& p, b4_gemv_config* cfg);
+
+// An NF4 shard at batch 1 on the x-pair table kernel when the workspace rule
+// takes its shape: y = the shard's partial GEMV (x fp16, or fp16(silu(gate) *
+// up) of fp32 gate/up rows when xgu is set), ws = the kernel's 256-byte
+// counters.  cudaErrorNotSupported when the rule does not take the shape.
+int launch_xtab_shard(const GemvProblem& p, const float* xgu, int flags, void* ws, cudaStream_t st);
 
 }  // namespace b4

@@ -19,6 +19,11 @@ struct b4_p2p {
     char* base = nullptr;                 // this rank's allocation
     char* peers[kP2pMaxRanks] = {};      // every rank's allocation as mapped here (own at [rank])
     size_t recv_bytes = 0, bytes = 0;
+    // after the receive slots: 256 bytes of call counter and error word, 256
+    // bytes of x-pair table kernel counters, then max_rows floats of this
+    // rank's partial y (the NF4 shard's GEMV before the all-reduce)
+    void* xtab_ws() const { return base + recv_bytes + 256; }
+    float* partial() const { return reinterpret_cast<float*>(base + recv_bytes + 512); }
 };
 
 namespace {
@@ -35,6 +40,31 @@ P2pArgs args_of(const b4_p2p* h)
     a.world = h->world;
     a.max_rows = h->max_rows;
     return a;
+}
+
+// The all-reduce of a row-parallel shard's partial y (part) over the ranks'
+// peer memory, as its own launch (after a GEMV that cannot carry it in its
+// epilogue): warp w of CTA c pushes rows 32 (8c + w) + 32 * 8 * gridDim.x * i
+// of this rank to every rank's slots, then sums every rank's copy of them in
+// rank order into y (and y16).  A programmatic dependent of the GEMV: it waits
+// for the GEMV's grid before it reads part.  A CTA waits only for the CTA of
+// the same index on the peers, and the grid (rows / 256 CTAs of 8 warps) is
+// small enough to be resident at once.
+__global__ void __launch_bounds__(256) p2p_allreduce_kernel(const P2pArgs a, const float* __restrict__ part,
+                                                             float* __restrict__ y, int rows)
+{
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t epoch = p2p_epoch(a);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int step = 32 * 8 * (int)gridDim.x;
+    for (int r0 = 32 * (8 * (int)blockIdx.x + warp); r0 < rows; r0 += step) {
+        const int n = min(32, rows - r0);
+        p2p_push(a, epoch, r0, n, lane < n ? part[r0 + lane] : 0.0f);
+    }
+    for (int r0 = 32 * (8 * (int)blockIdx.x + warp); r0 < rows; r0 += step) p2p_reduce(a, epoch, r0, min(32, rows - r0), y);
+    __syncthreads();   // every warp of the CTA has read the epoch
+    if (threadIdx.x == 0) p2p_finish(a, epoch);
 }
 
 }  // namespace
@@ -56,7 +86,7 @@ int b4_p2p_create(int rank, int world, int max_rows, b4_p2p** out)
     h->world = world;
     h->max_rows = max_rows;
     h->recv_bytes = (size_t)2 * world * max_rows * sizeof(unsigned long long);
-    h->bytes = h->recv_bytes + 256;
+    h->bytes = h->recv_bytes + 512 + (size_t)max_rows * sizeof(float);
     e = cudaMalloc(&h->base, h->bytes);
     if (e == cudaSuccess) e = cudaMemset(h->base, 0, h->bytes);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -142,7 +172,34 @@ int b4_tp_gemv_p2p_ex(int fmt, const uint32_t* qw_shard, const void* scale_shard
     a.y16 = static_cast<__half*>(y16);
     a.xgu = swiglu ? static_cast<const float*>(x_shard) : nullptr;
     const int lf = flags & B4_FLAG_PDL;
-    if (fmt == B4_FMT_NF4_B64) return launch_nf4_mma_p2p(p, a, lf, reinterpret_cast<cudaStream_t>(stream));
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (fmt == B4_FMT_NF4_B64) {
+        // shards the x-pair table kernel takes: that GEMV into this rank's
+        // partial y, then the all-reduce as its own launch (the kernel adds
+        // its slices' shares with atomics, so no CTA of it holds a finished
+        // row to push)
+        if (out_f <= h->max_rows) {
+            GemvProblem q = p;
+            q.y = h->partial();
+            e = launch_xtab_shard(q, a.xgu, lf, h->xtab_ws(), st);
+            if (e == cudaSuccess) {
+                a.xgu = nullptr;
+                cudaLaunchConfig_t lc = {};
+                lc.gridDim = dim3((unsigned)((out_f + 255) / 256));
+                lc.blockDim = dim3(256);
+                lc.stream = st;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+                attr[0].val.programmaticStreamSerializationAllowed = 1;
+                lc.attrs = attr;
+                lc.numAttrs = 1;
+                return cudaLaunchKernelEx(&lc, p2p_allreduce_kernel, a, static_cast<const float*>(h->partial()), y,
+                                          out_f);
+            }
+            if (e != cudaErrorNotSupported) return e;
+        }
+        return launch_nf4_mma_p2p(p, a, lf, st);
+    }
     b4_gemv_config c;
     default_config(p, &c);
     c.flags = lf;

@@ -97,34 +97,37 @@ __device__ __forceinline__ void p2p_push(const P2pArgs& a, uint32_t epoch, int r
 
 // Lane i < nrows waits for row r0 + i from every rank in this rank's own slots
 // and stores their sum, in rank order, into y[r0 + i].  Called by a whole warp.
+// Every rank's slot is read at once (one memory round trip when the rows are
+// there, not one per rank); only the ranks not yet arrived are polled again.
 __device__ __forceinline__ void p2p_reduce(const P2pArgs& a, uint32_t epoch, int r0, int nrows, float* y)
 {
     const int lane = threadIdx.x & 31;
     if (lane < nrows) {
         const unsigned long long* mine = a.recv[a.rank] + (size_t)(epoch & 1u) * a.world * a.max_rows + r0 + lane;
+        unsigned long long w[kP2pMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kP2pMaxRanks; ++r)
+            if (r < a.world) w[r] = ld_relaxed_sys_u64(mine + (size_t)r * a.max_rows);
         float s = 0.0f;
-        for (int r = 0; r < a.world; ++r) {
-            const unsigned long long* slot = mine + (size_t)r * a.max_rows;
-            unsigned long long w = ld_relaxed_sys_u64(slot);
+        bool ok = true;
+#pragma unroll
+        for (int r = 0; r < kP2pMaxRanks; ++r) {
+            if (r >= a.world || !ok) continue;
             long long n = 0;
-            bool arrived = true;
-            while ((uint32_t)(w >> 32) != epoch) {
+            while ((uint32_t)(w[r] >> 32) != epoch) {
                 // give up after kP2pMaxSpins polls, or at once when another wait
                 // of this call already gave up (a missing peer costs one timeout)
                 if (++n >= kP2pMaxSpins || ((n & 63) == 0 && *(volatile const uint32_t*)a.error)) {
                     atomicOr(a.error, kP2pErrTimeout);
-                    arrived = false;
+                    ok = false;
                     break;
                 }
                 __nanosleep(64);
-                w = ld_relaxed_sys_u64(slot);
+                w[r] = ld_relaxed_sys_u64(mine + (size_t)r * a.max_rows);
             }
-            if (!arrived) {
-                s = __int_as_float(0x7fffffff);   // a row with a missing rank is NaN, never a partial sum
-                break;
-            }
-            s += __uint_as_float((uint32_t)w);
+            if (ok) s += __uint_as_float((uint32_t)w[r]);
         }
+        if (!ok) s = __int_as_float(0x7fffffff);   // a row with a missing rank is NaN, never a partial sum
         y[r0 + lane] = s;
         if (a.y16) a.y16[r0 + lane] = __float2half_rn(s);
     }
