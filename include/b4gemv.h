@@ -374,7 +374,7 @@ int b4_tp_gemv_allreduce_ws(int fmt, const uint32_t* qw_shard, const void* scale
  * their rows of y are NaN, b4_p2p_status reports B4_STATUS_TIMEOUT, and the
  * GPU stays usable (then destroy and re-create the b4_p2p on every rank: the
  * call counters disagree).  Set-up, once per rank and device: b4_p2p_create
- * (one device allocation of 16 * world * max_rows + 4 * max_rows + 512 bytes, max_rows >=
+ * (one device allocation of 16 * world * max_rows + 4 * max_rows + 16896 bytes, max_rows >=
  * the out_f of every call), b4_p2p_ipc_handle -> send the 64-byte handle to
  * every peer -> b4_p2p_open_peer for each peer's handle.  One process per GPU
  * (CUDA IPC).  Every rank must make the same sequence of calls; the call

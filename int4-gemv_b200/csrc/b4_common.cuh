@@ -198,10 +198,16 @@ __device__ __forceinline__ void stage_x_words(const __half* x, int n, bool vec, 
 
 constexpr int kXUnroll = 8;   // x words in flight per thread while staging
 
-// The gated activation of the decode layer's MLP: silu(g) = g / (1 + e^-g).
-// The SwiGLU glue kernel and the GEMVs that compute their x from gate/up
-// rows use this one definition, so both round the same way.
-__device__ __forceinline__ float swiglu_silu(float g) { return g / (1.0f + expf(-g)); }
+// The gated activation of the decode layer's MLP: silu(g) = g / (1 + e^-g),
+// with the hardware exponential (__expf) and the approximate divide
+// (__fdividef): a few instructions, where expf and an IEEE divide cost tens,
+// which matters because every CTA of a GEMV that stages its x from gate/up
+// rows computes all in_f of them.  The relative error stays near 2^-20 for
+// |g| < 20 (far below the fp16 rounding of x that follows); a g below about
+// -87 gives -0 (the true value is below 1e-36).  The SwiGLU glue kernel and the
+// GEMVs that compute their x from gate/up rows use this one definition, so
+// both round the same way.
+__device__ __forceinline__ float swiglu_silu(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // stage_x_words for an x computed as fp16(silu(gate[k]) * up[k]) from fp32
 // gate = gu[0 .. n_words * 8), up = gu[n_words * 8 ..): gu 16-byte aligned.

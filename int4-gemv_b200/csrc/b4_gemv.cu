@@ -667,6 +667,7 @@ cudaError_t launch_persistent(void* fn, void* params, long long tiles, int threa
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem);
         if (e != cudaSuccess) return e;
         grid = std::min<long long>(grid, (long long)sm_count_cached(dev) * occ);
+        if (grid > kP2pEpochSlots) return cudaErrorInvalidValue;   // one call-counter copy per CTA
     }
     if (grid < 1) return cudaErrorInvalidValue;
     cudaLaunchConfig_t lc = {};

@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (P2P && p.p2p.xgu)   // x = the SwiGLU of this rank's gate/up rows
-        stage_x_swiglu<2>(p.p2p.xgu, words, [&](int w, uint4 v) { xs[w] = int4_pair_order(v); });
+        stage_x_swiglu<4>(p.p2p.xgu, words, [&](int w, uint4 v) { xs[w] = int4_pair_order(v); });
     else
         stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w] = int4_pair_order(v); });
     __syncthreads();
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_lean_kernel(const LeanParams p
             }
         }
         __syncthreads();   // every warp of the CTA has read the epoch
-        if (threadIdx.x == 0) p2p_finish(p.p2p, epoch);
+        p2p_finish(p.p2p, epoch);
     }
 }
 

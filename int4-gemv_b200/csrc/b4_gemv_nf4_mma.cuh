@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
     // slots 4q + i (+ 16 per step), and without the swap lanes q and q + 2 hit
     // the same banks (two wavefronts per load instead of one)
     if (P2P && p.p2p.xgu)   // x = the SwiGLU of this rank's gate/up rows
-        stage_x_swiglu<2>(p.p2p.xgu, words, [&](int w, uint4 v) { xs[w ^ ((w >> 2) & 2)] = v; });
+        stage_x_swiglu<(D >= 4 ? 2 : 4)>(p.p2p.xgu, words, [&](int w, uint4 v) { xs[w ^ ((w >> 2) & 2)] = v; });
     else
         stage_x_words<kXUnroll>(p.x, words, p.x_vec, [&](int w, uint4 v) { xs[w ^ ((w >> 2) & 2)] = v; });
     __syncthreads();
@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(256, 2) b4_gemv_nf4_mma_kernel(const LeanNf4Pa
             }
         }
         __syncthreads();   // every warp of the CTA has read the epoch
-        if (threadIdx.x == 0) p2p_finish(p.p2p, epoch);
+        p2p_finish(p.p2p, epoch);
     }
 }
 

@@ -5,6 +5,7 @@
 // the caller has (the Python layer uses torch.distributed), and each peer
 // maps it with cudaIpcOpenMemHandle.  Kernels only ever store to peers and
 // read their own memory; every wait in them is bounded.
+#include <algorithm>
 #include <cstring>
 #include <new>
 
@@ -19,11 +20,15 @@ struct b4_p2p {
     char* base = nullptr;                 // this rank's allocation
     char* peers[kP2pMaxRanks] = {};      // every rank's allocation as mapped here (own at [rank])
     size_t recv_bytes = 0, bytes = 0;
-    // after the receive slots: 256 bytes of call counter and error word, 256
-    // bytes of x-pair table kernel counters, then max_rows floats of this
-    // rank's partial y (the NF4 shard's GEMV before the all-reduce)
-    void* xtab_ws() const { return base + recv_bytes + 256; }
-    float* partial() const { return reinterpret_cast<float*>(base + recv_bytes + 512); }
+    // after the receive slots: 256 bytes holding the error word, the call
+    // counter's kP2pEpochSlots copies, 256 bytes of x-pair table kernel
+    // counters, then max_rows floats of this rank's partial y (the NF4
+    // shard's GEMV before the all-reduce)
+    static constexpr size_t kEpochBytes = kP2pEpochSlots * sizeof(uint32_t);
+    uint32_t* error_word() const { return reinterpret_cast<uint32_t*>(base + recv_bytes); }
+    uint32_t* epochs() const { return reinterpret_cast<uint32_t*>(base + recv_bytes + 256); }
+    void* xtab_ws() const { return base + recv_bytes + 256 + kEpochBytes; }
+    float* partial() const { return reinterpret_cast<float*>(base + recv_bytes + 512 + kEpochBytes); }
 };
 
 namespace {
@@ -32,10 +37,8 @@ P2pArgs args_of(const b4_p2p* h)
 {
     P2pArgs a = {};
     for (int r = 0; r < h->world; ++r) a.recv[r] = reinterpret_cast<unsigned long long*>(h->peers[r]);
-    uint32_t* tail = reinterpret_cast<uint32_t*>(h->base + h->recv_bytes);
-    a.epoch = tail;
-    a.done = tail + 1;
-    a.error = tail + 2;
+    a.epochs = h->epochs();
+    a.error = h->error_word();
     a.rank = h->rank;
     a.world = h->world;
     a.max_rows = h->max_rows;
@@ -64,7 +67,7 @@ __global__ void __launch_bounds__(256) p2p_allreduce_kernel(const P2pArgs a, con
     }
     for (int r0 = 32 * (8 * (int)blockIdx.x + warp); r0 < rows; r0 += step) p2p_reduce(a, epoch, r0, min(32, rows - r0), y);
     __syncthreads();   // every warp of the CTA has read the epoch
-    if (threadIdx.x == 0) p2p_finish(a, epoch);
+    p2p_finish(a, epoch);
 }
 
 }  // namespace
@@ -86,7 +89,7 @@ int b4_p2p_create(int rank, int world, int max_rows, b4_p2p** out)
     h->world = world;
     h->max_rows = max_rows;
     h->recv_bytes = (size_t)2 * world * max_rows * sizeof(unsigned long long);
-    h->bytes = h->recv_bytes + 512 + (size_t)max_rows * sizeof(float);
+    h->bytes = h->recv_bytes + 512 + b4_p2p::kEpochBytes + (size_t)max_rows * sizeof(float);
     e = cudaMalloc(&h->base, h->bytes);
     if (e == cudaSuccess) e = cudaMemset(h->base, 0, h->bytes);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -127,7 +130,7 @@ int b4_p2p_open_peer(b4_p2p* h, int peer, const void* handle64)
 int b4_p2p_status(b4_p2p* h, int clear)
 {
     if (!h) return cudaErrorInvalidValue;
-    uint32_t* err = reinterpret_cast<uint32_t*>(h->base + h->recv_bytes) + 2;
+    uint32_t* err = h->error_word();
     uint32_t v = 0;
     cudaError_t e = cudaMemcpy(&v, err, sizeof(v), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return e;
@@ -185,7 +188,7 @@ int b4_tp_gemv_p2p_ex(int fmt, const uint32_t* qw_shard, const void* scale_shard
             if (e == cudaSuccess) {
                 a.xgu = nullptr;
                 cudaLaunchConfig_t lc = {};
-                lc.gridDim = dim3((unsigned)((out_f + 255) / 256));
+                lc.gridDim = dim3((unsigned)std::min((out_f + 255) / 256, kP2pEpochSlots));
                 lc.blockDim = dim3(256);
                 lc.stream = st;
                 cudaLaunchAttribute attr[1];

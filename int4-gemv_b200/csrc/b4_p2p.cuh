@@ -3,8 +3,9 @@
 //
 // Each rank holds one device allocation (exported through CUDA IPC and mapped
 // by every peer):
-//   recv  uint64 [2][world][max_rows]   (epoch << 32) | fp32 bits of a partial row
-//   epoch uint32, done uint32, error uint32
+//   recv    uint64 [2][world][max_rows]   (epoch << 32) | fp32 bits of a partial row
+//   error   uint32
+//   epochs  uint32 [kP2pEpochSlots]       the call counter, one copy per CTA index
 // indexed first by the call's parity (epoch & 1), so a rank may start call
 // e+1 while a peer still reads call e's slots (call e+2 can only start after
 // every peer has finished call e: it needs their call e+1 rows, which they
@@ -23,10 +24,13 @@
 // call has given up, it records kP2pErrTimeout in the error word and stores
 // NaN for that row), sums the ranks in rank order and stores y.  Every rank
 // adds the same numbers in the same order: y is bit-identical on all ranks.
-// The epoch lives in device memory: every CTA reads it after
-// griddepcontrol.wait (the previous call has completed) and the last CTA to
-// finish advances it, so a call captured in a CUDA graph stays correct when
-// the graph is replayed.
+// The call counter lives in device memory, one copy per CTA index: CTA c
+// reads copy c after griddepcontrol.wait (every earlier call has completed,
+// so a plain load sees its value) and, as it leaves, writes the advanced
+// value into copies c, c + G, c + 2G, ... (G = the grid), so every call
+// advances all copies and calls of different grid sizes agree, with no
+// atomic and no fence on the way out.  Only CTA c reads copy c during a
+// call.  A call captured in a CUDA graph stays correct when it is replayed.
 #pragma once
 
 #include <cstdint>
@@ -37,11 +41,11 @@ namespace b4 {
 constexpr int kP2pMaxRanks = 8;
 constexpr uint32_t kP2pErrTimeout = 1u;
 constexpr long long kP2pMaxSpins = 1ll << 22;   // x ~0.2-1 us per poll: one to a few seconds
+constexpr int kP2pEpochSlots = 4096;            // copies of the call counter: the largest grid of a P2P launch
 
 struct P2pArgs {
     unsigned long long* recv[kP2pMaxRanks];   // every rank's slots (this rank's own at [rank])
-    uint32_t* epoch;                          // this rank's call counter
-    uint32_t* done;                           // CTAs of this call that have finished
+    uint32_t* epochs;                         // this rank's call counter, kP2pEpochSlots copies
     uint32_t* error;                          // this rank's error word
     int rank, world;
     int max_rows;
@@ -49,18 +53,6 @@ struct P2pArgs {
     const float* xgu;    // optional: x = fp16(silu(gate) * up) of fp32 gate = xgu[0 .. in_f),
                          // up = xgu[in_f .. 2 in_f), computed while x is staged
 };
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
-{
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p)
-{
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v)
 {
@@ -74,10 +66,10 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
     return v;
 }
 
-// The epoch of this call (read once per CTA, after griddepcontrol.wait).
+// The epoch of this call (read by the CTA's threads after griddepcontrol.wait).
 __device__ __forceinline__ uint32_t p2p_epoch(const P2pArgs& a)
 {
-    return ld_acquire_sys(a.epoch) + 1u;
+    return *(volatile const uint32_t*)(a.epochs + blockIdx.x) + 1u;
 }
 
 // Lane i < nrows holds row r0 + i of this rank's partial y in v: store it into
@@ -133,15 +125,12 @@ __device__ __forceinline__ void p2p_reduce(const P2pArgs& a, uint32_t epoch, int
     }
 }
 
-// The last CTA of the call to finish advances the epoch (called by thread 0 of
-// every CTA after its last block).
+// The CTA advances its copies of the call counter (called by every thread of
+// the CTA, after a barrier that follows every thread's p2p_epoch).
 __device__ __forceinline__ void p2p_finish(const P2pArgs& a, uint32_t epoch)
 {
-    __threadfence();
-    if (atomicAdd(a.done, 1u) == gridDim.x - 1) {
-        *a.done = 0;
-        st_release_sys(a.epoch, epoch);
-    }
+    for (int i = blockIdx.x + threadIdx.x * gridDim.x; i < kP2pEpochSlots; i += blockDim.x * gridDim.x)
+        a.epochs[i] = epoch;
 }
 
 }  // namespace b4

@@ -519,3 +519,34 @@ def test_p2p_ex_folds_the_glue_bit_identically(cuda, fmt, out_f, in_f):
         assert lib.b4_p2p_status(h, 1) == 0
     finally:
         lib.b4_p2p_destroy(h)
+
+
+def test_swiglu_glue_is_within_one_fp16_step_of_silu(cuda):
+    """b4_swiglu_f16 (the silu of the decode layer's MLP, the same code the
+    GEMVs with B4_FLAG_X_SWIGLU run while staging x) against silu(g) * u in
+    double precision, over g in [-100, 100]: every element within one fp16 step
+    of the exact value (the device silu is the fast exponential and divide,
+    its error far below fp16's), and g below -87 gives 0."""
+    import ctypes
+
+    import torch
+
+    from b4gemv._lib import load
+    lib = load()
+    n = 1 << 16
+    g = torch.Generator(device=cuda)
+    g.manual_seed(4)
+    gate = torch.cat([torch.linspace(-100.0, 100.0, n // 2, device=cuda),
+                      torch.randn((n // 2,), generator=g, device=cuda) * 4.0])
+    up = torch.randn((n,), generator=g, device=cuda) * 2.0
+    out = torch.empty((n,), dtype=torch.float16, device=cuda)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    assert lib.b4_swiglu_f16(P(gate), P(up), P(out), n, st) == 0
+    torch.cuda.synchronize()
+    gd, ud = gate.double().cpu(), up.double().cpu()
+    exact = gd / (1.0 + torch.exp(-gd)) * ud
+    got = out.double().cpu()
+    step = torch.clamp(exact.abs(), min=2.0 ** -14) * 2.0 ** -10
+    assert ((got - exact).abs() <= step).all(), float(((got - exact).abs() / step).max())
+    assert (got[gd < -87.5] == 0).all()
