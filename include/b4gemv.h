@@ -119,8 +119,8 @@ typedef struct b4_gemv_config {
  * scaled by their absmax, and the slices' shares of y are added in y with
  * fp32 atomics after every CTA has zeroed its rows (order of the slice
  * additions varies from run to run).  Needs a workspace (b4_gemv_ws,
- * b4_gemv_multi_ws) of B4_XTAB_WORKSPACE_BYTES: two counters, zero between
- * calls.  Codes and absmax 16-byte aligned.  row_groups = warps per CTA and
+ * b4_gemv_multi_ws) of B4_XTAB_WORKSPACE_BYTES: two running counters (the
+ * call's arrivals and their running base), equal between calls.  Codes and absmax 16-byte aligned.  row_groups = warps per CTA and
  * stages = batches of 16 rows each warp keeps in flight: (8, 4), (12, 2),
  * (12, 3), (16, 2), (20, 1) or (24, 1); the other fields are ignored. */
 #define B4_ENGINE_NF4_XTAB 8
@@ -144,8 +144,8 @@ typedef struct b4_gemv_config {
  * on B4_ENGINE_MMA_NF4), run them as the segments of one small-batch launch
  * (x staged per slice, so long rows of a whole batch fit in shared memory and
  * row blocks x slices spread over every SM), and sum the slices' partial y in
- * a fixed order in a second launch.  Needs a workspace of
- * slices * m * out_f * 4 bytes; only b4_gemv_ws takes it. */
+ * a fixed order in a second launch, which clears them.  Needs a workspace of
+ * 256 + slices * m * out_f * 4 bytes; only b4_gemv_ws takes it. */
 #define B4_FLAG_KSLICE 8
 
 /* ---- GEMV: y[b][r] = sum_k dequant(W)[r][k] * x[b][k], b < m ----------------
@@ -201,10 +201,15 @@ int b4_gemv_ex(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
  * b4_gemv_workspace_size: bytes of workspace the call with these arguments
  * needs on the current device (0 when the config needs none; cfg NULL or
  * B4_ENGINE_AUTO = the rule of b4_gemv_ws).  ws: device memory, 16-byte aligned, at least that
- * size, ZERO-FILLED before its first use (cudaMemset); every call leaves it
- * zeroed again, so it can be reused by later calls and by CUDA-graph
- * replays.  Calls that may run at the same time (different streams) need
- * different workspaces.  A workspace that is too small returns
+ * size, ZERO-FILLED before its first use (cudaMemset).  Its first
+ * B4_XTAB_WORKSPACE_BYTES hold the x-pair table kernel's running counters
+ * (left equal by every call); the split and k-slice paths use the bytes after
+ * them and leave zero what a later call expects zero (the split path's
+ * arrival counters; the k-slice partials are cleared once summed).  So one
+ * workspace serves every path, later
+ * calls and CUDA-graph replays, as long as it is not cleared or written
+ * between calls other than by zero-filling all of it.  Calls that may run at
+ * the same time (different streams) need different workspaces.  A workspace that is too small returns
  * cudaErrorInvalidValue before anything is launched. */
 int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_config* cfg, size_t* bytes);
 /* The dispatch rule of b4_gemv_ws (cfg NULL): the x-pair table kernel for NF4

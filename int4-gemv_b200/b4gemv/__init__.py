@@ -177,8 +177,11 @@ def workspace_size(fmt: int, in_f: int, out_f: int, m: int = 1, config: dict | N
 def workspace(device, nbytes: int):
     """The package's workspace for b4_gemv_ws on `device`: one zero-filled
     uint8 tensor per device, grown on demand (at least 1 MiB).  Every call
-    leaves it zeroed.  Calls on different streams that may overlap must not
-    share it: pass them their own (torch.zeros(n, dtype=torch.uint8))."""
+    leaves it ready for the next (the x-pair table kernel's running counters
+    in the first 256 bytes, the split path's counters zero after them).
+    Calls on different streams
+    that may overlap must not share it: pass them their own
+    (torch.zeros(n, dtype=torch.uint8))."""
     import torch
     dev = torch.device(device)
     idx = dev.index if dev.index is not None else torch.cuda.current_device()

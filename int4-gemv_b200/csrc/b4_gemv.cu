@@ -1005,8 +1005,9 @@ int launch_gemv_multi(int fmt, const b4_gemv_segment* segs, int nseg, const void
 // ---- k-sliced small batches ----------------------------------------------------
 
 // y[i] = part[0][i] + ... + part[S - 1][i] (fixed order), as a programmatic
-// dependent of the sliced GEMV.
-__global__ void slice_sum_kernel(const float* __restrict__ part, float* __restrict__ y, long long n, int S)
+// dependent of the sliced GEMV; the partials are zeroed once read, so the
+// workspace is left as b4_gemv_ws found it.
+__global__ void slice_sum_kernel(float* __restrict__ part, float* __restrict__ y, long long n, int S)
 {
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1014,6 +1015,7 @@ __global__ void slice_sum_kernel(const float* __restrict__ part, float* __restri
         float t = part[i];
         for (int s = 1; s < S; ++s) t += part[(long long)s * n + i];
         y[i] = t;
+        for (int s = 0; s < S; ++s) part[(long long)s * n + i] = 0.0f;
     }
 }
 
@@ -1081,7 +1083,7 @@ int launch_ksliced(const GemvProblem& p, const b4_gemv_config& c, void* ws, size
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    return cudaLaunchKernelEx(&lc, slice_sum_kernel, static_cast<const float*>(part), p.y, n, S);
+    return cudaLaunchKernelEx(&lc, slice_sum_kernel, part, p.y, n, S);
 }
 
 // ---- x-pair table NF4 launches (b4_gemv_xtab.cuh) --------------------------------
@@ -1102,7 +1104,7 @@ bool xtab_buffers(const b4_gemv_segment* segs, int nseg)
 // One launch of the x-pair table NF4 kernel over nseg weight matrices sharing
 // x (batch 1): one CTA per SM, all resident at once (the start-of-kernel
 // count-in waits for every CTA), the workspace's first 8 bytes as its two
-// counters (zero between calls).
+// running counters (equal between calls; zero-filled before the first).
 int launch_xtab_segs(const b4_gemv_segment* segs, int nseg, const void* x, int in_f, const b4_gemv_config& c,
                      void* ws, size_t ws_bytes, cudaStream_t st, const float* xgu)
 {
@@ -1448,6 +1450,20 @@ int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_confi
     return cudaSuccess;
 }
 
+// The workspace of b4_gemv_ws: its first B4_XTAB_WORKSPACE_BYTES hold the
+// x-pair table kernel's running counters, the split and k-slice paths use
+// what follows (their counters and partials are zero between calls), so one
+// workspace may serve every path.
+void* ws_past_counters(void* ws, size_t ws_bytes, size_t* rest)
+{
+    if (!ws || ws_bytes < B4_XTAB_WORKSPACE_BYTES) {
+        *rest = 0;
+        return nullptr;
+    }
+    *rest = ws_bytes - B4_XTAB_WORKSPACE_BYTES;
+    return static_cast<char*>(ws) + B4_XTAB_WORKSPACE_BYTES;
+}
+
 int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_config* cfg, size_t* bytes)
 {
     if (!bytes) return cudaErrorInvalidValue;
@@ -1467,14 +1483,14 @@ int b4_gemv_workspace_size(int fmt, int in_f, int out_f, int m, const b4_gemv_co
     if (c.flags & B4_FLAG_KSLICE) {
         int S = 0;
         if (!ksliced_shape(p, c, &S)) return cudaErrorInvalidValue;
-        *bytes = ksliced_ws_bytes(p, S);
+        *bytes = B4_XTAB_WORKSPACE_BYTES + ksliced_ws_bytes(p, S);
         return cudaSuccess;
     }
     if (!(c.flags & B4_FLAG_SPLIT)) return cudaSuccess;
     SplitPlan s;
     e = split_plan(p, c, &s);
     if (e != cudaSuccess) return e;
-    *bytes = s.ws_bytes;
+    *bytes = B4_XTAB_WORKSPACE_BYTES + s.ws_bytes;
     return cudaSuccess;
 }
 
@@ -1485,13 +1501,15 @@ int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
     int e = check_problem(p);
     if (e != cudaSuccess) return e;
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    size_t rest = 0;
+    void* const tail = ws_past_counters(ws, ws_bytes, &rest);
     if (!cfg || cfg->engine == B4_ENGINE_AUTO) {
         b4_gemv_config c;
         default_config_ws(p, &c);
         const int pdl = cfg ? cfg->flags & B4_FLAG_PDL : 0;
         if (c.flags & B4_FLAG_KSLICE) {
             c.flags |= pdl;
-            return launch_ksliced(p, c, ws, ws_bytes, st);
+            return launch_ksliced(p, c, tail, rest, st);
         }
         if (c.engine != B4_ENGINE_NF4_XTAB)   // the rule of b4_gemv_ws never splits
             return launch_default(p, pdl, st);
@@ -1499,8 +1517,8 @@ int b4_gemv_ws(int fmt, const uint32_t* qw, const void* scale, const void* x, fl
         return launch_gemv_xtab(p, c, ws, ws_bytes, st);
     }
     if (cfg->engine == B4_ENGINE_NF4_XTAB) return launch_gemv_xtab(p, *cfg, ws, ws_bytes, st);
-    if (cfg->flags & B4_FLAG_SPLIT) return launch_split(p, *cfg, ws, ws_bytes, st);
-    if (cfg->flags & B4_FLAG_KSLICE) return launch_ksliced(p, *cfg, ws, ws_bytes, st);
+    if (cfg->flags & B4_FLAG_SPLIT) return launch_split(p, *cfg, tail, rest, st);
+    if (cfg->flags & B4_FLAG_KSLICE) return launch_ksliced(p, *cfg, tail, rest, st);
     return launch_gemv(p, *cfg, st);
 }
 

@@ -55,12 +55,19 @@
 // fire and forget: no cross-CTA wait at the end of the kernel).  y must be zero
 // first: each CTA zeroes its share of y's rows right after the grid-dependency
 // wait and, once its first tables are built, counts itself in on a workspace
-// counter (a release reduction); a warp keeps the results of its first
-// kXtabHold batches in registers and waits (bounded) for all G arrivals before
-// its first add, which by then has normally happened, so the count-in is off
-// the critical path.  The last CTA to leave resets the two counters, so the
-// workspace is zero between calls.  Summation order across slices therefore
-// varies from run to run (within fp32 rounding); everything else is fixed.
+// counter; a warp keeps the results of its first kXtabHold batches in
+// registers and waits (bounded) for all G arrivals of this call before its
+// first add, which by then has normally happened, so the count-in is off the
+// critical path.  The workspace holds two running counters, arrivals and
+// base (the arrivals of all earlier calls): a call's CTAs read base after the
+// grid-dependency wait and wait for arrivals to reach base + G (compared
+// modulo 2^32); the CTA whose count-in completes the call (an acq_rel atomic
+// that returns the old count) advances base by G.  Every CTA has read base
+// before it counts in, so no read can see the advanced value, and nothing
+// happens on the way out: no fence, no atomic, no reset.  Between calls the
+// two counters are equal (zero-filled to start with).  Summation order across
+// slices varies from run to run (within fp32 rounding); everything else is
+// fixed.
 //
 // Waits: the arrival wait is the only one.  It is bounded (kXtabMaxPolls polls
 // with a short sleep); when it runs out the kernel raises its device error
@@ -103,7 +110,7 @@ struct XtabParams {
     int in_f;
     int nslice;          // in_f / 256
     const __half* x;
-    unsigned* bar;       // workspace: [0] arrivals, [1] departures; zero between calls
+    unsigned* bar;       // workspace: [0] arrivals, [1] base (equal between calls)
     uint32_t smem;       // dynamic shared memory of the launch (bytes)
     const float* xgu;    // non-null: x = fp16(silu(gate) * up) of fp32 gate = xgu[0 .. in_f), up = xgu[in_f ..)
 };
@@ -118,9 +125,23 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
     return v;
 }
 
-__device__ __forceinline__ void red_release_add_u32(unsigned* p, unsigned v)
+__device__ __forceinline__ unsigned atom_acq_rel_add_u32(unsigned* p, unsigned v)
 {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void red_relaxed_add_u32(unsigned* p, unsigned v)
+{
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // fire-and-forget fp32 add in L2 (a generic-address atomicAdd compiles to a
@@ -370,10 +391,11 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
     // (first item's) wait comes after them, by when the count is normally
     // complete.
     bool counted_in = false;
+    unsigned target = 0u;   // this call's arrivals end at base + G (set after the grid-dependency wait)
     auto wait_count = [&]() {
         if (lane == 0) {
             unsigned n = 0;
-            while (ld_acquire_u32(&p.bar[0]) < (unsigned)G) {
+            while ((int)(ld_acquire_u32(&p.bar[0]) - target) < 0) {
                 if (++n >= kXtabMaxPolls) {
                     atomicOr(&g_xtab_error, kErrXtabBarrier);
                     break;
@@ -397,6 +419,14 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
     });
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // base is read before this CTA counts in
+    target = ld_relaxed_u32(&p.bar[1]) + (unsigned)G;
+    // the count-in: the CTA that completes the call advances base (old is
+    // only looked at later, so the atomic's round trip is not waited for)
+    auto count_in = [&]() { return atom_acq_rel_add_u32(&p.bar[0], 1u); };
+    auto close_call = [&](unsigned old) {
+        if (old == target - 1u) red_relaxed_add_u32(&p.bar[1], (unsigned)G);
+    };
 
     // x of the tables' column pairs (columns xcol + 8t and the next, t = 0..3,
     // of slice sl): fp16 x, or fp16(silu(gate) * up) from fp32 gate/up rows
@@ -429,9 +459,10 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
         }
         if (!have) {
             __syncthreads();
-            if (threadIdx.x == 0) red_release_add_u32(&p.bar[0], 1u);
+            if (threadIdx.x == 0) close_call(count_in());
         }
     }
+    unsigned arrived = 0u;   // the count-in's old value (thread 32 (NW - 1) of a CTA with work)
 
     while (have) {
         // ---- the slice's tables: warp w fills byte values w, w + NW, ...
@@ -461,7 +492,7 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
             }
         }
         __syncthreads();
-        if (k_item == 0 && threadIdx.x == 32 * (NW - 1)) red_release_add_u32(&p.bar[0], 1u);   // count in
+        if (k_item == 0 && threadIdx.x == 32 * (NW - 1)) arrived = count_in();
         // the lookups' addresses, as values defined after the barrier (the shared
         // loads are not volatile and must not move above it)
 #pragma unroll
@@ -480,6 +511,7 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
                 hr[h] = compute(std::integral_constant<int, h % P>{}, h + P < nb);
             }
         });
+        if (k_item == 0 && threadIdx.x == 32 * (NW - 1)) close_call(arrived);
         if (!counted_in) wait_count();
         xtab_unroll<0, H>([&](auto hc) {
             constexpr int h = decltype(hc)::value;
@@ -517,17 +549,6 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
             constexpr int D = decltype(dc)::value;
             if (D < nb) issue(dc);
         });
-    }
-
-    // ---- leave: the last CTA out resets the counters for the next call ------------
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned old = atomicAdd(&p.bar[1], 1u);
-        if (old == (unsigned)G - 1) {
-            atomicExch(&p.bar[0], 0u);
-            atomicExch(&p.bar[1], 0u);
-        }
     }
 }
 

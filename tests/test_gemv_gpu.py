@@ -504,11 +504,12 @@ def test_ksliced_small_batch(cuda, oracle, fmt, m, out_f, in_f, slices):
     for pdl in (False, True):
         cfg = ksliced_config(fmt, in_f, out_f, m, slices, pdl)
         n = b4gemv.workspace_size(fmt, in_f, out_f, m, cfg)
-        assert n == slices * m * out_f * 4
+        assert n == b4gemv.XTAB_WORKSPACE_BYTES + slices * m * out_f * 4
         ws = torch.zeros(n, dtype=torch.uint8, device=cuda)
         y = b4gemv.gemv_ws(fmt, qw, sc, Xd, torch.full((m, out_f), float("nan"), device=cuda), config=cfg,
                            ws=ws).cpu().numpy()
         assert rel_err(y, ref) < TOL, (pdl, cfg)
+        assert int(ws.count_nonzero()) == 0   # the partials are cleared once summed
     lib, p = b4gemv.load(), ctypes.c_void_p
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     y = torch.empty((m, out_f), device=cuda)

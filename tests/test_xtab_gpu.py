@@ -7,8 +7,9 @@ double GEMV (max relative error below TOL, the metric of int4_gemv.cu:74-81)
 on the shapes that exercise each part of that scheme: one slice, slices shared
 by 10-11 CTAs, more slices than CTAs (each CTA loops over slices), rows not a
 multiple of the 16-row batch, several segments in one launch, y pre-filled with
-NaN (every row must be zeroed), back-to-back calls (the workspace counters
-must come back to zero), and the NaN rows of the reference's edge fixture.
+NaN (every row must be zeroed), back-to-back calls (the workspace's two
+running counters, arrivals and base, must be equal between calls and advance
+by the grid each call), and the NaN rows of the reference's edge fixture.
 """
 from __future__ import annotations
 
@@ -58,13 +59,18 @@ def test_xtab_every_variant_and_launch_kind(cuda, oracle, out_f, in_f):
     ref = f64_ref(oracle, 1, qw, am, X)
     x = to_dev(X, cuda)
     ws = torch.zeros(b4gemv.XTAB_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
+    grid = torch.cuda.get_device_properties(cuda).multi_processor_count   # one CTA per SM
+    calls = 0
     for warps, stages in VARIANTS:
         for flags in (0, b4gemv.FLAG_PDL):
             y = run_xtab(qw, am, x, out_f, in_f, xtab_cfg(warps, stages, flags), ws).cpu().numpy()
+            calls += 1
             assert np.isfinite(y).all(), (out_f, in_f, warps, stages, flags)
             assert rel_err(y, ref) < TOL, (out_f, in_f, warps, stages, flags)
+            counters = ws[:8].view(torch.int32).cpu().tolist()
+            assert counters == [calls * grid] * 2, (counters, calls, grid)
     torch.cuda.synchronize()
-    assert not ws.any().item(), "the counters must be zero between calls"
+    assert not ws[8:].any().item()
     assert load().b4_device_error(1) == 0
 
 
@@ -105,6 +111,46 @@ def test_xtab_back_to_back_calls_new_inputs(cuda, oracle):
     assert rel_err(outs[0], f64_ref(oracle, 1, qw, am, X1)) < TOL
     assert rel_err(outs[1], f64_ref(oracle, 1, qw, am, X2)) < TOL
     assert rel_err(outs[2], outs[0]) < 1e-6
+
+
+def test_one_workspace_serves_every_path_in_any_order(cuda, oracle):
+    """A b4_gemv_ws workspace keeps the x-pair table kernel's running counters
+    in its first 256 bytes and hands the rest to the split and k-slice paths
+    (the split's arrival counters first, zero after each call; the k-slice
+    partials, cleared once summed): x-pair table, k-slice and split calls
+    alternating on one workspace all stay within tolerance, and no arrival
+    wait times out."""
+    import torch
+    from test_gemv_gpu import ksliced_config
+    from test_split_gpu import split_config
+    rng = np.random.default_rng(21)
+    W1, X1 = rand_problem(rng, 2048, 3584)
+    qw1, am1 = quantised(1, W1, cuda)
+    W2, X2 = rand_problem(rng, 300, 4096, 3)
+    qw2, am2 = quantised(1, W2, cuda)
+    W3, X3 = rand_problem(rng, 3584, 3584)
+    qw3, sc3 = quantised(0, W3, cuda)
+    c1 = xtab_cfg(16, 2, b4gemv.FLAG_PDL)
+    c2 = ksliced_config(1, 4096, 300, 3, 2, pdl=True)
+    c3 = split_config(0, 2, 4)
+    need = max(b4gemv.workspace_size(1, 3584, 2048, 1, c1), b4gemv.workspace_size(1, 4096, 300, 3, c2),
+               b4gemv.workspace_size(0, 3584, 3584, 1, c3))
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
+    refs = {"xtab": f64_ref(oracle, 1, qw1, am1, X1), "kslice": f64_ref(oracle, 1, qw2, am2, X2),
+            "split": f64_ref(oracle, 0, qw3, sc3, X3)}
+    runs = {"xtab": lambda: b4gemv.gemv_ws(1, qw1, am1, to_dev(X1, cuda), config=c1, ws=ws),
+            "kslice": lambda: b4gemv.gemv_ws(1, qw2, am2, to_dev(X2, cuda), config=c2, ws=ws),
+            "split": lambda: b4gemv.gemv_ws(0, qw3, sc3, to_dev(X3, cuda), config=c3, ws=ws)}
+    load().b4_device_error(1)
+    for name in ("xtab", "kslice", "xtab", "split", "xtab", "kslice", "split", "kslice", "xtab"):
+        y = runs[name]().cpu().numpy()
+        assert rel_err(y, refs[name]) < TOL, name
+        counters = ws[:8].view(torch.int32).cpu().tolist()
+        assert counters[0] == counters[1], (name, counters)
+        assert int(ws[256: 256 + 224 * 4].count_nonzero()) == 0, name   # the split's 224 row-block counters
+        if name == "kslice":   # its 2 slices x 3 rows x 300 partials, cleared
+            assert int(ws[256: 256 + 2 * 3 * 300 * 4].count_nonzero()) == 0
+    assert load().b4_device_error(1) == 0
 
 
 def test_xtab_multi_segment_one_launch(cuda, oracle):
