@@ -22,8 +22,12 @@
 // 256-column SLICE of in_f: 32 packed words of 4 byte positions each.  The
 // matrix is cut into (slice, 16-row batch) units.  With S = in_f/256 slices
 // and G CTAs, slice s gets G/S or G/S + 1 CTAs that split its batches evenly
-// (S > G: each CTA takes slices c, c + G, ... with every batch).  A warp takes
-// the batches b0 + warp, b0 + warp + NW, ... of its CTA's range.
+// (S > G: each CTA takes slices c, c + G, ... with every batch), or, where the
+// host finds that uneven (xtab_tail), G/S main CTAs per slice split all but
+// its last `tail` batches and the other G % S CTAs share the S tails in equal
+// runs, one item (table build) per slice a run touches.  A warp takes the
+// batches b0 + warp, b0 + warp + NW, ... of its CTA's item; the next item's
+// first batches and x are requested before the barrier that ends an item.
 //
 // Codes go straight from global memory into registers, P batches ahead, in
 // whole 128-byte lines (the lookups are then the only shared-memory traffic
@@ -113,6 +117,7 @@ struct XtabParams {
     unsigned* bar;       // workspace: [0] arrivals, [1] base (equal between calls)
     uint32_t smem;       // dynamic shared memory of the launch (bytes)
     const float* xgu;    // non-null: x = fp16(silu(gate) * up) of fp32 gate = xgu[0 .. in_f), up = xgu[in_f ..)
+    int mains, tail;     // tail > 0: mains CTAs per slice and tail batches per slice for the others (xtab_item)
 };
 
 // The device error flag of this translation unit (read by xtab_device_error).
@@ -208,9 +213,34 @@ __device__ __forceinline__ void sts_f32(uint32_t addr, float v)
 }
 
 // The k-th (slice, batch range) work item of CTA c; false when there is none.
+// tail > 0: CTAs c < mains * S are a slice's main CTAs (slice c / mains), which
+// split its first nbatch - tail batches evenly, one item each; the other E
+// CTAs split the S tails of tail batches (slice-major) into equal runs, one
+// item per slice a run touches.  Otherwise slice s gets G/S or G/S + 1 CTAs
+// that split its batches evenly (S > G: slices c, c + G, ... with every batch).
 __device__ __forceinline__ bool xtab_item(const XtabParams& p, int c, int k, int& s, int& b0, int& b1)
 {
     const int G = gridDim.x;
+    if (p.tail > 0) {
+        const int km = p.mains * p.nslice, head = p.nbatch - p.tail;
+        if (c < km) {
+            if (k > 0) return false;
+            s = c / p.mains;
+            const int u = c % p.mains;
+            b0 = (int)((long long)u * head / p.mains);
+            b1 = (int)((long long)(u + 1) * head / p.mains);
+            return true;
+        }
+        const long long T = (long long)p.nslice * p.tail, E = G - km, e = c - km;
+        const long long lo = e * T / E, hi = (e + 1) * T / E;
+        s = (int)(lo / p.tail) + k;
+        const long long first = (long long)s * p.tail;
+        const long long a = lo > first ? lo : first, z = hi < first + p.tail ? hi : first + p.tail;
+        if (s >= p.nslice || a >= z) return false;
+        b0 = head + (int)(a - first);
+        b1 = head + (int)(z - first);
+        return true;
+    }
     if (p.nslice <= G) {
         if (k > 0) return false;
         const int base = G / p.nslice, extra = G % p.nslice;
@@ -467,7 +497,6 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
     while (have) {
         // ---- the slice's tables: warp w fills byte values w, w + NW, ...
         {
-            if (k_item > 0) load_x(s);
             float x0[4], x1[4];
             if (p.xgu) {   // rounded as the SwiGLU glue kernel rounds it
 #pragma unroll
@@ -535,9 +564,11 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
                     add(yd, nd, compute(std::integral_constant<int, D>{}, it + E + P < nb));
                 }
             });
+        // the next item's first batches and its x are requested before the
+        // barrier (registers only), so they are in flight while the slower
+        // warps finish and the tables are rebuilt
         ++k_item;
         have = xtab_item(p, c, k_item, s, b0, b1);
-        __syncthreads();   // every warp is done with the tables
         nb = have && b1 > b0 + warp ? (b1 - b0 - warp + NW - 1) / NW : 0;
         if (nb > 0) {
             sg = -1;
@@ -549,6 +580,8 @@ __global__ void __launch_bounds__(32 * NW, 1) b4_gemv_xtab_kernel(const XtabPara
             constexpr int D = decltype(dc)::value;
             if (D < nb) issue(dc);
         });
+        if (have) load_x(s);
+        __syncthreads();   // every warp is done with the tables
     }
 }
 

@@ -153,6 +153,57 @@ def test_one_workspace_serves_every_path_in_any_order(cuda, oracle):
     assert load().b4_device_error(1) == 0
 
 
+def _tail_split(S, nb, G, item_cost=45):
+    """The host's choice of tail batches per slice (xtab_tail in b4_gemv.cu),
+    restated to pick test shapes that take the main + tail split."""
+    if S > G or G % S == 0 or nb < 2:
+        return 0
+    k, E = G // S, G - (G // S) * S
+    even = -(-nb // k)
+    best, best_r = even, 0
+    for r in range(1, nb - k + 1):
+        worst = -(-(nb - r) // k)
+        T = S * r
+        for e in range(E):
+            lo, hi = e * T // E, (e + 1) * T // E
+            if hi > lo:
+                worst = max(worst, hi - lo + item_cost * ((hi - 1) // r - lo // r))
+            if worst >= best:
+                break
+        if worst < best:
+            best, best_r = worst, r
+    return best_r if 100 * best < 97 * even else 0
+
+
+@pytest.mark.parametrize("outs,in_f", [([8192], 14336), ([7168, 7168], 8192)])
+def test_xtab_main_and_tail_ctas(cuda, oracle, outs, in_f):
+    """Shapes whose slices divide unevenly over the SMs (56 and 32 slices on
+    148 SMs) run on main CTAs per slice plus tail CTAs whose runs cross slice
+    boundaries (several table builds per CTA, the next item's loads issued
+    before the barrier): every row within tolerance of the oracle, one and
+    two segments."""
+    import torch
+    G = torch.cuda.get_device_properties(cuda).multi_processor_count
+    nb = sum((o + 15) // 16 for o in outs)
+    if _tail_split(in_f // 256, nb, G) == 0:
+        pytest.skip(f"the even split is taken on {G} SMs")
+    rng = np.random.default_rng(sum(outs) + in_f)
+    X = rng.standard_normal((1, in_f)).astype(np.float16)
+    pairs, refs = [], []
+    for o in outs:
+        W = (rng.standard_normal((o, in_f)) * 0.02).astype(np.float32)
+        qw, am = quantised(1, W, cuda)
+        pairs.append((qw, am))
+        refs.append(f64_ref(oracle, 1, qw, am, X))
+    ws = torch.zeros(b4gemv.XTAB_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
+    load().b4_device_error(1)
+    for _ in range(2):
+        ys = b4gemv.gemv_multi(1, pairs, to_dev(X, cuda), ws=ws, pdl=True)
+        for y, ref in zip(ys, refs):
+            assert rel_err(y.cpu().numpy(), ref) < TOL
+    assert load().b4_device_error(1) == 0
+
+
 def test_xtab_multi_segment_one_launch(cuda, oracle):
     """q/k/v-like and ragged segments in one launch through b4_gemv_multi_ws."""
     import torch
