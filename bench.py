@@ -404,20 +404,26 @@ def empty_launch_floor(b4, torch, reps=200):
     return round(sorted(t)[len(t) // 2], 3)
 
 
-def e2e_steps(b4, torch, sets, xs, ys, n_steps, graph=True):
+def e2e_steps(b4, torch, sets, xs, ys, n_steps, graph=True, depth=1):
     """End to end through the public API with host buffers: every step copies
     its x (all seven projections, pinned host) to the device, runs the seven
     GEMVs through b4gemv.gemv_nf4 (the C ABI), copies y back and reads it.
     With `graph`, the seven b4gemv.gemv_nf4 calls of each weight set are
     captured once in a CUDA graph (as a decode loop runs them) and every step
     replays one between its copies; without, every step calls the Python API
-    seven times (its host cost included)."""
+    seven times (its host cost included).  depth 2: the host queues step s + 1
+    before it waits for step s and reads its y (two pinned y buffers; the
+    device work stays in one stream, in step order), so the GPU does not
+    idle while the host synchronises; depth 1: the host waits for every step
+    before it queues the next."""
     inputs = sorted(set(X_GROUP.values()))                # one x per input group
     in_sizes = [SHAPES[i][2] for i in inputs]
     out_sizes = [out_f for _, out_f, _ in SHAPES]
     hx = torch.empty(sum(in_sizes), dtype=torch.float16).pin_memory()
     hx.copy_(torch.cat([xs[i].reshape(-1).cpu() for i in inputs]))
-    hy = torch.empty(sum(out_sizes), dtype=torch.float32).pin_memory()
+    hys = [torch.empty(sum(out_sizes), dtype=torch.float32).pin_memory() for _ in range(depth)]
+    hy = hys[0]
+    done = [torch.cuda.Event() for _ in range(depth)]
     dx = torch.empty_like(hx, device=xs[0].device)
     dy = torch.empty_like(hy, device=xs[0].device)
     xg, yv, o = {}, [], 0
@@ -456,29 +462,141 @@ def e2e_steps(b4, torch, sets, xs, ys, n_steps, graph=True):
             torch.cuda.current_stream().wait_stream(cs)
             graphs.append(g)
 
-    def one(s):
-        nonlocal checksum
+    def queue(s):
         dx.copy_(hx, non_blocking=True)
         if graph:
             graphs[s % N_SETS].replay()
         else:
             gemvs(s)
-        hy.copy_(dy, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        checksum += float(hy[0])
+        hys[s % depth].copy_(dy, non_blocking=True)
+        done[s % depth].record()
 
-    for s in range(3):
-        one(s)
+    def read(s):
+        nonlocal checksum
+        done[s % depth].synchronize()
+        checksum += float(hys[s % depth][0])
+
+    def run(n):
+        for s in range(n):
+            queue(s)
+            if s >= depth - 1:
+                read(s - depth + 1)
+        for s in range(max(0, n - depth + 1), n):
+            read(s)
+
+    run(3)
     torch.cuda.synchronize()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
-    for s in range(n_steps):
-        one(s)
+    run(n_steps)
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
     return ms, hx.numel() * 2, hy.numel() * 4
+
+
+def e2e_overlap(b4, torch, sets, xs, n_steps):
+    """End to end as a serving loop over independent steps runs it: the same
+    public-API calls (b4gemv.gemv_nf4 / gemv_multi, captured once per weight
+    set and buffer in a CUDA graph), every step's x copied in from pinned
+    host memory and its y copied out and read on the host, with two device
+    buffers so that step s + 1's x goes in on one copy stream and step s - 1's
+    y comes out on another while step s computes.  Every wait is an event:
+    step s's GEMVs wait for its x; its x copy waits until step s - 2's GEMVs
+    are done with that buffer, and step s's GEMVs until step s - 2's y has been
+    copied out; the host reads step s - 1's y after it has queued step s.
+    Returns ms for n_steps, h2d and d2h bytes per step."""
+    inputs = sorted(set(X_GROUP.values()))
+    in_sizes = [SHAPES[i][2] for i in inputs]
+    out_sizes = [out_f for _, out_f, _ in SHAPES]
+    dev = xs[0].device
+    hx = torch.empty(sum(in_sizes), dtype=torch.float16).pin_memory()
+    hx.copy_(torch.cat([xs[i].reshape(-1).cpu() for i in inputs]))
+    hys = [torch.empty(sum(out_sizes), dtype=torch.float32).pin_memory() for _ in range(2)]
+    dxs = [torch.empty_like(hx, device=dev) for _ in range(2)]
+    dys = [torch.empty_like(hys[0], device=dev) for _ in range(2)]
+    views = []
+    for b in range(2):
+        xg, o = {}, 0
+        for i, n in zip(inputs, in_sizes):
+            xg[i] = dxs[b][o:o + n].view(1, n)
+            o += n
+        yv, o = [], 0
+        for n in out_sizes:
+            yv.append(dys[b][o:o + n].view(1, n))
+            o += n
+        views.append(([xg[X_GROUP[name]] for name, _, _ in SHAPES], yv))
+
+    def gemvs(k, b, stream=None):
+        xv, yv = views[b]
+        for group in FUSED_STEP:
+            if len(group) == 1:
+                i = group[0]
+                qw, sc = sets[k][i]
+                b4.gemv_nf4(qw, sc, xv[i], yv[i], stream=stream, pdl=True)
+            else:
+                b4.gemv_multi(1, [sets[k][i] for i in group], xv[group[0]], [yv[i] for i in group],
+                              stream=stream, pdl=True)
+
+    for k in range(N_SETS):
+        for b in range(2):
+            gemvs(k, b)
+    torch.cuda.synchronize()
+    graphs = {}
+    for k in range(N_SETS):
+        for b in range(2):
+            g = torch.cuda.CUDAGraph()
+            cs = torch.cuda.Stream()
+            cs.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(g, stream=cs):
+                gemvs(k, b, cs)
+            torch.cuda.current_stream().wait_stream(cs)
+            graphs[(k, b)] = g
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = {name: [torch.cuda.Event() for _ in range(2)] for name in ("x_in", "computed", "y_out")}
+    checksum = 0.0
+
+    def queue(s):
+        b = s % 2
+        with torch.cuda.stream(h2d):
+            if s >= 2:
+                h2d.wait_event(ev["computed"][b])
+            dxs[b].copy_(hx, non_blocking=True)
+            ev["x_in"][b].record(h2d)
+        comp.wait_event(ev["x_in"][b])
+        if s >= 2:
+            comp.wait_event(ev["y_out"][b])
+        graphs[(s % N_SETS, b)].replay()
+        ev["computed"][b].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(ev["computed"][b])
+            hys[b].copy_(dys[b], non_blocking=True)
+            ev["y_out"][b].record(d2h)
+
+    def read(s):
+        nonlocal checksum
+        ev["y_out"][s % 2].synchronize()
+        checksum += float(hys[s % 2][0])
+
+    def run(n):
+        for s in range(n):
+            queue(s)
+            if s >= 1:
+                read(s - 1)
+        read(n - 1)
+        comp.wait_event(ev["y_out"][(n - 1) % 2])
+
+    run(4)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    run(n_steps)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b), hx.numel() * 2, hys[0].numel() * 4
 
 
 def cpu_fused_baseline(sets, xs, budget_s=10.0):
@@ -933,7 +1051,9 @@ def run_single(args, b4, torch, dev, d):
 
     # end to end through the public API with host buffers
     e2e_n = max(3, min(K, 200))
-    e2e_ms, h2d, d2h = e2e_steps(b4, torch, sets, xs, ys, e2e_n)
+    e2e_ms, h2d, d2h = e2e_overlap(b4, torch, sets, xs, e2e_n)
+    e2e_queued_ms, _, _ = e2e_steps(b4, torch, sets, xs, ys, e2e_n, depth=2)
+    e2e_serial_ms, _, _ = e2e_steps(b4, torch, sets, xs, ys, e2e_n)
     e2e_eager_ms, _, _ = e2e_steps(b4, torch, sets, xs, ys, e2e_n, graph=False)
     floor = empty_launch_floor(b4, torch)
 
@@ -970,10 +1090,18 @@ def run_single(args, b4, torch, dev, d):
         "e2e": {"value": round(e2e_n * STEP_BYTES / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "how": "public API b4gemv.gemv_nf4 / gemv_multi (pdl=True) -> C ABI, the step's calls captured "
-                       "once in a CUDA graph and replayed; pinned x copied in and y copied out and read on the "
-                       "host every step", "steps": e2e_n,
+                       "once per weight set and buffer in a CUDA graph and replayed; every step's x copied in "
+                       "from pinned host memory and its y copied out and read on the host, on two copy streams "
+                       "and two device buffers so that step s + 1's x and step s - 1's y move while step s "
+                       "computes (independent steps, as a serving loop over requests)", "steps": e2e_n,
+                "queued_value": round(e2e_n * STEP_BYTES / (e2e_queued_ms / 1e3) / 1e9, 2),
+                "queued_how": "one stream, one device buffer: copy in, GEMVs, copy out in step order, the host "
+                              "queueing step s + 1 before it waits for and reads step s's y",
+                "serial_value": round(e2e_n * STEP_BYTES / (e2e_serial_ms / 1e3) / 1e9, 2),
+                "serial_how": "one stream, the host waiting for each step before it queues the next (a decode "
+                              "loop whose next x depends on this step's y)",
                 "eager_value": round(e2e_n * STEP_BYTES / (e2e_eager_ms / 1e3) / 1e9, 2),
-                "eager_how": "the same with the step's Python API calls made every step"},
+                "eager_how": "the same with the step's Python API calls made every step (serial)"},
         "shape_table": table,
         "empty_launch_floor_us": floor,
         "gpu_launches": K * q["launches_per_step"],
@@ -998,32 +1126,45 @@ def run_single(args, b4, torch, dev, d):
     print(json.dumps(result), flush=True)
 
 
-def tp_e2e(torch, tb, p2p, n_steps):
+def tp_e2e(torch, tb, p2p, n_steps, depth=2):
     """configs[3] end to end: every step copies x and this rank's attention
     shard from pinned host memory, replays the layer graph and copies y back
-    and reads it; ms, h2d and d2h bytes per step."""
+    and reads it; with depth 2 the host queues step s + 1 before it waits for
+    and reads step s's y (two pinned y buffers, device work in one stream in
+    step order).  ms, h2d and d2h bytes per step."""
     hx = tb.x.cpu().pin_memory()
     ha = tb.attn.cpu().pin_memory()
-    hy = torch.empty((1, 8192), dtype=torch.float32).pin_memory()
+    hys = [torch.empty((1, 8192), dtype=torch.float32).pin_memory() for _ in range(depth)]
+    hy = hys[0]
+    done = [torch.cuda.Event() for _ in range(depth)]
     g = tb.graph(p2p, 1)
     y = tb.layer.buf["y"]
 
-    def one():
+    def queue(s):
         tb.x.copy_(hx, non_blocking=True)
         tb.attn.copy_(ha, non_blocking=True)
         g.replay()
-        hy.copy_(y, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        return float(hy[0, 0])
+        hys[s % depth].copy_(y, non_blocking=True)
+        done[s % depth].record()
 
-    for _ in range(3):
-        one()
+    def read(s):
+        done[s % depth].synchronize()
+        return float(hys[s % depth][0, 0])
+
+    def run(n):
+        for s in range(n):
+            queue(s)
+            if s >= depth - 1:
+                read(s - depth + 1)
+        for s in range(max(0, n - depth + 1), n):
+            read(s)
+
+    run(3)
     tb.d.barrier()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(n_steps):
-        one()
+    run(n_steps)
     b.record()
     torch.cuda.synchronize()
     tb.d.barrier()
@@ -1130,7 +1271,8 @@ def run_multi(args, b4, torch, dev, d):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_n,
                 "how": "per step and rank: x and the rank's attention shard copied in from pinned host memory, "
                        "the layer (TPDecodeLayer, C ABI calls captured in a CUDA graph) replayed, y copied out "
-                       "and read on the host; max over ranks"},
+                       "and read on the host, the host queueing step s + 1 before it waits for step s; max "
+                       "over ranks"},
         "gpu_launches": steps * (4 if tb.glue_fused else 6),
         "clocks": clocks,
     }
