@@ -63,7 +63,7 @@ class Problem:
         self.y = torch.empty((m, out_f), device=dev)
         self.fmt, self.out_f, self.in_f, self.m = fmt, out_f, in_f, m
         self.ptrs = [(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(s.data_ptr())) for q, s in self.copies]
-        # one zero-filled workspace for the split configs (every call leaves it zeroed)
+        # one zero-filled workspace for every config (each call leaves it ready for the next)
         self.ws = torch.zeros(WS_BYTES, dtype=torch.uint8, device=dev)
 
     def launch(self, k, cfg, stream):
