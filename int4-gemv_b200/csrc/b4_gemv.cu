@@ -1501,8 +1501,9 @@ int b4_gemv_default_config_ws(int fmt, int in_f, int out_f, int m, b4_gemv_confi
 
 // The workspace of b4_gemv_ws: its first B4_XTAB_WORKSPACE_BYTES hold the
 // x-pair table kernel's running counters, the split and k-slice paths use
-// what follows (their counters and partials are zero between calls), so one
-// workspace may serve every path.
+// what follows (the split path's arrival counters are zero between calls,
+// its partial sums are written before they are read, and the k-slice sum
+// clears its partials), so one workspace may serve every path.
 void* ws_past_counters(void* ws, size_t ws_bytes, size_t* rest)
 {
     if (!ws || ws_bytes < B4_XTAB_WORKSPACE_BYTES) {

@@ -5,7 +5,8 @@ The split kernels cut a matrix into equal runs of (16-row block, k-step) units
 per warp and add a block's pieces through a workspace; these tests check y
 against the double-precision GEMV over the same dequantised weights (TOL, the
 north-star bar), against the unsplit kernels, bit-identical repeats, the
-workspace left zeroed after every call, and the argument checks.
+arrival counters (after the workspace's first 256 bytes) left zero after
+every call, and the argument checks.
 """
 from __future__ import annotations
 
