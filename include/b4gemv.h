@@ -45,7 +45,11 @@ extern "C" {
 #define B4_FMT_INT4_G128 0
 #define B4_FMT_NF4_B64 1
 
-#define B4_ABI_VERSION 7
+/* 8: a b4_gemv_ws workspace keeps the x-pair table kernel's running counters
+ *    in its first 256 bytes (equal, not zero, between calls), and the split
+ *    and k-slice workspace sizes include them; the b4_p2p allocation holds
+ *    one copy of the call counter per CTA index. */
+#define B4_ABI_VERSION 8
 
 /* Same type as cudaStream_t, spelled without the CUDA headers. */
 typedef struct CUstream_st* b4_stream_t;

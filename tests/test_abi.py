@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
         assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
-    assert lib.b4_abi_version() == 7
+    assert lib.b4_abi_version() == 8
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
