@@ -1111,9 +1111,10 @@ bool xtab_buffers(const b4_gemv_segment* segs, int nseg)
 // exactly for every tail; the tail split is taken where it beats the even
 // split by 3 %.  Returns tail (0: the even split), cached per shape.
 // A further item's cost in batches, fitted on B200 over the Qwen2.5-7B and
-// Llama-3-70B (tp 1, 2, 4, 8) NF4 shapes: 40-50 were within 2 % of the best
-// on each, 45 the best overall (Llama-3-70B gate/up 59.4 -> 53.4 us, down
-// 35.9 -> 31.0, tp 2 gate/up 32.0 -> 29.1, tp 2 down 20.4 -> 18.6).
+// Llama-3-70B (tp 1, 2, 4, 8) NF4 shapes with values from 15 to 90: 45 was
+// the best overall, 40 and 50 each lost up to 5 % on some shape (with 45:
+// Llama-3-70B gate/up 59.4 -> 53.4 us, down 35.9 -> 31.0, tp 2 gate/up
+// 32.0 -> 29.1, tp 2 down 20.4 -> 18.6).
 constexpr int kXtabItemCost = 45;
 
 int xtab_tail(int S, int nb, int G, int item_cost)
